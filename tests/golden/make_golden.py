@@ -1,0 +1,361 @@
+"""Generate golden vectors by running the reference's own Python code.
+
+Usage::
+
+    python tests/golden/make_golden.py --ref-src <vibecheck checkout>/src
+
+Imports ``vibecheck`` from the given source tree (with an empty ``gurobipy``
+stub: only ``gurobi_util.py:22`` imports it at module level and the bound
+path never calls it), runs the hot-path functions on small seeded cases on
+CPU, and writes ``tests/golden/*.npz``.  The committed fixtures are what the
+CPU tests check the oracle against; the reference itself is not needed at
+test time.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import types
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+
+def _import_reference(src):
+    sys.modules.setdefault('gurobipy', types.ModuleType('gurobipy'))
+    sys.path.insert(0, src)
+    import torch
+    torch.set_num_threads(4)
+    import vibecheck.verify_zono_bnb as vz
+    import vibecheck.verify_graph as vg
+    import vibecheck.verify_hybrid_acasxu as vh
+    import vibecheck.settings as vs
+    import vibecheck.spec as vspec
+    return vz, vg, vh, vs, vspec
+
+
+def _t(a, dtype):
+    import torch
+    return torch.as_tensor(np.asarray(a), dtype=dtype)
+
+
+def _n(t):
+    return t.detach().cpu().numpy()
+
+
+def _save(name, **arrays):
+    path = os.path.join(HERE, name + '.npz')
+    np.savez_compressed(path, **arrays)
+    print('wrote', path, sum(a.nbytes for a in arrays.values()), 'bytes raw')
+
+
+def _net_arrays(layers):
+    out = {}
+    for i, (W, b) in enumerate(layers):
+        out[f'W{i}'] = np.asarray(W, np.float32)
+        out[f'b{i}'] = np.asarray(b, np.float32)
+    out['n_layers'] = np.array(len(layers))
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--ref-src', required=True)
+    args = ap.parse_args()
+    vz, vg, vh, vs, vspec = _import_reference(args.ref_src)
+    import torch
+    from vibecheck_nn_b200 import workloads as wk
+
+    # ------------------------------------------------------------------ slopes
+    lo = np.array([1.0, 2.0, -3.0, -2.0, -1.0, 1.0, -1.0, -3.0, 0.0, -0.0,
+                   -5e-9, -1e-9, -0.2, -0.7], np.float32)
+    hi = np.array([3.0, 4.0, -1.0, -0.5, 3.0, 2.0, 1.0, -1.0, 0.0, 0.3,
+                   -1e-9, 0.0, 0.6, 0.3], np.float32)
+    rng = np.random.default_rng(11)
+    rl = rng.normal(size=200).astype(np.float32)
+    rh = (rl + np.abs(rng.normal(size=200))).astype(np.float32)
+    lo = np.concatenate([lo, rl])
+    hi = np.concatenate([hi, rh])
+    res = vz._make_slopes(_t(lo, torch.float32), _t(hi, torch.float32))
+    _save('slopes', lo=lo, hi=hi, lo_s=_n(res[0]), up_s=_n(res[1]),
+          up_t=_n(res[2]), active=_n(res[3]), dead=_n(res[4]),
+          unstable=_n(res[5]))
+
+    # --------------------------------------------- IBP + CROWN, small + ACAS
+    for tag, dims, B, Q, seed in (('small', (6, 9, 7, 4), 5, 3, 1),
+                                  ('acas', wk.ACAS_DIMS, 24, 4, 2)):
+        rng = np.random.default_rng(seed)
+        layers = wk.mlp_params(dims, rng)
+        centre = rng.uniform(-0.5, 0.5, (B, dims[0]))
+        half = rng.uniform(0.001, 0.3, (B, dims[0]))
+        xl = (centre - half).astype(np.float32)
+        xh = (centre + half).astype(np.float32)
+        SW = rng.integers(-1, 2, (Q, dims[-1])).astype(np.float32)
+        Sb = rng.normal(size=Q).astype(np.float32)
+        # clamps on layer 0: two neurons ON/OFF in alternating domains
+        n0 = dims[1]
+        cl = np.full((B, n0), -np.inf, np.float32)
+        ch = np.full((B, n0), np.inf, np.float32)
+        cl[::2, 0] = 0.0
+        ch[1::2, 0] = 0.0
+        ch[::3, 1] = 0.0
+        out = dict(_net_arrays(layers), xl=xl, xh=xh, spec_W=SW, spec_b=Sb,
+                   clamp_lo0=cl, clamp_hi0=ch)
+        for bits, dt in ((32, torch.float32), (64, torch.float64)):
+            gg = wk.mlp_gg(layers, 'cpu', dt)
+            spec_ew = {q: (_t(SW[q], dt), float(Sb[q])) for q in range(Q)}
+            txl, txh = _t(xl, dt), _t(xh, dt)
+            sb = vz._ibp_forward_graph_batched(txl, txh, gg, 'cpu', dt)
+            for L, (l_, h_) in sb.items():
+                out[f'ibp{bits}_lo{L}'] = _n(l_)
+                out[f'ibp{bits}_hi{L}'] = _n(h_)
+            lb, A, acc = vz._spec_backward_graph_batched(
+                sb, txl, txh, gg, spec_ew, 'cpu', dt, return_input_linear=True)
+            out[f'crown{bits}_lb'] = _n(lb)
+            out[f'crown{bits}_A'] = _n(A)
+            out[f'crown{bits}_acc'] = _n(acc)
+            sbc = vz._ibp_forward_graph_batched(
+                txl, txh, gg, 'cpu', dt,
+                relu_clamps={0: (_t(cl, dt), _t(ch, dt))})
+            for L, (l_, h_) in sbc.items():
+                out[f'ibpc{bits}_lo{L}'] = _n(l_)
+                out[f'ibpc{bits}_hi{L}'] = _n(h_)
+            lbc = vz._spec_backward_graph_batched(sbc, txl, txh, gg, spec_ew,
+                                                  'cpu', dt)
+            out[f'crownc{bits}_lb'] = _n(lbc)
+            # zonotope forward + CROWN intermediates + spec on them
+            zsb, (zc, zG) = vz._forward_zonotope_graph_batched(
+                txl, txh, gg, 'cpu', dt)
+            for L, (l_, h_) in zsb.items():
+                out[f'zono{bits}_lo{L}'] = _n(l_)
+                out[f'zono{bits}_hi{L}'] = _n(h_)
+            out[f'zono{bits}_c'] = _n(zc)
+            if bits == 32:
+                out[f'zono{bits}_G'] = _n(zG)
+            tight = vz._crown_intermediate_batched(gg, txl, txh, 'cpu', dt)
+            for L, (l_, h_) in tight.items():
+                out[f'interm{bits}_lo{L}'] = _n(l_)
+                out[f'interm{bits}_hi{L}'] = _n(h_)
+            lbi, Ai, acci = vz._spec_backward_graph_batched(
+                tight, txl, txh, gg, spec_ew, 'cpu', dt,
+                return_input_linear=True)
+            out[f'spec_interm{bits}_lb'] = _n(lbi)
+            out[f'spec_interm{bits}_A'] = _n(Ai)
+            out[f'spec_interm{bits}_acc'] = _n(acci)
+            # alpha-CROWN on the input-split leaves
+            lba = vz._run_alpha_crown_inputsplit_batched(
+                txl, txh, gg, spec_ew, 'cpu', dt, n_iters=6, lr=0.25,
+                lr_decay=0.98)
+            out[f'alpha{bits}_lb'] = _n(lba)
+        _save(f'mlp_{tag}', **out)
+
+    # zero-radius input dim (generator dropping) ------------------------------
+    rng = np.random.default_rng(5)
+    layers = wk.mlp_params((4, 6, 3), rng)
+    xl = rng.uniform(-1, 0, (3, 4)).astype(np.float32)
+    xh = (xl + rng.uniform(0.1, 1, (3, 4))).astype(np.float32)
+    xh[:, 2] = xl[:, 2]
+    gg = wk.mlp_gg(layers, 'cpu', torch.float32)
+    zsb, (zc, zG) = vz._forward_zonotope_graph_batched(
+        _t(xl, torch.float32), _t(xh, torch.float32), gg, 'cpu', torch.float32)
+    _save('zono_zero_radius', **_net_arrays(layers), xl=xl, xh=xh,
+          lo0=_n(zsb[0][0]), hi0=_n(zsb[0][1]), c=_n(zc), G=_n(zG))
+
+    # --------------------------------------------------------------- clipping
+    rng = np.random.default_rng(7)
+    B, Q, n = 40, 3, 5
+    xl = rng.uniform(-1, 0, (B, n)).astype(np.float32)
+    xh = (xl + rng.uniform(0.05, 1, (B, n))).astype(np.float32)
+    A = rng.normal(size=(B, Q, n)).astype(np.float32)
+    A[0, 0, 1] = 0.0
+    A[1, :, 2] = 1e-13
+    bb = rng.normal(size=(B, Q)).astype(np.float32)
+    xl2, xh2, feas = vg._clip_box_by_halfspaces_batched(
+        _t(xl, torch.float32), _t(xh, torch.float32), _t(A, torch.float32),
+        _t(bb, torch.float32))
+    _save('clip', xl=xl, xh=xh, A=A, b=bb, xl_new=_n(xl2), xh_new=_n(xh2),
+          feasible=_n(feas))
+
+    # ------------------------------------------------- alpha-CROWN on domains
+    # The alpha loop of verify_milp._ibp_crown_bab (:2762-2807) with beta
+    # held at zero, restated with the reference's own kernels + torch Adam.
+    rng = np.random.default_rng(9)
+    dims = (12, 16, 16, 16, 5)
+    layers = wk.mlp_params(dims, rng)
+    x0 = rng.uniform(0, 1, dims[0])
+    xl1 = np.clip(x0 - 0.08, 0, 1).astype(np.float32)
+    xh1 = np.clip(x0 + 0.08, 0, 1).astype(np.float32)
+    y0 = wk._mlp_forward64(layers, x0[None])[0]
+    t_lab = int(np.argmax(y0))
+    SW, Sb = wk.margin_rows(dims[-1], t_lab)
+    gg = wk.mlp_gg(layers, 'cpu', torch.float32)
+    dt = torch.float32
+    root = vz._ibp_forward_graph_batched(_t(xl1[None], dt), _t(xh1[None], dt),
+                                         gg, 'cpu', dt)
+    picked, clamps = wk.split_domains(
+        {L: _n(v[0][0]) for L, v in root.items()},
+        {L: _n(v[1][0]) for L, v in root.items()}, 3)
+    D = 1 << len(picked)
+    xl = np.broadcast_to(xl1, (D, dims[0])).copy()
+    xh = np.broadcast_to(xh1, (D, dims[0])).copy()
+    txl, txh = _t(xl, dt), _t(xh, dt)
+    rc = {L: (_t(c_[0], dt), _t(c_[1], dt)) for L, c_ in clamps.items()}
+    sb = vz._ibp_forward_graph_batched(txl, txh, gg, 'cpu', dt, relu_clamps=rc)
+    alpha = {}
+    for L, (l_, h_) in sb.items():
+        _, up_s, _, _, _, unst = vz._make_slopes(l_, h_)
+        alpha[L] = ((up_s > 0.5).to(dt) * unst.to(dt)).clone().requires_grad_(True)
+    spec_ew = {q: (_t(SW[q], dt), float(Sb[q])) for q in range(SW.shape[0])}
+    opt = torch.optim.Adam(list(alpha.values()), lr=0.1)
+    best = None
+    for _ in range(8):
+        opt.zero_grad()
+        lbs = vz._spec_backward_graph_batched(sb, txl, txh, gg, spec_ew, 'cpu',
+                                              dt, alpha_at_layer=alpha)
+        best = lbs.detach().clone() if best is None else torch.maximum(
+            best, lbs.detach())
+        if (best > 0).all():
+            break
+        (-lbs.sum()).backward()
+        opt.step()
+        with torch.no_grad():
+            for L in alpha:
+                alpha[L].clamp_(0.0, 1.0)
+    clamp_arrays = {}
+    for L, (c0, c1) in clamps.items():
+        clamp_arrays[f'clamp_lo{L}'] = c0
+        clamp_arrays[f'clamp_hi{L}'] = c1
+    _save('alpha_domains', **_net_arrays(layers), **clamp_arrays, xl=xl, xh=xh,
+          spec_W=SW, spec_b=Sb, n_iters=np.array(8), lr=np.array(0.1),
+          best_lb=_n(best))
+
+    # ------------------------------------------------------------------- conv
+    rng = np.random.default_rng(13)
+    k1 = (rng.standard_normal((4, 2, 3, 3)) * 0.4).astype(np.float32)
+    b1 = (rng.standard_normal(4) * 0.01).astype(np.float32)
+    W2 = (rng.standard_normal((6, 4 * 4 * 4)) * 0.2).astype(np.float32)
+    b2 = (rng.standard_normal(6) * 0.01).astype(np.float32)
+    W3 = (rng.standard_normal((3, 6)) * 0.5).astype(np.float32)
+    b3 = (rng.standard_normal(3) * 0.01).astype(np.float32)
+    ins = (2, 8, 8)
+    ggc = _small_cnn_gg(k1, b1, W2, b2, W3, b3, ins, dt)
+    B = 4
+    x0 = rng.uniform(0, 1, (B, int(np.prod(ins))))
+    xl = (x0 - 0.05).astype(np.float32)
+    xh = (x0 + 0.05).astype(np.float32)
+    SW = rng.integers(-1, 2, (2, 3)).astype(np.float32)
+    Sb = np.zeros(2, np.float32)
+    txl, txh = _t(xl, dt), _t(xh, dt)
+    spec_ew = {q: (_t(SW[q], dt), float(Sb[q])) for q in range(2)}
+    sb = vz._ibp_forward_graph_batched(txl, txh, ggc, 'cpu', dt)
+    lb, A, acc = vz._spec_backward_graph_batched(sb, txl, txh, ggc, spec_ew,
+                                                 'cpu', dt,
+                                                 return_input_linear=True)
+    zsb, (zc, zG) = vz._forward_zonotope_graph_batched(txl, txh, ggc, 'cpu', dt)
+    out = dict(k1=k1, b1=b1, W2=W2, b2=b2, W3=W3, b3=b3, xl=xl, xh=xh,
+               spec_W=SW, spec_b=Sb, lb=_n(lb), A=_n(A), acc=_n(acc),
+               zc=_n(zc))
+    for L, (l_, h_) in sb.items():
+        out[f'ibp_lo{L}'] = _n(l_)
+        out[f'ibp_hi{L}'] = _n(h_)
+    for L, (l_, h_) in zsb.items():
+        out[f'zono_lo{L}'] = _n(l_)
+        out[f'zono_hi{L}'] = _n(h_)
+    _save('conv_small', **out)
+
+    # ---------------------------------------------------------- batched PGD
+    rng = np.random.default_rng(17)
+    layers = wk.mlp_params((5, 20, 20, 4), rng)
+    gg = wk.mlp_gg(layers, 'cpu', dt)
+    Bp, R = 6, 16
+    c_ = rng.uniform(-0.5, 0.5, (Bp, 5))
+    h_ = rng.uniform(0.05, 0.3, (Bp, 5))
+    xl = (c_ - h_).astype(np.float32)
+    xh = (c_ + h_).astype(np.float32)
+    pts = xl[:, None, :] + (xh - xl)[:, None, :] * rng.random((Bp, 64, 5))
+    ys = wk._mlp_forward64(layers, pts.reshape(-1, 5).astype(np.float64))
+    spec_results = {}
+    for tag, thr in (('unsat', float(ys[:, 0].max() + 0.2)),
+                     ('sat', float(np.median(ys[:, 0])))):
+        spec = vspec.VNNSpec(
+            x_lo=xl[0].astype(np.float64), x_hi=xh[0].astype(np.float64),
+            disjuncts=[vspec.Conjunct([vspec.Constraint(0, '>=', thr)]),
+                       vspec.Conjunct([vspec.PairwiseConstraint(1, 2),
+                                       vspec.Constraint(3, '<=', -50.0)])])
+        torch.manual_seed(0)
+        lo_e = _t(xl, dt).unsqueeze(1).expand(Bp, R, 5).reshape(Bp * R, 5)
+        hi_e = _t(xh, dt).unsqueeze(1).expand(Bp, R, 5).reshape(Bp * R, 5)
+        x_init = lo_e + (hi_e - lo_e) * torch.rand(Bp * R, 5, dtype=dt)
+        sat, wit = vh._simple_pgd_batched(_t(xl, dt), _t(xh, dt), spec, gg, 4,
+                                          torch.device('cpu'), dt,
+                                          n_restarts=R, n_iter=30, lr=0.1,
+                                          seed=0)
+        spec_results[f'{tag}_thr'] = np.array(thr)
+        spec_results[f'{tag}_sat'] = np.array(bool(sat))
+        spec_results[f'{tag}_witness'] = (np.zeros(5, np.float32) if wit is None
+                                          else np.asarray(wit, np.float32))
+        spec_results[f'{tag}_x_init'] = _n(x_init)
+    _save('pgd', **_net_arrays(layers), xl=xl, xh=xh, R=np.array(R),
+          n_iter=np.array(30), **spec_results)
+
+    # --------------------------------------------------- full BaB driver cfg1
+    for seed in (0, 1):
+        w = wk.cfg1(seed)
+        gg = wk.mlp_gg(w['layers'], 'cpu', torch.float32)
+        spec = vspec.VNNSpec(
+            x_lo=w['xl'].astype(np.float64), x_hi=w['xh'].astype(np.float64),
+            disjuncts=[vspec.Conjunct([vspec.PairwiseConstraint(pred=1,
+                                                                comp=0)])])
+        res = {}
+        for ci, crown_i in ((1, True), (0, False)):
+            st = vs.default_settings(
+                device='cpu', bits=32, input_split_batched_enabled=True,
+                input_split_batch_size=2048, input_split_crown_intermediate=crown_i,
+                disable_sat_finding=True, total_timeout=600.0)
+            verdict, det = vg._input_split_batched(
+                types.SimpleNamespace(onnx_path=None), spec, st, gg,
+                torch.device('cpu'), torch.float32)
+            res[f'verdict_ci{ci}'] = np.array(verdict)
+            res[f'n_leaves_ci{ci}'] = np.array(det.get('batched_n_leaves', -1))
+            res[f'n_iters_ci{ci}'] = np.array(det.get('batched_n_iters', -1))
+            print('cfg1 seed', seed, 'crown_interm', crown_i, verdict, det)
+        _save(f'bab_cfg1_seed{seed}', **_net_arrays(w['layers']), xl=w['xl'],
+              xh=w['xh'], d=np.array(w['d']), **res)
+
+
+def _small_cnn_gg(k1, b1, W2, b2, W3, b3, ins, dt):
+    import torch
+    from vibecheck_nn_b200 import workloads as wk
+    stride, pad = (2, 2), (1, 1)
+    Ho, Wo = wk.conv_out_hw(ins[1], ins[2], k1.shape[2:], stride, pad)
+    out_shape = (k1.shape[0], Ho, Wo)
+    oph = ins[1] - ((Ho - 1) * stride[0] - 2 * pad[0] + k1.shape[2])
+    opw = ins[2] - ((Wo - 1) * stride[1] - 2 * pad[1] + k1.shape[3])
+    ops = [
+        {'name': 'conv0', 'type': 'conv', 'inputs': ['x'],
+         'kernel': torch.as_tensor(k1, dtype=dt),
+         'bias': torch.as_tensor(b1, dtype=dt),
+         'kernel_np': k1.astype(np.float64), 'bias_np': b1.astype(np.float64),
+         'in_shape': ins, 'out_shape': out_shape, 'stride': stride,
+         'padding': pad, 'output_padding': (oph, opw),
+         'n_out': int(np.prod(out_shape))},
+        {'name': 'relu0', 'type': 'relu', 'inputs': ['conv0'], 'layer_idx': 0},
+        {'name': 'flat', 'type': 'reshape', 'inputs': ['relu0']},
+        {'name': 'fc0', 'type': 'fc', 'inputs': ['flat'],
+         'W': torch.as_tensor(W2, dtype=dt), 'bias': torch.as_tensor(b2, dtype=dt),
+         'W_np': W2.astype(np.float64), 'bias_np': b2.astype(np.float64)},
+        {'name': 'relu1', 'type': 'relu', 'inputs': ['fc0'], 'layer_idx': 1},
+        {'name': 'fc1', 'type': 'fc', 'inputs': ['relu1'],
+         'W': torch.as_tensor(W3, dtype=dt), 'bias': torch.as_tensor(b3, dtype=dt),
+         'W_np': W3.astype(np.float64), 'bias_np': b3.astype(np.float64)},
+    ]
+    return {'ops': ops, 'relu_names': ['relu0', 'relu1'], 'fork_points': set(),
+            'n_relu': 2, 'input_name': 'x', 'input_n': int(np.prod(ins)),
+            'input_shape': (1,) + tuple(ins)}
+
+
+if __name__ == '__main__':
+    main()
