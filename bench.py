@@ -1,0 +1,377 @@
+#!/usr/bin/env python
+"""Benchmark: CROWN subdomain-bound throughput (cfg2) on B200.
+
+Workload (the headline metric's single-GPU config):
+a seeded 5->[50]x6->5 fp32 ReLU MLP (ACAS-Xu shape), 65,536 sub-boxes per
+step (centre U(-0.5,0.5), half-width U(0.001,0.1)), 4 spec rows with
+coefficients in {-1,0,1}; one step = IBP intermediate bounds + CROWN
+back-substitution for every box (one fused kernel launch, vcb_mlp_crown).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU; every rank bounds its own
+65,536 boxes (weak scaling, no data-path collective); the time is the max
+over ranks.  ``--impl reference`` times the CPU restatement of the
+reference's algorithm (oracle/, numpy, all host cores) on a bounded sample of
+the same workload.  Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = 'subdomain bounds/sec (CROWN, batched input-split)'
+UNIT = 'subdomains/s'
+N_BOXES = 65536
+N_Q = 4
+FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=200)
+    ap.add_argument('--warmup', type=int, default=10)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the oracle (numpy restatement of the reference algorithm)
+# ---------------------------------------------------------------------------
+
+_WORKER = {}
+
+
+def _cpu_worker(args):
+    os.environ['OMP_NUM_THREADS'] = '1'
+    os.environ['OPENBLAS_NUM_THREADS'] = '1'
+    lo, hi = args
+    from oracle import bounds as ob
+    if 'w' not in _WORKER:
+        from vibecheck_nn_b200 import workloads as wk
+        _WORKER['w'] = wk.cfg2(seed=0, n_boxes=N_BOXES, n_q=N_Q)
+        _WORKER['gg'] = wk.mlp_gg(_WORKER['w']['layers'])
+    w, gg = _WORKER['w'], _WORKER['gg']
+    t0 = time.perf_counter()
+    sb = ob.ibp_forward_batched(w['xl'][lo:hi], w['xh'][lo:hi], gg)
+    ob.spec_backward_batched(sb, w['xl'][lo:hi], w['xh'][lo:hi], gg,
+                             w['spec_W'], w['spec_b'])
+    return time.perf_counter() - t0
+
+
+def cpu_rate(pool, cores, sample):
+    """Boxes/s of the oracle on `sample` boxes split over `cores` processes."""
+    per = (sample + cores - 1) // cores
+    chunks = [(i * per, min(sample, (i + 1) * per)) for i in range(cores)]
+    t0 = time.perf_counter()
+    pool.map(_cpu_worker, chunks)
+    return sample / (time.perf_counter() - t0)
+
+
+def make_pool():
+    import multiprocessing as mp
+    cores = os.cpu_count() or 1
+    pool = mp.get_context('spawn').Pool(cores)
+    pool.map(_cpu_worker, [(0, 64)] * cores)  # import + warm each worker
+    return pool, cores
+
+
+def cpu_baseline(pool, cores, budget_s=12.0):
+    sample = 4096 * cores
+    rates = []
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or len(rates) < 2:
+        rates.append(cpu_rate(pool, cores, sample))
+    return {'value': statistics.median(rates), 'unit': UNIT, 'cores': cores,
+            'kind': 'port',
+            'sample': f'{sample} of the 65,536 cfg2 boxes per repetition, '
+                      f'{len(rates)} repetitions (median), numpy oracle '
+                      f'(oracle/bounds.py) in {cores} spawn processes'}
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    pool, cores = make_pool()
+    sample = 4096 * cores
+    for _ in range(args.warmup):
+        cpu_rate(pool, cores, sample)
+    rates = [cpu_rate(pool, cores, sample) for _ in range(args.steps)]
+    pool.close()
+    v = statistics.median(rates)
+    line = {
+        'impl': 'reference', 'metric': METRIC, 'value': v, 'unit': UNIT,
+        'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': 1000.0 * N_BOXES / v, 'higher_is_better': True,
+        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+        'data': 'synthetic (seeded)',
+        'config': config_dict(args.gpus),
+        'cpu_baseline': {'value': v, 'unit': UNIT, 'cores': cores,
+                         'kind': 'port',
+                         'sample': f'each step: {sample} cfg2 boxes, numpy '
+                                   f'oracle in {cores} spawn processes'},
+        'e2e': {'value': v, 'unit': UNIT, 'h2d_bytes_per_step': 0,
+                'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(n):
+    return {'workload': 'cfg2: CROWN microbench, 5x[50]x6x5 fp32 ReLU MLP, '
+                        'IBP intermediates + CROWN back-substitution',
+            'boxes_per_gpu': N_BOXES, 'spec_rows': N_Q,
+            'global_batch': N_BOXES * n,
+            'l2': 'flushed (256 MiB write) between timed steps',
+            'parallelism': f'{n} GPU(s), boxes sharded, no data-path collective'}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ('clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,'
+              'clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,'
+              'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', '-i', str(self.gpu_id),
+                 f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                 '-lms', '20'], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown',
+                 'sw_power_cap']
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(',')]
+            if len(parts) != 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[2:]):
+                if v.lower() == 'active':
+                    reasons.add(nm)
+        if not sm:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': [],
+                    'samples': 0}
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(mx),
+                'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+
+def read_traffic():
+    """Per-launch DRAM bytes of vcb_mlp_crown on cfg2 from the committed ncu
+    summary (profiles/crown_mlp_cfg2.md, line 'traffic_bytes_per_launch: N')."""
+    path = os.path.join(ROOT, 'profiles', 'crown_mlp_cfg2.md')
+    try:
+        for ln in open(path):
+            if ln.startswith('traffic_bytes_per_launch:'):
+                return float(ln.split(':', 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+def measured_fp32_peak(dev):
+    """TFLOP/s of the FFMA probe kernel (vcb_probe_ffma) on this GPU now."""
+    import torch
+    from vibecheck_nn_b200 import _lib
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks = sms * 8
+    iters = 4096
+    out = torch.empty(blocks * 256, device=dev)
+    st = _lib.stream_of(dev)
+    best = 0.0
+    for _ in range(5):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        _lib.check(_lib.lib().vcb_probe_ffma(_lib.ptr(out), blocks, iters, st))
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1)
+        best = max(best, blocks * 256.0 * iters * 128 / (ms * 1e-3) / 1e12)
+    return best
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    pool = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        pool, cores = make_pool()  # spawn before the first GPU call
+    dev = torch.device(f'cuda:{local}')
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', timeout=timedelta(seconds=120),
+                                device_id=dev)
+    from vibecheck_nn_b200 import ops, workloads as wk
+    w = wk.cfg2(seed=0, n_boxes=N_BOXES, n_q=N_Q)
+    gg = wk.mlp_gg(w['layers'], dev)
+    spec = ops.spec_matrix(wk.spec_ew_from(w['spec_W'], w['spec_b'], dev), dev)
+    xl = torch.as_tensor(w['xl'], device=dev)
+    xh = torch.as_tensor(w['xh'], device=dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return ops.ibp_crown_batched(xl, xh, gg, spec, dev)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    peak = measured_fp32_peak(dev)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    props = torch.cuda.get_device_properties(dev)
+    gpu_id = getattr(props, 'uuid', None)
+    gpu_id = f'GPU-{gpu_id}' if gpu_id is not None else local
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(gpu_id) as clk:
+        t_wall0 = time.perf_counter()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+        t_wall = time.perf_counter() - t_wall0
+    if world > 1:
+        dist.barrier()
+    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    t_ms = sum(per_step)
+    t_max = torch.tensor([t_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    t_max = float(t_max.item())
+    value = world * N_BOXES * args.steps / (t_max * 1e-3)
+
+    # ---- e2e through the public API with host buffers (pinned)
+    xl_h = torch.as_tensor(w['xl']).pin_memory()
+    xh_h = torch.as_tensor(w['xh']).pin_memory()
+    lb_h = torch.empty((N_BOXES, N_Q), dtype=torch.float32).pin_memory()
+    xl_d = torch.empty_like(xl)
+    xh_d = torch.empty_like(xh)
+    for _ in range(3):
+        xl_d.copy_(xl_h, non_blocking=True)
+        xh_d.copy_(xh_h, non_blocking=True)
+        lb_h.copy_(ops.ibp_crown_batched(xl_d, xh_d, gg, spec, dev), non_blocking=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        xl_d.copy_(xl_h, non_blocking=True)
+        xh_d.copy_(xh_h, non_blocking=True)
+        lb_h.copy_(ops.ibp_crown_batched(xl_d, xh_d, gg, spec, dev), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    e2e_value = world * N_BOXES * args.steps / (float(e2e_ms.item()) * 1e-3)
+
+    sum_w = sum(a * b for a, b in zip((5,) + (50,) * 6, (50,) * 6 + (5,)))
+    flop_per_box = (4 + 2 * N_Q) * sum_w
+    mean_ms = t_ms / args.steps
+    achieved = N_BOXES * flop_per_box / (mean_ms * 1e-3) / 1e12
+    cpu = None
+    if pool is not None:
+        cpu = cpu_baseline(pool, cores)
+        pool.close()
+    if rank == 0:
+        line = {
+            'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world,
+            'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': t_max / args.steps, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic (seeded numpy rng; no public dataset for this path)',
+            'config': config_dict(world),
+            'e2e': {'value': e2e_value, 'unit': UNIT,
+                    'h2d_bytes_per_step': int(xl_h.numel() * 4 * 2),
+                    'd2h_bytes_per_step': int(lb_h.numel() * 4)},
+            'gpu_launches': args.steps,
+            'roofline': {'bound': 'fp32_simt', 'achieved': achieved,
+                         'peak': peak, 'unit': 'TFLOP/s',
+                         'frac': achieved / peak if peak else None,
+                         'traffic': read_traffic(),
+                         'kernel': 'vcb_mlp_crown (crown_mlp_kernel)',
+                         'flop_per_box': flop_per_box,
+                         'peak_source': 'measured live: vcb_probe_ffma FFMA '
+                                        'loop (MEASURED_PEAKS.json has no '
+                                        'FP32 SIMT figure)'},
+            'clocks': clk.summary(),
+            'wall_s_timed_region': t_wall,
+        }
+        if cpu is not None:
+            line['cpu_baseline'] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == '__main__':
+    main()

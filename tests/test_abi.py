@@ -1,0 +1,95 @@
+"""CPU checks of the C ABI and the host-side lowering (no GPU compute)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from vibecheck_nn_b200 import _lib, netdesc, workloads as wk
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    src = open(os.path.join(ROOT, 'include', 'vcb.h')).read()
+    src = re.sub(r'/\*.*?\*/', '', src, flags=re.S)
+    return sorted(set(re.findall(r'^\s*(?:int|const char\*)\s+(vcb_\w+)\s*\(',
+                                 src, flags=re.M)))
+
+
+def test_library_builds_and_loads():
+    from vibecheck_nn_b200 import build
+    build.build()
+    lib = _lib.lib()
+    assert lib.vcb_version() >= 100
+
+
+def test_exports_every_header_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    names = header_functions()
+    assert 'vcb_mlp_crown' in names
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f'{name} missing from _lib.SIGNATURES'
+
+
+def test_invalid_arguments_return_status_not_crash():
+    lib = _lib.lib()
+    rc = lib.vcb_mlp_crown(None, 4, None, None, None, None, None, None, None,
+                           None, 1, None, None, None, None, None, None, None,
+                           None)
+    assert rc == _lib.VCB_ERR_INVALID
+    assert 'NULL' in _lib.last_error()
+    with pytest.raises(ValueError):
+        _lib.check(rc, 'x')
+    s = _lib.VcbMlp()
+    s.n_fc = 0
+    rc = lib.vcb_mlp_crown(ctypes.byref(s), 4, None, None, None, None, None,
+                           None, None, None, 1, None, None, None, None, None,
+                           None, None, None)
+    assert rc == _lib.VCB_ERR_UNSUPPORTED
+    with pytest.raises(NotImplementedError):
+        _lib.check(rc, 'x')
+    rc = lib.vcb_probe_ffma(None, 0, 0, None)
+    assert rc == _lib.VCB_ERR_INVALID
+
+
+def test_status_mapping():
+    with pytest.raises(torch.cuda.OutOfMemoryError):
+        _lib.check(_lib.VCB_ERR_OOM)
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.VCB_ERR_CUDA)
+    with pytest.raises(TimeoutError):
+        _lib.check(_lib.VCB_ERR_TIMEOUT)
+
+
+def test_lower_mlp_chain_and_folding():
+    rng = np.random.default_rng(0)
+    layers = wk.mlp_params((4, 6, 3), rng)
+    gg = wk.mlp_gg(layers)
+    out = netdesc.lower_mlp(gg)
+    assert len(out) == 2
+    np.testing.assert_array_equal(out[0][0], layers[0][0].astype(np.float64))
+    # add-bias after the last fc folds into its bias
+    gg['ops'].append({'name': 'badd', 'type': 'add', 'inputs': ['fc1'],
+                      'is_merge': False, 'bias': np.ones(3)})
+    out = netdesc.lower_mlp(gg)
+    np.testing.assert_allclose(out[1][1], layers[1][1].astype(np.float64) + 1)
+
+
+def test_lower_rejects_unsupported():
+    rng = np.random.default_rng(0)
+    gg = wk.mlp_gg(wk.mlp_params((4, 6, 3), rng))
+    gg['ops'].insert(1, {'name': 'sg', 'type': 'sigmoid', 'inputs': ['fc0']})
+    with pytest.raises(NotImplementedError):
+        netdesc.lower_mlp(gg)
+
+
+def test_cpu_device_is_refused():
+    from vibecheck_nn_b200 import ops
+    gg = wk.mlp_gg(wk.mlp_params((4, 6, 3), np.random.default_rng(0)))
+    with pytest.raises(RuntimeError):
+        ops._ibp_forward_graph_batched(torch.zeros(2, 4), torch.ones(2, 4), gg,
+                                       'cpu', torch.float32)

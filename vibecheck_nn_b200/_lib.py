@@ -1,0 +1,103 @@
+"""ctypes binding of libvcb.so (the C ABI declared in include/vcb.h).
+
+The library is built in-tree (``python -m vibecheck_nn_b200.build``).  There
+is no fallback: if the library is missing or the device is not a CUDA GPU,
+every operator raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, 'libvcb.so')
+MAX_FC = 16
+
+VCB_OK = 0
+VCB_ERR_INVALID = 1
+VCB_ERR_UNSUPPORTED = 2
+VCB_ERR_CUDA = 3
+VCB_ERR_OOM = 4
+VCB_ERR_TIMEOUT = 5
+
+
+class VcbMlp(ctypes.Structure):
+    _fields_ = [('n_fc', ctypes.c_int32),
+                ('dims', ctypes.c_int32 * (MAX_FC + 1)),
+                ('W', ctypes.c_void_p),
+                ('b', ctypes.c_void_p)]
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int32
+
+# name -> argtypes; every function returns int (status) unless listed below.
+SIGNATURES = {
+    'vcb_version': [],
+    'vcb_last_error': [],
+    'vcb_mlp_crown': [ctypes.POINTER(VcbMlp), _I, _P, _P, _P, _P, _P, _P, _P,
+                      _P, _I, _P, _P, _P, _P, _P, _P, _P, _P],
+    'vcb_probe_ffma': [_P, _I, _I, _P],
+}
+RESTYPES = {'vcb_last_error': ctypes.c_char_p}
+
+_lib = None
+
+
+def lib():
+    """Load libvcb.so once; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f'{LIB_PATH} is missing: build it with '
+                '`python -m vibecheck_nn_b200.build` (no CPU fallback exists)')
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = args
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
+        _lib = handle
+    return _lib
+
+
+def last_error():
+    msg = lib().vcb_last_error()
+    return msg.decode() if msg else ''
+
+
+def check(rc, what='vcb'):
+    """Map a VCB_* status to the exception type the reference's callers
+    handle (ValueError / NotImplementedError / RuntimeError / OOM)."""
+    if rc == VCB_OK:
+        return
+    msg = f'{what}: {last_error()}'
+    if rc == VCB_ERR_INVALID:
+        raise ValueError(msg)
+    if rc == VCB_ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    if rc == VCB_ERR_OOM:
+        raise torch.cuda.OutOfMemoryError(msg)
+    if rc == VCB_ERR_TIMEOUT:
+        raise TimeoutError(msg)
+    raise RuntimeError(msg)
+
+
+def ptr(t):
+    """Device pointer of a tensor (None -> NULL)."""
+    if t is None:
+        return None
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda(t, name='tensor'):
+    if not (isinstance(t, torch.Tensor) and t.is_cuda):
+        raise RuntimeError(
+            f'vibecheck_nn_b200: {name} must be a CUDA tensor (the B200 path '
+            'has no CPU fallback)')
