@@ -20,6 +20,7 @@
 #ifndef VCB_H
 #define VCB_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -75,6 +76,9 @@ const char* vcb_last_error(void);
  *                 (spec_q(x) >= A[b,q].x + acc[b,q]), or NULL.
  *   sb_out_lo/hi  optional packed per-layer IBP bounds out (the bounds the
  *                 relaxation used, after clamps and crossing repair).
+ *   workspace     device scratch of at least vcb_mlp_crown_workspace(net, B,
+ *                 Q) bytes, 16-byte aligned (per-CTA ReLU slope slots).
+ *                 Calls that overlap on the GPU must not share it.
  */
 int vcb_mlp_crown(const vcb_mlp* net, int32_t B,
                   const float* xl, const float* xh,
@@ -84,7 +88,12 @@ int vcb_mlp_crown(const vcb_mlp* net, int32_t B,
                   int32_t Q, const float* spec_W, const float* spec_b,
                   float* lb, float* A, float* acc,
                   float* sb_out_lo, float* sb_out_hi,
+                  void* workspace, size_t workspace_bytes,
                   void* stream);
+
+/* Workspace bytes vcb_mlp_crown needs for (net, B, Q); 0 on bad arguments
+ * (vcb_mlp_crown then reports the error). */
+size_t vcb_mlp_crown_workspace(const vcb_mlp* net, int32_t B, int32_t Q);
 
 /* Diagnostic: FP32 FFMA throughput probe (no reference counterpart).  Runs
  * `blocks` CTAs of 256 threads, each thread `iters` x 64 dependent-chain FMAs

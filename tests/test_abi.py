@@ -15,8 +15,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def header_functions():
     src = open(os.path.join(ROOT, 'include', 'vcb.h')).read()
     src = re.sub(r'/\*.*?\*/', '', src, flags=re.S)
-    return sorted(set(re.findall(r'^\s*(?:int|const char\*)\s+(vcb_\w+)\s*\(',
-                                 src, flags=re.M)))
+    return sorted(set(re.findall(
+        r'^\s*(?:int|const char\*|size_t)\s+(vcb_\w+)\s*\(', src, flags=re.M)))
 
 
 def test_library_builds_and_loads():
@@ -39,7 +39,7 @@ def test_invalid_arguments_return_status_not_crash():
     lib = _lib.lib()
     rc = lib.vcb_mlp_crown(None, 4, None, None, None, None, None, None, None,
                            None, 1, None, None, None, None, None, None, None,
-                           None)
+                           None, 0, None)
     assert rc == _lib.VCB_ERR_INVALID
     assert 'NULL' in _lib.last_error()
     with pytest.raises(ValueError):
@@ -48,7 +48,15 @@ def test_invalid_arguments_return_status_not_crash():
     s.n_fc = 0
     rc = lib.vcb_mlp_crown(ctypes.byref(s), 4, None, None, None, None, None,
                            None, None, None, 1, None, None, None, None, None,
-                           None, None, None)
+                           None, None, None, 0, None)
+    assert rc == _lib.VCB_ERR_INVALID  # NULL weights are caught first
+    assert lib.vcb_mlp_crown_workspace(ctypes.byref(s), 4, 1) == 0
+    # non-NULL (never dereferenced) pointers: the n_fc check rejects it first
+    s.W = s.b = 16
+    fake = ctypes.c_void_p(16)
+    rc = lib.vcb_mlp_crown(ctypes.byref(s), 4, fake, fake, None, None, None,
+                           None, None, None, 0, None, None, None, None, None,
+                           None, None, None, 0, None)
     assert rc == _lib.VCB_ERR_UNSUPPORTED
     with pytest.raises(NotImplementedError):
         _lib.check(rc, 'x')

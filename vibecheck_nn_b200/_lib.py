@@ -38,10 +38,13 @@ SIGNATURES = {
     'vcb_version': [],
     'vcb_last_error': [],
     'vcb_mlp_crown': [ctypes.POINTER(VcbMlp), _I, _P, _P, _P, _P, _P, _P, _P,
-                      _P, _I, _P, _P, _P, _P, _P, _P, _P, _P],
+                      _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t,
+                      _P],
+    'vcb_mlp_crown_workspace': [ctypes.POINTER(VcbMlp), _I, _I],
     'vcb_probe_ffma': [_P, _I, _I, _P],
 }
-RESTYPES = {'vcb_last_error': ctypes.c_char_p}
+RESTYPES = {'vcb_last_error': ctypes.c_char_p,
+            'vcb_mlp_crown_workspace': ctypes.c_size_t}
 
 _lib = None
 
@@ -90,6 +93,15 @@ def ptr(t):
     if t is None:
         return None
     return ctypes.c_void_p(t.data_ptr())
+
+
+def workspace(nbytes, device):
+    """Scratch buffer from torch's stream-aware caching allocator (>= 16-byte
+    aligned); None when no scratch is needed."""
+    if not nbytes:
+        return None
+    return torch.empty((nbytes + 15) // 16 * 4, dtype=torch.float32,
+                       device=device)
 
 
 def stream_of(device):

@@ -1,19 +1,25 @@
 // Fused IBP forward + CROWN back-substitution for ReLU MLPs whose weights fit
 // in shared memory (ACAS-Xu-sized networks).
 //
-// One persistent CTA per SM slot walks tiles of TB subdomains.  Per tile:
+// One persistent CTA per SM slot (two per SM) walks tiles of TB subdomains.
+// All fc weights stay in shared memory (bias stored as an extra weight
+// column).  Per tile:
 //   * IBP forward (verify_zono_bnb.py:1066-1153): per fc layer a register-
-//     tiled fp32 GEMM of the (TB x n_in) mid/rad tile against the resident
-//     weights, with the ReLU clamp / crossing repair and the CROWN slope rule
-//     (verify_zono_bnb.py:503-522) fused into the epilogue.  The slopes stay
-//     in shared memory, sign-encoded in two floats per neuron.
+//     tiled fp32 GEMM of the (TB x n_in) mid/rad tile against the weights
+//     (ping-pong buffers, one barrier per layer); the ReLU clamp / crossing
+//     repair and the CROWN slope rule (verify_zono_bnb.py:503-522) run in its
+//     epilogue.  Slopes go to the CTA's slot of the caller's workspace
+//     (sign-encoded float2 per neuron, rewritten every tile, so the workspace
+//     stays resident in L2).
 //   * CROWN back-substitution (verify_zono_bnb.py:4270-5134): the (TB*Q x n)
-//     coefficient tile walks the layers in reverse; each step is a GEMM
-//     against the same resident weights (bias stored as an extra weight
-//     column, so the bias dot falls out of the GEMM), and the ReLU relaxation
-//     plus the intercept partial sums are fused into its epilogue.
-//   * Concretisation against the input box, optional A / acc outputs.
-// Nothing but the inputs, the outputs and the weights touches HBM.
+//     coefficient tile walks the layers in reverse, one GEMM per fc layer
+//     whose epilogue applies the ReLU relaxation and sums the intercepts; the
+//     bias dot is the GEMM's extra column.  The first step (spec rows times
+//     the last layer) is identical for every box and is computed once per CTA.
+//   * Concretisation against the input box; optional A / acc outputs.
+// Thread tiles are laid out so a warp's weight loads are broadcasts: in the
+// forward a warp covers 16 boxes x 2 output groups, in the backward 32 row
+// groups x 1 column group.
 #include <algorithm>
 
 #include "vcb_common.cuh"
@@ -21,7 +27,7 @@
 namespace vcb {
 namespace {
 
-constexpr int kNT = 128;  // threads per CTA
+constexpr int kNT = 256;  // threads per CTA
 
 struct CrownParams {
   int n_fc;
@@ -34,58 +40,63 @@ struct CrownParams {
   int pw[VCB_MAX_FC];
   int wrows[VCB_MAX_FC];
   long long relu_goff[VCB_MAX_FC];
-  int sl_soff, ps;
-  int act_soff, pa;
-  int ew_soff, pe, ew_rows;
+  int sl_loff[VCB_MAX_FC];   // float2 offset of relu layer L inside a slot
+  long long slot_f2;         // float2 per CTA slot
+  int act_soff, pa;          // forward: 2 x (mid | rad), each TB x pa
+  int ew_soff, pe, ew_rows;  // backward coefficients (ew_rows x pe, swizzled)
   int acc_soff, bd_soff, part_soff, rt_max;
   int x_soff;
-  int spec_soff;
+  int v_soff, pv;            // spec x last layer: Q x pv (+ bias column)
   int smem_floats;
   int B, Q, TB, ntiles;
   const float *xl, *xh, *clo, *chi, *sblo, *sbhi, *alpha, *beta, *specW, *specb;
   float *lb, *A, *accout, *sbolo, *sbohi;
+  float2* slopes;            // workspace: gridDim.x slots
 };
 
 __device__ __forceinline__ float4 ld4(const float* p) {
   return *reinterpret_cast<const float4*>(p);
 }
 
-// CROWN slope rule (verify_zono_bnb.py:511-521), sign-encoded:
-//   a = dead ? -up_s : up_s,   c = active ? -0.0f : up_t.
-__device__ __forceinline__ void encode_slope(float lo, float hi, float* a,
-                                             float* c) {
-  const float lb_r = fminf(lo, 0.f);
-  float ub_r = fmaxf(hi, 0.f);
-  ub_r = fmaxf(ub_r, __fadd_rn(lb_r, 1e-8f));
-  const float up_s = __fdiv_rn(ub_r, __fsub_rn(ub_r, lb_r));
-  const float up_t = __fmul_rn(-lb_r, up_s);
-  const bool active = lo >= 0.f;
-  const bool dead = hi <= 0.f;
-  *a = dead ? -up_s : up_s;
-  *c = active ? -0.0f : up_t;
+// Logical column k of coefficient row r -> swizzled offset inside the row.
+// Rows are pe floats (pe a multiple of 32); the 16-byte chunk index is XORed
+// with bits 2..4 of the row so the 4-row register tiles of neighbouring row
+// groups hit distinct bank groups.
+__device__ __forceinline__ int swz(int r, int k) {
+  return ((((k >> 2) ^ ((r >> 2) & 7))) << 2) | (k & 3);
 }
 
-// ReLU backward step for one coefficient e (verify_zono_bnb.py:4409-4449):
-// returns ep*lo_s + en*up_s and adds en*up_t to *part.  Exactly one of ep/en
-// is non-zero, so the single product below rounds like the reference's sum.
-__device__ __forceinline__ float relu_back(float e, float a, float c,
-                                           const float* alpha_ptr,
-                                           float* part) {
-  if (signbit(c)) return e;  // active: identity, zero intercept
-  if (signbit(a)) {          // dead (lo_s = 0)
-    if (e < 0.f) {
-      *part += __fmul_rn(e, c);
-      return __fmul_rn(e, -a);
-    }
-    return 0.f * e;
+// CROWN slope rule (verify_zono_bnb.py:511-521), sign-encoded:
+//   x = dead ? -up_s : up_s,   y = active ? -0.0f : up_t.
+// The division only runs where lo < 0 < hi or in the dead corner where
+// lo + 1e-8 > 0 (elsewhere up_s is exactly 1 or 0).
+__device__ __forceinline__ float2 encode_slope(float lo, float hi) {
+  if (lo >= 0.f) return make_float2(1.f, -0.0f);  // active
+  const bool dead = hi <= 0.f;
+  const float ub_r = fmaxf(fmaxf(hi, 0.f), __fadd_rn(lo, 1e-8f));
+  if (ub_r == 0.f) return make_float2(-0.0f, 0.0f);  // dead, up_s = 0
+  const float up_s = __fdiv_rn(ub_r, __fsub_rn(ub_r, lo));
+  const float up_t = __fmul_rn(-lo, up_s);
+  return make_float2(dead ? -up_s : up_s, up_t);
+}
+
+struct Slope {
+  float pos, neg, icp;  // multiplier for e >= 0, for e < 0, intercept factor
+};
+
+// Decoded relaxation of one neuron; alpha (may be NULL) replaces the
+// min-area lower slope of unstable neurons (verify_zono_bnb.py:4420-4433).
+__device__ __forceinline__ Slope decode_slope(float2 v, const float* alpha) {
+  Slope s;
+  if (signbit(v.y)) {  // active: identity, no intercept
+    s.pos = 1.f; s.neg = 1.f; s.icp = 0.f;
+  } else if (signbit(v.x)) {  // dead (lower slope 0)
+    s.pos = 0.f; s.neg = -v.x; s.icp = v.y;
+  } else {  // unstable
+    s.pos = alpha ? __ldg(alpha) : (v.x > 0.5f ? 1.f : 0.f);
+    s.neg = v.x; s.icp = v.y;
   }
-  // unstable
-  if (e < 0.f) {
-    *part += __fmul_rn(e, c);
-    return __fmul_rn(e, a);
-  }
-  const float lo_s = alpha_ptr ? *alpha_ptr : (a > 0.5f ? 1.f : 0.f);
-  return __fmul_rn(e, lo_s);
+  return s;
 }
 
 __global__ void __launch_bounds__(kNT, 2)
@@ -97,34 +108,64 @@ __global__ void __launch_bounds__(kNT, 2)
   const int nL = p.dims[nfc];
   const int Q = p.Q;
   const int TB = p.TB;
+  float2* slot = p.slopes + (long long)blockIdx.x * p.slot_f2;
 
-  // ---- resident weights: row o of layer l = [W[o,0..n_in), b[o], 0...]
+  // per-thread tile coordinates (fixed for the whole kernel)
+  const int SG = TB >> 1;
+  const int f_og = tid / SG;                 // forward output group
+  const int f_sg = tid - f_og * SG;          // forward box pair (rows sg, sg+SG)
+  const int RT = TB * Q;
+  const int RG = (RT + 3) >> 2;
+  const int b_cg = tid / RG;                 // backward column group
+  const int b_rg = tid - b_cg * RG;          // backward row group
+  const int r0 = 4 * b_rg;
+  int rs[4], rq[4];                          // box and spec row of rows r0..r0+3
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int r = r0 + j;
+    rs[j] = Q > 0 ? min(r / Q, TB - 1) : 0;
+    rq[j] = Q > 0 ? min(r - rs[j] * Q, Q - 1) : 0;
+  }
+
+  // ---- resident weights: row o of layer l = [W[o,0..n_in), b[o], 0...],
+  // copied with cp.async so every element's load is in flight at once.
   for (int l = 0; l < nfc; ++l) {
     const int nin = p.dims[l], nout = p.dims[l + 1], pw = p.pw[l];
-    const int total = p.wrows[l] * pw;
     float* dst = sm + p.w_soff[l];
     const float* Wg = p.W + p.w_goff[l];
     const float* bg = p.b + p.b_goff[l];
-    for (int idx = tid; idx < total; idx += kNT) {
-      const int o = idx / pw;
-      const int i = idx - o * pw;
-      float v = 0.f;
-      if (o < nout) v = (i < nin) ? Wg[(long long)o * nin + i] : (i == nin ? bg[o] : 0.f);
-      dst[idx] = v;
+    for (int o = tid >> 5; o < p.wrows[l]; o += kNT / 32) {
+      for (int i = tid & 31; i < pw; i += 32) {
+        const bool inside = o < nout && i <= nin;
+        const float* src = !inside ? p.W : (i < nin ? Wg + (long long)o * nin + i : bg + o);
+        const unsigned saddr = static_cast<unsigned>(__cvta_generic_to_shared(dst + o * pw + i));
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(saddr),
+                     "l"(src), "r"(inside ? 4 : 0));
+      }
     }
   }
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
   if (tid < 8) sm[p.w_soff[nfc - 1] + p.wrows[nfc - 1] * p.pw[nfc - 1] + tid] = 0.f;
+  // ---- spec rows times the last fc layer (identical for every box)
   if (Q > 0) {
-    float* ssp = sm + p.spec_soff;
-    for (int idx = tid; idx < Q * nL; idx += kNT) ssp[idx] = p.specW[idx];
-    for (int idx = tid; idx < Q; idx += kNT) ssp[Q * nL + idx] = p.specb[idx];
+    const int nprev = p.dims[nfc - 1];
+    const float* Wg = p.W + p.w_goff[nfc - 1];
+    const float* bg = p.b + p.b_goff[nfc - 1];
+    float* V = sm + p.v_soff;
+    for (int q = tid >> 5; q < Q; q += kNT / 32) {
+      for (int c = tid & 31; c <= nprev; c += 32) {
+        float s = 0.f;
+        for (int o = 0; o < nL; ++o)
+          s = fmaf(__ldg(p.specW + q * nL + o),
+                   c < nprev ? __ldg(Wg + (long long)o * nprev + c) : __ldg(bg + o), s);
+        V[q * p.pv + c] = s;
+      }
+    }
   }
   __syncthreads();
 
   float* sXl = sm + p.x_soff;
   float* sXh = sXl + TB * n0;
-  const int n0p = pad4(n0);
-  const int RT = TB * Q;
 
   for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
     const int s0 = tile * TB;
@@ -132,115 +173,121 @@ __global__ void __launch_bounds__(kNT, 2)
     const long long gbase = (long long)s0 * n0;
     for (int idx = tid; idx < TB * n0; idx += kNT) {
       const bool v = idx < nb * n0;
-      sXl[idx] = v ? p.xl[gbase + idx] : 0.f;
-      sXh[idx] = v ? p.xh[gbase + idx] : 0.f;
+      sXl[idx] = v ? __ldg(p.xl + gbase + idx) : 0.f;
+      sXh[idx] = v ? __ldg(p.xh + gbase + idx) : 0.f;
     }
+    __syncthreads();
 
     if (p.sblo == nullptr) {
       // ------------------------------------------------------ IBP forward
-      float* mid = sm + p.act_soff;
-      float* rad = mid + TB * p.pa;
-      for (int idx = tid; idx < TB * n0p; idx += kNT) {
-        const int s = idx / n0p, i = idx - s * n0p;
-        float m = 0.f, r = 0.f;
-        if (s < nb && i < n0) {
-          const float l = p.xl[gbase + s * n0 + i], h = p.xh[gbase + s * n0 + i];
-          m = __fmul_rn(__fadd_rn(l, h), 0.5f);
-          r = __fmul_rn(__fsub_rn(h, l), 0.5f);
+      float* act_buf = sm + p.act_soff;
+      const int half = 2 * TB * p.pa;  // one (mid | rad) buffer
+      {
+        const int n0p = pad4(n0);
+        for (int s = tid >> 5; s < TB; s += kNT / 32) {
+          for (int i = tid & 31; i < n0p; i += 32) {
+            float m = 0.f, r = 0.f;
+            if (i < n0) {
+              const float lo = sXl[s * n0 + i], hi = sXh[s * n0 + i];
+              m = __fmul_rn(__fadd_rn(lo, hi), 0.5f);
+              r = __fmul_rn(__fsub_rn(hi, lo), 0.5f);
+            }
+            act_buf[s * p.pa + i] = m;
+            act_buf[TB * p.pa + s * p.pa + i] = r;
+          }
         }
-        mid[s * p.pa + i] = m;
-        rad[s * p.pa + i] = r;
       }
       __syncthreads();
       for (int l = 0; l < nfc - 1; ++l) {
+        const float* mid = act_buf + (l & 1) * half;
+        const float* rad = mid + TB * p.pa;
+        float* mid_o = act_buf + ((l + 1) & 1) * half;
+        float* rad_o = mid_o + TB * p.pa;
         const int nin = p.dims[l], nout = p.dims[l + 1], pw = p.pw[l];
         const float* sW = sm + p.w_soff[l];
-        const int SG = TB >> 1;
         const int G = (nout + 3) >> 2;
-        const bool act = tid < SG * G;
-        const int sg = tid % SG, og = tid / SG;
-        const int kend = pad4(nin);
-        float am[2][4], ar[2][4];
+        if (f_og < G) {
+          float am[2][4], ar[2][4];
 #pragma unroll
-        for (int s = 0; s < 2; ++s)
+          for (int s = 0; s < 2; ++s)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) am[s][j] = ar[s][j] = 0.f;
-        if (act) {
-          const float* w0 = sW + og * pw;
-          const float* m0 = mid + sg * p.pa;
-          const float* m1 = mid + (sg + SG) * p.pa;
-          const float* r0 = rad + sg * p.pa;
-          const float* r1 = rad + (sg + SG) * p.pa;
+            for (int j = 0; j < 4; ++j) am[s][j] = ar[s][j] = 0.f;
+          const float* w0 = sW + f_og * pw;
+          const float* m0 = mid + f_sg * p.pa;
+          const float* m1 = mid + (f_sg + SG) * p.pa;
+          const float* q0 = rad + f_sg * p.pa;
+          const float* q1 = rad + (f_sg + SG) * p.pa;
           const int gstride = G * pw;
+          const int kend = pad4(nin);
+#pragma unroll 2
           for (int k = 0; k < kend; k += 4) {
             float4 w[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) w[j] = ld4(w0 + j * gstride + k);
             const float4 M0 = ld4(m0 + k), M1 = ld4(m1 + k);
-            const float4 R0 = ld4(r0 + k), R1 = ld4(r1 + k);
+            const float4 R0 = ld4(q0 + k), R1 = ld4(q1 + k);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               am[0][j] = fmaf(M0.x, w[j].x, am[0][j]);
-              am[0][j] = fmaf(M0.y, w[j].y, am[0][j]);
-              am[0][j] = fmaf(M0.z, w[j].z, am[0][j]);
-              am[0][j] = fmaf(M0.w, w[j].w, am[0][j]);
               am[1][j] = fmaf(M1.x, w[j].x, am[1][j]);
+              am[0][j] = fmaf(M0.y, w[j].y, am[0][j]);
               am[1][j] = fmaf(M1.y, w[j].y, am[1][j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              am[0][j] = fmaf(M0.z, w[j].z, am[0][j]);
               am[1][j] = fmaf(M1.z, w[j].z, am[1][j]);
+              am[0][j] = fmaf(M0.w, w[j].w, am[0][j]);
               am[1][j] = fmaf(M1.w, w[j].w, am[1][j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
               const float ax = fabsf(w[j].x), ay = fabsf(w[j].y);
-              const float az = fabsf(w[j].z), aw = fabsf(w[j].w);
               ar[0][j] = fmaf(R0.x, ax, ar[0][j]);
-              ar[0][j] = fmaf(R0.y, ay, ar[0][j]);
-              ar[0][j] = fmaf(R0.z, az, ar[0][j]);
-              ar[0][j] = fmaf(R0.w, aw, ar[0][j]);
               ar[1][j] = fmaf(R1.x, ax, ar[1][j]);
+              ar[0][j] = fmaf(R0.y, ay, ar[0][j]);
               ar[1][j] = fmaf(R1.y, ay, ar[1][j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float az = fabsf(w[j].z), aw = fabsf(w[j].w);
+              ar[0][j] = fmaf(R0.z, az, ar[0][j]);
               ar[1][j] = fmaf(R1.z, az, ar[1][j]);
+              ar[0][j] = fmaf(R0.w, aw, ar[0][j]);
               ar[1][j] = fmaf(R1.w, aw, ar[1][j]);
             }
           }
-        }
-        __syncthreads();
-        if (act) {
-          float* slA = sm + p.sl_soff + l * 2 * TB * p.ps;
-          float* slC = slA + TB * p.ps;
-          const long long goff = p.relu_goff[l];
+          float2* sl = slot + p.sl_loff[l];
 #pragma unroll
           for (int s = 0; s < 2; ++s) {
-            const int row = sg + s * SG;
+            const int row = f_sg + s * SG;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const int o = og + G * j;
+              const int o = f_og + G * j;
               float mo = 0.f, ro = 0.f;
               if (row < nb && o < nout) {
                 const float mc = __fadd_rn(am[s][j], sW[o * pw + nin]);
                 const float rc = ar[s][j];
                 float lo = __fsub_rn(mc, rc);
                 float hi = __fadd_rn(mc, rc);
-                const long long gi = goff + (long long)(s0 + row) * nout + o;
                 if (p.clo) {
-                  lo = fmaxf(lo, p.clo[gi]);
-                  hi = fminf(hi, p.chi[gi]);
+                  const long long gi = p.relu_goff[l] + (long long)(s0 + row) * nout + o;
+                  lo = fmaxf(lo, __ldg(p.clo + gi));
+                  hi = fminf(hi, __ldg(p.chi + gi));
                 }
                 hi = fmaxf(hi, lo);
                 if (p.sbolo) {
+                  const long long gi = p.relu_goff[l] + (long long)(s0 + row) * nout + o;
                   p.sbolo[gi] = lo;
                   p.sbohi[gi] = hi;
                 }
-                float a, c;
-                encode_slope(lo, hi, &a, &c);
-                slA[row * p.ps + o] = a;
-                slC[row * p.ps + o] = c;
+                sl[row * nout + o] = encode_slope(lo, hi);
                 const float lc = fmaxf(lo, 0.f), hc = fmaxf(hi, 0.f);
                 mo = __fmul_rn(__fadd_rn(lc, hc), 0.5f);
                 ro = __fmul_rn(__fsub_rn(hc, lc), 0.5f);
-              } else if (o < nout) {
-                slA[row * p.ps + o] = 0.f;
-                slC[row * p.ps + o] = 0.f;
               }
-              mid[row * p.pa + o] = mo;
-              rad[row * p.pa + o] = ro;
+              mid_o[row * p.pa + o] = mo;
+              rad_o[row * p.pa + o] = ro;
             }
           }
         }
@@ -250,16 +297,10 @@ __global__ void __launch_bounds__(kNT, 2)
       // --------------------------------- caller-supplied intermediate bounds
       for (int L = 0; L < nfc - 1; ++L) {
         const int n = p.dims[L + 1];
-        float* slA = sm + p.sl_soff + L * 2 * TB * p.ps;
-        float* slC = slA + TB * p.ps;
+        float2* sl = slot + p.sl_loff[L];
         const long long goff = p.relu_goff[L] + (long long)s0 * n;
-        for (int idx = tid; idx < TB * n; idx += kNT) {
-          const int s = idx / n, c = idx - s * n;
-          float a = 0.f, cc = 0.f;
-          if (s < nb) encode_slope(p.sblo[goff + idx], p.sbhi[goff + idx], &a, &cc);
-          slA[s * p.ps + c] = a;
-          slC[s * p.ps + c] = cc;
-        }
+        for (int idx = tid; idx < nb * n; idx += kNT)
+          sl[idx] = encode_slope(__ldg(p.sblo + goff + idx), __ldg(p.sbhi + goff + idx));
       }
       __syncthreads();
     }
@@ -270,90 +311,136 @@ __global__ void __launch_bounds__(kNT, 2)
       float* sAcc = sm + p.acc_soff;
       float* sBd = sm + p.bd_soff;
       float* sPart = sm + p.part_soff;
-      const float* ssp = sm + p.spec_soff;
-      for (int idx = tid; idx < p.ew_rows * p.pe; idx += kNT) {
-        const int r = idx / p.pe, o = idx - r * p.pe;
-        float v = 0.f;
-        if (r < nb * Q && o < nL) v = ssp[(r % Q) * nL + o];
-        ew[idx] = v;
+      const float* V = sm + p.v_soff;
+      const int nvalid = nb * Q;
+      for (int r = tid; r < RT; r += kNT) {
+        const int q = r - min(r / Q, TB - 1) * Q;
+        sAcc[r] = (r < nvalid) ? __ldg(p.specb + q) : 0.f;
       }
-      for (int r = tid; r < RT; r += kNT) sAcc[r] = (r < nb * Q) ? ssp[Q * nL + r % Q] : 0.f;
-      __syncthreads();
-      const int RG = (RT + 3) >> 2;
       for (int l = nfc - 1; l >= 0; --l) {
         const int nin = p.dims[l], nout = p.dims[l + 1], pw = p.pw[l];
         const float* sW = sm + p.w_soff[l];
         const int CG = (nin + 1 + 7) >> 3;
-        const bool act = tid < RG * CG;
-        const int rg = tid % RG, cg = tid / RG;
-        const int kend = pad4(nout);
+        const bool act = b_cg < CG;
+        const int L = l - 1;  // relu feeding fc l
+        // prefetch the slopes of this thread's first box (hidden by the GEMM)
+        float2 pre[8];
+        const float2* sl = slot + (L >= 0 ? p.sl_loff[L] : 0);
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          const int c = 8 * b_cg + c8;
+          pre[c8] = (act && L >= 0 && c < nin && rs[0] < nb) ? sl[rs[0] * nin + c]
+                                                             : make_float2(0.f, 0.f);
+        }
         float acc[4][8];
+        if (l == nfc - 1) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+          for (int j = 0; j < 4; ++j)
 #pragma unroll
-          for (int c = 0; c < 8; ++c) acc[j][c] = 0.f;
-        if (act) {
-          const float* e0 = ew + rg * p.pe;
-          const int rstride = RG * p.pe;
-          const float* wcol = sW + 8 * cg;
-          for (int k = 0; k < kend; k += 4) {
-            float4 e[4];
+            for (int c8 = 0; c8 < 8; ++c8) {
+              const int c = 8 * b_cg + c8;
+              acc[j][c8] = (act && c <= nin) ? V[rq[j] * p.pv + c] : 0.f;
+            }
+        } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) e[j] = ld4(e0 + j * rstride + k);
+          for (int j = 0; j < 4; ++j)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const float4 wa = ld4(wcol + (k + kk) * pw);
-              const float4 wb = ld4(wcol + (k + kk) * pw + 4);
+            for (int c = 0; c < 8; ++c) acc[j][c] = 0.f;
+          if (act) {
+            const float* e0 = ew + r0 * p.pe;
+            const int xr = b_rg & 7;
+            const float* wcol = sW + 8 * b_cg;
+            const int kend = pad4(nout);
+#pragma unroll 2
+            for (int k = 0; k < kend; k += 4) {
+              const int kc = (((k >> 2) ^ xr) << 2);
+              float4 e[4];
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float ev = kk == 0 ? e[j].x : kk == 1 ? e[j].y : kk == 2 ? e[j].z : e[j].w;
-                acc[j][0] = fmaf(ev, wa.x, acc[j][0]);
-                acc[j][1] = fmaf(ev, wa.y, acc[j][1]);
-                acc[j][2] = fmaf(ev, wa.z, acc[j][2]);
-                acc[j][3] = fmaf(ev, wa.w, acc[j][3]);
-                acc[j][4] = fmaf(ev, wb.x, acc[j][4]);
-                acc[j][5] = fmaf(ev, wb.y, acc[j][5]);
-                acc[j][6] = fmaf(ev, wb.z, acc[j][6]);
-                acc[j][7] = fmaf(ev, wb.w, acc[j][7]);
+              for (int j = 0; j < 4; ++j) e[j] = ld4(e0 + j * p.pe + kc);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const float4 wa = ld4(wcol + (k + kk) * pw);
+                const float4 wb = ld4(wcol + (k + kk) * pw + 4);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float ev = kk == 0 ? e[j].x : kk == 1 ? e[j].y : kk == 2 ? e[j].z : e[j].w;
+                  acc[j][0] = fmaf(ev, wa.x, acc[j][0]);
+                  acc[j][1] = fmaf(ev, wa.y, acc[j][1]);
+                  acc[j][2] = fmaf(ev, wa.z, acc[j][2]);
+                  acc[j][3] = fmaf(ev, wa.w, acc[j][3]);
+                  acc[j][4] = fmaf(ev, wb.x, acc[j][4]);
+                  acc[j][5] = fmaf(ev, wb.y, acc[j][5]);
+                  acc[j][6] = fmaf(ev, wb.z, acc[j][6]);
+                  acc[j][7] = fmaf(ev, wb.w, acc[j][7]);
+                }
               }
             }
           }
         }
-        __syncthreads();
+        __syncthreads();  // every thread has read the coefficient rows
         if (act) {
-          const int L = l - 1;  // relu feeding fc l
-          const float* slA = sm + p.sl_soff + (L < 0 ? 0 : L) * 2 * TB * p.ps;
-          const float* slC = slA + TB * p.ps;
-          const long long goff = L < 0 ? 0 : p.relu_goff[L];
+          const float* alpha = (L >= 0 && p.alpha) ? p.alpha + p.relu_goff[L] + (long long)s0 * nin : nullptr;
+          const float* beta = (L >= 0 && p.beta) ? p.beta + p.relu_goff[L] + (long long)s0 * nin : nullptr;
+          Slope sv[8];
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const int c = 8 * b_cg + c8;
+            if (L < 0) {
+              sv[c8].pos = sv[c8].neg = (c < nin) ? 1.f : 0.f;
+              sv[c8].icp = 0.f;
+            } else {
+              sv[c8] = decode_slope(pre[c8], (alpha && c < nin) ? alpha + rs[0] * nin + c : nullptr);
+              if (!(c < nin)) sv[c8].pos = sv[c8].neg = sv[c8].icp = 0.f;
+            }
+          }
+          int s_cur = rs[0];
+          const int bcg = nin >> 3, bc8 = nin & 7;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const int r = rg + RG * j;
-            if (r >= RT) continue;
-            const bool rv = r < nb * Q;
-            const int s = r / Q;
-            float part = 0.f;
+            const int r = r0 + j;
+            const bool rv = r < nvalid;
+            const int s = rs[j];
+            if (L >= 0 && rv && s != s_cur) {  // rows of a second box
+              s_cur = s;
 #pragma unroll
-            for (int c8 = 0; c8 < 8; ++c8) {
-              const int c = 8 * cg + c8;
-              float v = acc[j][c8];
-              if (c < nin) {
-                if (!rv) {
-                  v = 0.f;
-                } else if (L >= 0) {
-                  const long long gi = goff + (long long)(s0 + s) * nin + c;
-                  v = relu_back(v, slA[s * p.ps + c], slC[s * p.ps + c],
-                                p.alpha ? p.alpha + gi : nullptr, &part);
-                  if (p.beta) v = __fadd_rn(v, p.beta[gi]);
-                }
-                ew[r * p.pe + c] = v;
-              } else if (c == nin) {
-                sBd[r] = rv ? v : 0.f;
-                if (c < p.pe) ew[r * p.pe + c] = 0.f;
-              } else if (c < p.pe) {
-                ew[r * p.pe + c] = 0.f;
+              for (int c8 = 0; c8 < 8; ++c8) {
+                const int c = 8 * b_cg + c8;
+                sv[c8] = decode_slope(c < nin ? sl[s * nin + c] : make_float2(0.f, 0.f),
+                                      (alpha && c < nin) ? alpha + s * nin + c : nullptr);
+                if (!(c < nin)) sv[c8].pos = sv[c8].neg = sv[c8].icp = 0.f;
               }
             }
-            sPart[cg * p.rt_max + r] = part;
+            float bj = 0.f;
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8)
+              if (c8 == bc8) bj = acc[j][c8];
+            const float keep = rv ? 1.f : 0.f;
+            float pj = 0.f;
+            float out[8];
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8) {
+              const float v = acc[j][c8] * keep;
+              const float m = v < 0.f ? sv[c8].neg : sv[c8].pos;
+              pj = fmaf(fminf(v, 0.f), sv[c8].icp, pj);
+              out[c8] = __fmul_rn(v, m);
+            }
+            if (beta && rv) {
+#pragma unroll
+              for (int c8 = 0; c8 < 8; ++c8) {
+                const int c = 8 * b_cg + c8;
+                if (c < nin) out[c8] = __fadd_rn(out[c8], __ldg(beta + s * nin + c));
+              }
+            }
+            float* row = ew + r * p.pe;
+            const int xr = (r >> 2) & 7;
+            *reinterpret_cast<float4*>(row + ((((2 * b_cg) ^ xr)) << 2)) =
+                make_float4(out[0], out[1], out[2], out[3]);
+            *reinterpret_cast<float4*>(row + ((((2 * b_cg + 1) ^ xr)) << 2)) =
+                make_float4(out[4], out[5], out[6], out[7]);
+            if (r < RT) {
+              if (b_cg == bcg) sBd[r] = rv ? bj : 0.f;
+              sPart[b_cg * p.rt_max + r] = pj;
+            }
           }
         }
         __syncthreads();
@@ -366,30 +453,28 @@ __global__ void __launch_bounds__(kNT, 2)
           }
           sAcc[r] = a;
         }
-        // the next GEMM reads only ew (written before the barrier above); the
-        // next epilogue's writes to sBd/sPart happen after its own barrier.
+        // the next GEMM reads only ew (complete at the barrier above); the
+        // next epilogue rewrites sBd/sPart only after its own barrier.
       }
       __syncthreads();
       // --------------------------------------------------- concretisation
-      for (int r = tid; r < nb * Q; r += kNT) {
+      for (int r = tid; r < nvalid; r += kNT) {
         const int s = r / Q;
         const float* e = ew + r * p.pe;
         const float* xls = sXl + s * n0;
         const float* xhs = sXh + s * n0;
         float s1 = 0.f, s2 = 0.f;
+        const long long go = (long long)s0 * Q + r;
+        float* Ar = p.A ? p.A + go * n0 : nullptr;
         for (int i = 0; i < n0; ++i) {
-          const float ei = e[i];
+          const float ei = e[swz(r, i)];
           s1 = fmaf(fmaxf(ei, 0.f), xls[i], s1);
           s2 = fmaf(fminf(ei, 0.f), xhs[i], s2);
+          if (Ar) Ar[i] = ei;
         }
-        const long long go = (long long)s0 * Q + r;
         const float accv = sAcc[r];
         p.lb[go] = __fadd_rn(__fadd_rn(accv, s1), s2);
         if (p.accout) p.accout[go] = accv;
-        if (p.A) {
-          float* Ar = p.A + go * n0;
-          for (int i = 0; i < n0; ++i) Ar[i] = e[i];
-        }
       }
     }
     __syncthreads();
@@ -401,42 +486,40 @@ struct Layout {
   int bytes;
 };
 
-// Computes the shared-memory layout for tile size TB; returns false when a
-// phase would need more than one work item per thread.
+// Shared-memory layout for tile size TB; false when a phase would need more
+// than one work item per thread.
 bool make_layout(const vcb_mlp* net, int TB, int Q, Layout* out) {
   CrownParams& p = out->p;
   const int nfc = net->n_fc;
   int off = 0;
-  int max_relu = 1, max_in1 = 1, max_w = 1, cg_max = 1, g_max = 1;
+  int max_w = 1, cg_max = 1, g_max = 1;
+  long long slot = 0;
   for (int l = 0; l < nfc; ++l) {
     const int nin = net->dims[l], nout = net->dims[l + 1];
     p.pw[l] = pad4odd(nin + 1);
     p.wrows[l] = pad4(nout);
     p.w_soff[l] = off;
     off += p.wrows[l] * p.pw[l];
-    max_in1 = std::max(max_in1, nin + 1);
     max_w = std::max(max_w, nin);
     cg_max = std::max(cg_max, (nin + 1 + 7) / 8);
     if (l < nfc - 1) {
-      max_relu = std::max(max_relu, nout);
       g_max = std::max(g_max, (nout + 3) / 4);
+      p.sl_loff[l] = (int)slot;
+      slot += (long long)TB * nout;
     }
   }
-  max_in1 = std::max(max_in1, net->dims[nfc] + 1);
+  p.slot_f2 = std::max(slot, 1LL);
   off += 8;
   off = pad4(off);
-  p.sl_soff = off;
-  p.ps = pad4(max_relu);
-  off += (nfc - 1) * 2 * TB * p.ps;
   const int SG = TB / 2;
   if (nfc > 1 && SG * g_max > kNT) return false;
   const int RT = TB * Q;
   const int RG = (RT + 3) / 4;
   if (Q > 0 && RG * cg_max > kNT) return false;
   p.pa = pad4odd(std::max(max_w, net->dims[0]));
-  p.pe = pad4odd(max_in1);
+  p.pe = std::max(32, (8 * cg_max + 31) / 32 * 32);
   p.ew_rows = 4 * RG;
-  const int fwd = 2 * TB * p.pa;
+  const int fwd = 4 * TB * p.pa;
   const int bwd = Q > 0 ? p.ew_rows * p.pe : 0;
   p.act_soff = p.ew_soff = off;
   off += pad4(std::max(fwd, bwd));
@@ -449,15 +532,71 @@ bool make_layout(const vcb_mlp* net, int TB, int Q, Layout* out) {
   off += cg_max * p.rt_max;
   p.x_soff = off;
   off += pad4(2 * TB * net->dims[0]);
-  p.spec_soff = off;
-  off += pad4(Q * net->dims[nfc] + Q);
+  p.pv = pad4(net->dims[nfc - 1] + 1);
+  p.v_soff = off;
+  off += pad4(std::max(Q, 1) * p.pv);
   p.smem_floats = off;
   out->bytes = off * 4;
   return true;
 }
 
+struct Plan {
+  Layout lay;
+  int grid;
+  size_t ws_bytes;
+};
+
+int plan_crown(const vcb_mlp* net, int B, int Q, Plan* plan) {
+  const int nfc = net->n_fc;
+  if (nfc < 1 || nfc > VCB_MAX_FC)
+    return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_crown: n_fc=%d outside [1,%d]", nfc, VCB_MAX_FC);
+  for (int l = 0; l <= nfc; ++l)
+    if (net->dims[l] <= 0)
+      return fail(VCB_ERR_INVALID, "vcb_mlp_crown: dims[%d]=%d", l, net->dims[l]);
+  if (B < 0 || Q < 0) return fail(VCB_ERR_INVALID, "vcb_mlp_crown: B=%d Q=%d", B, Q);
+  // Largest even tile (<= 32) with one work item per thread and two CTAs per
+  // SM; otherwise one CTA per SM.
+  const int two_cta = (233472 - 2 * 1024) / 2;
+  const int one_cta = 232448;
+  // Small batches (a BaB iteration) use smaller tiles so every CTA slot gets
+  // work: the largest even TB <= 32 with at least two tiles per SM.
+  int tb_max = 32;
+  while (tb_max > 2 && (long long)B < (long long)tb_max * 2 * sm_count()) tb_max -= 2;
+  bool found = false;
+  for (int pass = 0; pass < 2 && !found; ++pass) {
+    const int limit = pass == 0 ? two_cta : one_cta;
+    for (int TB = tb_max; TB >= 2; TB -= 2) {
+      Layout t{};
+      if (make_layout(net, TB, Q, &t) && t.bytes <= limit) {
+        plan->lay = t;
+        plan->lay.p.TB = TB;
+        found = true;
+        break;
+      }
+    }
+  }
+  if (!found)
+    return fail(VCB_ERR_UNSUPPORTED,
+                "vcb_mlp_crown: network does not fit the shared-memory-resident kernel");
+  const int TB = plan->lay.p.TB;
+  const int ntiles = B > 0 ? (B + TB - 1) / TB : 0;
+  const int per_sm = plan->lay.bytes <= two_cta ? 2 : 1;
+  plan->grid = std::max(1, std::min(ntiles, sm_count() * per_sm));
+  plan->ws_bytes = (size_t)plan->grid * (size_t)plan->lay.p.slot_f2 * sizeof(float2);
+  return VCB_OK;
+}
+
 }  // namespace
 }  // namespace vcb
+
+extern "C" size_t vcb_mlp_crown_workspace(const vcb_mlp* net, int32_t B,
+                                          int32_t Q) {
+  using namespace vcb;
+  if (!net || B <= 0) return 0;
+  Plan plan;
+  if (plan_crown(net, B, Q, &plan) != VCB_OK) return 0;
+  return plan.ws_bytes;
+}
 
 extern "C" int vcb_mlp_crown(const vcb_mlp* net, int32_t B, const float* xl,
                              const float* xh, const float* clamp_lo,
@@ -466,17 +605,13 @@ extern "C" int vcb_mlp_crown(const vcb_mlp* net, int32_t B, const float* xl,
                              const float* beta, int32_t Q, const float* spec_W,
                              const float* spec_b, float* lb, float* A,
                              float* acc, float* sb_out_lo, float* sb_out_hi,
+                             void* workspace, size_t workspace_bytes,
                              void* stream) {
   using namespace vcb;
   if (!net) return fail(VCB_ERR_INVALID, "vcb_mlp_crown: net is NULL");
-  const int nfc = net->n_fc;
-  if (nfc < 1 || nfc > VCB_MAX_FC)
-    return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_crown: n_fc=%d outside [1,%d]", nfc, VCB_MAX_FC);
-  for (int l = 0; l <= nfc; ++l)
-    if (net->dims[l] <= 0)
-      return fail(VCB_ERR_INVALID, "vcb_mlp_crown: dims[%d]=%d", l, net->dims[l]);
   if (B < 0 || Q < 0) return fail(VCB_ERR_INVALID, "vcb_mlp_crown: B=%d Q=%d", B, Q);
-  if (!net->W || !net->b || (B > 0 && (!xl || !xh)))
+  if (B == 0) return VCB_OK;  // nothing to bound; output pointers may be NULL
+  if (!net->W || !net->b || !xl || !xh)
     return fail(VCB_ERR_INVALID, "vcb_mlp_crown: NULL weight or box pointer");
   if ((clamp_lo == nullptr) != (clamp_hi == nullptr) ||
       (sb_in_lo == nullptr) != (sb_in_hi == nullptr) ||
@@ -486,30 +621,17 @@ extern "C" int vcb_mlp_crown(const vcb_mlp* net, int32_t B, const float* xl,
     return fail(VCB_ERR_INVALID, "vcb_mlp_crown: Q>0 needs spec_W, spec_b and lb");
   if (sb_in_lo && (clamp_lo || sb_out_lo))
     return fail(VCB_ERR_INVALID, "vcb_mlp_crown: sb_in excludes clamps and sb_out");
-  if (B == 0) return VCB_OK;
-
-  // Largest even tile that keeps one work item per thread and fits two CTAs
-  // per SM; otherwise one CTA per SM.
-  Layout lay{};
-  bool found = false;
-  const int two_cta = (233472 - 2 * 1024) / 2;
-  const int one_cta = 232448;
-  for (int pass = 0; pass < 2 && !found; ++pass) {
-    const int limit = pass == 0 ? two_cta : one_cta;
-    for (int TB = 16; TB >= 2; TB -= 2) {
-      Layout t{};
-      if (make_layout(net, TB, Q, &t) && t.bytes <= limit) {
-        lay = t;
-        lay.p.TB = TB;
-        found = true;
-        break;
-      }
-    }
-  }
-  if (!found)
-    return fail(VCB_ERR_UNSUPPORTED,
-                "vcb_mlp_crown: network does not fit the shared-memory-resident kernel");
-  CrownParams& p = lay.p;
+  Plan plan;
+  int rc = plan_crown(net, B, Q, &plan);
+  if (rc) return rc;
+  if (!workspace || workspace_bytes < plan.ws_bytes)
+    return fail(VCB_ERR_INVALID,
+                "vcb_mlp_crown: workspace of %zu bytes needed (got %zu)",
+                plan.ws_bytes, workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0)
+    return fail(VCB_ERR_INVALID, "vcb_mlp_crown: workspace must be 16-byte aligned");
+  CrownParams& p = plan.lay.p;
+  const int nfc = net->n_fc;
   p.n_fc = nfc;
   long long woff = 0;
   int boff = 0;
@@ -545,15 +667,9 @@ extern "C" int vcb_mlp_crown(const vcb_mlp* net, int32_t B, const float* xl,
   p.accout = acc;
   p.sbolo = sb_out_lo;
   p.sbohi = sb_out_hi;
-
-  int rc = ensure_smem(reinterpret_cast<const void*>(crown_mlp_kernel), lay.bytes);
+  p.slopes = static_cast<float2*>(workspace);
+  rc = ensure_smem(reinterpret_cast<const void*>(crown_mlp_kernel), plan.lay.bytes);
   if (rc) return rc;
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      &per_sm, crown_mlp_kernel, kNT, lay.bytes);
-  if (e != cudaSuccess) return cuda_fail(e, "vcb_mlp_crown: occupancy");
-  if (per_sm < 1) per_sm = 1;
-  const int grid = std::min(p.ntiles, sm_count() * per_sm);
-  crown_mlp_kernel<<<grid, kNT, lay.bytes, static_cast<cudaStream_t>(stream)>>>(p);
+  crown_mlp_kernel<<<plan.grid, kNT, plan.lay.bytes, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("vcb_mlp_crown: launch");
 }

@@ -134,11 +134,15 @@ def mlp_crown(desc, xl, xh, *, clamps=(None, None), sb_in=(None, None),
         out['sb_lo'] = torch.empty(total, dtype=F32, device=device)
         out['sb_hi'] = torch.empty(total, dtype=F32, device=device)
     P = _lib.ptr
-    rc = _lib.lib().vcb_mlp_crown(
+    L = _lib.lib()
+    ws_bytes = L.vcb_mlp_crown_workspace(desc.struct, B, Q) if B > 0 else 0
+    ws = _lib.workspace(ws_bytes, device)
+    rc = L.vcb_mlp_crown(
         desc.struct, B, P(xl), P(xh), P(clamps[0]), P(clamps[1]),
         P(sb_in[0]), P(sb_in[1]), P(alpha), P(beta), Q, P(W_q), P(b_q),
         P(out.get('lb')), P(out.get('A')), P(out.get('acc')),
-        P(out.get('sb_lo')), P(out.get('sb_hi')), _lib.stream_of(device))
+        P(out.get('sb_lo')), P(out.get('sb_hi')), P(ws), ws_bytes,
+        _lib.stream_of(device))
     _lib.check(rc, 'vcb_mlp_crown')
     return out
 
