@@ -95,6 +95,59 @@ int vcb_mlp_crown(const vcb_mlp* net, int32_t B,
  * (vcb_mlp_crown then reports the error). */
 size_t vcb_mlp_crown_workspace(const vcb_mlp* net, int32_t B, int32_t Q);
 
+/* Batched DeepZ zonotope forward for ReLU MLPs (shared-memory-resident
+ * weights).  Replaces _forward_zonotope_graph_batched(xl, xh, gg, device,
+ * dtype) (src/vibecheck/verify_zono_bnb.py:3079).
+ *
+ *   sb_lo/hi      packed per-layer pre-activation bounds out (or NULL).
+ *   unstable_any  per relu layer, per neuron int flags (layers back to back,
+ *                 dims[1..n_fc-1]); set to 1 where the neuron is unstable in
+ *                 some box (the caller zeroes it first), or NULL.
+ *   c_out, g_out, k_out  when c_out is non-NULL the last fc layer runs too:
+ *                 c_out (B, dims[n_fc]), g_out (B, dims[n_fc], kmax) with the
+ *                 box's own generators first and zeros after, k_out (B,) the
+ *                 generator count; kmax = vcb_mlp_zono_kmax(net).
+ */
+int vcb_mlp_zono(const vcb_mlp* net, int32_t B, const float* xl,
+                 const float* xh, float* sb_lo, float* sb_hi,
+                 int32_t* unstable_any, float* c_out, float* g_out,
+                 int32_t* k_out, void* stream);
+
+/* Generator capacity of the zonotope: dims[0] + sum of relu widths. */
+int vcb_mlp_zono_kmax(const vcb_mlp* net);
+
+/* CROWN intermediate-bound intersection for one relu layer of width n
+ * (src/vibecheck/verify_zono_bnb.py:4140-4146): lb_rows (B, 2n) holds the
+ * backward-CROWN lower bounds of [+z_j; -z_j]; where unstable_any[j] is set,
+ * lo = max(lo, lb_j) and hi = max(min(hi, -lb_{n+j}), lo), in place on the
+ * (B, n) lo/hi arrays. */
+int vcb_interm_intersect(int32_t B, int32_t n, const float* lb_rows,
+                         const int32_t* unstable_any, float* lo, float* hi,
+                         void* stream);
+
+/* One input-split BaB step for a batch of B leaves (single-CTA launch):
+ * closure, halfspace clipping, branching and child emission, following
+ * _input_split_batched_inner (src/vibecheck/verify_graph.py:12899-13382) and
+ * _clip_box_by_halfspaces_batched (verify_graph.py:12363).
+ *
+ *   query_disjunct (Q) disjunct id of each deduplicated query, 0..D-1.
+ *   q_sens         leading queries summed into the SB branching score (the
+ *                  unique halfspaces; later rows repeat one for another
+ *                  disjunct); <= 0 means all Q.
+ *   xl, xh (B, n_in); lb (B, Q); A (B, Q, n_in), acc (B, Q): the CROWN
+ *   input-space linear form (needed when clip or branch_sb).
+ *   lo_xl/lo_xh, hi_xl/hi_xh (B, n_in): the low-half and high-half children
+ *   of the usable leaves, compacted in leaf order.
+ *   counters[4]: leaves closed by CROWN, closed by clipping, split (= rows
+ *   written to each child block), degenerate (width <= 1e-12, left open).
+ */
+int vcb_bab_step(int32_t B, int32_t n_in, int32_t Q, int32_t D,
+                 int32_t q_sens, const int32_t* query_disjunct, const float* xl,
+                 const float* xh, const float* lb, const float* A,
+                 const float* acc, int32_t clip, int32_t branch_sb,
+                 float* lo_xl, float* lo_xh, float* hi_xl, float* hi_xh,
+                 int64_t* counters, void* stream);
+
 /* Diagnostic: FP32 FFMA throughput probe (no reference counterpart).  Runs
  * `blocks` CTAs of 256 threads, each thread `iters` x 64 dependent-chain FMAs
  * (8 independent chains); FLOPs = blocks * 256 * iters * 128.  `out` must

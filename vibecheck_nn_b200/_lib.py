@@ -42,6 +42,12 @@ SIGNATURES = {
                       _P],
     'vcb_mlp_crown_workspace': [ctypes.POINTER(VcbMlp), _I, _I],
     'vcb_probe_ffma': [_P, _I, _I, _P],
+    'vcb_mlp_zono': [ctypes.POINTER(VcbMlp), _I, _P, _P, _P, _P, _P, _P, _P,
+                     _P, _P],
+    'vcb_mlp_zono_kmax': [ctypes.POINTER(VcbMlp)],
+    'vcb_interm_intersect': [_I, _I, _P, _P, _P, _P, _P],
+    'vcb_bab_step': [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P,
+                     _P, _P, _P, _P, _P],
 }
 RESTYPES = {'vcb_last_error': ctypes.c_char_p,
             'vcb_mlp_crown_workspace': ctypes.c_size_t}

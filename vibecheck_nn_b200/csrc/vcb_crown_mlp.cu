@@ -111,8 +111,8 @@ __global__ void __launch_bounds__(kNT, 2)
   float2* slot = p.slopes + (long long)blockIdx.x * p.slot_f2;
 
   // per-thread tile coordinates (fixed for the whole kernel)
-  const int SG = TB >> 1;
-  const int f_og = tid / SG;                 // forward output group
+  const int SG = TB >> 1;                    // 0 when the forward is skipped
+  const int f_og = SG > 0 ? tid / SG : 0;    // forward output group
   const int f_sg = tid - f_og * SG;          // forward box pair (rows sg, sg+SG)
   const int RT = TB * Q;
   const int RG = (RT + 3) >> 2;
@@ -513,6 +513,7 @@ bool make_layout(const vcb_mlp* net, int TB, int Q, Layout* out) {
   off = pad4(off);
   const int SG = TB / 2;
   if (nfc > 1 && SG * g_max > kNT) return false;
+  if (TB < 1) return false;
   const int RT = TB * Q;
   const int RG = (RT + 3) / 4;
   if (Q > 0 && RG * cg_max > kNT) return false;
@@ -546,7 +547,7 @@ struct Plan {
   size_t ws_bytes;
 };
 
-int plan_crown(const vcb_mlp* net, int B, int Q, Plan* plan) {
+int plan_crown(const vcb_mlp* net, int B, int Q, bool ibp, Plan* plan) {
   const int nfc = net->n_fc;
   if (nfc < 1 || nfc > VCB_MAX_FC)
     return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_crown: n_fc=%d outside [1,%d]", nfc, VCB_MAX_FC);
@@ -562,10 +563,13 @@ int plan_crown(const vcb_mlp* net, int B, int Q, Plan* plan) {
   // work: the largest even TB <= 32 with at least two tiles per SM.
   int tb_max = 32;
   while (tb_max > 2 && (long long)B < (long long)tb_max * 2 * sm_count()) tb_max -= 2;
+  // Without the IBP forward (caller-supplied bounds) a tile may hold a single
+  // box, which many-row specs (the CROWN-intermediate seeds) need.
+  const int tb_step = ibp ? 2 : 1;
   bool found = false;
   for (int pass = 0; pass < 2 && !found; ++pass) {
     const int limit = pass == 0 ? two_cta : one_cta;
-    for (int TB = tb_max; TB >= 2; TB -= 2) {
+    for (int TB = tb_max; TB >= tb_step; TB -= tb_step) {
       Layout t{};
       if (make_layout(net, TB, Q, &t) && t.bytes <= limit) {
         plan->lay = t;
@@ -593,9 +597,14 @@ extern "C" size_t vcb_mlp_crown_workspace(const vcb_mlp* net, int32_t B,
                                           int32_t Q) {
   using namespace vcb;
   if (!net || B <= 0) return 0;
-  Plan plan;
-  if (plan_crown(net, B, Q, &plan) != VCB_OK) return 0;
-  return plan.ws_bytes;
+  // Large enough for either mode (the caller-supplied-bounds mode may use a
+  // different tile size).
+  size_t bytes = 0;
+  for (bool ibp : {true, false}) {
+    Plan plan;
+    if (plan_crown(net, B, Q, ibp, &plan) == VCB_OK) bytes = std::max(bytes, plan.ws_bytes);
+  }
+  return bytes;
 }
 
 extern "C" int vcb_mlp_crown(const vcb_mlp* net, int32_t B, const float* xl,
@@ -622,7 +631,7 @@ extern "C" int vcb_mlp_crown(const vcb_mlp* net, int32_t B, const float* xl,
   if (sb_in_lo && (clamp_lo || sb_out_lo))
     return fail(VCB_ERR_INVALID, "vcb_mlp_crown: sb_in excludes clamps and sb_out");
   Plan plan;
-  int rc = plan_crown(net, B, Q, &plan);
+  int rc = plan_crown(net, B, Q, /*ibp=*/sb_in_lo == nullptr, &plan);
   if (rc) return rc;
   if (!workspace || workspace_bytes < plan.ws_bytes)
     return fail(VCB_ERR_INVALID,
