@@ -95,6 +95,31 @@ int vcb_mlp_crown(const vcb_mlp* net, int32_t B,
  * (vcb_mlp_crown then reports the error). */
 size_t vcb_mlp_crown_workspace(const vcb_mlp* net, int32_t B, int32_t Q);
 
+/* Allocation-free variant of vcb_mlp_crown (no counterpart in the
+ * reference).  For callers that cannot allocate device memory while they
+ * bound boxes -- a host application whose memory pool already owns the GPU,
+ * or a latency-bound loop that must not call cudaMalloc -- it takes no
+ * workspace: the ReLU-slope scratch is a file-scope __device__ array of
+ * vcb_mlp_crown_noalloc_capacity() bytes (4 MiB) that every GPU loading the
+ * library holds until exit.  The array caps the number of persistent CTAs;
+ * a network whose single tile needs more than the array returns
+ * VCB_ERR_UNSUPPORTED.  The first call on a device looks up the array's
+ * device address, so make it before any stream capture.  All calls share
+ * the array: calls that overlap on the GPU race on it.  Arguments and
+ * results are those of vcb_mlp_crown. */
+int vcb_mlp_crown_noalloc(const vcb_mlp* net, int32_t B,
+                          const float* xl, const float* xh,
+                          const float* clamp_lo, const float* clamp_hi,
+                          const float* sb_in_lo, const float* sb_in_hi,
+                          const float* alpha, const float* beta,
+                          int32_t Q, const float* spec_W, const float* spec_b,
+                          float* lb, float* A, float* acc,
+                          float* sb_out_lo, float* sb_out_hi,
+                          void* stream);
+
+/* Bytes of the static scratch behind vcb_mlp_crown_noalloc. */
+size_t vcb_mlp_crown_noalloc_capacity(void);
+
 /* Batched DeepZ zonotope forward for ReLU MLPs (shared-memory-resident
  * weights).  Replaces _forward_zonotope_graph_batched(xl, xh, gg, device,
  * dtype) (src/vibecheck/verify_zono_bnb.py:3079).

@@ -41,6 +41,9 @@ SIGNATURES = {
                       _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t,
                       _P],
     'vcb_mlp_crown_workspace': [ctypes.POINTER(VcbMlp), _I, _I],
+    'vcb_mlp_crown_noalloc': [ctypes.POINTER(VcbMlp), _I, _P, _P, _P, _P, _P,
+                              _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P],
+    'vcb_mlp_crown_noalloc_capacity': [],
     'vcb_probe_ffma': [_P, _I, _I, _P],
     'vcb_mlp_zono': [ctypes.POINTER(VcbMlp), _I, _P, _P, _P, _P, _P, _P, _P,
                      _P, _P],
@@ -50,7 +53,8 @@ SIGNATURES = {
                      _P, _P, _P, _P, _P],
 }
 RESTYPES = {'vcb_last_error': ctypes.c_char_p,
-            'vcb_mlp_crown_workspace': ctypes.c_size_t}
+            'vcb_mlp_crown_workspace': ctypes.c_size_t,
+            'vcb_mlp_crown_noalloc_capacity': ctypes.c_size_t}
 
 _lib = None
 

@@ -21,6 +21,7 @@
 // forward a warp covers 16 boxes x 2 output groups, in the backward 32 row
 // groups x 1 column group.
 #include <algorithm>
+#include <mutex>
 
 #include "vcb_common.cuh"
 
@@ -607,38 +608,50 @@ extern "C" size_t vcb_mlp_crown_workspace(const vcb_mlp* net, int32_t B,
   return bytes;
 }
 
-extern "C" int vcb_mlp_crown(const vcb_mlp* net, int32_t B, const float* xl,
-                             const float* xh, const float* clamp_lo,
-                             const float* clamp_hi, const float* sb_in_lo,
-                             const float* sb_in_hi, const float* alpha,
-                             const float* beta, int32_t Q, const float* spec_W,
-                             const float* spec_b, float* lb, float* A,
-                             float* acc, float* sb_out_lo, float* sb_out_hi,
-                             void* workspace, size_t workspace_bytes,
-                             void* stream) {
-  using namespace vcb;
-  if (!net) return fail(VCB_ERR_INVALID, "vcb_mlp_crown: net is NULL");
-  if (B < 0 || Q < 0) return fail(VCB_ERR_INVALID, "vcb_mlp_crown: B=%d Q=%d", B, Q);
+namespace vcb {
+namespace {
+
+// Validates the arguments, plans the launch and runs crown_mlp_kernel with
+// `slots` as the slope scratch: either `slots_bytes` of caller workspace
+// (grid as planned, error if too small) or, when cap_grid is set, a fixed
+// buffer whose size caps the number of persistent CTAs.
+int launch_crown(const vcb_mlp* net, int32_t B, const float* xl, const float* xh,
+                 const float* clamp_lo, const float* clamp_hi, const float* sb_in_lo,
+                 const float* sb_in_hi, const float* alpha, const float* beta, int32_t Q,
+                 const float* spec_W, const float* spec_b, float* lb, float* A, float* acc,
+                 float* sb_out_lo, float* sb_out_hi, void* slots, size_t slots_bytes,
+                 bool cap_grid, void* stream, const char* who) {
+  if (!net) return fail(VCB_ERR_INVALID, "%s: net is NULL", who);
+  if (B < 0 || Q < 0) return fail(VCB_ERR_INVALID, "%s: B=%d Q=%d", who, B, Q);
   if (B == 0) return VCB_OK;  // nothing to bound; output pointers may be NULL
   if (!net->W || !net->b || !xl || !xh)
-    return fail(VCB_ERR_INVALID, "vcb_mlp_crown: NULL weight or box pointer");
+    return fail(VCB_ERR_INVALID, "%s: NULL weight or box pointer", who);
   if ((clamp_lo == nullptr) != (clamp_hi == nullptr) ||
       (sb_in_lo == nullptr) != (sb_in_hi == nullptr) ||
       (sb_out_lo == nullptr) != (sb_out_hi == nullptr))
-    return fail(VCB_ERR_INVALID, "vcb_mlp_crown: lo/hi pointers must be given in pairs");
+    return fail(VCB_ERR_INVALID, "%s: lo/hi pointers must be given in pairs", who);
   if (Q > 0 && (!spec_W || !spec_b || !lb))
-    return fail(VCB_ERR_INVALID, "vcb_mlp_crown: Q>0 needs spec_W, spec_b and lb");
+    return fail(VCB_ERR_INVALID, "%s: Q>0 needs spec_W, spec_b and lb", who);
   if (sb_in_lo && (clamp_lo || sb_out_lo))
-    return fail(VCB_ERR_INVALID, "vcb_mlp_crown: sb_in excludes clamps and sb_out");
+    return fail(VCB_ERR_INVALID, "%s: sb_in excludes clamps and sb_out", who);
   Plan plan;
   int rc = plan_crown(net, B, Q, /*ibp=*/sb_in_lo == nullptr, &plan);
   if (rc) return rc;
-  if (!workspace || workspace_bytes < plan.ws_bytes)
-    return fail(VCB_ERR_INVALID,
-                "vcb_mlp_crown: workspace of %zu bytes needed (got %zu)",
-                plan.ws_bytes, workspace_bytes);
-  if ((reinterpret_cast<uintptr_t>(workspace) & 15) != 0)
-    return fail(VCB_ERR_INVALID, "vcb_mlp_crown: workspace must be 16-byte aligned");
+  const size_t slot_bytes = (size_t)plan.lay.p.slot_f2 * sizeof(float2);
+  int grid = plan.grid;
+  if (cap_grid) {
+    const size_t fit = slot_bytes ? slots_bytes / slot_bytes : 0;
+    if (fit < 1)
+      return fail(VCB_ERR_UNSUPPORTED,
+                  "%s: one tile's ReLU slopes need %zu bytes, more than the %zu-byte "
+                  "static scratch", who, slot_bytes, slots_bytes);
+    grid = (int)std::min<size_t>((size_t)grid, fit);
+  } else if (!slots || slots_bytes < plan.ws_bytes) {
+    return fail(VCB_ERR_INVALID, "%s: workspace of %zu bytes needed (got %zu)", who,
+                plan.ws_bytes, slots_bytes);
+  }
+  if ((reinterpret_cast<uintptr_t>(slots) & 15) != 0)
+    return fail(VCB_ERR_INVALID, "%s: workspace must be 16-byte aligned", who);
   CrownParams& p = plan.lay.p;
   const int nfc = net->n_fc;
   p.n_fc = nfc;
@@ -676,9 +689,98 @@ extern "C" int vcb_mlp_crown(const vcb_mlp* net, int32_t B, const float* xl,
   p.accout = acc;
   p.sbolo = sb_out_lo;
   p.sbohi = sb_out_hi;
-  p.slopes = static_cast<float2*>(workspace);
+  p.slopes = static_cast<float2*>(slots);
   rc = ensure_smem(reinterpret_cast<const void*>(crown_mlp_kernel), plan.lay.bytes);
   if (rc) return rc;
-  crown_mlp_kernel<<<plan.grid, kNT, plan.lay.bytes, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch("vcb_mlp_crown: launch");
+  crown_mlp_kernel<<<grid, kNT, plan.lay.bytes, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch(who);
 }
+
+}  // namespace
+}  // namespace vcb
+
+extern "C" int vcb_mlp_crown(const vcb_mlp* net, int32_t B, const float* xl,
+                             const float* xh, const float* clamp_lo,
+                             const float* clamp_hi, const float* sb_in_lo,
+                             const float* sb_in_hi, const float* alpha,
+                             const float* beta, int32_t Q, const float* spec_W,
+                             const float* spec_b, float* lb, float* A,
+                             float* acc, float* sb_out_lo, float* sb_out_hi,
+                             void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  return vcb::launch_crown(net, B, xl, xh, clamp_lo, clamp_hi, sb_in_lo, sb_in_hi,
+                           alpha, beta, Q, spec_W, spec_b, lb, A, acc, sb_out_lo,
+                           sb_out_hi, workspace, workspace_bytes, /*cap_grid=*/false,
+                           stream, "vcb_mlp_crown");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of vcb_mlp_crown.
+//
+// Some callers cannot allocate device memory when they bound boxes: a host
+// application whose memory pool has already claimed the GPU, or a
+// latency-bound loop in which a cudaMalloc (and the device synchronisation it
+// can imply) is not allowed.  This entry point takes no workspace: the ReLU
+// slope slots live in a file-scope __device__ array of kStaticSlopeBytes that
+// every GPU which loads this library holds until the process exits.  The
+// array bounds the number of persistent CTAs (one slot each), so a network
+// whose single tile needs more than the array is rejected with
+// VCB_ERR_UNSUPPORTED.  Every call shares the array: calls that overlap on
+// the GPU (different streams, or without ordering between them) race on it.
+// Nothing in it needs clearing, because each tile writes its slopes before
+// it reads them.
+// ---------------------------------------------------------------------------
+namespace vcb {
+namespace {
+
+constexpr size_t kStaticSlopeBytes = size_t(4) << 20;  // 4 MiB per device
+__device__ __align__(256) float2 g_static_slopes[kStaticSlopeBytes / sizeof(float2)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_addr[kMaxDevices] = {};
+
+// Device address of g_static_slopes on the current device.  The host-side
+// symbol is only a stand-in, so the address is looked up once per device
+// (with that device current) and cached.
+int static_slopes_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "vcb_mlp_crown_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_crown_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_addr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_static_slopes);
+    if (e != cudaSuccess)
+      return cuda_fail(e, "vcb_mlp_crown_noalloc: cudaGetSymbolAddress(g_static_slopes)");
+    g_static_addr[dev] = ptr;
+  }
+  *out = g_static_addr[dev];
+  return VCB_OK;
+}
+
+}  // namespace
+}  // namespace vcb
+
+extern "C" int vcb_mlp_crown_noalloc(const vcb_mlp* net, int32_t B, const float* xl,
+                                     const float* xh, const float* clamp_lo,
+                                     const float* clamp_hi, const float* sb_in_lo,
+                                     const float* sb_in_hi, const float* alpha,
+                                     const float* beta, int32_t Q, const float* spec_W,
+                                     const float* spec_b, float* lb, float* A,
+                                     float* acc, float* sb_out_lo, float* sb_out_hi,
+                                     void* stream) {
+  using namespace vcb;
+  if (B == 0 && net && Q >= 0) return VCB_OK;
+  void* slots = nullptr;
+  int rc = static_slopes_address(&slots);
+  if (rc) return rc;
+  return launch_crown(net, B, xl, xh, clamp_lo, clamp_hi, sb_in_lo, sb_in_hi, alpha,
+                      beta, Q, spec_W, spec_b, lb, A, acc, sb_out_lo, sb_out_hi, slots,
+                      kStaticSlopeBytes, /*cap_grid=*/true, stream,
+                      "vcb_mlp_crown_noalloc");
+}
+
+extern "C" size_t vcb_mlp_crown_noalloc_capacity(void) { return vcb::kStaticSlopeBytes; }
