@@ -173,6 +173,25 @@ int vcb_bab_step(int32_t B, int32_t n_in, int32_t Q, int32_t D,
                  float* lo_xl, float* lo_xh, float* hi_xl, float* hi_xh,
                  int64_t* counters, void* stream);
 
+/* Batched sign-gradient PGD for ReLU MLPs (widths <= 128); replaces the loop
+ * of _simple_pgd / _simple_pgd_batched (src/vibecheck/verify_hybrid_acasxu.py:
+ * 39, 103).
+ *
+ *   x (N, n_in)    samples, updated in place; sample s belongs to box s / R
+ *                  of lo/hi ((N / R), n_in).
+ *   C (ncon, n_out), cb (ncon): margin rows; cdis (ncon) disjunct of each
+ *                  (0..D-1).  loss = min_d max_{c in d} (C_c . y + cb_c).
+ *   best           *best must be initialised to ~0ull; on return it holds
+ *                  (iteration << 32 | sample) of the SAT sample (loss <= 1e-6)
+ *                  the reference's loop would return first, or stays ~0ull.
+ *                  That sample's row of x is the witness.
+ */
+int vcb_mlp_pgd(const vcb_mlp* net, int32_t N, int32_t R, float* x,
+                const float* lo, const float* hi, int32_t ncon,
+                const float* C, const float* cb, const int32_t* cdis,
+                int32_t D, int32_t n_iter, float lr,
+                unsigned long long* best, void* stream);
+
 /* Diagnostic: FP32 FFMA throughput probe (no reference counterpart).  Runs
  * `blocks` CTAs of 256 threads, each thread `iters` x 64 dependent-chain FMAs
  * (8 independent chains); FLOPs = blocks * 256 * iters * 128.  `out` must

@@ -49,6 +49,8 @@ SIGNATURES = {
                      _P, _P],
     'vcb_mlp_zono_kmax': [ctypes.POINTER(VcbMlp)],
     'vcb_interm_intersect': [_I, _I, _P, _P, _P, _P, _P],
+    'vcb_mlp_pgd': [ctypes.POINTER(VcbMlp), _I, _I, _P, _P, _P, _I, _P, _P, _P,
+                    _I, _I, ctypes.c_float, _P, _P],
     'vcb_bab_step': [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P,
                      _P, _P, _P, _P, _P],
 }
