@@ -101,3 +101,15 @@ def test_cpu_device_is_refused():
     with pytest.raises(RuntimeError):
         ops._ibp_forward_graph_batched(torch.zeros(2, 4), torch.ones(2, 4), gg,
                                        'cpu', torch.float32)
+
+
+def test_install_rebinds_reference_functions():
+    import types
+    from vibecheck_nn_b200 import install, ops, bab, pgd
+    mods = {name: types.ModuleType(name) for name in install.BINDINGS}
+    done = install.install(mods)
+    assert mods['vibecheck.verify_zono_bnb']._spec_backward_graph_batched is \
+        ops._spec_backward_graph_batched
+    assert mods['vibecheck.verify_graph']._input_split_batched is bab._input_split_batched
+    assert mods['vibecheck.verify_hybrid_acasxu']._simple_pgd_batched is pgd._simple_pgd_batched
+    assert sum(len(v) for v in done.values()) == 8

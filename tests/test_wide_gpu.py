@@ -1,0 +1,185 @@
+"""GPU parity of the layer-wise (wide-network) IBP / CROWN / alpha-CROWN path."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import close, golden_layers, load_golden, max_excess
+from oracle import bounds as ob
+from vibecheck_nn_b200 import wide, workloads as wk
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device('cuda:0') if torch.cuda.is_available() else None
+
+
+def T(a):
+    return torch.as_tensor(np.asarray(a), device=DEV)
+
+
+def N(t):
+    return t.detach().cpu().numpy()
+
+
+@pytest.mark.parametrize('tag', ['small', 'acas'])
+def test_wide_ibp_crown_golden(tag):
+    g = load_golden(f'mlp_{tag}')
+    gg = wk.mlp_gg(golden_layers(g), DEV)
+    wn = wide.wide_net(gg, DEV)
+    sb = wide.wide_ibp(wn, T(g['xl']), T(g['xh']))
+    for L, (lo, hi) in sb.items():
+        assert close(N(lo), g[f'ibp32_lo{L}']) and close(N(hi), g[f'ibp32_hi{L}'])
+    out = wide.wide_crown(wn, T(g['xl']), T(g['xh']), sb, T(g['spec_W']), T(g['spec_b']),
+                          want_A=True)
+    assert close(N(out['lb']), g['crown32_lb']), max_excess(N(out['lb']), g['crown32_lb'])
+    assert close(N(out['A']), g['crown32_A']) and close(N(out['acc']), g['crown32_acc'])
+    clamps = {0: (T(g['clamp_lo0']), T(g['clamp_hi0']))}
+    sbc = wide.wide_ibp(wn, T(g['xl']), T(g['xh']), clamps)
+    for L, (lo, hi) in sbc.items():
+        assert close(N(lo), g[f'ibpc32_lo{L}']) and close(N(hi), g[f'ibpc32_hi{L}'])
+    lbc = wide.wide_crown(wn, T(g['xl']), T(g['xh']), sbc, T(g['spec_W']), T(g['spec_b']))['lb']
+    assert close(N(lbc), g['crownc32_lb'])
+
+
+def test_wide_alpha_gradient_matches_oracle():
+    """One adjoint evaluation against the oracle's hand-written adjoint, which
+    is itself pinned to torch autograd through the reference (float64)."""
+    rng = np.random.default_rng(21)
+    dims = (40, 64, 64, 48, 7)
+    layers = wk.mlp_params(dims, rng)
+    D, Q = 37, 3
+    x0 = rng.uniform(0, 1, (D, dims[0]))
+    xl = (x0 - 0.05).astype(np.float32)
+    xh = (x0 + 0.05).astype(np.float32)
+    SW = rng.normal(size=(Q, dims[-1])).astype(np.float32)
+    Sb = rng.normal(size=Q).astype(np.float32)
+    ggc = wk.mlp_gg(layers)
+    sb = ob.ibp_forward_batched(xl, xh, ggc)
+    alpha = {}
+    for L, (lo, hi) in sb.items():
+        alpha[L] = rng.uniform(0, 1, lo.shape).astype(np.float32)
+    lb_ref, grads = ob.alpha_grad(sb, xl, xh, ggc, SW, Sb, alpha)
+    gg = wk.mlp_gg(layers, DEV)
+    wn = wide.wide_net(gg, DEV)
+    sbd = {L: (T(lo), T(hi)) for L, (lo, hi) in sb.items()}
+    lb, contrib = wide.wide_alpha_grad(wn, T(xl), T(xh), sbd, T(SW), T(Sb),
+                                       {L: T(a) for L, a in alpha.items()})
+    assert close(N(lb), lb_ref), max_excess(N(lb), lb_ref)
+    for L, g in grads.items():
+        dc, ldo = contrib[L]
+        got = N(dc)[:, :g.shape[1]].reshape(D, Q, -1).sum(axis=1)
+        scale = np.abs(g).max() + 1e-12
+        assert np.allclose(got, g, rtol=1e-4, atol=1e-5 * scale), (L, np.abs(got - g).max())
+
+
+def test_alpha_domains_golden():
+    """The cfg3-style alpha loop against the reference's recorded best lb
+    (fp32 alpha trajectories agree to ~1e-3 relative; see the oracle tests)."""
+    g = load_golden('alpha_domains')
+    layers = golden_layers(g)
+    gg = wk.mlp_gg(layers, DEV)
+    clamps = {}
+    for L in range(len(layers) - 1):
+        if f'clamp_lo{L}' in g:
+            clamps[L] = (g[f'clamp_lo{L}'], g[f'clamp_hi{L}'])
+    best, _ = wide.alpha_crown_domains(g['xl'], g['xh'], gg, g['spec_W'], g['spec_b'],
+                                       clamps, DEV, n_iters=int(g['n_iters']),
+                                       lr=float(g['lr']))
+    assert close(N(best), g['best_lb'], rtol=5e-3, atol=1e-5), max_excess(
+        N(best), g['best_lb'], rtol=5e-3, atol=1e-5)
+
+
+def test_cfg3_small_domains_against_oracle():
+    """cfg3 network and domain construction at 64 domains x 4 iterations."""
+    w = wk.cfg3(seed=0)
+    ggc = wk.mlp_gg(w['layers'])
+    root = ob.ibp_forward_batched(w['xl'][None], w['xh'][None], ggc)
+    picked, clamps = wk.split_domains({L: v[0][0] for L, v in root.items()},
+                                      {L: v[1][0] for L, v in root.items()}, 6)
+    Dn = 1 << len(picked)
+    xl = np.broadcast_to(w['xl'], (Dn, w['xl'].size)).copy()
+    xh = np.broadcast_to(w['xh'], (Dn, w['xh'].size)).copy()
+    ref, _ = ob.alpha_beta_crown_domains(xl, xh, ggc, w['spec_W'], w['spec_b'], clamps,
+                                         n_iters=4, lr=0.1)
+    gg = wk.mlp_gg(w['layers'], DEV)
+    best, _ = wide.alpha_crown_domains(xl, xh, gg, w['spec_W'], w['spec_b'], clamps, DEV,
+                                       n_iters=4, lr=0.1)
+    assert close(N(best), ref, rtol=5e-3, atol=1e-4), max_excess(N(best), ref, rtol=5e-3,
+                                                                 atol=1e-4)
+
+
+@pytest.mark.parametrize('tag', ['small', 'acas'])
+def test_alpha_inputsplit_golden(tag):
+    """_run_alpha_crown_inputsplit_batched vs the reference's recorded lb
+    (6 iterations, lr 0.25, decay 0.98; fp32 alpha trajectories agree to
+    ~1e-3 relative)."""
+    from vibecheck_nn_b200 import alpha
+    g = load_golden(f'mlp_{tag}')
+    gg = wk.mlp_gg(golden_layers(g), DEV)
+    spec_ew = wk.spec_ew_from(g['spec_W'], g['spec_b'], DEV)
+    lb = alpha._run_alpha_crown_inputsplit_batched(T(g['xl']), T(g['xh']), gg, spec_ew, DEV,
+                                                   torch.float32, n_iters=6, lr=0.25,
+                                                   lr_decay=0.98)
+    assert close(N(lb), g['alpha32_lb'], rtol=5e-3, atol=1e-5), max_excess(
+        N(lb), g['alpha32_lb'], rtol=5e-3, atol=1e-5)
+
+
+def test_reference_style_autograd_loop():
+    """The reference's own alpha loop (torch Adam, (-lb.sum()).backward())
+    through ops._spec_backward_graph_batched, whose gradient is the
+    hand-written adjoint, reproduces the recorded best lb."""
+    from vibecheck_nn_b200 import ops
+    g = load_golden('alpha_domains')
+    layers = golden_layers(g)
+    gg = wk.mlp_gg(layers, DEV)
+    clamps = {}
+    for L in range(len(layers) - 1):
+        if f'clamp_lo{L}' in g:
+            clamps[L] = (T(g[f'clamp_lo{L}']), T(g[f'clamp_hi{L}']))
+    xl, xh = T(g['xl']), T(g['xh'])
+    sb = ops._ibp_forward_graph_batched(xl, xh, gg, DEV, torch.float32, relu_clamps=clamps)
+    alpha = {}
+    for L, (lo, hi) in sb.items():
+        lb_r = torch.clamp(lo, max=0)
+        ub_r = torch.maximum(torch.clamp(hi, min=0), lb_r + 1e-8)
+        up_s = ub_r / (ub_r - lb_r)
+        unst = (lo < 0) & (hi > 0)
+        alpha[L] = ((up_s > 0.5).float() * unst.float()).clone().requires_grad_(True)
+    spec_ew = wk.spec_ew_from(g['spec_W'], g['spec_b'], DEV)
+    opt = torch.optim.Adam(list(alpha.values()), lr=float(g['lr']))
+    best = None
+    for _ in range(int(g['n_iters'])):
+        opt.zero_grad()
+        lbs = ops._spec_backward_graph_batched(sb, xl, xh, gg, spec_ew, DEV, torch.float32,
+                                               alpha_at_layer=alpha)
+        best = lbs.detach().clone() if best is None else torch.maximum(best, lbs.detach())
+        if (best > 0).all():
+            break
+        (-lbs.sum()).backward()
+        opt.step()
+        with torch.no_grad():
+            for a in alpha.values():
+                a.clamp_(0.0, 1.0)
+    assert close(N(best), g['best_lb'], rtol=5e-3, atol=1e-5), max_excess(
+        N(best), g['best_lb'], rtol=5e-3, atol=1e-5)
+
+
+def test_bab_with_boundary_alpha_and_leaf_pgd():
+    """acasxu_2023.yaml-style settings (CROWN intermediates, boundary
+    alpha-CROWN, leaf PGD every 3 iterations) on cfg1: still verified, with
+    no more leaves than plain CROWN (alpha only tightens)."""
+    from vibecheck_nn_b200 import bab
+    w = wk.cfg1(0)
+    gg = wk.mlp_gg(w['layers'], DEV)
+    spec = bab.LinearSpec(w['xl'], w['xh'], [[('pair', 1, 0)]])
+    st = type('S', (), {})()
+    st.input_split_batch_size = 2048
+    st.input_split_crown_intermediate = True
+    st.input_split_batched_alpha_boundary_eps = 10.0
+    st.input_split_batched_alpha_iters = 20
+    st.input_split_batched_alpha_max_leaves = 2048
+    st.input_split_leaf_pgd_every = 3
+    st.input_split_leaf_pgd_max_leaves = 128
+    st.input_split_leaf_pgd_restarts = 256
+    st.input_split_leaf_pgd_iters = 50
+    v, det = bab._input_split_batched(None, spec, st, gg, DEV, torch.float32)
+    assert v == 'verified', det
+    assert det['batched_n_leaves'] <= int(load_golden('bab_cfg1_seed0')['n_leaves_ci1'])

@@ -1,0 +1,139 @@
+"""alpha-CROWN on the B200 kernels (no autograd through any kernel).
+
+* ``_run_alpha_crown_inputsplit_batched`` -- reference signature
+  (verify_zono_bnb.py:5137-5288): zonotope intermediates, min-area alpha
+  init, Adam(lr) with per-iteration lr decay on -sum(lb), clamp to [0, 1],
+  best-of-iterations lb, stop when every lb > 0 or the batch max improves by
+  less than ``early_stop_eps``.
+* ``alpha_boundary_refine`` -- the BaB's selective alpha-CROWN on boundary
+  leaves (verify_graph.py:12927-12975).
+* ``spec_backward_with_grad`` -- ``_spec_backward_graph_batched`` with alpha
+  (and beta) tensors that require grad: a ``torch.autograd.Function`` whose
+  backward is the hand-written adjoint kernel, so the reference's own
+  ``(-lbs.sum()).backward()`` loops work unchanged.
+"""
+from __future__ import annotations
+
+import torch
+
+from .interm import mlp_zono
+from .netdesc import mlp_desc
+from .ops import F32, _check_dtype, _dev, _f32, _unpack_layers, spec_matrix
+from . import wide
+
+
+def _sb_dict(desc, B, lo, hi):
+    lo_d = _unpack_layers(desc, B, lo)
+    hi_d = _unpack_layers(desc, B, hi)
+    return {L: (lo_d[L].contiguous(), hi_d[L].contiguous()) for L in lo_d}
+
+
+def zonotope_sb(desc, xl, xh):
+    lo, hi, _, _ = mlp_zono(desc, xl, xh)
+    return _sb_dict(desc, xl.shape[0], lo, hi)
+
+
+def _run_alpha_crown_inputsplit_batched(xl, xh, gg, spec_ew, device, dtype,
+                                        n_iters=10, lr=0.25, lr_decay=0.98,
+                                        early_stop_eps=1e-6):
+    """Batched alpha-CROWN for input-split leaves; returns best lb (B, Q)."""
+    _check_dtype(dtype)
+    device = _dev(device)
+    xl = _f32(xl, device)
+    xh = _f32(xh, device)
+    desc = mlp_desc(gg, device)
+    W_q, b_q = spec_ew if isinstance(spec_ew, tuple) else spec_matrix(spec_ew, device)
+    sb = zonotope_sb(desc, xl, xh)
+    wn = wide.wide_net(gg, device)
+    return wide.alpha_loop(wn, xl, xh, sb, W_q, b_q, n_iters, lr, lr_decay,
+                           early_stop_eps)
+
+
+def alpha_boundary_refine(desc, xl, xh, lb, W_q, b_q, qd, D, eps, iters,
+                          max_leaves, alpha_all, gg=None):
+    """Tighten the spec lbs of the unclosed leaves whose worst disjunct's best
+    query is within ``eps`` of 0 (or all unclosed leaves), at most
+    ``max_leaves`` of them ordered by that margin, with alpha-CROWN
+    (lr 0.25, decay 0.98) and keep the elementwise max."""
+    qd = qd.long()
+    closed = torch.ones(lb.shape[0], dtype=torch.bool, device=lb.device)
+    best_per = []
+    for d in range(D):
+        cols = (qd == d).nonzero(as_tuple=True)[0]
+        sub = lb[:, cols]
+        closed &= (sub > 0).any(dim=1)
+        best_per.append(sub.max(dim=1).values)
+    if bool(closed.all()):
+        return lb
+    worst = torch.stack(best_per, dim=1).min(dim=1).values
+    mask = ~closed if alpha_all else (~closed) & (worst > -eps)
+    idx = mask.nonzero(as_tuple=True)[0]
+    if idx.numel() == 0:
+        return lb
+    if not alpha_all:
+        order = worst[idx].argsort(descending=True)
+        idx = idx[order[:max_leaves]]
+    xl_c, xh_c = xl[idx].contiguous(), xh[idx].contiguous()
+    sb = zonotope_sb(desc, xl_c, xh_c)
+    wn = desc.__dict__.get('_wide') or wide.WideNet(desc)
+    desc.__dict__['_wide'] = wn
+    try:
+        new = wide.alpha_loop(wn, xl_c, xh_c, sb, W_q, b_q, iters, 0.25, 0.98, 1e-6)
+    except (RuntimeError, torch.cuda.OutOfMemoryError):
+        return lb  # opportunistic tightener, as in the reference
+    lb = lb.clone()
+    lb[idx] = torch.maximum(lb[idx], new)
+    return lb
+
+
+class _SpecBackwardAlpha(torch.autograd.Function):
+    """lb = CROWN(alpha); backward by the hand-written adjoint."""
+
+    @staticmethod
+    def forward(ctx, wn, xl, xh, sb, W_q, b_q, Ls, *alphas):
+        alpha = {L: a.detach().contiguous() for L, a in zip(Ls, alphas)}
+        with torch.no_grad():
+            lb, contrib = wide.wide_alpha_grad(wn, xl, xh, sb, W_q, b_q, alpha)
+        ctx.Q = W_q.shape[0]
+        ctx.Ls = Ls
+        ctx.widths = [alpha[L].shape[1] for L in Ls]
+        ctx.contrib = contrib
+        return lb
+
+    @staticmethod
+    def backward(ctx, grad):
+        w = grad.flatten()
+        if not bool((w == w[0]).all()):
+            raise NotImplementedError(
+                'vibecheck_nn_b200: alpha gradient only for a uniform weighting '
+                'of the spec lower bounds (the loss -sum(lb) the reference uses)')
+        scale = w[0]
+        outs = []
+        for L, n in zip(ctx.Ls, ctx.widths):
+            dc, ldo = ctx.contrib[L]
+            D = dc.shape[0] // ctx.Q
+            outs.append(dc.view(D, ctx.Q, ldo).sum(dim=1)[:, :n] * scale)
+        res = [None] * 7
+        for L, g in zip(ctx.Ls, outs):
+            res.append(g)
+        return tuple(res)
+
+
+def spec_backward_with_grad(desc, lo, hi, xl, xh, spec, alpha_at_layer,
+                            relu_split_beta, return_input_linear):
+    if relu_split_beta is not None and any(
+            bool(b.requires_grad) for b in relu_split_beta.values()):
+        raise NotImplementedError('vibecheck_nn_b200: gradients with respect to beta')
+    if relu_split_beta is not None and any(bool((b != 0).any()) for b in relu_split_beta.values()):
+        raise NotImplementedError('vibecheck_nn_b200: non-zero beta with alpha gradients')
+    if return_input_linear:
+        raise NotImplementedError('vibecheck_nn_b200: return_input_linear with alpha gradients')
+    B = xl.shape[0]
+    sb = _sb_dict(desc, B, lo, hi)
+    wn = desc.__dict__.get('_wide') or wide.WideNet(desc)
+    desc.__dict__['_wide'] = wn
+    W_q, b_q = spec
+    Ls = sorted(alpha_at_layer)
+    out = _SpecBackwardAlpha.apply(wn, xl, xh, sb, W_q, b_q, Ls,
+                                   *[alpha_at_layer[L] for L in Ls])
+    return out

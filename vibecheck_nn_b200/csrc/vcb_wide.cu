@@ -1,0 +1,481 @@
+// Layer-wise bound propagation for ReLU MLPs too wide for the
+// shared-memory-resident kernels (e.g. 784 -> [256] x 6 -> 10).
+//
+// Every layer is one launch of a tiled fp32 GEMM (128 x 64 tiles, 256
+// threads, 8 x 4 register tiles, double-buffered shared-memory k-slices)
+// whose epilogue carries the layer's bound arithmetic:
+//   * IBP (verify_zono_bnb.py:1115-1138): mid @ W^T and rad @ |W|^T in one
+//     pass, bias, clamps, crossing repair, bounds out, relu'd mid/rad out;
+//   * CROWN back-substitution (verify_zono_bnb.py:4379-4453): coef @ [W | b]
+//     with the ReLU relaxation (min-area or alpha lower slope) of the
+//     preceding layer, the raw coefficients recorded for the alpha adjoint,
+//     and per-tile intercept partial sums (reduced later in a fixed order);
+//   * alpha adjoint: g @ W^T + b with the derivative of the relaxation, the
+//     hand-written counterpart of autograd through the back-substitution
+//     (clamp(min=0) and clamp(max=0) both pass gradient at 0).
+// Small kernels finish the row sums, concretise against the input box, reduce
+// d(sum lb)/d(alpha) over the spec rows of each domain and run Adam + clamp.
+// All row-major buffers have leading dimensions that are multiples of 4.
+#include <algorithm>
+#include <cmath>
+
+#include "vcb_common.cuh"
+
+namespace vcb {
+namespace {
+
+constexpr int TM = 128, TN = 64, TK = 16, GT = 256;
+
+// Relaxation of one neuron from its pre-activation bounds
+// (verify_zono_bnb.py:511-521, 4413-4433): multiplier for e >= 0 (lower
+// slope; alpha for unstable neurons when given), for e < 0 (upper slope) and
+// the intercept factor (applied to min(e, 0)).
+struct Relax {
+  float pos, neg, icp;
+  bool unstable;
+};
+
+__device__ __forceinline__ Relax relax_of(float lo, float hi, const float* alpha) {
+  Relax r;
+  const float lb_r = fminf(lo, 0.f);
+  float ub_r = fmaxf(hi, 0.f);
+  ub_r = fmaxf(ub_r, __fadd_rn(lb_r, 1e-8f));
+  const float up_s = __fdiv_rn(ub_r, __fsub_rn(ub_r, lb_r));
+  const float up_t = __fmul_rn(-lb_r, up_s);
+  const bool active = lo >= 0.f, dead = hi <= 0.f;
+  r.unstable = !active && !dead;
+  r.neg = up_s;
+  r.icp = up_t;
+  if (active) r.pos = 1.f;
+  else if (dead) r.pos = 0.f;
+  else r.pos = alpha ? *alpha : (up_s > 0.5f ? 1.f : 0.f);
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// GEMM mainloop: acc[8][4] (+ acc2 when DUAL) for rows m0 + ty*8 + i,
+// cols n0 + tx*4 + j.  C = A (M x K) * op(B); op(B) = B^T (B is N x K) when
+// BT, else B (K x N).  DUAL also accumulates A2 * op(B2) (same shapes).
+// ---------------------------------------------------------------------------
+template <bool BT, bool DUAL>
+__device__ __forceinline__ void mainloop(int M, int N, int K, const float* __restrict__ A,
+                                         int lda, const float* __restrict__ B, int ldb,
+                                         const float* __restrict__ A2,
+                                         const float* __restrict__ B2, float (&acc)[8][4],
+                                         float (&acc2)[8][4], float* smem) {
+  const int tid = threadIdx.x;
+  const int ty = tid >> 4, tx = tid & 15;
+  const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN;
+  float* As = smem;                      // [2][TK][TM + 4]
+  float* Bs = As + 2 * TK * (TM + 4);    // [2][TK][TN + 4]
+  float* As2 = Bs + 2 * TK * (TN + 4);
+  float* Bs2 = As2 + (DUAL ? 2 * TK * (TM + 4) : 0);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = acc2[i][j] = 0.f;
+  // per-thread load assignments: A tile 128 x 16 = 2048 floats (8 per thread)
+  float ra[8], rb[4], ra2[8], rb2[4];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = tid + u * GT;          // 0..2047
+      const int mm = idx >> 4, kk = idx & 15;
+      const int gm = m0 + mm, gk = k0 + kk;
+      const bool ok = gm < M && gk < K;
+      ra[u] = ok ? __ldg(A + (long long)gm * lda + gk) : 0.f;
+      if (DUAL) ra2[u] = ok ? __ldg(A2 + (long long)gm * lda + gk) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int idx = tid + u * GT;          // 0..1023
+      int nn, kk;
+      if (BT) { nn = idx >> 4; kk = idx & 15; } else { kk = idx >> 6; nn = idx & 63; }
+      const int gn = n0 + nn, gk = k0 + kk;
+      const bool ok = gn < N && gk < K;
+      const long long off = BT ? (long long)gn * ldb + gk : (long long)gk * ldb + gn;
+      rb[u] = ok ? __ldg(B + off) : 0.f;
+      if (DUAL) rb2[u] = ok ? __ldg(B2 + off) : 0.f;
+    }
+  };
+  auto store = [&](int buf) {
+    float* as = As + buf * TK * (TM + 4);
+    float* bs = Bs + buf * TK * (TN + 4);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = tid + u * GT;
+      as[(idx & 15) * (TM + 4) + (idx >> 4)] = ra[u];
+      if (DUAL) As2[buf * TK * (TM + 4) + (idx & 15) * (TM + 4) + (idx >> 4)] = ra2[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int idx = tid + u * GT;
+      int nn, kk;
+      if (BT) { nn = idx >> 4; kk = idx & 15; } else { kk = idx >> 6; nn = idx & 63; }
+      bs[kk * (TN + 4) + nn] = rb[u];
+      if (DUAL) Bs2[buf * TK * (TN + 4) + kk * (TN + 4) + nn] = rb2[u];
+    }
+  };
+  const int nk = (K + TK - 1) / TK;
+  load(0);
+  store(0);
+  __syncthreads();
+  for (int t = 0; t < nk; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < nk) load((t + 1) * TK);
+    const float* as = As + buf * TK * (TM + 4);
+    const float* bs = Bs + buf * TK * (TN + 4);
+    const float* as2 = As2 + buf * TK * (TM + 4);
+    const float* bs2 = Bs2 + buf * TK * (TN + 4);
+#pragma unroll
+    for (int kk = 0; kk < TK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(as + kk * (TM + 4) + ty * 8);
+      const float4 a1 = *reinterpret_cast<const float4*>(as + kk * (TM + 4) + ty * 8 + 4);
+      const float4 b0 = *reinterpret_cast<const float4*>(bs + kk * (TN + 4) + tx * 4);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[4] = {b0.x, b0.y, b0.z, b0.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      if (DUAL) {
+        const float4 c0 = *reinterpret_cast<const float4*>(as2 + kk * (TM + 4) + ty * 8);
+        const float4 c1 = *reinterpret_cast<const float4*>(as2 + kk * (TM + 4) + ty * 8 + 4);
+        const float4 d0 = *reinterpret_cast<const float4*>(bs2 + kk * (TN + 4) + tx * 4);
+        const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const float dv[4] = {d0.x, d0.y, d0.z, d0.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc2[i][j] = fmaf(cv[i], dv[j], acc2[i][j]);
+      }
+    }
+    if (t + 1 < nk) store(buf ^ 1);
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// IBP layer: mid/rad (D x n_in, ld lda) -> bounds and relu'd mid/rad out.
+// ---------------------------------------------------------------------------
+struct IbpArgs {
+  int D, nin, nout, lda, ldo;
+  const float *mid, *rad, *W, *Wabs, *b, *clo, *chi;  // W, Wabs: nout x nin (ld nin)
+  float *sblo, *sbhi, *mid_o, *rad_o;                 // sb: D x nout; mid_o/rad_o: D x ldo
+};
+
+__global__ void __launch_bounds__(GT) ibp_layer_kernel(const IbpArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  float acc[8][4], acc2[8][4];
+  mainloop<true, true>(a.D, a.nout, a.nin, a.mid, a.lda, a.W, a.nin, a.rad, a.Wabs, acc, acc2,
+                       smem);
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  const int m0 = blockIdx.x * TM + ty * 8, n0 = blockIdx.y * TN + tx * 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + i;
+    if (m >= a.D) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + j;
+      if (n >= a.nout) continue;
+      const float mc = __fadd_rn(acc[i][j], a.b[n]);
+      const float rc = acc2[i][j];
+      float lo = __fsub_rn(mc, rc), hi = __fadd_rn(mc, rc);
+      const long long gi = (long long)m * a.nout + n;
+      if (a.clo) {
+        lo = fmaxf(lo, a.clo[gi]);
+        hi = fminf(hi, a.chi[gi]);
+      }
+      hi = fmaxf(hi, lo);
+      if (a.sblo) {
+        a.sblo[gi] = lo;
+        a.sbhi[gi] = hi;
+      }
+      if (a.mid_o) {
+        const float lc = fmaxf(lo, 0.f), hc = fmaxf(hi, 0.f);
+        a.mid_o[(long long)m * a.ldo + n] = __fmul_rn(__fadd_rn(lc, hc), 0.5f);
+        a.rad_o[(long long)m * a.ldo + n] = __fmul_rn(__fsub_rn(hc, lc), 0.5f);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CROWN backward layer: t = coef (R x nout, ld ldc) @ [W | b] -> coef_o
+// (R x nin, ld ldo) after the relaxation of relu layer L (bounds sb of box
+// r / Q), raw coefficients to rec (R x nin, ld ldo) when given, the bias dot
+// to bd (R), intercept partial sums to part (R x gridDim.y).
+// ---------------------------------------------------------------------------
+struct BackArgs {
+  int R, Q, nin, nout, ldc, ldo;
+  const float *coef, *Waug;   // Waug: nout x (nin + 1), ld lda_w
+  int ldw;
+  const float *sblo, *sbhi, *alpha, *beta;  // (R / Q) x nin, or NULL (no relu)
+  float *coef_o, *rec, *bd, *part;
+};
+
+__global__ void __launch_bounds__(GT) crown_back_kernel(const BackArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  float acc[8][4], acc2[8][4];
+  mainloop<false, false>(a.R, a.nin + 1, a.nout, a.coef, a.ldc, a.Waug, a.ldw, nullptr,
+                         nullptr, acc, acc2, smem);
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  const int m0 = blockIdx.x * TM + ty * 8, n0 = blockIdx.y * TN + tx * 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + i;
+    float pt = 0.f;
+    if (m < a.R) {
+      const int box = m / a.Q;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int n = n0 + j;
+        const float v = acc[i][j];
+        if (n < a.nin) {
+          float o = v;
+          if (a.sblo) {
+            const long long gi = (long long)box * a.nin + n;
+            const Relax r = relax_of(a.sblo[gi], a.sbhi[gi], a.alpha ? a.alpha + gi : nullptr);
+            if (a.rec) a.rec[(long long)m * a.ldo + n] = v;
+            if (v < 0.f) {
+              pt = fmaf(v, r.icp, pt);
+              o = __fmul_rn(v, r.neg);
+            } else {
+              o = __fmul_rn(v, r.pos);
+            }
+            if (a.beta) o = __fadd_rn(o, a.beta[gi]);
+          }
+          a.coef_o[(long long)m * a.ldo + n] = o;
+        } else if (n == a.nin) {
+          a.bd[m] = v;
+        } else if (n < a.ldo) {
+          a.coef_o[(long long)m * a.ldo + n] = 0.f;
+        }
+      }
+    }
+    // reduce the intercept partials of row m over the 16 column threads
+    for (int off = 8; off > 0; off >>= 1) pt += __shfl_xor_sync(0xffffffffu, pt, off, 16);
+    if (tx == 0 && m < a.R) a.part[(long long)m * gridDim.y + blockIdx.y] = pt;
+  }
+}
+
+// acc[r] = (acc[r] + bd[r]) + sum_t part[r][t]  (fixed order)
+__global__ void rowsum_kernel(int R, int nparts, int with_part, const float* bd,
+                              const float* part, float* acc) {
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < R; r += gridDim.x * blockDim.x) {
+    float a = __fadd_rn(acc[r], bd[r]);
+    if (with_part) {
+      float s = 0.f;
+      for (int t = 0; t < nparts; ++t) s = __fadd_rn(s, part[(long long)r * nparts + t]);
+      a = __fadd_rn(a, s);
+    }
+    acc[r] = a;
+  }
+}
+
+// lb[r] = acc[r] + sum_i pos(e)*xl[box] + sum_i neg(e)*xh[box]; optional A
+// copy and the adjoint seed g0 = d lb / d e = xl [e >= 0] + xh [e <= 0].
+__global__ void concretize_kernel(int R, int Q, int n0, int lde, const float* e,
+                                  const float* acc, const float* xl, const float* xh,
+                                  float* lb, float* A, float* g0) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (int r = warp; r < R; r += nwarps) {
+    const int box = r / Q;
+    float s1 = 0.f, s2 = 0.f;
+    for (int i = lane; i < n0; i += 32) {
+      const float ei = e[(long long)r * lde + i];
+      const float l = xl[(long long)box * n0 + i], h = xh[(long long)box * n0 + i];
+      s1 = fmaf(fmaxf(ei, 0.f), l, s1);
+      s2 = fmaf(fminf(ei, 0.f), h, s2);
+      if (A) A[(long long)r * n0 + i] = ei;
+      if (g0) g0[(long long)r * lde + i] = (ei >= 0.f ? l : 0.f) + (ei <= 0.f ? h : 0.f);
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, off);
+    }
+    if (lane == 0) lb[r] = __fadd_rn(__fadd_rn(acc[r], s1), s2);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// alpha adjoint layer: ga = g (R x nin, ld ldg) @ W^T + b  (R x nout) is
+// d(sum lb)/d(coefficient after relu L's relaxation); with rec (the raw
+// coefficient entering that relaxation) it gives
+//   dcontrib[r][j] = [unstable] * max(e, 0) * ga            (alpha gradient)
+//   g_o[r][j] = [e >= 0] pos * ga + [e <= 0] (neg * ga + icp).
+// ---------------------------------------------------------------------------
+struct AdjArgs {
+  int R, Q, nin, nout, ldg, ldo;
+  const float *g, *W, *b;       // W: nout x nin (ld nin)
+  const float *rec, *sblo, *sbhi, *alpha;  // rec: R x nout (ld ldo); sb/alpha (R/Q) x nout
+  float *g_o, *dcontrib;        // R x nout (ld ldo)
+};
+
+__global__ void __launch_bounds__(GT) alpha_adjoint_kernel(const AdjArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  float acc[8][4], acc2[8][4];
+  mainloop<true, false>(a.R, a.nout, a.nin, a.g, a.ldg, a.W, a.nin, nullptr, nullptr, acc,
+                        acc2, smem);
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  const int m0 = blockIdx.x * TM + ty * 8, n0 = blockIdx.y * TN + tx * 4;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + i;
+    if (m >= a.R) continue;
+    const int box = m / a.Q;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + j;
+      if (n >= a.nout) {
+        if (n < a.ldo) a.g_o[(long long)m * a.ldo + n] = 0.f;
+        continue;
+      }
+      const float ga = __fadd_rn(acc[i][j], a.b[n]);
+      const long long gi = (long long)box * a.nout + n;
+      const float e = a.rec[(long long)m * a.ldo + n];
+      const Relax r = relax_of(a.sblo[gi], a.sbhi[gi], a.alpha ? a.alpha + gi : nullptr);
+      a.dcontrib[(long long)m * a.ldo + n] = r.unstable ? __fmul_rn(fmaxf(e, 0.f), ga) : 0.f;
+      float go = 0.f;
+      if (e >= 0.f) go = __fmul_rn(r.pos, ga);
+      if (e <= 0.f) go = __fadd_rn(go, __fadd_rn(__fmul_rn(r.neg, ga), r.icp));
+      a.g_o[(long long)m * a.ldo + n] = go;
+    }
+  }
+}
+
+// grad[box][j] = sum_q dcontrib[box*Q + q][j]; then Adam (torch defaults
+// betas (0.9, 0.999), eps 1e-8) on the loss -sum(lb), and clamp to [0, 1].
+__global__ void alpha_adam_kernel(int D, int Q, int n, int ldc, const float* dcontrib,
+                                  float* alpha, float* m1, float* m2, float step_size,
+                                  float bc2_sqrt) {
+  const long long total = (long long)D * n;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long box = i / n;
+    const int j = (int)(i - box * n);
+    float gsum = 0.f;
+    for (int q = 0; q < Q; ++q) gsum = __fadd_rn(gsum, dcontrib[(box * Q + q) * ldc + j]);
+    const float g = -gsum;
+    // torch's foreach Adam: m.lerp_(g, 0.1); v = v*0.999 + 0.001*g*g;
+    // p -= step_size * m / (sqrt(v)/sqrt(bias_correction2) + eps)
+    const float mm = __fadd_rn(m1[i], __fmul_rn(0.1f, __fsub_rn(g, m1[i])));
+    const float vv = __fadd_rn(__fmul_rn(m2[i], 0.999f), __fmul_rn(__fmul_rn(g, g), 0.001f));
+    m1[i] = mm;
+    m2[i] = vv;
+    const float denom = __fadd_rn(__fdiv_rn(sqrtf(vv), bc2_sqrt), 1e-8f);
+    const float p = __fsub_rn(alpha[i], __fmul_rn(step_size, __fdiv_rn(mm, denom)));
+    alpha[i] = fminf(fmaxf(p, 0.f), 1.f);
+  }
+}
+
+int smem_bytes(bool dual) {
+  return (2 * TK * (TM + 4) + 2 * TK * (TN + 4)) * (dual ? 2 : 1) * 4;
+}
+
+dim3 gemm_grid(int M, int N) { return dim3((M + TM - 1) / TM, (N + TN - 1) / TN); }
+
+int grid1(long long n) {
+  return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, 8LL * sm_count()));
+}
+
+}  // namespace
+}  // namespace vcb
+
+using namespace vcb;
+
+extern "C" int vcb_wide_ibp_layer(int32_t D, int32_t nin, int32_t nout, const float* mid,
+                                  const float* rad, int32_t lda, const float* W,
+                                  const float* Wabs, const float* b, const float* clo,
+                                  const float* chi, float* sb_lo, float* sb_hi,
+                                  float* mid_o, float* rad_o, int32_t ldo, void* stream) {
+  if (D < 0 || nin <= 0 || nout <= 0) return fail(VCB_ERR_INVALID, "vcb_wide_ibp_layer: shape");
+  if (D == 0) return VCB_OK;
+  if (!mid || !rad || !W || !Wabs || !b || (lda & 3) || (mid_o && (ldo & 3)))
+    return fail(VCB_ERR_INVALID, "vcb_wide_ibp_layer: NULL pointer or ld not a multiple of 4");
+  IbpArgs a{D, nin, nout, lda, ldo, mid, rad, W, Wabs, b, clo, chi, sb_lo, sb_hi, mid_o, rad_o};
+  const int sm = smem_bytes(true);
+  int rc = ensure_smem(reinterpret_cast<const void*>(ibp_layer_kernel), sm);
+  if (rc) return rc;
+  ibp_layer_kernel<<<gemm_grid(D, nout), GT, sm, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("vcb_wide_ibp_layer");
+}
+
+extern "C" int vcb_wide_back_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
+                                   const float* coef, int32_t ldc, const float* Waug,
+                                   int32_t ldw, const float* sb_lo, const float* sb_hi,
+                                   const float* alpha, const float* beta, float* coef_o,
+                                   float* rec, int32_t ldo, float* bd, float* part,
+                                   void* stream) {
+  if (R < 0 || Q <= 0 || nin <= 0 || nout <= 0)
+    return fail(VCB_ERR_INVALID, "vcb_wide_back_layer: shape");
+  if (R == 0) return VCB_OK;
+  if (!coef || !Waug || !coef_o || !bd || !part || (ldc & 3) || (ldo & 3) || ldw < nin + 1 ||
+      ldo < nin + 1)
+    return fail(VCB_ERR_INVALID, "vcb_wide_back_layer: NULL pointer or bad leading dimension");
+  BackArgs a{R, Q, nin, nout, ldc, ldo, coef, Waug, ldw, sb_lo, sb_hi, alpha, beta,
+             coef_o, rec, bd, part};
+  const int sm = smem_bytes(false);
+  int rc = ensure_smem(reinterpret_cast<const void*>(crown_back_kernel), sm);
+  if (rc) return rc;
+  crown_back_kernel<<<gemm_grid(R, nin + 1), GT, sm, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("vcb_wide_back_layer");
+}
+
+extern "C" int vcb_wide_back_parts(int32_t R, int32_t nin) {
+  (void)R;
+  return (nin + 1 + TN - 1) / TN;
+}
+
+extern "C" int vcb_wide_rowsum(int32_t R, int32_t nparts, int32_t with_part, const float* bd,
+                               const float* part, float* acc, void* stream) {
+  if (R < 0) return fail(VCB_ERR_INVALID, "vcb_wide_rowsum: R");
+  if (R == 0) return VCB_OK;
+  rowsum_kernel<<<grid1(R), 256, 0, static_cast<cudaStream_t>(stream)>>>(R, nparts, with_part,
+                                                                         bd, part, acc);
+  return check_launch("vcb_wide_rowsum");
+}
+
+extern "C" int vcb_wide_concretize(int32_t R, int32_t Q, int32_t n0, int32_t lde,
+                                   const float* e, const float* acc, const float* xl,
+                                   const float* xh, float* lb, float* A, float* g0,
+                                   void* stream) {
+  if (R < 0 || Q <= 0 || n0 <= 0) return fail(VCB_ERR_INVALID, "vcb_wide_concretize: shape");
+  if (R == 0) return VCB_OK;
+  concretize_kernel<<<grid1((long long)R * 32), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      R, Q, n0, lde, e, acc, xl, xh, lb, A, g0);
+  return check_launch("vcb_wide_concretize");
+}
+
+extern "C" int vcb_wide_adjoint_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
+                                      const float* g, int32_t ldg, const float* W,
+                                      const float* b, const float* rec, const float* sb_lo,
+                                      const float* sb_hi, const float* alpha, float* g_o,
+                                      float* dcontrib, int32_t ldo, void* stream) {
+  if (R < 0 || Q <= 0 || nin <= 0 || nout <= 0)
+    return fail(VCB_ERR_INVALID, "vcb_wide_adjoint_layer: shape");
+  if (R == 0) return VCB_OK;
+  if (!g || !W || !b || !rec || !sb_lo || !sb_hi || !g_o || !dcontrib || (ldg & 3) || (ldo & 3))
+    return fail(VCB_ERR_INVALID, "vcb_wide_adjoint_layer: NULL pointer or bad ld");
+  AdjArgs a{R, Q, nin, nout, ldg, ldo, g, W, b, rec, sb_lo, sb_hi, alpha, g_o, dcontrib};
+  const int sm = smem_bytes(false);
+  int rc = ensure_smem(reinterpret_cast<const void*>(alpha_adjoint_kernel), sm);
+  if (rc) return rc;
+  alpha_adjoint_kernel<<<gemm_grid(R, nout), GT, sm, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("vcb_wide_adjoint_layer");
+}
+
+extern "C" int vcb_wide_alpha_adam(int32_t D, int32_t Q, int32_t n, int32_t ldc,
+                                   const float* dcontrib, float* alpha, float* m1, float* m2,
+                                   float lr, int32_t step, void* stream) {
+  if (D < 0 || Q <= 0 || n <= 0 || step < 1) return fail(VCB_ERR_INVALID, "vcb_wide_alpha_adam");
+  if (D == 0) return VCB_OK;
+  const double bc1 = 1.0 - std::pow(0.9, step);
+  const double bc2 = 1.0 - std::pow(0.999, step);
+  alpha_adam_kernel<<<grid1((long long)D * n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      D, Q, n, ldc, dcontrib, alpha, m1, m2, (float)((double)lr / bc1), (float)std::sqrt(bc2));
+  return check_launch("vcb_wide_alpha_adam");
+}

@@ -1,0 +1,44 @@
+"""Bind the B200 operators in place of vibecheck's batched bound kernels.
+
+The reference driver imports its kernels at call time
+(verify_graph.py:12485-12486, :12514-12515, :12858, :12937), so rebinding the
+module attributes before ``verify_graph`` runs routes the input-split BaB
+through this package.  ``verify_hybrid_acasxu`` binds its PGD helpers at
+import (verify_hybrid_acasxu.py:31-34), so they are rebound there too.
+"""
+from __future__ import annotations
+
+import importlib
+
+BINDINGS = {
+    'vibecheck.verify_zono_bnb': {
+        '_ibp_forward_graph_batched': ('ops', '_ibp_forward_graph_batched'),
+        '_spec_backward_graph_batched': ('ops', '_spec_backward_graph_batched'),
+        '_forward_zonotope_graph_batched': ('interm', '_forward_zonotope_graph_batched'),
+        '_crown_intermediate_batched': ('interm', '_crown_intermediate_batched'),
+        '_run_alpha_crown_inputsplit_batched': ('alpha', '_run_alpha_crown_inputsplit_batched'),
+    },
+    'vibecheck.verify_graph': {
+        '_input_split_batched': ('bab', '_input_split_batched'),
+    },
+    'vibecheck.verify_hybrid_acasxu': {
+        '_simple_pgd': ('pgd', '_simple_pgd'),
+        '_simple_pgd_batched': ('pgd', '_simple_pgd_batched'),
+    },
+}
+
+
+def install(modules=None):
+    """Rebind the reference's functions; returns {module: [names]} of what
+    was rebound.  ``modules`` maps module names to already-imported module
+    objects (default: import them)."""
+    done = {}
+    for mod_name, names in BINDINGS.items():
+        mod = (modules or {}).get(mod_name)
+        if mod is None:
+            mod = importlib.import_module(mod_name)
+        for attr, (sub, fn) in names.items():
+            impl = getattr(importlib.import_module(f'{__package__}.{sub}'), fn)
+            setattr(mod, attr, impl)
+            done.setdefault(mod_name, []).append(attr)
+    return done

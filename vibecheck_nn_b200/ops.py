@@ -151,6 +151,17 @@ def mlp_crown(desc, xl, xh, *, clamps=(None, None), sb_in=(None, None),
 # reference-signature operators
 # ---------------------------------------------------------------------------
 
+def fits_smem(desc, Q):
+    """True when the shared-memory-resident kernel takes this network (else
+    the layer-wise wide path runs)."""
+    key = ('_fits', Q)
+    v = desc.__dict__.get(key)
+    if v is None:
+        v = bool(_lib.lib().vcb_mlp_crown_workspace(desc.struct, 64, Q))
+        desc.__dict__[key] = v
+    return v
+
+
 def _ibp_forward_graph_batched(xl, xh, gg, device, dtype, relu_clamps=None,
                                root_sb=None):
     """Batched interval forward (verify_zono_bnb.py:1066-1153).
@@ -164,6 +175,13 @@ def _ibp_forward_graph_batched(xl, xh, gg, device, dtype, relu_clamps=None,
     desc = mlp_desc(gg, device)
     B = xl.shape[0]
     clo, chi = _clamp_arrays(desc, B, relu_clamps, root_sb, device)
+    if not fits_smem(desc, 0):
+        from . import wide
+        clamps = None
+        if clo is not None:
+            lo_d, hi_d = _unpack_layers(desc, B, clo), _unpack_layers(desc, B, chi)
+            clamps = {L: (lo_d[L], hi_d[L]) for L in lo_d}
+        return wide.wide_ibp(wide.wide_net(gg, device), xl, xh, clamps)
     out = mlp_crown(desc, xl, xh, clamps=(clo, chi), want_sb=True)
     lo = _unpack_layers(desc, B, out['sb_lo'])
     hi = _unpack_layers(desc, B, out['sb_hi'])
@@ -213,6 +231,20 @@ def _spec_backward_graph_batched(tight, xl, xh, gg, spec_ew, device, dtype,
         return spec_backward_with_grad(desc, lo, hi, xl, xh, spec,
                                        alpha_at_layer, relu_split_beta,
                                        return_input_linear)
+    if not fits_smem(desc, spec[0].shape[0]):
+        from . import wide
+        sb = {L: (tight[L][0].to(F32).contiguous(), tight[L][1].to(F32).contiguous())
+              for L in range(len(desc.relu_widths))}
+        out = wide.wide_crown(
+            wide.wide_net(gg, device), xl, xh, sb, spec[0], spec[1],
+            alpha=None if alpha_at_layer is None else
+            {L: a.detach().to(F32).contiguous() for L, a in alpha_at_layer.items()},
+            beta=None if relu_split_beta is None else
+            {L: b.detach().to(F32).contiguous() for L, b in relu_split_beta.items()},
+            want_A=return_input_linear)
+        if return_input_linear:
+            return out['lb'], out['A'], out['acc']
+        return out['lb']
     alpha = (None if alpha_at_layer is None else
              _packed_layers(desc, B, {L: a.detach() for L, a in alpha_at_layer.items()},
                             device, fill=0.0))
