@@ -192,6 +192,100 @@ int vcb_mlp_pgd(const vcb_mlp* net, int32_t N, int32_t R, float* x,
                 int32_t D, int32_t n_iter, float lr,
                 unsigned long long* best, void* stream);
 
+/* ---- layer-wise kernels (networks too wide for the shared-memory path,
+ * and convolutional networks).  All row-major buffers are float32; "ld"
+ * arguments are leading dimensions in elements.  They replace, one layer at a
+ * time, the fc / conv / relu branches of _ibp_forward_graph_batched
+ * (src/vibecheck/verify_zono_bnb.py:1093-1152) and of
+ * _spec_backward_graph_batched (:4379-4593), and the autograd pass of the
+ * alpha-CROWN loops (:5248-5288, verify_milp.py:2785-2807). ---- */
+
+/* IBP fc layer: mid/rad (D x nin, ld lda, lda % 4 == 0) times W^T / |W|^T
+ * (W: nout x nin) plus b; clamps (D x nout) or NULL; writes the
+ * pre-activation bounds sb_lo/hi (D x nout) and, if mid_o is non-NULL, the
+ * relu'd mid/rad (D x ldo). */
+int vcb_wide_ibp_layer(int32_t D, int32_t nin, int32_t nout, const float* mid,
+                       const float* rad, int32_t lda, const float* W,
+                       const float* Wabs, const float* b, const float* clo,
+                       const float* chi, float* sb_lo, float* sb_hi,
+                       float* mid_o, float* rad_o, int32_t ldo, void* stream);
+
+/* CROWN fc step: coef (R x nout, ld ldc) times Waug = [W | b] (nout x
+ * (nin+1), ld ldw) -> coef_o (R x nin, ld ldo >= nin+1) and the bias dot bd
+ * (R).  With sb_lo/hi ((R/Q) x nin, the bounds of the relu feeding this fc)
+ * the relu relaxation (alpha / beta optional, (R/Q) x nin) is applied, the
+ * raw coefficients are written to rec (R x ldo) when non-NULL and intercept
+ * partial sums to part (R x vcb_wide_back_parts(R, nin)). */
+int vcb_wide_back_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
+                        const float* coef, int32_t ldc, const float* Waug,
+                        int32_t ldw, const float* sb_lo, const float* sb_hi,
+                        const float* alpha, const float* beta, float* coef_o,
+                        float* rec, int32_t ldo, float* bd, float* part,
+                        void* stream);
+int vcb_wide_back_parts(int32_t R, int32_t nin);
+
+/* acc[r] = (acc[r] + bd[r]) + sum_t part[r][t] (if with_part), fixed order. */
+int vcb_wide_rowsum(int32_t R, int32_t nparts, int32_t with_part,
+                    const float* bd, const float* part, float* acc,
+                    void* stream);
+
+/* lb[r] = acc[r] + sum pos(e) xl[r/Q] + sum neg(e) xh[r/Q] over the n0 input
+ * coefficients e (R x n0, ld lde); optional A copy (R x n0) and adjoint seed
+ * g0 (R x lde) = xl [e >= 0] + xh [e <= 0]. */
+int vcb_wide_concretize(int32_t R, int32_t Q, int32_t n0, int32_t lde,
+                        const float* e, const float* acc, const float* xl,
+                        const float* xh, float* lb, float* A, float* g0,
+                        void* stream);
+
+/* alpha adjoint fc step: ga = g (R x nin, ld ldg) W^T + b; with rec (R x
+ * nout, ld ldo), the raw coefficients entering relu layer L's relaxation,
+ * writes g_o (the adjoint before that relu) and dcontrib (per-row alpha
+ * gradient, [unstable] max(e,0) ga). */
+int vcb_wide_adjoint_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
+                           const float* g, int32_t ldg, const float* W,
+                           const float* b, const float* rec,
+                           const float* sb_lo, const float* sb_hi,
+                           const float* alpha, float* g_o, float* dcontrib,
+                           int32_t ldo, void* stream);
+
+/* Adam (betas 0.9/0.999, eps 1e-8, as torch.optim.Adam) step `step` on the
+ * loss -sum(lb): gradient = -sum over the Q rows of each domain of dcontrib;
+ * alpha, m1, m2 (D x n) updated in place; alpha clamped to [0, 1]. */
+int vcb_wide_alpha_adam(int32_t D, int32_t Q, int32_t n, int32_t ldc,
+                        const float* dcontrib, float* alpha, float* m1,
+                        float* m2, float lr, int32_t step, void* stream);
+
+/* Convolution geometry arrays are int32[12] on the host:
+ * {C, H, W, C_out, H_out, W_out, kh, kw, stride_h, stride_w, pad_h, pad_w}. */
+
+/* IBP conv layer (NCHW, D boxes): lo/hi = conv(mid, K) + b -/+ conv(rad, |K|). */
+int vcb_conv_ibp(int32_t D, const int32_t* geometry, const float* mid,
+                 const float* rad, const float* K, const float* Kabs,
+                 const float* b, float* lo, float* hi, void* stream);
+
+/* CROWN conv step: e_in (R x C x H x W) = conv_transpose(e (R x C_out x H_out
+ * x W_out), K) -- the adjoint of the convolution. */
+int vcb_conv_back(int32_t R, const int32_t* geometry, const float* e,
+                  const float* K, float* e_in, void* stream);
+
+/* bd[r] = sum_{c, p} e[r][c][p] b[c] (conv bias dot, e: R x Co x hw). */
+int vcb_conv_bias_dot(int32_t R, int32_t Co, int32_t hw, const float* e,
+                      const float* b, float* bd, void* stream);
+
+/* IBP relu: clamps (or NULL), crossing repair, sb out, relu'd mid/rad (D x ldo). */
+int vcb_ibp_relu(int32_t D, int32_t n, const float* lo, const float* hi,
+                 const float* clo, const float* chi, float* sb_lo,
+                 float* sb_hi, float* mid, float* rad, int32_t ldo,
+                 void* stream);
+
+/* CROWN relu relaxation of coefficient rows e (R x n, ld lde) -> e_out (ld
+ * ldo) with the bounds of box r/Q (alpha / beta optional); part[r] = sum of
+ * min(e, 0) * up_t. */
+int vcb_relu_back(int32_t R, int32_t Q, int32_t n, const float* e,
+                  int32_t lde, float* e_out, int32_t ldo, const float* sb_lo,
+                  const float* sb_hi, const float* alpha, const float* beta,
+                  float* part, void* stream);
+
 /* Diagnostic: FP32 FFMA throughput probe (no reference counterpart).  Runs
  * `blocks` CTAs of 256 threads, each thread `iters` x 64 dependent-chain FMAs
  * (8 independent chains); FLOPs = blocks * 256 * iters * 128.  `out` must

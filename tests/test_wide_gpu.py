@@ -183,3 +183,59 @@ def test_bab_with_boundary_alpha_and_leaf_pgd():
     v, det = bab._input_split_batched(None, spec, st, gg, DEV, torch.float32)
     assert v == 'verified', det
     assert det['batched_n_leaves'] <= int(load_golden('bab_cfg1_seed0')['n_leaves_ci1'])
+
+
+def _small_cnn(g, device):
+    import importlib.util
+    import os
+    spec = importlib.util.spec_from_file_location(
+        'mkg', os.path.join(os.path.dirname(__file__), 'golden', 'make_golden.py'))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    gg = mod._small_cnn_gg(g['k1'], g['b1'], g['W2'], g['b2'], g['W3'], g['b3'], (2, 8, 8),
+                           torch.float32)
+    return wk.gg_to(gg, device)
+
+
+def test_conv_ibp_crown_golden():
+    from vibecheck_nn_b200 import ops
+    g = load_golden('conv_small')
+    gg = _small_cnn(g, DEV)
+    sb = ops._ibp_forward_graph_batched(T(g['xl']), T(g['xh']), gg, DEV, torch.float32)
+    for L, (lo, hi) in sb.items():
+        assert close(N(lo), g[f'ibp_lo{L}']) and close(N(hi), g[f'ibp_hi{L}']), L
+    spec_ew = wk.spec_ew_from(g['spec_W'], g['spec_b'], DEV)
+    lb, A, acc = ops._spec_backward_graph_batched(sb, T(g['xl']), T(g['xh']), gg, spec_ew, DEV,
+                                                  torch.float32, return_input_linear=True)
+    assert close(N(lb), g['lb']), max_excess(N(lb), g['lb'])
+    assert close(N(A), g['A']) and close(N(acc), g['acc'])
+
+
+def test_cfg4_cnn_against_oracle():
+    """cfg4 CNN (3x32x32 -> conv16 -> conv32 -> fc100 -> fc10), 16 split
+    domains, IBP with clamps + CROWN through conv-transpose."""
+    from vibecheck_nn_b200 import ops
+    w = wk.cfg4(seed=0)
+    ggc = wk.cnn_gg(w['params'])
+    root = ob.ibp_forward_batched(w['xl'][None], w['xh'][None], ggc)
+    picked, clamps = wk.split_domains({L: v[0][0] for L, v in root.items()},
+                                      {L: v[1][0] for L, v in root.items()}, 4)
+    Dn = 1 << len(picked)
+    xl = np.broadcast_to(w['xl'], (Dn, w['xl'].size)).copy()
+    xh = np.broadcast_to(w['xh'], (Dn, w['xh'].size)).copy()
+    y0 = ob.ibp_forward_batched(w['x0'][None], w['x0'][None], ggc)
+    SW, Sb = wk.margin_rows(10, 3)
+    sb_ref = ob.ibp_forward_batched(xl, xh, ggc, relu_clamps=clamps)
+    lb_ref, A_ref, acc_ref = ob.spec_backward_batched(sb_ref, xl, xh, ggc, SW, Sb,
+                                                      return_input_linear=True)
+    gg = wk.cnn_gg(w['params'], DEV)
+    tclamps = {L: (T(c[0]), T(c[1])) for L, c in clamps.items()}
+    sb = ops._ibp_forward_graph_batched(T(xl), T(xh), gg, DEV, torch.float32, relu_clamps=tclamps)
+    for L in sb_ref:
+        assert close(N(sb[L][0]), sb_ref[L][0]) and close(N(sb[L][1]), sb_ref[L][1]), L
+    lb, A, acc = ops._spec_backward_graph_batched(sb, T(xl), T(xh), gg,
+                                                  wk.spec_ew_from(SW, Sb, DEV), DEV,
+                                                  torch.float32, return_input_linear=True)
+    assert close(N(lb), lb_ref), max_excess(N(lb), lb_ref)
+    assert close(N(acc), acc_ref)
+    _ = y0

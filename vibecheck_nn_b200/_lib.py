@@ -62,6 +62,11 @@ SIGNATURES = {
                                _P, _P, _I, _P],
     'vcb_wide_alpha_adam': [_I, _I, _I, _I, _P, _P, _P, _P, ctypes.c_float, _I,
                             _P],
+    'vcb_conv_ibp': [_I, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    'vcb_conv_back': [_I, _P, _P, _P, _P, _P],
+    'vcb_conv_bias_dot': [_I, _I, _I, _P, _P, _P, _P],
+    'vcb_ibp_relu': [_I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P],
+    'vcb_relu_back': [_I, _I, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P],
     'vcb_bab_step': [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P,
                      _P, _P, _P, _P, _P],
 }

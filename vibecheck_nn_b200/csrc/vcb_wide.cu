@@ -20,11 +20,11 @@
 #include <cmath>
 
 #include "vcb_common.cuh"
+#include "vcb_gemm.cuh"
 
 namespace vcb {
 namespace {
 
-constexpr int TM = 128, TN = 64, TK = 16, GT = 256;
 
 // Relaxation of one neuron from its pre-activation bounds
 // (verify_zono_bnb.py:511-521, 4413-4433): multiplier for e >= 0 (lower
@@ -53,109 +53,6 @@ __device__ __forceinline__ Relax relax_of(float lo, float hi, const float* alpha
 }
 
 // ---------------------------------------------------------------------------
-// GEMM mainloop: acc[8][4] (+ acc2 when DUAL) for rows m0 + ty*8 + i,
-// cols n0 + tx*4 + j.  C = A (M x K) * op(B); op(B) = B^T (B is N x K) when
-// BT, else B (K x N).  DUAL also accumulates A2 * op(B2) (same shapes).
-// ---------------------------------------------------------------------------
-template <bool BT, bool DUAL>
-__device__ __forceinline__ void mainloop(int M, int N, int K, const float* __restrict__ A,
-                                         int lda, const float* __restrict__ B, int ldb,
-                                         const float* __restrict__ A2,
-                                         const float* __restrict__ B2, float (&acc)[8][4],
-                                         float (&acc2)[8][4], float* smem) {
-  const int tid = threadIdx.x;
-  const int ty = tid >> 4, tx = tid & 15;
-  const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN;
-  float* As = smem;                      // [2][TK][TM + 4]
-  float* Bs = As + 2 * TK * (TM + 4);    // [2][TK][TN + 4]
-  float* As2 = Bs + 2 * TK * (TN + 4);
-  float* Bs2 = As2 + (DUAL ? 2 * TK * (TM + 4) : 0);
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = acc2[i][j] = 0.f;
-  // per-thread load assignments: A tile 128 x 16 = 2048 floats (8 per thread)
-  float ra[8], rb[4], ra2[8], rb2[4];
-  auto load = [&](int k0) {
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int idx = tid + u * GT;          // 0..2047
-      const int mm = idx >> 4, kk = idx & 15;
-      const int gm = m0 + mm, gk = k0 + kk;
-      const bool ok = gm < M && gk < K;
-      ra[u] = ok ? __ldg(A + (long long)gm * lda + gk) : 0.f;
-      if (DUAL) ra2[u] = ok ? __ldg(A2 + (long long)gm * lda + gk) : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int idx = tid + u * GT;          // 0..1023
-      int nn, kk;
-      if (BT) { nn = idx >> 4; kk = idx & 15; } else { kk = idx >> 6; nn = idx & 63; }
-      const int gn = n0 + nn, gk = k0 + kk;
-      const bool ok = gn < N && gk < K;
-      const long long off = BT ? (long long)gn * ldb + gk : (long long)gk * ldb + gn;
-      rb[u] = ok ? __ldg(B + off) : 0.f;
-      if (DUAL) rb2[u] = ok ? __ldg(B2 + off) : 0.f;
-    }
-  };
-  auto store = [&](int buf) {
-    float* as = As + buf * TK * (TM + 4);
-    float* bs = Bs + buf * TK * (TN + 4);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int idx = tid + u * GT;
-      as[(idx & 15) * (TM + 4) + (idx >> 4)] = ra[u];
-      if (DUAL) As2[buf * TK * (TM + 4) + (idx & 15) * (TM + 4) + (idx >> 4)] = ra2[u];
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int idx = tid + u * GT;
-      int nn, kk;
-      if (BT) { nn = idx >> 4; kk = idx & 15; } else { kk = idx >> 6; nn = idx & 63; }
-      bs[kk * (TN + 4) + nn] = rb[u];
-      if (DUAL) Bs2[buf * TK * (TN + 4) + kk * (TN + 4) + nn] = rb2[u];
-    }
-  };
-  const int nk = (K + TK - 1) / TK;
-  load(0);
-  store(0);
-  __syncthreads();
-  for (int t = 0; t < nk; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < nk) load((t + 1) * TK);
-    const float* as = As + buf * TK * (TM + 4);
-    const float* bs = Bs + buf * TK * (TN + 4);
-    const float* as2 = As2 + buf * TK * (TM + 4);
-    const float* bs2 = Bs2 + buf * TK * (TN + 4);
-#pragma unroll
-    for (int kk = 0; kk < TK; ++kk) {
-      const float4 a0 = *reinterpret_cast<const float4*>(as + kk * (TM + 4) + ty * 8);
-      const float4 a1 = *reinterpret_cast<const float4*>(as + kk * (TM + 4) + ty * 8 + 4);
-      const float4 b0 = *reinterpret_cast<const float4*>(bs + kk * (TN + 4) + tx * 4);
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float bv[4] = {b0.x, b0.y, b0.z, b0.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
-      if (DUAL) {
-        const float4 c0 = *reinterpret_cast<const float4*>(as2 + kk * (TM + 4) + ty * 8);
-        const float4 c1 = *reinterpret_cast<const float4*>(as2 + kk * (TM + 4) + ty * 8 + 4);
-        const float4 d0 = *reinterpret_cast<const float4*>(bs2 + kk * (TN + 4) + tx * 4);
-        const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-        const float dv[4] = {d0.x, d0.y, d0.z, d0.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc2[i][j] = fmaf(cv[i], dv[j], acc2[i][j]);
-      }
-    }
-    if (t + 1 < nk) store(buf ^ 1);
-    __syncthreads();
-  }
-}
-
-// ---------------------------------------------------------------------------
 // IBP layer: mid/rad (D x n_in, ld lda) -> bounds and relu'd mid/rad out.
 // ---------------------------------------------------------------------------
 struct IbpArgs {
@@ -167,8 +64,8 @@ struct IbpArgs {
 __global__ void __launch_bounds__(GT) ibp_layer_kernel(const IbpArgs a) {
   extern __shared__ __align__(16) float smem[];
   float acc[8][4], acc2[8][4];
-  mainloop<true, true>(a.D, a.nout, a.nin, a.mid, a.lda, a.W, a.nin, a.rad, a.Wabs, acc, acc2,
-                       smem);
+  mainloop<true>(a.D, a.nout, a.nin, RowLoad{a.mid, a.lda}, RowLoad{a.W, a.nin},
+                 RowLoad{a.rad, a.lda}, RowLoad{a.Wabs, a.nin}, acc, acc2, smem);
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
   const int m0 = blockIdx.x * TM + ty * 8, n0 = blockIdx.y * TN + tx * 4;
 #pragma unroll
@@ -218,8 +115,8 @@ struct BackArgs {
 __global__ void __launch_bounds__(GT) crown_back_kernel(const BackArgs a) {
   extern __shared__ __align__(16) float smem[];
   float acc[8][4], acc2[8][4];
-  mainloop<false, false>(a.R, a.nin + 1, a.nout, a.coef, a.ldc, a.Waug, a.ldw, nullptr,
-                         nullptr, acc, acc2, smem);
+  mainloop<false>(a.R, a.nin + 1, a.nout, RowLoad{a.coef, a.ldc}, ColLoad{a.Waug, a.ldw},
+                  RowLoad{nullptr, 0}, ColLoad{nullptr, 0}, acc, acc2, smem);
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
   const int m0 = blockIdx.x * TM + ty * 8, n0 = blockIdx.y * TN + tx * 4;
 #pragma unroll
@@ -318,8 +215,8 @@ struct AdjArgs {
 __global__ void __launch_bounds__(GT) alpha_adjoint_kernel(const AdjArgs a) {
   extern __shared__ __align__(16) float smem[];
   float acc[8][4], acc2[8][4];
-  mainloop<true, false>(a.R, a.nout, a.nin, a.g, a.ldg, a.W, a.nin, nullptr, nullptr, acc,
-                        acc2, smem);
+  mainloop<false>(a.R, a.nout, a.nin, RowLoad{a.g, a.ldg}, RowLoad{a.W, a.nin},
+                  RowLoad{nullptr, 0}, RowLoad{nullptr, 0}, acc, acc2, smem);
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
   const int m0 = blockIdx.x * TM + ty * 8, n0 = blockIdx.y * TN + tx * 4;
 #pragma unroll
@@ -372,11 +269,7 @@ __global__ void alpha_adam_kernel(int D, int Q, int n, int ldc, const float* dco
   }
 }
 
-int smem_bytes(bool dual) {
-  return (2 * TK * (TM + 4) + 2 * TK * (TN + 4)) * (dual ? 2 : 1) * 4;
-}
-
-dim3 gemm_grid(int M, int N) { return dim3((M + TM - 1) / TM, (N + TN - 1) / TN); }
+int smem_bytes(bool dual) { return gemm_smem_bytes(dual); }
 
 int grid1(long long n) {
   return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, 8LL * sm_count()));

@@ -162,6 +162,33 @@ def fits_smem(desc, Q):
     return v
 
 
+def _mlp_or_graph(gg, device):
+    """(MlpDesc, None) for fc/relu chains, else (None, GraphNet) for chains
+    with convolutions; NotImplementedError for anything else."""
+    try:
+        return mlp_desc(gg, device), None
+    except NotImplementedError:
+        from .graph import graph_net
+        return None, graph_net(gg, device)
+
+
+def _graph_clamps(G, B, relu_clamps, root_sb, device):
+    if not relu_clamps and not root_sb:
+        return None
+    out = {}
+    for L, n in enumerate(G.relu_widths):
+        lo = torch.full((B, n), -math.inf, dtype=F32, device=device)
+        hi = torch.full((B, n), math.inf, dtype=F32, device=device)
+        if root_sb is not None and L in root_sb:
+            lo.copy_(_f32(root_sb[L][0], device).reshape(1, n).expand(B, n))
+            hi.copy_(_f32(root_sb[L][1], device).reshape(1, n).expand(B, n))
+        if relu_clamps is not None and L in relu_clamps:
+            torch.maximum(lo, _f32(relu_clamps[L][0], device).expand(B, n), out=lo)
+            torch.minimum(hi, _f32(relu_clamps[L][1], device).expand(B, n), out=hi)
+        out[L] = (lo, hi)
+    return out
+
+
 def _ibp_forward_graph_batched(xl, xh, gg, device, dtype, relu_clamps=None,
                                root_sb=None):
     """Batched interval forward (verify_zono_bnb.py:1066-1153).
@@ -172,7 +199,10 @@ def _ibp_forward_graph_batched(xl, xh, gg, device, dtype, relu_clamps=None,
     device = _dev(device)
     xl = _f32(xl, device)
     xh = _f32(xh, device)
-    desc = mlp_desc(gg, device)
+    desc, G = _mlp_or_graph(gg, device)
+    if G is not None:
+        from .graph import graph_ibp
+        return graph_ibp(G, xl, xh, _graph_clamps(G, xl.shape[0], relu_clamps, root_sb, device))
     B = xl.shape[0]
     clo, chi = _clamp_arrays(desc, B, relu_clamps, root_sb, device)
     if not fits_smem(desc, 0):
@@ -213,7 +243,23 @@ def _spec_backward_graph_batched(tight, xl, xh, gg, spec_ew, device, dtype,
         raise NotImplementedError('vibecheck_nn_b200: bilinear alpha terms')
     xl = _f32(xl, device)
     xh = _f32(xh, device)
-    desc = mlp_desc(gg, device)
+    desc, G = _mlp_or_graph(gg, device)
+    if G is not None:
+        from .graph import graph_crown
+        if alpha_at_layer is not None and any(bool(a.requires_grad) for a in alpha_at_layer.values()) \
+                and torch.is_grad_enabled():
+            raise NotImplementedError('vibecheck_nn_b200: alpha gradients on conv graphs')
+        W_q, b_q = spec_matrix(spec_ew, device)
+        sb = {L: (_f32(v[0], device), _f32(v[1], device)) for L, v in tight.items()}
+        out = graph_crown(G, xl, xh, sb, W_q, b_q,
+                          alpha=None if alpha_at_layer is None else
+                          {L: _f32(a.detach(), device) for L, a in alpha_at_layer.items()},
+                          beta=None if relu_split_beta is None else
+                          {L: _f32(b.detach(), device) for L, b in relu_split_beta.items()},
+                          want_A=return_input_linear)
+        if return_input_linear:
+            return out['lb'], out['A'], out['acc']
+        return out['lb']
     B = xl.shape[0]
     lo = _packed_layers(desc, B, {L: v[0] for L, v in tight.items()}, device)
     hi = _packed_layers(desc, B, {L: v[1] for L, v in tight.items()}, device)
