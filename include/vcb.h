@@ -192,6 +192,54 @@ int vcb_mlp_pgd(const vcb_mlp* net, int32_t N, int32_t R, float* x,
                 int32_t D, int32_t n_iter, float lr,
                 unsigned long long* best, void* stream);
 
+/* The restart loop of pgd_attack_general (src/vibecheck/pgd.py:233-524) for
+ * ReLU MLPs (widths <= 128), OSI initialisation included, in one launch.
+ *
+ *   x (N, n_in)      restarts' initial draw, updated in place; sample s
+ *                    belongs to box s / R of lo/hi ((N / R), n_in) and is
+ *                    restart s % R.
+ *   step0            (step_rows, n_in) initial step (eps_input * alpha_frac);
+ *                    step_rows = 1 (shared) or R (multi-alpha, one per restart).
+ *   w_d (R, n_out)   OSI projections; n_osi sign-ascent steps on w_r . f(x)
+ *                    with step0 before the loop (n_osi = 0: uniform init).
+ *   optim            0 sign_sgd, 1 adam_sign, 2 adam_clipping (_PGDOptim).
+ *   lr_decay, hinge  step decay per iteration; hinge-loss clamp threshold
+ *                    (margins compare with its float32 value, the plateau
+ *                    rule with the double).
+ *   plateau          pgd_plateau_iters; applied in the kernel when all R
+ *                    restarts fit one tile (R <= 64), else only recorded.
+ *   inv_bc1, inv_sbc2 (n_iter): float32 reciprocals of (1 - 0.9^t) and
+ *                    sqrt(1 - 0.999^t), t = 1..n_iter, as the GPU's
+ *                    scalar-divisor rounds them.
+ *   C, cb, cdis      margin rows (margin > 0 = safe), each row's disjunct
+ *                    0..D-1; cact the row's ordinal among the attacked
+ *                    disjuncts (0..n_act-1) or -1 for a disjunct that is
+ *                    only checked (restrict_disj).
+ *   per_restart_disj restart r descends only attacked disjunct r % n_act.
+ *   confirm_thr      spec.check's unsat_margin_bloat.
+ *   budget_ns        wall-time budget of the loop (0 = none).
+ *   best             init ~0ull; (screen << 32 | sample) of the first
+ *                    confirmed witness (screens 1..n_iter precede the updates,
+ *                    n_iter + 1 is the final check); that row of x is it.
+ *   gmin (n_iter+2)  init 0xffffffff; per screen the minimum attacked margin
+ *                    over all restarts, order-encoded (u >= 2^31: u - 2^31 is
+ *                    the bits of a non-negative float; else ~u the bits of a
+ *                    negative one) -- the host replays the plateau give-up.
+ *   t_stop           init INT32_MAX; the screen at which the budget ran out.
+ */
+int vcb_mlp_pgd_general(const vcb_mlp* net, int32_t N, int32_t R, float* x,
+                        const float* lo, const float* hi, const float* step0,
+                        int32_t step_rows, const float* w_d, int32_t n_osi,
+                        int32_t n_iter, int32_t optim, float lr_decay,
+                        double hinge, int32_t plateau, const float* inv_bc1,
+                        const float* inv_sbc2, int32_t ncon, const float* C,
+                        const float* cb, const int32_t* cdis,
+                        const int32_t* cact, int32_t D, int32_t n_act,
+                        int32_t per_restart_disj, double confirm_thr,
+                        unsigned long long budget_ns,
+                        unsigned long long* best, uint32_t* gmin,
+                        int32_t* t_stop, void* stream);
+
 /* ---- layer-wise kernels (networks too wide for the shared-memory path,
  * and convolutional networks).  All row-major buffers are float32; "ld"
  * arguments are leading dimensions in elements.  They replace, one layer at a

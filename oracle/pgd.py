@@ -9,6 +9,11 @@ samples are an input (the reference draws them from torch's generator after
 ``torch.manual_seed(seed)``; tests feed both implementations the same draw).
 Gradients follow torch autograd: F.relu passes gradient where the
 pre-activation is > 0; max/min route it to the first extremal index.
+
+``pgd_attack_general`` restates ``pgd_attack_general`` (``pgd.py:233-524``)
+with its optimiser ``_PGDOptim`` (:127-187) and margin rows
+``_build_constraint_matrices`` (:75-118).  Test infrastructure only: nothing
+in the product imports this module.
 """
 from __future__ import annotations
 
@@ -98,3 +103,156 @@ def pgd_batched(x0, lo, hi, gg, mats, n_iter=50, lr=0.1, dtype=np.float32):
         step = lr * np.sign(g) * width
         x = np.maximum(np.minimum(x - step, hi), lo)
     return False, None, n_iter
+
+
+def _forward_acts(layers, x):
+    """Forward pass keeping the pre-activations of the hidden layers."""
+    acts = []
+    a = x
+    for i, (W, b) in enumerate(layers):
+        z = a @ W.T + b
+        if i < len(layers) - 1:
+            acts.append(z)
+            a = np.maximum(z, 0)
+        else:
+            a = z
+    return a, acts
+
+
+def _backward(layers, acts, g):
+    """d(g . f(x))/dx with autograd's ReLU rule (gradient where z > 0)."""
+    for i in range(len(layers) - 1, -1, -1):
+        W, _ = layers[i]
+        g = g @ W
+        if i > 0:
+            g = g * (acts[i - 1] > 0)
+    return g
+
+
+def _fma32(a, b, c):
+    """fl32(a * b + c) with one rounding of the exact product (float64 holds
+    the product of two float32 values exactly)."""
+    return (a.astype(np.float64) * np.float64(b) + c.astype(np.float64)).astype(np.float32)
+
+
+def pgd_attack_general(xl, xh, gg, disjuncts, x_init, w_d=None, *, n_iter=100,
+                       lr_decay=0.99, hinge_thr=-1e-5, alpha_frac=0.25,
+                       alpha_fracs=None, optim='adam_clipping', osi_iters=50,
+                       plateau_iters=100, per_restart_disj=False, active=None,
+                       div='cuda', max_iters=None):
+    """Restatement of ``pgd_attack_general`` (pgd.py:233-524) in float32.
+
+    xl, xh (n_in,): the (already widened) search box.  disjuncts: the spec's
+    DNF in the tuple form of ``margin_matrices``.  x_init (R, n_in): the
+    restarts' uniform draw (pgd.py:375); w_d (R, n_out): the OSI projection
+    draw (pgd.py:384) or None for ``pgd_init_mode='uniform'``.  ``active``:
+    indices of the disjuncts to attack (``restrict_disj``), None = all.
+    ``alpha_fracs``: the multi-alpha list (pgd.py:306-321), None = single
+    ``alpha_frac``.  ``div``: how ``base_step / bc1`` rounds -- 'cuda'
+    multiplies by the float32 reciprocal (ATen's scalar-divisor path on the
+    GPU), 'cpu' divides.  ``max_iters`` stops the loop early without a final
+    screen (trajectory comparisons only).
+
+    Returns (sat, witness or None, info) with info = dict(t=screen index of
+    the witness, x=final iterate).
+    """
+    f32 = np.float32
+    layers = _mlp_layers(gg, f32)
+    xl = np.asarray(xl, f32).reshape(-1)
+    xh = np.asarray(xh, f32).reshape(-1)
+    x = np.asarray(x_init, f32).copy()
+    R = x.shape[0]
+    n_out = layers[-1][0].shape[0]
+    mats_all = margin_matrices(disjuncts, n_out, f32)
+    act_idx = list(range(len(disjuncts))) if active is None else sorted(active)
+    act_idx = [d for d in act_idx if len(disjuncts[d])]
+    mats = [mats_all[d] for d in act_idx]
+    if not mats:
+        return False, None, {'t': None, 'x': x}
+    eps_input = (xh - xl) / f32(2.0)
+    if alpha_fracs is not None:
+        pra = np.asarray([alpha_fracs[i % len(alpha_fracs)] for i in range(R)], f32)
+        step0 = eps_input[None, :] * pra[:, None]
+    else:
+        step0 = np.broadcast_to(eps_input * f32(alpha_frac), x.shape).astype(f32)
+    # OSI init (pgd.py:378-402): ascend w_d . f(x) with sign steps
+    if w_d is not None:
+        w_d = np.asarray(w_d, f32)
+        for _ in range(osi_iters):
+            _, acts = _forward_acts(layers, x)
+            g = _backward(layers, acts, w_d)
+            x = np.minimum(np.maximum(x + step0 * np.sign(g).astype(f32), xl), xh)
+    n_act = len(mats)
+    prd = bool(per_restart_disj) and n_act > 1
+    assign = np.arange(R) % n_act
+
+    def screen(out):
+        """Index of the first confirmed witness (pgd.py:443-451) or None."""
+        flat = np.concatenate([out @ W.T + b for W, b in mats], axis=1)
+        cand = flat.min(axis=1) <= 0
+        for bi in np.nonzero(cand)[0]:
+            worst = min(float((out[bi] @ W.T + b).max()) for W, b in mats_all
+                        if W.shape[0])
+            if worst <= 0.0:
+                return int(bi), flat
+        return None, flat
+
+    m1 = np.zeros_like(x)
+    m2 = np.zeros_like(x)
+    cur = step0.copy()
+    best_min = float('inf')
+    nimp = 0
+    b1, b2, eps_a = 0.9, 0.999, 1e-8
+    t_run = 0
+    for t in range(1, n_iter + 1):
+        if max_iters is not None and t > max_iters:
+            return False, None, {'t': None, 'x': x}
+        out, acts = _forward_acts(layers, x)
+        bi, flat = screen(out)
+        if bi is not None:
+            return True, x[bi].copy(), {'t': t, 'x': x}
+        curr_min = float(flat.min())
+        if curr_min > hinge_thr:
+            if curr_min < best_min - 1e-6:
+                best_min = curr_min
+                nimp = 0
+            else:
+                nimp += 1
+            if nimp >= plateau_iters:
+                break
+        else:
+            nimp = 0
+        # d/dy of sum clamp(margin, min=thr): rows with margin >= thr
+        g = np.zeros_like(out)
+        col = 0
+        for d, (W, b) in enumerate(mats):
+            m = flat[:, col:col + W.shape[0]]
+            sel = (m >= f32(hinge_thr)).astype(f32)
+            if prd:
+                sel = sel * (assign == d)[:, None]
+            g = g + sel @ W
+            col += W.shape[0]
+        grad = _backward(layers, acts, g)
+        t_run = t
+        if optim == 'sign_sgd':
+            delta = cur * np.sign(grad).astype(f32)
+        else:
+            m1 = _fma32(grad, f32(1 - b1), (m1 * f32(b1)).astype(f32))
+            m2 = _fma32(grad * grad, f32(1 - b2), (m2 * f32(b2)).astype(f32))
+            bc1 = 1.0 - b1 ** t
+            bc2 = 1.0 - b2 ** t
+            denom = np.sqrt(m2) / f32(bc2 ** 0.5) + f32(eps_a)
+            direction = np.sign(m1 / denom).astype(f32)
+            if optim == 'adam_sign':
+                delta = cur * direction
+            elif div == 'cuda':
+                delta = (cur * (f32(1.0) / f32(bc1))) * direction
+            else:
+                delta = (cur / f32(bc1)) * direction
+        x = np.minimum(np.maximum(x - delta, xl), xh)
+        cur = cur * f32(lr_decay)
+    out, _ = _forward_acts(layers, x)
+    bi, _ = screen(out)
+    if bi is not None:
+        return True, x[bi].copy(), {'t': t_run + 1, 'x': x}
+    return False, None, {'t': None, 'x': x}

@@ -64,10 +64,15 @@ def _net_arrays(layers):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--ref-src', required=True)
+    ap.add_argument('--only', default=None, choices=['pgd_general'],
+                    help='regenerate one fixture only')
     args = ap.parse_args()
     vz, vg, vh, vs, vspec = _import_reference(args.ref_src)
     import torch
     from vibecheck_nn_b200 import workloads as wk
+    if args.only == 'pgd_general':
+        _golden_pgd_general(vspec, wk)
+        return
 
     # ------------------------------------------------------------------ slopes
     lo = np.array([1.0, 2.0, -3.0, -2.0, -1.0, 1.0, -1.0, -3.0, 0.0, -0.0,
@@ -324,6 +329,109 @@ def main():
             print('cfg1 seed', seed, 'crown_interm', crown_i, verdict, det)
         _save(f'bab_cfg1_seed{seed}', **_net_arrays(w['layers']), xl=w['xl'],
               xh=w['xh'], d=np.array(w['d']), **res)
+
+
+# Cases of pgd_attack_general: (tag, net, case seed, threshold offsets q0, q3,
+# settings).  q0 puts the 'Y0 >= thr' disjunct q0 sample-std above the
+# sampled max of y0; q3 puts 'Y3 <= thr3' q3 std below the sampled min of y3.
+PGD_GENERAL_CASES = (
+    ('clip_osi_a', 'deep', 0, 0.1, 5.0, {}),
+    ('clip_osi_b', 'deep', 1, 0.2, 5.0, {}),
+    ('clip_osi_c', 'deep', 2, 0.4, 5.0, {}),
+    ('clip_osi_unsat', 'deep', 3, 3.0, 5.0, {}),
+    ('sign_sgd_uniform', 'deep', 4, 0.1, 0.1,
+     {'pgd_optim': 'sign_sgd', 'pgd_init_mode': 'uniform'}),
+    ('adam_sign_multi_prd', 'deep', 5, 0.1, 0.1,
+     {'pgd_optim': 'adam_sign', 'pgd_init_mode': 'uniform', 'pgd_alpha_multi': True,
+      'pgd_per_restart_disjunct': True}),
+    ('restrict_disj1', 'deep', 6, 0.0, 0.05, {'restrict_disj': {1}}),
+    ('plateau', 'deep', 7, 3.0, 5.0, {'pgd_plateau_iters': 6, 'no_pair': True}),
+    ('small_osi10', 'small', 8, 0.05, 5.0, {'pgd_osi_iters': 10, 'pgd_iter': 30,
+                                            'pgd_restarts': 16}),
+    ('small_unsat', 'small', 9, 2.0, 5.0, {'pgd_osi_iters': 10, 'pgd_iter': 30,
+                                           'pgd_restarts': 16}),
+)
+
+
+def _golden_pgd_general(vspec, wk):
+    """pgd_attack_general (pgd.py:233-524) on two seeded MLPs: the restarts'
+    initial draw, the OSI projections, the (sat, witness) result and the
+    last iterate the reference screened (recorded by wrapping the traced
+    forward, so UNSAT trajectories are pinned too)."""
+    import torch
+    import vibecheck.pgd as vp
+    nets = {'deep': wk.mlp_params(wk.ACAS_DIMS, np.random.default_rng(5)),
+            'small': wk.mlp_params((5, 20, 20, 4), np.random.default_rng(2))}
+    out = {}
+    for name, layers in nets.items():
+        for k, v in _net_arrays(layers).items():
+            out[f'{name}_{k}'] = v
+    orig = vp._get_traced_forward
+    for tag, net, cs, q0, q3, extra in PGD_GENERAL_CASES:
+        layers = nets[net]
+        gg = wk.mlp_gg(layers, 'cpu', torch.float32)
+        n_in, n_out = layers[0][0].shape[1], layers[-1][0].shape[0]
+        rng = np.random.default_rng(1000 + cs)
+        c = rng.uniform(-0.5, 0.5, n_in)
+        h = rng.uniform(0.05, 0.3, n_in)
+        xl = (c - h).astype(np.float32)
+        xh = (c + h).astype(np.float32)
+        pts = xl + (xh - xl) * rng.random((4096, n_in))
+        ys = wk._mlp_forward64(layers, pts)
+        thr = float(ys[:, 0].max() + q0 * ys[:, 0].std())
+        thr3 = float(ys[:, 3].min() - q3 * ys[:, 3].std())
+        second = [vspec.Constraint(3, '<=', thr3)]
+        if not extra.get('no_pair'):
+            second.insert(0, vspec.PairwiseConstraint(1, 2))
+        spec = vspec.VNNSpec(
+            x_lo=xl.astype(np.float64), x_hi=xh.astype(np.float64),
+            disjuncts=[vspec.Conjunct([vspec.Constraint(0, '>=', thr)]),
+                       vspec.Conjunct(second)])
+        st = dict(pgd_restarts=30, pgd_iter=100, pgd_optim='adam_clipping',
+                  pgd_init_mode='osi', pgd_osi_iters=50, pgd_plateau_iters=100)
+        st.update({k: v for k, v in extra.items() if k not in ('restrict_disj', 'no_pair')})
+        restrict = extra.get('restrict_disj')
+        R = st['pgd_restarts']
+        xlt, xht = torch.tensor(xl), torch.tensor(xh)
+        torch.manual_seed(cs)
+        x_init = xlt + (xht - xlt) * torch.rand(R, n_in)
+        w_d = (torch.rand(R, n_out) - 0.5) * 2.0
+        seen = []
+
+        def wrapped(gg_, sample, _seen=seen):
+            fn = orig(gg_, sample)
+
+            def rec(x):
+                if x.shape[0] == R:
+                    _seen.append(x.detach().clone())
+                return fn(x)
+            return rec
+        vp._get_traced_forward = wrapped
+        try:
+            sat, wit = vp.pgd_attack_general(xlt, xht, spec, gg, types.SimpleNamespace(**st),
+                                             restrict_disj=restrict, seed=cs)
+        finally:
+            vp._get_traced_forward = orig
+        n_osi = st['pgd_osi_iters'] if st['pgd_init_mode'] == 'osi' else 0
+        print('pgd_general', tag, 'sat', sat, 'screens', len(seen) - n_osi)
+        p = f'{tag}_'
+        out[p + 'net'] = np.array(net)
+        out[p + 'xl'] = xl
+        out[p + 'xh'] = xh
+        out[p + 'thr'] = np.array(thr)
+        out[p + 'thr3'] = np.array(thr3)
+        out[p + 'settings'] = np.array(repr(sorted(st.items())))
+        out[p + 'no_pair'] = np.array(bool(extra.get('no_pair')))
+        out[p + 'restrict'] = np.array(-1 if restrict is None else sorted(restrict)[0])
+        out[p + 'x_init'] = _n(x_init)
+        out[p + 'w_d'] = _n(w_d)
+        out[p + 'sat'] = np.array(bool(sat))
+        out[p + 'witness'] = (np.zeros(n_in, np.float32) if wit is None
+                              else np.asarray(wit, np.float32))
+        out[p + 'screens'] = np.array(len(seen) - n_osi)
+        out[p + 'x_last'] = _n(seen[-1])
+    out['tags'] = np.array([c[0] for c in PGD_GENERAL_CASES])
+    _save('pgd_general', **out)
 
 
 def _small_cnn_gg(k1, b1, W2, b2, W3, b3, ins, dt):

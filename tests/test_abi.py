@@ -112,4 +112,5 @@ def test_install_rebinds_reference_functions():
         ops._spec_backward_graph_batched
     assert mods['vibecheck.verify_graph']._input_split_batched is bab._input_split_batched
     assert mods['vibecheck.verify_hybrid_acasxu']._simple_pgd_batched is pgd._simple_pgd_batched
-    assert sum(len(v) for v in done.values()) == 8
+    assert mods['vibecheck.pgd'].pgd_attack_general is pgd.pgd_attack_general
+    assert sum(len(v) for v in done.values()) == 9

@@ -10,7 +10,8 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import close, golden_layers, load_golden, max_excess
+from conftest import (close, golden_layers, load_golden, max_excess, oracle_pgd_general,
+                      pgd_general_case)
 from oracle import bab as obab
 from oracle import bounds as ob
 from oracle import pgd as opgd
@@ -197,6 +198,25 @@ def test_pgd(tag):
         np.testing.assert_allclose(wit, g[f'{tag}_witness'], rtol=1e-5,
                                    atol=1e-6)
     _ = B
+
+
+PGD_GENERAL_TAGS = [str(t) for t in load_golden('pgd_general')['tags']]
+
+
+@pytest.mark.parametrize('tag', PGD_GENERAL_TAGS)
+def test_pgd_attack_general(tag):
+    """The pgd_attack_general restatement reproduces the reference bit for
+    bit: verdict, witness, the screen it was found at and the last iterate
+    the reference screened (CPU tensor semantics: base_step / bc1 divides)."""
+    g = load_golden('pgd_general')
+    case = pgd_general_case(g, tag)
+    gg = wk.mlp_gg(case['layers'])
+    sat, wit, info = oracle_pgd_general(case, gg, 'cpu')
+    assert sat == case['sat']
+    if sat:
+        np.testing.assert_array_equal(wit, case['witness'])
+        assert info['t'] == case['screens']
+    np.testing.assert_array_equal(info['x'], case['x_last'])
 
 
 @pytest.mark.parametrize('seed', [0, pytest.param(1, marks=pytest.mark.skipif(

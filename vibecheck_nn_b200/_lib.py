@@ -51,6 +51,10 @@ SIGNATURES = {
     'vcb_interm_intersect': [_I, _I, _P, _P, _P, _P, _P],
     'vcb_mlp_pgd': [ctypes.POINTER(VcbMlp), _I, _I, _P, _P, _P, _I, _P, _P, _P,
                     _I, _I, ctypes.c_float, _P, _P],
+    'vcb_mlp_pgd_general': [ctypes.POINTER(VcbMlp), _I, _I, _P, _P, _P, _P, _I, _P, _I,
+                            _I, _I, ctypes.c_float, ctypes.c_double, _I, _P, _P, _I, _P, _P,
+                            _P, _P, _I, _I, _I, ctypes.c_double, ctypes.c_uint64, _P,
+                            _P, _P, _P],
     'vcb_wide_ibp_layer': [_I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P,
                            _P, _P, _I, _P],
     'vcb_wide_back_layer': [_I, _I, _I, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P,

@@ -201,9 +201,9 @@ def _input_split_batched(graph, spec, settings, gg, device, dtype):
 
     if sat_finding and bool(_setting(settings, 'pgd_phase0_enabled', True)):
         from .pgd import root_pgd
-        sat, wit = root_pgd(spec, gg, n_output, device, settings)
+        sat, wit, phase = root_pgd(spec, gg, n_output, device, settings)
         if sat:
-            return 'sat', {'phase': 'batched_simple_pgd', 'witness': wit}
+            return 'sat', {'phase': phase, 'witness': wit}
 
     queries = spec.as_linear_queries(n_output)
     if not queries:

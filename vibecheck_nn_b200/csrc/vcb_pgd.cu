@@ -1,20 +1,35 @@
-// Batched sign-gradient PGD for ReLU MLPs (verify_hybrid_acasxu.py:39-161).
+// Batched PGD counterexample search for ReLU MLPs.
 //
-// Each sample x (a restart inside its box [lo, hi]) runs n_iter steps of
-//   y = f(x);  m_d = max_c (C_c . y + cb_c) over the constraints of disjunct d
-//   loss = min_d m_d;  SAT when loss <= 1e-6;
-//   x <- clamp(x - lr * sign(dloss/dx) * (hi - lo), lo, hi).
-// The gradient follows torch autograd on the reference's expression: F.relu
-// passes it where the pre-activation is > 0, max/min route it to the first
-// extremal index.  A sample that becomes SAT stops moving; the reported
-// witness is the SAT sample with the smallest (iteration, index) -- the
-// sample the reference's loop, which checks every sample once per iteration
-// and returns the first SAT one, would return.
+// Two kernels share one shared-memory layout (fc weights resident, one tile of
+// kPS samples per CTA, pre-activations kept for the ReLU masks) and the same
+// tile forward / backward passes:
 //
-// One CTA per tile of kPS samples with the fc weights resident in shared
-// memory; the tile's pre-activations (kept for the ReLU masks), activations
-// and gradients stay in shared memory for all iterations.
+// * pgd_mlp_kernel -- the sign-gradient PGD of _simple_pgd / _simple_pgd_batched
+//   (verify_hybrid_acasxu.py:39-161).  Each sample x (a restart inside its box
+//   [lo, hi]) runs n_iter steps of
+//     y = f(x);  m_d = max_c (C_c . y + cb_c) over the constraints of disjunct d
+//     loss = min_d m_d;  SAT when loss <= 1e-6;
+//     x <- clamp(x - lr * sign(dloss/dx) * (hi - lo), lo, hi).
+//   max/min route the gradient to the first extremal index (torch autograd).
+//   A sample that becomes SAT stops moving; the reported witness is the SAT
+//   sample with the smallest (iteration, index) -- the sample the reference's
+//   loop, which checks every sample once per iteration and returns the first
+//   SAT one, would return.
+//
+// * pgd_general_kernel -- pgd_attack_general (pgd.py:233-524): optional OSI
+//   initialisation (sign ascent on w_r . f(x), :378-402), then per iteration a
+//   witness screen (:443-451), the hinge loss sum_c clamp(m_c, min=thr) over the
+//   active disjuncts' rows (:469-492, optionally only restart r's disjunct),
+//   its gradient, the sign_sgd / adam_sign / adam_clipping step of _PGDOptim
+//   (:127-187) and the per-iteration step decay; a final screen after the loop.
+//   The plateau give-up (:453-467) depends on the minimum margin over all
+//   restarts, so the kernel records that minimum per iteration and the host
+//   replays the give-up rule; the wall-time budget is checked in the kernel on
+//   the GPU's global timer.
+//
+// F.relu passes the gradient where the pre-activation is > 0 in both.
 #include <algorithm>
+#include <climits>
 
 #include "vcb_common.cuh"
 
@@ -24,8 +39,10 @@ namespace {
 constexpr int kPT = 256;   // threads per CTA
 constexpr int kPS = 64;    // samples per tile
 constexpr int kPMaxW = 128;
+constexpr int kStep = kPT / kPS;
 
-struct PgdParams {
+// Shared-memory layout of the network and one sample tile (offsets in floats).
+struct PgdNet {
   int n_fc;
   int dims[VCB_MAX_FC + 1];
   const float* W;
@@ -40,6 +57,10 @@ struct PgdParams {
   int act_soff;           // 2 ping-pong activation buffers, kPS x pa
   int z_soff;             // n_fc pre-activation buffers, kPS x pz
   int g_soff, x_soff, c_soff;
+};
+
+struct PgdParams {
+  PgdNet net;
   int N, R, n_iter, ncon, D;
   float lr;
   float* x;               // (N, n_in) in/out
@@ -49,34 +70,148 @@ struct PgdParams {
   unsigned long long* best;  // min over SAT samples of (iter << 32 | index)
 };
 
-__global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__ PgdParams p) {
-  extern __shared__ __align__(16) float sm[];
-  __shared__ int done[kPS];
-  __shared__ int cstar[kPS];
-  __shared__ int stop;
-  const int tid = threadIdx.x;
-  const int nfc = p.n_fc;
-  const int n0 = p.dims[0];
-  const int nL = p.dims[nfc];
-  for (int l = 0; l < nfc; ++l) {
-    const int nin = p.dims[l], nout = p.dims[l + 1], pw = p.pw[l];
-    float* dst = sm + p.w_soff[l];
-    const float* Wg = p.W + p.w_goff[l];
-    const float* bg = p.b + p.b_goff[l];
-    for (int o = tid >> 5; o < p.wrows[l]; o += kPT / 32)
+struct PgdGenParams {
+  PgdNet net;
+  int N, R, n_osi, n_iter, ncon, D, n_act, prd, optim, step_rows, plateau;
+  int m1_soff, m2_soff, cur_soff, mg_soff;
+  float hinge, decay, beta1, beta2, one_m_beta1, one_m_beta2, eps;
+  double confirm_thr, hinge_d;
+  unsigned long long budget_ns;   // 0: no wall-time budget
+  float* x;                       // (N, n_in) in/out
+  const float *lo, *hi;           // (N / R, n_in)
+  const float* step0;             // (step_rows, n_in); row s % R when step_rows == R
+  const float* w_d;               // (R, n_out) OSI projections, or NULL
+  const float* inv_bc1;           // (n_iter) float32(1 / float32(1 - beta1^t))
+  const float* inv_sbc2;          // (n_iter) float32(1 / float32(sqrt(1 - beta2^t)))
+  const float *C, *cb;            // (ncon, n_out), (ncon,)
+  const int* cdis;                // disjunct of each row among all D
+  const int* cact;                // ordinal of the row's disjunct among the active ones, or -1
+  unsigned long long* best;       // min over confirmed witnesses of (screen << 32 | index)
+  unsigned int* gmin;             // (n_iter + 2) order-encoded min active margin per screen
+  int* t_stop;                    // screen at which the wall-time budget ended the loop
+};
+
+__device__ __forceinline__ float sgnf(float v) { return v > 0.f ? 1.f : (v < 0.f ? -1.f : 0.f); }
+
+// Monotone float -> unsigned map, so atomicMin on the code is a float minimum.
+__device__ __forceinline__ unsigned int order_code(float f) {
+  const unsigned int u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float order_decode(unsigned int u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Weights (+ bias column) of every fc layer into shared memory.
+__device__ void load_net(const PgdNet& n, float* sm, int tid) {
+  for (int l = 0; l < n.n_fc; ++l) {
+    const int nin = n.dims[l], nout = n.dims[l + 1], pw = n.pw[l];
+    float* dst = sm + n.w_soff[l];
+    const float* Wg = n.W + n.w_goff[l];
+    const float* bg = n.b + n.b_goff[l];
+    for (int o = tid >> 5; o < n.wrows[l]; o += kPT / 32)
       for (int i = tid & 31; i < pw; i += 32) {
         float v = 0.f;
         if (o < nout) v = (i < nin) ? Wg[(long long)o * nin + i] : (i == nin ? bg[o] : 0.f);
         dst[o * pw + i] = v;
       }
   }
-  float* Cs = sm + p.c_soff;
+}
+
+// Forward pass of the tile's samples xs (kPS x n0): z_l kept for the masks,
+// a_{l+1} = relu(z_l); the network output is z_{n_fc-1}.
+__device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int tid) {
+  const int n0 = n.dims[0], pa = n.pa, pz = n.pz;
+  float* a_cur = sm + n.act_soff;
+  const int n0p = pad4(n0);
+  for (int idx = tid; idx < kPS * n0p; idx += kPT) {
+    const int s = idx / n0p, i = idx - s * n0p;
+    a_cur[s * pa + i] = i < n0 ? xs[s * n0 + i] : 0.f;
+  }
+  __syncthreads();
+  for (int l = 0; l < n.n_fc; ++l) {
+    const int nin = n.dims[l], nout = n.dims[l + 1], pw = n.pw[l];
+    const float* sW = sm + n.w_soff[l];
+    const float* ain = sm + n.act_soff + (l & 1) * kPS * pa;
+    float* aout = sm + n.act_soff + ((l + 1) & 1) * kPS * pa;
+    float* z = sm + n.z_soff + l * kPS * pz;
+    const int kend = pad4(nin);
+    const int noutp = pad4(nout);
+    for (int idx = tid; idx < kPS * noutp; idx += kPT) {
+      const int o = idx / kPS, s = idx - o * kPS;
+      if (o >= nout) {
+        aout[s * pa + o] = 0.f;
+        continue;
+      }
+      float acc = 0.f;
+      const float* ar = ain + s * pa;
+      const float* wr = sW + o * pw;
+      for (int k = 0; k < kend; k += 4) {
+        const float4 av = *reinterpret_cast<const float4*>(ar + k);
+        const float4 wv = *reinterpret_cast<const float4*>(wr + k);
+        acc = fmaf(av.x, wv.x, acc);
+        acc = fmaf(av.y, wv.y, acc);
+        acc = fmaf(av.z, wv.z, acc);
+        acc = fmaf(av.w, wv.w, acc);
+      }
+      const float zz = __fadd_rn(acc, wr[nin]);
+      z[s * pz + o] = zz;
+      aout[s * pa + o] = fmaxf(zz, 0.f);
+    }
+    __syncthreads();
+  }
+}
+
+// Backward pass: g (kPS x pz, seeded with d loss / d y, zero past n_out) is
+// replaced by d loss / d x in its first n0 columns.
+__device__ void tile_backward(const PgdNet& n, float* sm, int tid) {
+  const int pz = n.pz;
+  float* g = sm + n.g_soff;
+  for (int l = n.n_fc - 1; l >= 0; --l) {
+    const int nin = n.dims[l], nout = n.dims[l + 1], pw = n.pw[l];
+    const float* sW = sm + n.w_soff[l];
+    const float* zprev = (l > 0) ? sm + n.z_soff + (l - 1) * kPS * pz : nullptr;
+    float vals[(kPMaxW + kStep - 1) / kStep];
+    const int sl = tid % kPS, i0 = tid / kPS;
+    int cnt = 0;
+    for (int i = i0; i < nin; i += kStep) {
+      float acc = 0.f;
+      for (int o = 0; o < nout; ++o) acc = fmaf(g[sl * pz + o], sW[o * pw + i], acc);
+      if (zprev && !(zprev[sl * pz + i] > 0.f)) acc = 0.f;
+      vals[cnt++] = acc;
+    }
+    __syncthreads();  // every thread has read g
+    cnt = 0;
+    for (int i = i0; i < pz; i += kStep) g[sl * pz + i] = (i < nin) ? vals[cnt++] : 0.f;
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__ PgdParams p) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ int done[kPS];
+  __shared__ int cstar[kPS];
+  __shared__ int stop;
+  const PgdNet& n = p.net;
+  const int tid = threadIdx.x;
+  const int nfc = n.n_fc;
+  const int n0 = n.dims[0];
+  const int nL = n.dims[nfc];
+  load_net(n, sm, tid);
+  float* Cs = sm + n.c_soff;
   for (int idx = tid; idx < p.ncon * nL; idx += kPT) Cs[idx] = p.C[idx];
   for (int idx = tid; idx < p.ncon; idx += kPT) Cs[p.ncon * nL + idx] = p.cb[idx];
   __syncthreads();
-  const int pa = p.pa, pz = p.pz;
-  float* xs = sm + p.x_soff;  // kPS x n0 current samples
-  float* g = sm + p.g_soff;   // kPS x pz gradient rows
+  const int pz = n.pz;
+  float* xs = sm + n.x_soff;  // kPS x n0 current samples
+  float* g = sm + n.g_soff;   // kPS x pz gradient rows
   const int ntiles = (p.N + kPS - 1) / kPS;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int s0 = tile * kPS;
@@ -95,47 +230,9 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
       }
       __syncthreads();
       if (stop) break;
-      // ---- forward: z_l stored for the masks, a_{l+1} = relu(z_l)
-      float* a_cur = sm + p.act_soff;
-      const int n0p = pad4(n0);
-      for (int idx = tid; idx < kPS * n0p; idx += kPT) {
-        const int s = idx / n0p, i = idx - s * n0p;
-        a_cur[s * pa + i] = i < n0 ? xs[s * n0 + i] : 0.f;
-      }
-      __syncthreads();
-      for (int l = 0; l < nfc; ++l) {
-        const int nin = p.dims[l], nout = p.dims[l + 1], pw = p.pw[l];
-        const float* sW = sm + p.w_soff[l];
-        const float* ain = sm + p.act_soff + (l & 1) * kPS * pa;
-        float* aout = sm + p.act_soff + ((l + 1) & 1) * kPS * pa;
-        float* z = sm + p.z_soff + l * kPS * pz;
-        const int kend = pad4(nin);
-        const int noutp = pad4(nout);
-        for (int idx = tid; idx < kPS * noutp; idx += kPT) {
-          const int o = idx / kPS, s = idx - o * kPS;
-          if (o >= nout) {
-            aout[s * pa + o] = 0.f;
-            continue;
-          }
-          float acc = 0.f;
-          const float* ar = ain + s * pa;
-          const float* wr = sW + o * pw;
-          for (int k = 0; k < kend; k += 4) {
-            const float4 av = *reinterpret_cast<const float4*>(ar + k);
-            const float4 wv = *reinterpret_cast<const float4*>(wr + k);
-            acc = fmaf(av.x, wv.x, acc);
-            acc = fmaf(av.y, wv.y, acc);
-            acc = fmaf(av.z, wv.z, acc);
-            acc = fmaf(av.w, wv.w, acc);
-          }
-          const float zz = __fadd_rn(acc, wr[nin]);
-          z[s * pz + o] = zz;
-          aout[s * pa + o] = fmaxf(zz, 0.f);
-        }
-        __syncthreads();
-      }
+      tile_forward(n, sm, xs, tid);
       // ---- margins, SAT check and the output gradient row
-      const float* y = sm + p.z_soff + (nfc - 1) * kPS * pz;
+      const float* y = sm + n.z_soff + (nfc - 1) * kPS * pz;
       for (int s = tid; s < kPS; s += kPT) {
         if (done[s]) continue;
         float dmin = 0.f;
@@ -171,25 +268,7 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
         g[idx] = (o < nL && !done[s]) ? Cs[cstar[s] * nL + o] : 0.f;
       }
       __syncthreads();
-      for (int l = nfc - 1; l >= 0; --l) {
-        const int nin = p.dims[l], nout = p.dims[l + 1], pw = p.pw[l];
-        const float* sW = sm + p.w_soff[l];
-        const float* zprev = (l > 0) ? sm + p.z_soff + (l - 1) * kPS * pz : nullptr;
-        constexpr int kStep = kPT / kPS;
-        float vals[(kPMaxW + kStep - 1) / kStep];
-        const int sl = tid % kPS, i0 = tid / kPS;
-        int cnt = 0;
-        for (int i = i0; i < nin; i += kStep) {
-          float acc = 0.f;
-          for (int o = 0; o < nout; ++o) acc = fmaf(g[sl * pz + o], sW[o * pw + i], acc);
-          if (zprev && !(zprev[sl * pz + i] > 0.f)) acc = 0.f;
-          vals[cnt++] = acc;
-        }
-        __syncthreads();  // every thread has read g
-        cnt = 0;
-        for (int i = i0; i < pz; i += kStep) g[sl * pz + i] = (i < nin) ? vals[cnt++] : 0.f;
-        __syncthreads();
-      }
+      tile_backward(n, sm, tid);
       // ---- sign step and clamp (SAT samples keep the x that was SAT)
       for (int idx = tid; idx < ns * n0; idx += kPT) {
         const int s = idx / n0, i = idx - s * n0;
@@ -197,8 +276,7 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
         const long long bi = (long long)((s0 + s) / p.R) * n0 + i;
         const float lo = p.lo[bi], hi = p.hi[bi];
         const float gv = g[s * pz + i];
-        const float sg = gv > 0.f ? 1.f : (gv < 0.f ? -1.f : 0.f);
-        const float step = __fmul_rn(__fmul_rn(p.lr, sg), __fsub_rn(hi, lo));
+        const float step = __fmul_rn(__fmul_rn(p.lr, sgnf(gv)), __fsub_rn(hi, lo));
         const float xn = __fsub_rn(xs[s * n0 + i], step);
         xs[s * n0 + i] = fmaxf(fminf(xn, hi), lo);
       }
@@ -208,6 +286,242 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
     __syncthreads();
   }
 }
+
+__global__ void __launch_bounds__(kPT, 1)
+    pgd_general_kernel(const __grid_constant__ PgdGenParams p) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ int stop, final_screen, found, gave_up;
+  __shared__ unsigned int tile_min;
+  __shared__ double best_min;
+  __shared__ int no_improve;
+  const PgdNet& n = p.net;
+  const int tid = threadIdx.x;
+  const int nfc = n.n_fc;
+  const int n0 = n.dims[0];
+  const int nL = n.dims[nfc];
+  const int ncon = p.ncon;
+  const unsigned long long t0 = global_ns();
+  load_net(n, sm, tid);
+  float* Cs = sm + n.c_soff;
+  for (int idx = tid; idx < ncon * nL; idx += kPT) Cs[idx] = p.C[idx];
+  for (int idx = tid; idx < ncon; idx += kPT) Cs[ncon * nL + idx] = p.cb[idx];
+  __syncthreads();
+  const int pz = n.pz;
+  float* xs = sm + n.x_soff;     // kPS x n0 current iterate
+  float* g = sm + n.g_soff;      // kPS x pz gradient rows
+  float* m1 = sm + p.m1_soff;    // kPS x n0 Adam first moment
+  float* m2 = sm + p.m2_soff;    // kPS x n0 Adam second moment
+  float* cur = sm + p.cur_soff;  // kPS x n0 decayed step size
+  float* mg = sm + p.mg_soff;    // kPS x ncon margins of the current screen
+  const float* y = sm + n.z_soff + (nfc - 1) * kPS * pz;
+  const int ntiles = (p.N + kPS - 1) / kPS;
+  // with one tile the CTA sees every restart and applies the plateau give-up
+  // itself; otherwise the host replays it from gmin
+  const bool whole_pool = ntiles == 1;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int s0 = tile * kPS;
+    const int ns = min(kPS, p.N - s0);
+    if (tid == 0) {
+      best_min = __longlong_as_double(0x7FF0000000000000ll);  // +inf
+      no_improve = 0;
+    }
+    for (int idx = tid; idx < kPS * n0; idx += kPT) {
+      const int s = idx / n0, i = idx - s * n0;
+      float xv = 0.f, st = 0.f;
+      if (s < ns) {
+        xv = p.x[(long long)(s0 + s) * n0 + i];
+        const int row = p.step_rows == 1 ? 0 : (s0 + s) % p.R;
+        st = p.step0[(long long)row * n0 + i];
+      }
+      xs[idx] = xv;
+      cur[idx] = st;
+      m1[idx] = 0.f;
+      m2[idx] = 0.f;
+    }
+    __syncthreads();
+    // ---- OSI: x <- clamp(x + step0 * sign(d (w_r . f(x)) / dx), lo, hi)
+    for (int k = 0; k < p.n_osi; ++k) {
+      tile_forward(n, sm, xs, tid);
+      for (int idx = tid; idx < kPS * pz; idx += kPT) {
+        const int s = idx / pz, o = idx - s * pz;
+        g[idx] = (o < nL && s < ns) ? p.w_d[(long long)((s0 + s) % p.R) * nL + o] : 0.f;
+      }
+      __syncthreads();
+      tile_backward(n, sm, tid);
+      for (int idx = tid; idx < ns * n0; idx += kPT) {
+        const int s = idx / n0, i = idx - s * n0;
+        const long long bi = (long long)((s0 + s) / p.R) * n0 + i;
+        const int row = p.step_rows == 1 ? 0 : (s0 + s) % p.R;
+        const float st = p.step0[(long long)row * n0 + i];
+        const float xn = __fadd_rn(xs[idx], __fmul_rn(st, sgnf(g[s * pz + i])));
+        xs[idx] = fminf(fmaxf(xn, p.lo[bi]), p.hi[bi]);
+      }
+      __syncthreads();
+    }
+    // ---- screens 1..n_iter with an update after each, then the final screen
+    for (int t = 1; t <= p.n_iter + 1; ++t) {
+      if (tid == 0) {
+        const unsigned long long bk = *reinterpret_cast<volatile unsigned long long*>(p.best);
+        stop = (bk >> 32) < (unsigned long long)t;
+        final_screen = (t == p.n_iter + 1) ||
+                       (p.budget_ns != 0ull && global_ns() - t0 > p.budget_ns);
+        found = 0;
+        gave_up = 0;
+        tile_min = 0xFFFFFFFFu;
+      }
+      __syncthreads();
+      if (stop) break;
+      tile_forward(n, sm, xs, tid);
+      for (int idx = tid; idx < kPS * ncon; idx += kPT) {
+        const int s = idx / ncon, c = idx - s * ncon;
+        float m = 0.f;
+        for (int o = 0; o < nL; ++o) m = fmaf(y[s * pz + o], Cs[c * nL + o], m);
+        mg[idx] = __fadd_rn(m, Cs[ncon * nL + c]);
+      }
+      __syncthreads();
+      // witness screen: a candidate has an active margin <= 0; it is confirmed
+      // when some disjunct has every margin <= the spec's bloat (spec.check)
+      for (int s = tid; s < ns; s += kPT) {
+        const float* ms = mg + s * ncon;
+        float amin = 0.f;
+        bool have = false;
+        for (int c = 0; c < ncon; ++c)
+          if (p.cact[c] >= 0) {
+            amin = have ? fminf(amin, ms[c]) : ms[c];
+            have = true;
+          }
+        if (have) atomicMin(&tile_min, order_code(amin));
+        if (!(have && amin <= 0.f)) continue;
+        bool conf = false;
+        for (int d = 0; d < p.D && !conf; ++d) {
+          bool any = false;
+          float dmax = 0.f;
+          for (int c = 0; c < ncon; ++c)
+            if (p.cdis[c] == d) {
+              dmax = any ? fmaxf(dmax, ms[c]) : ms[c];
+              any = true;
+            }
+          conf = any && (double)dmax <= p.confirm_thr;
+        }
+        if (conf) {
+          found = 1;
+          atomicMin(p.best, ((unsigned long long)t << 32) | (unsigned long long)(s0 + s));
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        if (t <= p.n_iter && tile_min != 0xFFFFFFFFu) atomicMin(p.gmin + t, tile_min);
+        if (final_screen && t <= p.n_iter) atomicMin(p.t_stop, t);
+        if (whole_pool && !found && !final_screen && tile_min != 0xFFFFFFFFu) {
+          // pgd.py:453-467 in double, as the host evaluates it
+          const double cur_min = (double)order_decode(tile_min);
+          if (cur_min > (double)p.hinge_d) {
+            if (cur_min < best_min - 1e-6) {
+              best_min = cur_min;
+              no_improve = 0;
+            } else {
+              ++no_improve;
+            }
+            gave_up = no_improve >= p.plateau;
+          } else {
+            no_improve = 0;
+          }
+        }
+      }
+      __syncthreads();
+      if (found || final_screen || gave_up) break;  // block-uniform
+      // ---- hinge-loss gradient: sum of the active rows with margin >= thr
+      for (int idx = tid; idx < kPS * pz; idx += kPT) {
+        const int s = idx / pz, o = idx - s * pz;
+        float gv = 0.f;
+        if (o < nL && s < ns) {
+          const int target = p.prd ? ((s0 + s) % p.R) % p.n_act : -1;
+          for (int c = 0; c < ncon; ++c) {
+            const int a = p.cact[c];
+            if (a < 0 || (target >= 0 && a != target)) continue;
+            if (mg[s * ncon + c] >= p.hinge) gv = __fadd_rn(gv, Cs[c * nL + o]);
+          }
+        }
+        g[idx] = gv;
+      }
+      __syncthreads();
+      tile_backward(n, sm, tid);
+      // ---- optimiser step, clamp, step decay
+      const float sc1 = p.inv_bc1[t - 1], sc2 = p.inv_sbc2[t - 1];
+      for (int idx = tid; idx < ns * n0; idx += kPT) {
+        const int s = idx / n0, i = idx - s * n0;
+        const long long bi = (long long)((s0 + s) / p.R) * n0 + i;
+        const float gv = g[s * pz + i];
+        const float step = cur[idx];
+        float delta;
+        if (p.optim == 0) {
+          delta = __fmul_rn(step, sgnf(gv));
+        } else {
+          // m.mul_(b1).add_(g, alpha=1-b1); v.mul_(b2).addcmul_(g, g, value=1-b2)
+          const float a = fmaf(gv, p.one_m_beta1, __fmul_rn(m1[idx], p.beta1));
+          const float v = fmaf(__fmul_rn(gv, gv), p.one_m_beta2, __fmul_rn(m2[idx], p.beta2));
+          m1[idx] = a;
+          m2[idx] = v;
+          const float denom = __fadd_rn(__fmul_rn(__fsqrt_rn(v), sc2), p.eps);
+          const float dir = sgnf(__fdiv_rn(a, denom));
+          delta = p.optim == 1 ? __fmul_rn(step, dir) : __fmul_rn(__fmul_rn(step, sc1), dir);
+        }
+        const float xn = __fsub_rn(xs[idx], delta);
+        xs[idx] = fminf(fmaxf(xn, p.lo[bi]), p.hi[bi]);
+        cur[idx] = __fmul_rn(step, p.decay);
+      }
+      __syncthreads();
+    }
+    for (int idx = tid; idx < ns * n0; idx += kPT) p.x[(long long)s0 * n0 + idx] = xs[idx];
+    __syncthreads();
+  }
+}
+
+// Shared-memory plan of the network and a sample tile; returns the next free
+// offset (floats) or -1 when a width is out of range.
+int plan_net(const vcb_mlp* net, int ncon, PgdNet& n, const char* who) {
+  const int nfc = net->n_fc;
+  n.n_fc = nfc;
+  int off = 0, maxw = 1;
+  long long woff = 0;
+  int boff = 0;
+  for (int l = 0; l <= nfc; ++l) {
+    n.dims[l] = net->dims[l];
+    if (net->dims[l] <= 0 || net->dims[l] > kPMaxW) {
+      fail(VCB_ERR_UNSUPPORTED, "%s: width %d (max %d)", who, net->dims[l], kPMaxW);
+      return -1;
+    }
+    maxw = std::max(maxw, net->dims[l]);
+  }
+  for (int l = 0; l < nfc; ++l) {
+    n.w_goff[l] = woff;
+    n.b_goff[l] = boff;
+    woff += (long long)net->dims[l] * net->dims[l + 1];
+    boff += net->dims[l + 1];
+    n.pw[l] = pad4odd(net->dims[l] + 1);
+    n.wrows[l] = pad4(net->dims[l + 1]);
+    n.w_soff[l] = off;
+    off += n.wrows[l] * n.pw[l];
+  }
+  off = pad4(off + 8);
+  n.pa = pad4odd(maxw);
+  n.pz = pad4(maxw) + 1;
+  n.act_soff = off;
+  off += 2 * kPS * n.pa;
+  n.z_soff = off;
+  off += pad4(nfc * kPS * n.pz);
+  n.g_soff = off;
+  off += pad4(kPS * n.pz);
+  n.x_soff = off;
+  off += pad4(kPS * net->dims[0]);
+  n.c_soff = off;
+  off += pad4(ncon * net->dims[nfc] + ncon);
+  n.W = net->W;
+  n.b = net->b;
+  return off;
+}
+
+constexpr int kSmemCap = 220 * 1024;
 
 }  // namespace
 }  // namespace vcb
@@ -229,44 +543,11 @@ extern "C" int vcb_mlp_pgd(const vcb_mlp* net, int32_t N, int32_t R, float* x,
   if (!x || !lo || !hi || !C || !cb || !cdis || !best || !net->W || !net->b)
     return fail(VCB_ERR_INVALID, "vcb_mlp_pgd: NULL pointer");
   PgdParams p{};
-  p.n_fc = nfc;
-  int off = 0, maxw = 1;
-  long long woff = 0;
-  int boff = 0;
-  for (int l = 0; l <= nfc; ++l) {
-    p.dims[l] = net->dims[l];
-    if (net->dims[l] <= 0 || net->dims[l] > kPMaxW)
-      return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_pgd: width %d (max %d)", net->dims[l], kPMaxW);
-    maxw = std::max(maxw, net->dims[l]);
-  }
-  for (int l = 0; l < nfc; ++l) {
-    p.w_goff[l] = woff;
-    p.b_goff[l] = boff;
-    woff += (long long)net->dims[l] * net->dims[l + 1];
-    boff += net->dims[l + 1];
-    p.pw[l] = pad4odd(net->dims[l] + 1);
-    p.wrows[l] = pad4(net->dims[l + 1]);
-    p.w_soff[l] = off;
-    off += p.wrows[l] * p.pw[l];
-  }
-  off = pad4(off + 8);
-  p.pa = pad4odd(maxw);
-  p.pz = pad4(maxw) + 1;
-  p.act_soff = off;
-  off += 2 * kPS * p.pa;
-  p.z_soff = off;
-  off += pad4(nfc * kPS * p.pz);
-  p.g_soff = off;
-  off += pad4(kPS * p.pz);
-  p.x_soff = off;
-  off += pad4(kPS * net->dims[0]);
-  p.c_soff = off;
-  off += pad4(ncon * net->dims[nfc] + ncon);
+  const int off = plan_net(net, ncon, p.net, "vcb_mlp_pgd");
+  if (off < 0) return VCB_ERR_UNSUPPORTED;
   const int bytes = off * 4;
-  if (bytes > 220 * 1024)
+  if (bytes > kSmemCap)
     return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_pgd: network needs %d bytes of shared memory", bytes);
-  p.W = net->W;
-  p.b = net->b;
   p.N = N;
   p.R = R;
   p.n_iter = n_iter;
@@ -286,4 +567,87 @@ extern "C" int vcb_mlp_pgd(const vcb_mlp* net, int32_t N, int32_t R, float* x,
   const int grid = std::max(1, std::min(ntiles, sm_count()));
   pgd_mlp_kernel<<<grid, kPT, bytes, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("vcb_mlp_pgd: launch");
+}
+
+extern "C" int vcb_mlp_pgd_general(
+    const vcb_mlp* net, int32_t N, int32_t R, float* x, const float* lo, const float* hi,
+    const float* step0, int32_t step_rows, const float* w_d, int32_t n_osi, int32_t n_iter,
+    int32_t optim, float lr_decay, double hinge, int32_t plateau, const float* inv_bc1, const float* inv_sbc2,
+    int32_t ncon, const float* C, const float* cb, const int32_t* cdis, const int32_t* cact,
+    int32_t D, int32_t n_act, int32_t per_restart_disj, double confirm_thr,
+    unsigned long long budget_ns, unsigned long long* best, uint32_t* gmin, int32_t* t_stop,
+    void* stream) {
+  using namespace vcb;
+  if (!net) return fail(VCB_ERR_INVALID, "vcb_mlp_pgd_general: net is NULL");
+  const int nfc = net->n_fc;
+  if (nfc < 1 || nfc > VCB_MAX_FC)
+    return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_pgd_general: n_fc=%d", nfc);
+  if (N < 0 || R <= 0 || ncon <= 0 || D <= 0 || n_act <= 0 || n_iter < 0 || n_osi < 0 ||
+      optim < 0 || optim > 2 || (step_rows != 1 && step_rows != R))
+    return fail(VCB_ERR_INVALID,
+                "vcb_mlp_pgd_general: N=%d R=%d ncon=%d D=%d n_act=%d n_iter=%d n_osi=%d "
+                "optim=%d step_rows=%d",
+                N, R, ncon, D, n_act, n_iter, n_osi, optim, step_rows);
+  if (N == 0) return VCB_OK;
+  if (!x || !lo || !hi || !step0 || !C || !cb || !cdis || !cact || !best || !gmin || !t_stop ||
+      !net->W || !net->b || (n_osi > 0 && !w_d) || (n_iter > 0 && (!inv_bc1 || !inv_sbc2)))
+    return fail(VCB_ERR_INVALID, "vcb_mlp_pgd_general: NULL pointer");
+  PgdGenParams p{};
+  int off = plan_net(net, ncon, p.net, "vcb_mlp_pgd_general");
+  if (off < 0) return VCB_ERR_UNSUPPORTED;
+  const int n0 = net->dims[0];
+  p.m1_soff = off;
+  off += pad4(kPS * n0);
+  p.m2_soff = off;
+  off += pad4(kPS * n0);
+  p.cur_soff = off;
+  off += pad4(kPS * n0);
+  p.mg_soff = off;
+  off += pad4(kPS * ncon);
+  const int bytes = off * 4;
+  if (bytes > kSmemCap)
+    return fail(VCB_ERR_UNSUPPORTED,
+                "vcb_mlp_pgd_general: network needs %d bytes of shared memory", bytes);
+  p.N = N;
+  p.R = R;
+  p.n_osi = n_osi;
+  p.n_iter = n_iter;
+  p.ncon = ncon;
+  p.D = D;
+  p.n_act = n_act;
+  p.prd = per_restart_disj ? 1 : 0;
+  p.optim = optim;
+  p.step_rows = step_rows;
+  p.hinge = static_cast<float>(hinge);
+  p.hinge_d = hinge;
+  p.plateau = plateau;
+  p.decay = lr_decay;
+  // the optimiser's Python-float constants, each rounded once to float32
+  p.beta1 = static_cast<float>(0.9);
+  p.beta2 = static_cast<float>(0.999);
+  p.one_m_beta1 = static_cast<float>(1.0 - 0.9);
+  p.one_m_beta2 = static_cast<float>(1.0 - 0.999);
+  p.eps = 1e-8f;
+  p.confirm_thr = confirm_thr;
+  p.budget_ns = budget_ns;
+  p.x = x;
+  p.lo = lo;
+  p.hi = hi;
+  p.step0 = step0;
+  p.w_d = w_d;
+  p.inv_bc1 = inv_bc1;
+  p.inv_sbc2 = inv_sbc2;
+  p.C = C;
+  p.cb = cb;
+  p.cdis = cdis;
+  p.cact = cact;
+  p.best = best;
+  p.gmin = gmin;
+  p.t_stop = t_stop;
+  int rc = ensure_smem(reinterpret_cast<const void*>(pgd_general_kernel), bytes);
+  if (rc) return rc;
+  const int ntiles = (N + kPS - 1) / kPS;
+  const int grid = std::max(1, std::min(ntiles, sm_count()));
+  pgd_general_kernel<<<grid, kPT, bytes, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("vcb_mlp_pgd_general: launch");
 }

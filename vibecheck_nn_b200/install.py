@@ -4,7 +4,9 @@ The reference driver imports its kernels at call time
 (verify_graph.py:12485-12486, :12514-12515, :12858, :12937), so rebinding the
 module attributes before ``verify_graph`` runs routes the input-split BaB
 through this package.  ``verify_hybrid_acasxu`` binds its PGD helpers at
-import (verify_hybrid_acasxu.py:31-34), so they are rebound there too.
+import (verify_hybrid_acasxu.py:31-34), so they are rebound there too; the
+general PGD attack is rebound in ``vibecheck.pgd``, which the reference's
+``_pgd_attack_general`` wrapper imports at call time.
 """
 from __future__ import annotations
 
@@ -24,6 +26,11 @@ BINDINGS = {
     'vibecheck.verify_hybrid_acasxu': {
         '_simple_pgd': ('pgd', '_simple_pgd'),
         '_simple_pgd_batched': ('pgd', '_simple_pgd_batched'),
+    },
+    # verify_milp._pgd_attack_general (verify_milp.py:111-124), which every
+    # caller uses, looks this attribute up at call time
+    'vibecheck.pgd': {
+        'pgd_attack_general': ('pgd', 'pgd_attack_general'),
     },
 }
 

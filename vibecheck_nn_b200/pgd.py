@@ -1,12 +1,17 @@
-"""Batched sign-gradient PGD on ``vcb_mlp_pgd``.
+"""Batched PGD counterexample search on ``vcb_mlp_pgd`` / ``vcb_mlp_pgd_general``.
 
 ``_simple_pgd`` / ``_simple_pgd_batched`` keep the reference's signatures
 (verify_hybrid_acasxu.py:39, :103): margin rows per disjunct from the spec,
 ``torch.manual_seed(seed)`` then ``lo + (hi - lo) * torch.rand(...)`` for the
 restarts (the same draw as the reference on the same device), and the
-(sat, witness) result.  The iterations run in one kernel launch.
+(sat, witness) result.  ``pgd_attack_general`` keeps the signature and the
+random draws of pgd.py:233 (restart init, OSI projections).  The iterations
+run in one kernel launch each.
 """
 from __future__ import annotations
+
+import math
+import time
 
 import numpy as np
 import torch
@@ -16,44 +21,58 @@ from .netdesc import mlp_desc
 from .ops import F32, _dev
 
 NO_SAT = 0xFFFFFFFFFFFFFFFF
+INT32_MAX = 2 ** 31 - 1
+
+
+def _disjunct_tuples(spec):
+    """The spec's DNF as lists of ('pair', pred, comp) | ('ge', i, v) |
+    ('le', i, v), from a LinearSpec or the reference's VNNSpec; None for a
+    constraint kind PGD does not handle."""
+    raw = getattr(spec, 'disjuncts_raw', None)
+    if raw is not None:
+        return [list(conj) for conj in raw]
+    out = []
+    for conj in spec.disjuncts:
+        cur = []
+        for c in conj.constraints:
+            if hasattr(c, 'pred'):
+                cur.append(('pair', int(c.pred), int(c.comp)))
+            elif c.op in ('>=', '<='):
+                cur.append(('ge' if c.op == '>=' else 'le', int(c.index), float(c.value)))
+            else:
+                return None
+        out.append(cur)
+    return out
+
+
+def _rows_of(disjuncts, n_output):
+    """Margin rows (margin > 0 = safe; pgd.py:75-118): w, b and the disjunct of
+    each row."""
+    rows, bs, dis = [], [], []
+    for d, conj in enumerate(disjuncts):
+        for c in conj:
+            w = np.zeros(n_output)
+            if c[0] == 'pair':
+                w[c[1]], w[c[2]] = 1.0, -1.0
+                b = 0.0
+            elif c[0] == 'ge':
+                w[c[1]] = -1.0
+                b = float(c[2])
+            else:
+                w[c[1]] = 1.0
+                b = -float(c[2])
+            rows.append(w), bs.append(b), dis.append(d)
+    return rows, bs, dis
 
 
 def _constraint_rows(spec, n_output):
     """Margin rows (C, cb) and the disjunct of each row
     (verify_hybrid_acasxu.py:117-130).  Returns None for a constraint kind
     the reference's PGD does not handle (it then reports no witness)."""
-    rows, bs, dis = [], [], []
-    disjuncts = getattr(spec, 'disjuncts_raw', None)
-    if disjuncts is not None:
-        for d, conj in enumerate(disjuncts):
-            for c in conj:
-                w = np.zeros(n_output)
-                if c[0] == 'pair':
-                    w[c[1]], w[c[2]] = 1.0, -1.0
-                    b = 0.0
-                elif c[0] == 'ge':
-                    w[c[1]] = -1.0
-                    b = float(c[2])
-                else:
-                    w[c[1]] = 1.0
-                    b = -float(c[2])
-                rows.append(w), bs.append(b), dis.append(d)
-    else:
-        for d, conj in enumerate(spec.disjuncts):
-            for c in conj.constraints:
-                w = np.zeros(n_output)
-                if hasattr(c, 'pred'):
-                    w[c.pred], w[c.comp] = 1.0, -1.0
-                    b = 0.0
-                elif c.op == '>=':
-                    w[c.index] = -1.0
-                    b = float(c.value)
-                elif c.op == '<=':
-                    w[c.index] = 1.0
-                    b = -float(c.value)
-                else:
-                    return None
-                rows.append(w), bs.append(b), dis.append(d)
+    disjuncts = _disjunct_tuples(spec)
+    if disjuncts is None:
+        return None
+    rows, bs, dis = _rows_of(disjuncts, n_output)
     D = (max(dis) + 1) if dis else 0
     return np.stack(rows).astype(np.float32), np.asarray(bs, np.float32), \
         np.asarray(dis, np.int32), D
@@ -133,13 +152,211 @@ def _simple_pgd(xl, xh, spec, gg, n_output, device, dtype, n_restarts=10000,
     return False, None
 
 
+def pgd_box_expand_amount(settings):
+    """Per-side widening of the search box (pgd.py:190-203): 0 when
+    ``pgd_input_box_expand`` is unset; it may not exceed
+    ``sat_validate_atol``."""
+    b = float(getattr(settings, 'pgd_input_box_expand', 0.0) or 0.0)
+    if b <= 0.0:
+        return 0.0
+    atol = float(getattr(settings, 'sat_validate_atol', 1e-4))
+    assert b <= atol + 1e-12, (
+        f'pgd_input_box_expand ({b}) must be <= sat_validate_atol ({atol})')
+    return b
+
+
+def expand_search_box(lo, hi, settings):
+    """(lo, hi) widened by ``pgd_box_expand_amount`` (pgd.py:206-212)."""
+    b = pgd_box_expand_amount(settings)
+    return (lo, hi) if b == 0.0 else (lo - b, hi + b)
+
+
+_OPTIM = {'sign_sgd': 0, 'adam_sign': 1, 'adam_clipping': 2}
+
+
+def _num(settings, key, default):
+    v = getattr(settings, key, default)
+    return default if v is None or not isinstance(v, (int, float, str, bool)) else v
+
+
+def _decode_min(u):
+    """Inverse of the kernel's order encoding of a float32."""
+    u &= 0xFFFFFFFF
+    bits = (u & 0x7FFFFFFF) if u & 0x80000000 else (~u & 0xFFFFFFFF)
+    return float(np.array([bits], np.uint32).view(np.float32)[0])
+
+
+def _bc_tables(n_iter, device):
+    """float32 reciprocals of the Adam bias corrections, rounded as the GPU
+    divides a tensor by a Python scalar: float32(1) / float32(c)."""
+    t = np.arange(1, n_iter + 1, dtype=np.float64)
+    bc1 = (1.0 - 0.9 ** t).astype(np.float32)
+    sbc2 = ((1.0 - 0.999 ** t) ** 0.5).astype(np.float32)
+    inv1 = (np.float32(1.0) / bc1).astype(np.float32)
+    inv2 = (np.float32(1.0) / sbc2).astype(np.float32)
+    return (torch.as_tensor(inv1, device=device), torch.as_tensor(inv2, device=device))
+
+
+def pgd_attack_general(xl, xh, spec, gg, settings, restrict_disj=None,
+                       time_budget=None, per_restart_disj=None, seed=None):
+    """PGD counterexample search for a DNF spec (pgd.py:233-524): restarts
+    drawn uniformly in the box, optional OSI initialisation, hinge loss over
+    the attacked disjuncts, sign_sgd / adam_sign / adam_clipping steps with
+    step decay, plateau give-up and wall-time budget.  One kernel launch runs
+    every restart and iteration.  Returns (is_sat, witness ndarray or None).
+    """
+    t_start = time.perf_counter()
+    xl, xh = expand_search_box(xl, xh, settings)
+    dev = xl.device
+    dt = xl.dtype
+    if dt != F32:
+        raise NotImplementedError('vibecheck_nn_b200: pgd_attack_general runs in float32')
+    if isinstance(seed, (int, float)):
+        torch.manual_seed(int(seed))
+    n_restarts = int(_num(settings, 'pgd_restarts', 10))
+    n_iter = int(_num(settings, 'pgd_iter', 100))
+    lr_decay = float(_num(settings, 'pgd_lr_decay', 0.99))
+    hinge_thr = float(_num(settings, 'pgd_hinge_threshold', -1e-5))
+    alpha_frac = float(_num(settings, 'pgd_alpha_frac', 0.25))
+    if time_budget is None:
+        tb = getattr(settings, 'pgd_time_budget', None)
+        if isinstance(tb, (int, float)):
+            time_budget = float(tb)
+    eps_input = (xh - xl) / 2.0
+    if bool(_num(settings, 'pgd_alpha_multi', False)):
+        fr = list(getattr(settings, 'pgd_alpha_multi_fractions', [0.25, 0.05, 0.01, 0.002]))
+        pra = torch.tensor([fr[i % len(fr)] for i in range(n_restarts)], dtype=dt, device=dev)
+        while pra.dim() < eps_input.dim() + 1:
+            pra = pra.unsqueeze(-1)
+        step = eps_input.unsqueeze(0) * pra
+    else:
+        step = eps_input * alpha_frac
+    optim = str(_num(settings, 'pgd_optim', 'adam_sign'))
+    if optim not in _OPTIM:
+        raise AssertionError(f'unknown pgd_optim {optim!r}; valid: {tuple(_OPTIM)}')
+    disjuncts = _disjunct_tuples(spec)
+    if disjuncts is None:
+        raise ValueError('unknown constraint op')
+    act = list(range(len(disjuncts))) if restrict_disj is None else sorted(restrict_disj)
+    if not act:
+        return False, None
+    act = [d for d in act if disjuncts[d]]
+    if not act:
+        return False, None
+    if per_restart_disj is None:
+        per_restart_disj = bool(_num(settings, 'pgd_per_restart_disjunct', False))
+    prd = bool(per_restart_disj) and len(act) > 1
+    init_mode = str(_num(settings, 'pgd_init_mode', 'uniform'))
+    x = xl + (xh - xl) * torch.rand(n_restarts, *xl.shape, dtype=dt, device=dev)
+    desc = mlp_desc(gg, dev)
+    n_out = desc.n_out
+    n_in = desc.dims[0]
+    w_d = None
+    n_osi = 0
+    if init_mode == 'osi':
+        w_d = ((torch.rand(n_restarts, n_out, dtype=dt, device=dev) - 0.5) * 2.0).contiguous()
+        n_osi = int(_num(settings, 'pgd_osi_iters', 50))
+    plateau = int(_num(settings, 'pgd_plateau_iters', 100))
+    budget_ns = 0
+    if time_budget is not None:
+        left = time_budget - (time.perf_counter() - t_start)
+        budget_ns = max(1, int(left * 1e9))
+    x = x.reshape(n_restarts, n_in).contiguous()
+    idx = pgd_general_run(desc, x, xl.reshape(1, n_in), xh.reshape(1, n_in),
+                          step.reshape(-1, n_in), w_d, n_osi, n_iter, optim, lr_decay,
+                          hinge_thr, plateau, disjuncts, act, prd,
+                          float(getattr(spec, 'unsat_margin_bloat', 0.0) or 0.0), budget_ns)
+    if idx is None:
+        return False, None
+    return True, x[idx].reshape(xl.shape).detach().cpu().numpy()
+
+
+def pgd_general_run(desc, x, lo, hi, step, w_d, n_osi, n_iter, optim, lr_decay, hinge_thr,
+                    plateau, disjuncts, act, prd, bloat=0.0, budget_ns=0):
+    """One ``vcb_mlp_pgd_general`` launch over the restarts x (R, n_in)
+    (updated in place) and the host replay of the loop's give-up rules.
+    Returns the restart index of the confirmed witness or None."""
+    dev = x.device
+    R, n_in = x.shape
+    n_out = desc.n_out
+    rows, bs, dis = _rows_of(disjuncts, n_out)
+    ordinal = {d: i for i, d in enumerate(act)}
+    cact = [ordinal.get(d, -1) for d in dis]
+    lo = lo.to(F32).contiguous()
+    hi = hi.to(F32).contiguous()
+    step = step.to(F32).contiguous()
+    C = torch.as_tensor(np.stack(rows), dtype=F32, device=dev)
+    cb = torch.as_tensor(np.asarray(bs, np.float32), device=dev)
+    cdis = torch.as_tensor(np.asarray(dis, np.int32), device=dev)
+    cact_t = torch.as_tensor(np.asarray(cact, np.int32), device=dev)
+    inv1, inv2 = _bc_tables(max(n_iter, 1), dev)
+    # [best (2 x int32) | gmin (n_iter + 2) | t_stop]
+    state = torch.full((2 + n_iter + 2 + 1,), -1, dtype=torch.int32, device=dev)
+    state[-1] = INT32_MAX
+    base = state.data_ptr()
+    rc = _lib.lib().vcb_mlp_pgd_general(
+        desc.struct, R, R, _lib.ptr(x), _lib.ptr(lo), _lib.ptr(hi), _lib.ptr(step),
+        step.shape[0], _lib.ptr(w_d), n_osi if w_d is not None else 0, n_iter,
+        _OPTIM[optim], lr_decay, hinge_thr, int(plateau), _lib.ptr(inv1), _lib.ptr(inv2), len(rows),
+        _lib.ptr(C), _lib.ptr(cb), _lib.ptr(cdis), _lib.ptr(cact_t), len(disjuncts),
+        len(act), int(prd), float(bloat), int(budget_ns), base, base + 8,
+        base + 4 * (2 + n_iter + 2), _lib.stream_of(dev))
+    _lib.check(rc, 'vcb_mlp_pgd_general')
+    host = state.cpu().numpy().view(np.uint32)  # the one host sync
+    key = int(host[0]) | (int(host[1]) << 32)
+    t_w = (key >> 32) if key != NO_SAT else None
+    t_stop = int(np.int32(host[-1]))
+    gmin = host[2:2 + n_iter + 2]
+    # replay of the loop's control flow (pgd.py:440-467, :494-512)
+    best_min = float('inf')
+    nimp = 0
+    final = n_iter + 1
+    for t in range(1, n_iter + 1):
+        if t >= t_stop:
+            final = t
+            break
+        if t_w == t:
+            return key & 0xFFFFFFFF
+        curr_min = _decode_min(int(gmin[t]))
+        if curr_min > hinge_thr:
+            if curr_min < best_min - 1e-6:
+                best_min = curr_min
+                nimp = 0
+            else:
+                nimp += 1
+            if nimp >= plateau:
+                return None
+        else:
+            nimp = 0
+    if t_w == final:
+        return key & 0xFFFFFFFF
+    return None
+
+
 def root_pgd(spec, gg, n_output, device, settings):
-    """Root SAT search before the BaB: the reference's simple-PGD stage
-    (10,000 restarts x 50 iterations, verify_graph.py:12604-12619)."""
-    xl = torch.as_tensor(np.asarray(spec.x_lo), dtype=F32, device=device).flatten()
-    xh = torch.as_tensor(np.asarray(spec.x_hi), dtype=F32, device=device).flatten()
-    return _simple_pgd(xl.unsqueeze(0), xh.unsqueeze(0), spec, gg, n_output,
-                       device, torch.float32, n_restarts=10000, n_iter=50)
+    """Root SAT search before the BaB (verify_graph.py:12586-12619):
+    ``pgd_attack_general`` within ``pgd_time_budget_phase0``, then the
+    simple-PGD stage (10,000 restarts x 50 iterations).  Each is best-effort:
+    a RuntimeError (NotImplementedError included) or OOM falls through.
+    Returns (sat, witness, phase)."""
+    xl = torch.as_tensor(np.asarray(spec.x_lo), dtype=F32, device=device)
+    xh = torch.as_tensor(np.asarray(spec.x_hi), dtype=F32, device=device)
+    try:
+        budget = float(_num(settings, 'pgd_time_budget_phase0', 5.0))
+        sat, wit = pgd_attack_general(xl, xh, spec, gg, settings, time_budget=budget)
+        if sat and wit is not None:
+            return True, wit, 'batched_pgd'
+    except (RuntimeError, torch.cuda.OutOfMemoryError):
+        pass
+    try:
+        sat, wit = _simple_pgd(xl.flatten().unsqueeze(0), xh.flatten().unsqueeze(0), spec,
+                               gg, n_output, device, torch.float32, n_restarts=10000,
+                               n_iter=50)
+        if sat:
+            return True, wit, 'batched_simple_pgd'
+    except (RuntimeError, torch.cuda.OutOfMemoryError):
+        pass
+    return False, None, None
 
 
 def leaf_pgd(xl_b, xh_b, lb, qd, D, spec, gg, n_output, device, settings):
