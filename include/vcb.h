@@ -240,6 +240,39 @@ int vcb_mlp_pgd_general(const vcb_mlp* net, int32_t N, int32_t R, float* x,
                         unsigned long long* best, uint32_t* gmin,
                         int32_t* t_stop, void* stream);
 
+/* Per-iteration pieces of both PGD attacks for networks outside the
+ * shared-memory kernels (the forward / backward passes then run on the
+ * layer kernels below).
+ *
+ * vcb_pgd_screen: y (N, n_out, ld ldy) the network outputs of screen t.
+ *   simple = 1 (_simple_pgd): loss_s = min_d max_{c in d} margin; SAT at
+ *     <= 1e-6 -> atomicMin(best, t << 32 | s); g row = C[routed row].
+ *   simple = 0 (pgd_attack_general): candidate = some attacked margin <= 0,
+ *     confirmed when a disjunct has every margin <= confirm_thr ->
+ *     atomicMin(best, t << 32 | s); *gmin_t = order-encoded minimum attacked
+ *     margin (as vcb_mlp_pgd_general's gmin); g row = sum of the attacked rows
+ *     with margin >= hinge (restart s % R's disjunct only when
+ *     per_restart_disj).
+ * vcb_pgd_step: x (N, n_in) in place, box s / R of lo/hi; g (ld ldg) the
+ *   input gradient.  mode 0: _PGDOptim step (optim 0/1/2 as above, Adam
+ *   state m1/m2 and decayed step cur (N, n_in), sc1 / sc2 this iteration's
+ *   reciprocal bias corrections) then cur *= decay; mode 1: OSI ascent
+ *   x + step0 * sign(g); mode 2: _simple_pgd's x - lr * sign(g) * (hi - lo).
+ *   Every mode clamps x to its box. */
+int vcb_pgd_screen(int32_t N, int32_t n_out, const float* y, int32_t ldy,
+                   int32_t ncon, const float* C, const float* cb,
+                   const int32_t* cdis, const int32_t* cact, int32_t D,
+                   int32_t n_act, int32_t per_restart_disj, int32_t R,
+                   int32_t simple, float hinge, double confirm_thr, int32_t t,
+                   unsigned long long* best, uint32_t* gmin_t, float* g,
+                   int32_t ldg, void* stream);
+
+int vcb_pgd_step(int32_t N, int32_t R, int32_t n_in, float* x, const float* lo,
+                 const float* hi, const float* g, int32_t ldg, int32_t mode,
+                 int32_t optim, int32_t t, const float* step0,
+                 int32_t step_rows, float* cur, float* m1, float* m2,
+                 float sc1, float sc2, float decay, float lr, void* stream);
+
 /* ---- layer-wise kernels (networks too wide for the shared-memory path,
  * and convolutional networks).  All row-major buffers are float32; "ld"
  * arguments are leading dimensions in elements.  They replace, one layer at a
@@ -333,6 +366,36 @@ int vcb_relu_back(int32_t R, int32_t Q, int32_t n, const float* e,
                   int32_t lde, float* e_out, int32_t ldo, const float* sb_lo,
                   const float* sb_hi, const float* alpha, const float* beta,
                   float* part, void* stream);
+
+/* ---- concrete (point) evaluation: the fc / conv / relu branches of
+ * _forward_batch_graph (src/vibecheck/verify_zono_bnb.py:554-770) and their
+ * vector-Jacobian products (the autograd backward of PGD's loss,
+ * src/vibecheck/pgd.py:494, verify_hybrid_acasxu.py:155). ---- */
+
+/* z = x W^T + b for N points (x: N x nin, ld ldx; W: nout x nin); writes the
+ * pre-activation z (ld ldz) and / or relu(z) a (ld lda); either may be NULL,
+ * not both. */
+int vcb_fc_forward(int32_t N, int32_t nin, int32_t nout, const float* x,
+                   int32_t ldx, const float* W, const float* b, float* z,
+                   int32_t ldz, float* a, int32_t lda, void* stream);
+
+/* g_o (N x nin, ld ldo) = g (N x nout, ld ldg) W, zeroed where mask (the
+ * pre-activation feeding this fc's input ReLU, ld ldm) is <= 0; mask NULL =
+ * no ReLU before the fc. */
+int vcb_fc_backward(int32_t N, int32_t nin, int32_t nout, const float* g,
+                    int32_t ldg, const float* W, const float* mask,
+                    int32_t ldm, float* g_o, int32_t ldo, void* stream);
+
+/* Conv forward (NCHW): z = conv(x, K) + b, a = relu(z); either may be NULL. */
+int vcb_conv_forward(int32_t N, const int32_t* geometry, const float* x,
+                     const float* K, const float* b, float* z, float* a,
+                     void* stream);
+
+/* Conv vector-Jacobian product: g_in (N x C x H x W) = conv_transpose(g, K),
+ * zeroed where mask (same shape as g_in, or NULL) is <= 0. */
+int vcb_conv_backward(int32_t N, const int32_t* geometry, const float* g,
+                      const float* K, const float* mask, float* g_in,
+                      void* stream);
 
 /* Diagnostic: FP32 FFMA throughput probe (no reference counterpart).  Runs
  * `blocks` CTAs of 256 threads, each thread `iters` x 64 dependent-chain FMAs

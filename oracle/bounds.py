@@ -91,6 +91,88 @@ def conv_transpose2d(g, K, stride, pad, in_hw):
 
 
 # ---------------------------------------------------------------------------
+# concrete forward  (verify_zono_bnb.py:554-596) and its vector-Jacobian product
+# ---------------------------------------------------------------------------
+
+def _point_bias(a, op, sign, dtype):
+    """a + sign * bias with the reference's broadcast (_point_bcast_bias,
+    verify_zono_bnb.py:525-551): scalar or full-width biases add elementwise,
+    others right-align against the op's ``out_shape_nd``."""
+    b = _np(op.get('bias'), dtype)
+    if b is None:
+        return a
+    sb = b * dtype(sign)
+    if b.size in (1, a.shape[1]):
+        return a + sb.reshape(-1)
+    N = a.shape[0]
+    out_sh = tuple(int(d) for d in op['out_shape_nd'])
+    if int(np.prod(out_sh)) != a.shape[1]:
+        raise NotImplementedError('oracle forward: outer broadcast')
+    return (a.reshape(N, *out_sh) + sb).reshape(N, -1)
+
+
+def forward_batch_graph(x, gg, dtype=np.float32, capture=None, keep=False):
+    """Concrete forward of N points (N, n_in) through fc / conv / relu /
+    reshape / bias add-sub ops.  Returns the output (or ``capture``'s
+    activation); with ``keep`` also {relu op name: its input}."""
+    x = np.asarray(x, dtype)
+    N = x.shape[0]
+    act = {gg['input_name']: x.reshape(N, -1)}
+    relu_in = {}
+    out = act[gg['input_name']]
+    for op in gg['ops']:
+        t = op['type']
+        a = act[op['inputs'][0]]
+        if t == 'conv':
+            p = op_arrays(op, dtype)
+            v = conv2d(a.reshape(N, *op['in_shape']), p['K'], p['b'], op['stride'],
+                       op['padding']).reshape(N, -1)
+        elif t == 'fc':
+            p = op_arrays(op, dtype)
+            v = a @ p['W'].T + p['b']
+        elif t == 'relu':
+            relu_in[op['name']] = a
+            v = np.maximum(a, 0)
+        elif t == 'reshape':
+            v = a
+        elif t in ('add', 'sub') and not op.get('is_merge'):
+            v = _point_bias(a, op, 1.0 if t == 'add' else -1.0, dtype)
+        else:
+            raise NotImplementedError(f'oracle forward: unsupported op {t!r}')
+        act[op['name']] = v
+        out = v
+        if capture is not None and op['name'] == capture:
+            break
+    if capture is not None:
+        out = act[capture]
+    return (out, relu_in) if keep else out
+
+
+def forward_vjp(gg, relu_in, g, dtype=np.float32):
+    """d(g . f(x))/dx for a chain (autograd's rules: F.relu passes the
+    gradient where its input is > 0)."""
+    g = np.asarray(g, dtype)
+    N = g.shape[0]
+    for op in reversed(gg['ops']):
+        t = op['type']
+        if t == 'fc':
+            g = g @ op_arrays(op, dtype)['W']
+        elif t == 'conv':
+            K = op_arrays(op, dtype)['K']
+            ins = op['in_shape']
+            Co, Ho, Wo = op['out_shape']
+            g = conv_transpose2d(g.reshape(N, Co, Ho, Wo), K, op['stride'], op['padding'],
+                                 ins[1:]).reshape(N, -1)
+        elif t == 'relu':
+            g = g * (relu_in[op['name']] > 0)
+        elif t in ('reshape', 'add', 'sub'):
+            pass
+        else:
+            raise NotImplementedError(f'oracle vjp: unsupported op {t!r}')
+    return g
+
+
+# ---------------------------------------------------------------------------
 # ReLU slopes  (verify_zono_bnb.py:503-522)
 # ---------------------------------------------------------------------------
 

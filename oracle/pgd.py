@@ -60,23 +60,14 @@ def pgd_batched(x0, lo, hi, gg, mats, n_iter=50, lr=0.1, dtype=np.float32):
     """x0, lo, hi: (N, n_in) samples and their (expanded) box bounds.
 
     Returns (sat, witness or None, iterations run)."""
-    layers = _mlp_layers(gg, dtype)
+    fwd, bwd = _net_fns(gg, dtype)
     x = np.asarray(x0, dtype).copy()
     lo = np.asarray(lo, dtype)
     hi = np.asarray(hi, dtype)
     width = hi - lo
     lr = dtype(lr)
     for it in range(n_iter):
-        acts = []
-        a = x
-        for i, (W, b) in enumerate(layers):
-            z = a @ W.T + b
-            if i < len(layers) - 1:
-                acts.append(z)
-                a = np.maximum(z, 0)
-            else:
-                a = z
-        out = a
+        out, acts = fwd(x)
         per_d = []
         arg_c = []
         for W, b in mats:
@@ -95,11 +86,7 @@ def pgd_batched(x0, lo, hi, gg, mats, n_iter=50, lr=0.1, dtype=np.float32):
             sel = d_arg == d
             if sel.any():
                 g[sel] += W[arg_c[d][sel]]
-        for i in range(len(layers) - 1, -1, -1):
-            W, _ = layers[i]
-            g = g @ W
-            if i > 0:
-                g = g * (acts[i - 1] > 0)
+        g = bwd(acts, g)
         step = lr * np.sign(g) * width
         x = np.maximum(np.minimum(x - step, hi), lo)
     return False, None, n_iter
@@ -127,6 +114,17 @@ def _backward(layers, acts, g):
         if i > 0:
             g = g * (acts[i - 1] > 0)
     return g
+
+
+def _net_fns(gg, dtype):
+    """(forward(x) -> (out, acts), backward(acts, g) -> dx): the MLP
+    matrices for fc/relu chains, the graph walker (conv, bias ops) else."""
+    try:
+        layers = _mlp_layers(gg, dtype)
+    except NotImplementedError:
+        return (lambda x: ob.forward_batch_graph(x, gg, dtype, keep=True),
+                lambda acts, g: ob.forward_vjp(gg, acts, g, dtype))
+    return (lambda x: _forward_acts(layers, x), lambda acts, g: _backward(layers, acts, g))
 
 
 def _fma32(a, b, c):
@@ -157,12 +155,12 @@ def pgd_attack_general(xl, xh, gg, disjuncts, x_init, w_d=None, *, n_iter=100,
     the witness, x=final iterate).
     """
     f32 = np.float32
-    layers = _mlp_layers(gg, f32)
+    fwd, bwd = _net_fns(gg, f32)
     xl = np.asarray(xl, f32).reshape(-1)
     xh = np.asarray(xh, f32).reshape(-1)
     x = np.asarray(x_init, f32).copy()
     R = x.shape[0]
-    n_out = layers[-1][0].shape[0]
+    n_out = fwd(x[:1])[0].shape[1]
     mats_all = margin_matrices(disjuncts, n_out, f32)
     act_idx = list(range(len(disjuncts))) if active is None else sorted(active)
     act_idx = [d for d in act_idx if len(disjuncts[d])]
@@ -179,8 +177,8 @@ def pgd_attack_general(xl, xh, gg, disjuncts, x_init, w_d=None, *, n_iter=100,
     if w_d is not None:
         w_d = np.asarray(w_d, f32)
         for _ in range(osi_iters):
-            _, acts = _forward_acts(layers, x)
-            g = _backward(layers, acts, w_d)
+            _, acts = fwd(x)
+            g = bwd(acts, w_d)
             x = np.minimum(np.maximum(x + step0 * np.sign(g).astype(f32), xl), xh)
     n_act = len(mats)
     prd = bool(per_restart_disj) and n_act > 1
@@ -207,7 +205,7 @@ def pgd_attack_general(xl, xh, gg, disjuncts, x_init, w_d=None, *, n_iter=100,
     for t in range(1, n_iter + 1):
         if max_iters is not None and t > max_iters:
             return False, None, {'t': None, 'x': x}
-        out, acts = _forward_acts(layers, x)
+        out, acts = fwd(x)
         bi, flat = screen(out)
         if bi is not None:
             return True, x[bi].copy(), {'t': t, 'x': x}
@@ -232,7 +230,7 @@ def pgd_attack_general(xl, xh, gg, disjuncts, x_init, w_d=None, *, n_iter=100,
                 sel = sel * (assign == d)[:, None]
             g = g + sel @ W
             col += W.shape[0]
-        grad = _backward(layers, acts, g)
+        grad = bwd(acts, g)
         t_run = t
         if optim == 'sign_sgd':
             delta = cur * np.sign(grad).astype(f32)
@@ -251,7 +249,7 @@ def pgd_attack_general(xl, xh, gg, disjuncts, x_init, w_d=None, *, n_iter=100,
                 delta = (cur / f32(bc1)) * direction
         x = np.minimum(np.maximum(x - delta, xl), xh)
         cur = cur * f32(lr_decay)
-    out, _ = _forward_acts(layers, x)
+    out, _ = fwd(x)
     bi, _ = screen(out)
     if bi is not None:
         return True, x[bi].copy(), {'t': t_run + 1, 'x': x}

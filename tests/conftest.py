@@ -75,3 +75,32 @@ def oracle_pgd_general(case, gg, div):
         alpha_fracs=[0.25, 0.05, 0.01, 0.002] if st.get('pgd_alpha_multi') else None,
         per_restart_disj=st.get('pgd_per_restart_disjunct', False),
         active=case['restrict'], div=div)
+
+
+def golden_script():
+    """tests/golden/make_golden.py as a module (graph builders shared by the
+    fixtures and the tests; it imports the reference only when run)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location('make_golden',
+                                                  os.path.join(GOLDEN, 'make_golden.py'))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def forward_fixture(device='cpu'):
+    """The concrete-forward fixture: (CNN gg, MLP gg, arrays)."""
+    import torch
+    from vibecheck_nn_b200 import workloads as wk
+    g = load_golden('forward')
+    mg = golden_script()
+    gg = mg.forward_cnn_gg(g['k1'], g['b1'], g['cb'], g['W2'], g['b2'], g['W3'], g['b3'],
+                           g['fb'], (3, 12, 12), torch.float32)
+    if str(device) != 'cpu':
+        for op in gg['ops']:
+            for k in ('W', 'bias', 'kernel'):
+                if isinstance(op.get(k), torch.Tensor):
+                    op[k] = op[k].to(device)
+    n = int(g['mlp_n_layers'])
+    layers = [(g[f'mlp_W{i}'], g[f'mlp_b{i}']) for i in range(n)]
+    return gg, wk.mlp_gg(layers, device), g

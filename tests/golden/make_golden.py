@@ -64,7 +64,7 @@ def _net_arrays(layers):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--ref-src', required=True)
-    ap.add_argument('--only', default=None, choices=['pgd_general'],
+    ap.add_argument('--only', default=None, choices=['pgd_general', 'forward'],
                     help='regenerate one fixture only')
     args = ap.parse_args()
     vz, vg, vh, vs, vspec = _import_reference(args.ref_src)
@@ -72,6 +72,9 @@ def main():
     from vibecheck_nn_b200 import workloads as wk
     if args.only == 'pgd_general':
         _golden_pgd_general(vspec, wk)
+        return
+    if args.only == 'forward':
+        _golden_forward(vz, wk)
         return
 
     # ------------------------------------------------------------------ slopes
@@ -432,6 +435,62 @@ def _golden_pgd_general(vspec, wk):
         out[p + 'x_last'] = _n(seen[-1])
     out['tags'] = np.array([c[0] for c in PGD_GENERAL_CASES])
     _save('pgd_general', **out)
+
+
+def forward_cnn_gg(k1, b1, cb, W2, b2, W3, b3, fb, ins, dt):
+    """CNN of the concrete-forward fixture: conv -> add (per-channel bias)
+    -> relu -> flatten -> fc -> relu -> fc -> sub (elementwise bias)."""
+    import torch
+    g = _small_cnn_gg(k1, b1, W2, b2, W3, b3, ins, dt)
+    ops = g['ops']
+    conv = ops[0]
+    add = {'name': 'cadd', 'type': 'add', 'inputs': ['conv0'],
+           'bias': torch.as_tensor(cb, dtype=dt), 'out_shape_nd': conv['out_shape']}
+    ops[1]['inputs'] = ['cadd']
+    sub = {'name': 'fsub', 'type': 'sub', 'inputs': ['fc1'],
+           'bias': torch.as_tensor(fb, dtype=dt), 'out_shape_nd': (fb.size,)}
+    g['ops'] = [conv, add] + ops[1:] + [sub]
+    return g
+
+
+def _golden_forward(vz, wk):
+    """_forward_batch_graph (verify_zono_bnb.py:554) on a CNN with bias ops and
+    on an ACAS-sized MLP: outputs, two captures and the autograd gradient of
+    g . f(x)."""
+    import torch
+    dt = torch.float32
+    rng = np.random.default_rng(41)
+    ins = (3, 12, 12)
+    k1 = (rng.standard_normal((8, 3, 4, 4)) * 0.3).astype(np.float32)
+    b1 = (rng.standard_normal(8) * 0.05).astype(np.float32)
+    cb = (rng.standard_normal((8, 1, 1)) * 0.05).astype(np.float32)
+    W2 = (rng.standard_normal((20, 8 * 6 * 6)) * 0.08).astype(np.float32)
+    b2 = (rng.standard_normal(20) * 0.05).astype(np.float32)
+    W3 = (rng.standard_normal((5, 20)) * 0.3).astype(np.float32)
+    b3 = (rng.standard_normal(5) * 0.05).astype(np.float32)
+    fb = (rng.standard_normal(5) * 0.05).astype(np.float32)
+    gg = forward_cnn_gg(k1, b1, cb, W2, b2, W3, b3, fb, ins, dt)
+    N = 19
+    x = rng.uniform(0, 1, (N, int(np.prod(ins)))).astype(np.float32)
+    gw = rng.standard_normal((N, 5)).astype(np.float32)
+    xt = torch.as_tensor(x).requires_grad_(True)
+    out = vz._forward_batch_graph(xt, gg)
+    (out * torch.as_tensor(gw)).sum().backward()
+    with torch.no_grad():
+        cap_relu = vz._forward_batch_graph(torch.as_tensor(x), gg, capture='relu0')
+        cap_fc = vz._forward_batch_graph(torch.as_tensor(x), gg, capture='fc0')
+    res = dict(k1=k1, b1=b1, cb=cb, W2=W2, b2=b2, W3=W3, b3=b3, fb=fb, x=x, gw=gw,
+               out=_n(out), grad=_n(xt.grad), cap_relu0=_n(cap_relu), cap_fc0=_n(cap_fc))
+    layers = wk.mlp_params(wk.ACAS_DIMS, np.random.default_rng(43))
+    ggm = wk.mlp_gg(layers, 'cpu', dt)
+    xm = rng.uniform(-1, 1, (N, 5)).astype(np.float32)
+    gm = rng.standard_normal((N, 5)).astype(np.float32)
+    xmt = torch.as_tensor(xm).requires_grad_(True)
+    outm = vz._forward_batch_graph(xmt, ggm)
+    (outm * torch.as_tensor(gm)).sum().backward()
+    res.update(mlp_x=xm, mlp_gw=gm, mlp_out=_n(outm), mlp_grad=_n(xmt.grad),
+               **{f'mlp_{k}': v for k, v in _net_arrays(layers).items()})
+    _save('forward', **res)
 
 
 def _small_cnn_gg(k1, b1, W2, b2, W3, b3, ins, dt):

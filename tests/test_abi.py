@@ -113,4 +113,19 @@ def test_install_rebinds_reference_functions():
     assert mods['vibecheck.verify_graph']._input_split_batched is bab._input_split_batched
     assert mods['vibecheck.verify_hybrid_acasxu']._simple_pgd_batched is pgd._simple_pgd_batched
     assert mods['vibecheck.pgd'].pgd_attack_general is pgd.pgd_attack_general
-    assert sum(len(v) for v in done.values()) == 9
+    assert sum(len(v) for v in done.values()) == 11
+
+
+def test_install_forward_delegates_outside_the_kernels():
+    import types
+    from vibecheck_nn_b200 import install, forward
+    calls = []
+    mod = types.ModuleType('vibecheck.verify_zono_bnb')
+    mod._forward_batch_graph = lambda x, gg, capture=None: calls.append(x) or 'reference'
+    mods = {name: types.ModuleType(name) for name in install.BINDINGS}
+    mods['vibecheck.verify_zono_bnb'] = mod
+    install.install(mods)
+    fn = mod._forward_batch_graph
+    assert fn.__wrapped__ is forward._forward_batch_graph
+    # a CPU tensor is outside the kernels: the reference's function answers
+    assert fn(torch.zeros(2, 3), {}) == 'reference' and len(calls) == 1

@@ -10,8 +10,8 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import (close, golden_layers, load_golden, max_excess, oracle_pgd_general,
-                      pgd_general_case)
+from conftest import (close, forward_fixture, golden_layers, load_golden, max_excess,
+                      oracle_pgd_general, pgd_general_case)
 from oracle import bab as obab
 from oracle import bounds as ob
 from oracle import pgd as opgd
@@ -245,3 +245,20 @@ def test_cfg1_workload_matches_fixture():
     for i, (W, b) in enumerate(w['layers']):
         np.testing.assert_array_equal(W, g[f'W{i}'])
         np.testing.assert_array_equal(b, g[f'b{i}'])
+
+
+def test_forward_batch_graph():
+    """The concrete forward and its vector-Jacobian product restate
+    _forward_batch_graph and autograd through it (bias add / sub broadcast,
+    conv, captures)."""
+    gg, ggm, g = forward_fixture()
+    for dt, tol in ((np.float64, dict(rtol=1e-5, atol=1e-6)), (np.float32, {})):
+        out, acts = ob.forward_batch_graph(g['x'], gg, dt, keep=True)
+        assert close(out, g['out'], **tol), max_excess(out, g['out'])
+        grad = ob.forward_vjp(gg, acts, g['gw'], dt)
+        assert close(grad, g['grad'], **tol), max_excess(grad, g['grad'])
+        assert close(ob.forward_batch_graph(g['x'], gg, dt, capture='relu0'), g['cap_relu0'])
+        assert close(ob.forward_batch_graph(g['x'], gg, dt, capture='fc0'), g['cap_fc0'])
+        outm, actm = ob.forward_batch_graph(g['mlp_x'], ggm, dt, keep=True)
+        assert close(outm, g['mlp_out'], **tol)
+        assert close(ob.forward_vjp(ggm, actm, g['mlp_gw'], dt), g['mlp_grad'], **tol)

@@ -68,6 +68,14 @@ SIGNATURES = {
                             _P],
     'vcb_conv_ibp': [_I, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     'vcb_conv_back': [_I, _P, _P, _P, _P, _P],
+    'vcb_pgd_screen': [_I, _I, _P, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I,
+                       ctypes.c_float, ctypes.c_double, _I, _P, _P, _P, _I, _P],
+    'vcb_pgd_step': [_I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _P, _I, _P, _P, _P,
+                     ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P],
+    'vcb_conv_forward': [_I, _P, _P, _P, _P, _P, _P, _P],
+    'vcb_conv_backward': [_I, _P, _P, _P, _P, _P, _P],
+    'vcb_fc_forward': [_I, _I, _I, _P, _I, _P, _P, _P, _I, _P, _I, _P],
+    'vcb_fc_backward': [_I, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P],
     'vcb_conv_bias_dot': [_I, _I, _I, _P, _P, _P, _P],
     'vcb_ibp_relu': [_I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P],
     'vcb_relu_back': [_I, _I, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P],

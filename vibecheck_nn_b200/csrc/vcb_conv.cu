@@ -10,6 +10,10 @@
 //   output-pixel coefficient that each kernel tap of a stride-s convolution
 //   maps onto the input pixel (zero where no output pixel does), so every sum
 //   has a fixed order and no atomics are needed.
+// * concrete conv forward (the conv branch of _forward_batch_graph,
+//   verify_zono_bnb.py:569-575) as the same implicit GEMM with a bias +
+//   optional ReLU epilogue, and its vector-Jacobian product (the transposed
+//   convolution, masked by the pre-activation of the ReLU feeding the conv).
 // * per-row bias dot of a conv layer (the coefficient times the per-channel
 //   bias repeated over the spatial positions).
 // * IBP ReLU (verify_zono_bnb.py:1123-1138) and CROWN ReLU relaxation
@@ -112,11 +116,46 @@ __global__ void __launch_bounds__(GT) conv_ibp_kernel(const ConvIbpArgs a) {
   }
 }
 
+struct ConvFwdArgs {
+  int N;
+  ConvGeom g;
+  const float *x, *K, *b;
+  float *z, *a;  // N x Co x Ho x Wo pre-activation / relu'd output (each optional)
+};
+
+__global__ void __launch_bounds__(GT) conv_fwd_kernel(const ConvFwdArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  float acc[8][4], acc2[8][4];
+  const int KD = a.g.C * a.g.kh * a.g.kw;
+  const int M = a.N * a.g.Ho * a.g.Wo;
+  mainloop<false>(M, a.g.Co, KD, Im2col{a.x, a.g}, RowLoad{a.K, KD}, Im2col{nullptr, a.g},
+                  RowLoad{nullptr, KD}, acc, acc2, smem);
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  const int m0 = blockIdx.x * TM + ty * 8, n0 = blockIdx.y * TN + tx * 4;
+  const int hw = a.g.Ho * a.g.Wo;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + i;
+    if (m >= M) continue;
+    const int d = m / hw, pix = m - d * hw;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + j;
+      if (n >= a.g.Co) continue;
+      const float v = __fadd_rn(acc[i][j], a.b[n]);
+      const long long o = ((long long)d * a.g.Co + n) * hw + pix;
+      if (a.z) a.z[o] = v;
+      if (a.a) a.a[o] = fmaxf(v, 0.f);
+    }
+  }
+}
+
 struct ConvBackArgs {
   int R;
   ConvGeom g;
   const float *e, *K;
-  float* e_in;  // R x C x H x W
+  float* e_in;        // R x C x H x W
+  const float* mask;  // R x C x H x W pre-activations: keep e_in where > 0; or NULL
 };
 
 __global__ void __launch_bounds__(GT) conv_back_kernel(const ConvBackArgs a) {
@@ -138,7 +177,8 @@ __global__ void __launch_bounds__(GT) conv_back_kernel(const ConvBackArgs a) {
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + j;
       if (n >= a.g.C) continue;
-      a.e_in[((long long)r * a.g.C + n) * hw + pix] = acc[i][j];
+      const long long o = ((long long)r * a.g.C + n) * hw + pix;
+      a.e_in[o] = (a.mask && !(a.mask[o] > 0.f)) ? 0.f : acc[i][j];
     }
   }
 }
@@ -254,13 +294,43 @@ extern "C" int vcb_conv_back(int32_t R, const int32_t* geometry, const float* e,
   if (R < 0 || !geometry) return fail(VCB_ERR_INVALID, "vcb_conv_back: bad arguments");
   if (R == 0) return VCB_OK;
   if (!e || !K || !e_in) return fail(VCB_ERR_INVALID, "vcb_conv_back: NULL pointer");
-  ConvBackArgs a{R, geom(geometry), e, K, e_in};
+  ConvBackArgs a{R, geom(geometry), e, K, e_in, nullptr};
   const int sm = gemm_smem_bytes(false);
   int rc = ensure_smem(reinterpret_cast<const void*>(conv_back_kernel), sm);
   if (rc) return rc;
   conv_back_kernel<<<gemm_grid(R * a.g.H * a.g.W, a.g.C), GT, sm,
                      static_cast<cudaStream_t>(stream)>>>(a);
   return check_launch("vcb_conv_back");
+}
+
+extern "C" int vcb_conv_forward(int32_t N, const int32_t* geometry, const float* x,
+                                const float* K, const float* b, float* z, float* a,
+                                void* stream) {
+  if (N < 0 || !geometry) return fail(VCB_ERR_INVALID, "vcb_conv_forward: bad arguments");
+  if (N == 0) return VCB_OK;
+  if (!x || !K || !b || (!z && !a)) return fail(VCB_ERR_INVALID, "vcb_conv_forward: NULL pointer");
+  ConvFwdArgs args{N, geom(geometry), x, K, b, z, a};
+  const int sm = gemm_smem_bytes(false);
+  int rc = ensure_smem(reinterpret_cast<const void*>(conv_fwd_kernel), sm);
+  if (rc) return rc;
+  conv_fwd_kernel<<<gemm_grid(N * args.g.Ho * args.g.Wo, args.g.Co), GT, sm,
+                    static_cast<cudaStream_t>(stream)>>>(args);
+  return check_launch("vcb_conv_forward");
+}
+
+extern "C" int vcb_conv_backward(int32_t N, const int32_t* geometry, const float* g,
+                                 const float* K, const float* mask, float* g_in,
+                                 void* stream) {
+  if (N < 0 || !geometry) return fail(VCB_ERR_INVALID, "vcb_conv_backward: bad arguments");
+  if (N == 0) return VCB_OK;
+  if (!g || !K || !g_in) return fail(VCB_ERR_INVALID, "vcb_conv_backward: NULL pointer");
+  ConvBackArgs a{N, geom(geometry), g, K, g_in, mask};
+  const int sm = gemm_smem_bytes(false);
+  int rc = ensure_smem(reinterpret_cast<const void*>(conv_back_kernel), sm);
+  if (rc) return rc;
+  conv_back_kernel<<<gemm_grid(N * a.g.H * a.g.W, a.g.C), GT, sm,
+                     static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("vcb_conv_backward");
 }
 
 extern "C" int vcb_conv_bias_dot(int32_t R, int32_t Co, int32_t hw, const float* e,

@@ -477,6 +477,141 @@ __global__ void __launch_bounds__(kPT, 1)
   }
 }
 
+// ---- layer-wise PGD pieces (networks outside the shared-memory kernels):
+// the forward / backward passes run on the layer kernels; these two kernels
+// are the per-iteration screen and update of both attacks.
+
+struct ScreenArgs {
+  int N, n_out, ldy, ldg, ncon, D, n_act, prd, R, t, simple;
+  float hinge;
+  double confirm_thr;
+  const float *y, *C, *cb;
+  const int *cdis, *cact;
+  unsigned long long* best;
+  unsigned int* gmin;
+  float* g;  // (N, n_out) gradient seed of the loss w.r.t. the output
+};
+
+// general: hinge-loss seed, witness screen and per-screen minimum margin;
+// simple: loss = min_d max_c margin, SAT at <= 1e-6, seed = the routed row.
+__global__ void __launch_bounds__(256) pgd_screen_kernel(const ScreenArgs a) {
+  __shared__ unsigned int blk_min;
+  if (threadIdx.x == 0) blk_min = 0xFFFFFFFFu;
+  __syncthreads();
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s < a.N) {
+    const float* ys = a.y + (long long)s * a.ldy;
+    float* gs = a.g + (long long)s * a.ldg;
+    auto margin = [&](int c) {
+      float m = 0.f;
+      for (int o = 0; o < a.n_out; ++o) m = fmaf(ys[o], a.C[c * a.n_out + o], m);
+      return __fadd_rn(m, a.cb[c]);
+    };
+    if (a.simple) {
+      float dmin = 0.f;
+      int cbest = 0;
+      for (int d = 0; d < a.D; ++d) {
+        float dmax = 0.f;
+        int carg = -1;
+        for (int c = 0; c < a.ncon; ++c) {
+          if (a.cdis[c] != d) continue;
+          const float m = margin(c);
+          if (carg < 0 || m > dmax) {
+            dmax = m;
+            carg = c;
+          }
+        }
+        if (d == 0 || dmax < dmin) {
+          dmin = dmax;
+          cbest = carg;
+        }
+      }
+      if (dmin <= 1e-6f)
+        atomicMin(a.best, ((unsigned long long)a.t << 32) | (unsigned long long)s);
+      for (int o = 0; o < a.n_out; ++o) gs[o] = a.C[cbest * a.n_out + o];
+    } else {
+      float amin = 0.f;
+      bool have = false;
+      for (int c = 0; c < a.ncon; ++c)
+        if (a.cact[c] >= 0) {
+          const float m = margin(c);
+          amin = have ? fminf(amin, m) : m;
+          have = true;
+        }
+      if (have) atomicMin(&blk_min, order_code(amin));
+      if (have && amin <= 0.f) {
+        bool conf = false;
+        for (int d = 0; d < a.D && !conf; ++d) {
+          bool any = false;
+          float dmax = 0.f;
+          for (int c = 0; c < a.ncon; ++c)
+            if (a.cdis[c] == d) {
+              const float m = margin(c);
+              dmax = any ? fmaxf(dmax, m) : m;
+              any = true;
+            }
+          conf = any && (double)dmax <= a.confirm_thr;
+        }
+        if (conf) atomicMin(a.best, ((unsigned long long)a.t << 32) | (unsigned long long)s);
+      }
+      const int target = a.prd ? (s % a.R) % a.n_act : -1;
+      for (int o = 0; o < a.n_out; ++o) gs[o] = 0.f;
+      for (int c = 0; c < a.ncon; ++c) {
+        const int ac = a.cact[c];
+        if (ac < 0 || (target >= 0 && ac != target)) continue;
+        if (!(margin(c) >= a.hinge)) continue;
+        for (int o = 0; o < a.n_out; ++o) gs[o] = __fadd_rn(gs[o], a.C[c * a.n_out + o]);
+      }
+    }
+  }
+  __syncthreads();
+  if (!a.simple && threadIdx.x == 0 && blk_min != 0xFFFFFFFFu) atomicMin(a.gmin, blk_min);
+}
+
+struct StepArgs {
+  int N, R, n_in, ldg, step_rows, mode, optim, t;  // mode 0 update, 1 OSI ascent, 2 simple
+  float decay, lr, beta1, beta2, one_m_beta1, one_m_beta2, eps, sc1, sc2;
+  float* x;
+  const float *lo, *hi, *g, *step0;
+  float *cur, *m1, *m2;
+};
+
+__global__ void __launch_bounds__(256) pgd_step_kernel(const StepArgs a) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)a.N * a.n_in) return;
+  const int s = (int)(idx / a.n_in), i = (int)(idx - (long long)s * a.n_in);
+  const long long bi = (long long)(s / a.R) * a.n_in + i;
+  const float lo = a.lo[bi], hi = a.hi[bi];
+  const float gv = a.g[(long long)s * a.ldg + i];
+  const float xv = a.x[idx];
+  if (a.mode == 2) {  // _simple_pgd: x - lr * sign(g) * width
+    const float step = __fmul_rn(__fmul_rn(a.lr, sgnf(gv)), __fsub_rn(hi, lo));
+    a.x[idx] = fmaxf(fminf(__fsub_rn(xv, step), hi), lo);
+    return;
+  }
+  const int row = a.step_rows == 1 ? 0 : s % a.R;
+  if (a.mode == 1) {  // OSI: x + step0 * sign(g)
+    const float st = a.step0[(long long)row * a.n_in + i];
+    a.x[idx] = fminf(fmaxf(__fadd_rn(xv, __fmul_rn(st, sgnf(gv))), lo), hi);
+    return;
+  }
+  const float step = a.cur[idx];
+  float delta;
+  if (a.optim == 0) {
+    delta = __fmul_rn(step, sgnf(gv));
+  } else {
+    const float m = fmaf(gv, a.one_m_beta1, __fmul_rn(a.m1[idx], a.beta1));
+    const float v = fmaf(__fmul_rn(gv, gv), a.one_m_beta2, __fmul_rn(a.m2[idx], a.beta2));
+    a.m1[idx] = m;
+    a.m2[idx] = v;
+    const float denom = __fadd_rn(__fmul_rn(__fsqrt_rn(v), a.sc2), a.eps);
+    const float dir = sgnf(__fdiv_rn(m, denom));
+    delta = a.optim == 1 ? __fmul_rn(step, dir) : __fmul_rn(__fmul_rn(step, a.sc1), dir);
+  }
+  a.x[idx] = fminf(fmaxf(__fsub_rn(xv, delta), lo), hi);
+  a.cur[idx] = __fmul_rn(step, a.decay);
+}
+
 // Shared-memory plan of the network and a sample tile; returns the next free
 // offset (floats) or -1 when a width is out of range.
 int plan_net(const vcb_mlp* net, int ncon, PgdNet& n, const char* who) {
@@ -650,4 +785,47 @@ extern "C" int vcb_mlp_pgd_general(
   const int grid = std::max(1, std::min(ntiles, sm_count()));
   pgd_general_kernel<<<grid, kPT, bytes, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("vcb_mlp_pgd_general: launch");
+}
+
+extern "C" int vcb_pgd_screen(int32_t N, int32_t n_out, const float* y, int32_t ldy,
+                              int32_t ncon, const float* C, const float* cb,
+                              const int32_t* cdis, const int32_t* cact, int32_t D,
+                              int32_t n_act, int32_t per_restart_disj, int32_t R,
+                              int32_t simple, float hinge, double confirm_thr, int32_t t,
+                              unsigned long long* best, uint32_t* gmin_t, float* g,
+                              int32_t ldg, void* stream) {
+  using namespace vcb;
+  if (N < 0 || n_out <= 0 || ldy < n_out || ldg < n_out || ncon <= 0 || D <= 0 || R <= 0 ||
+      t < 0 || (!simple && n_act <= 0))
+    return fail(VCB_ERR_INVALID, "vcb_pgd_screen: N=%d n_out=%d ncon=%d D=%d", N, n_out, ncon,
+                D);
+  if (N == 0) return VCB_OK;
+  if (!y || !C || !cb || !cdis || !best || !g || (!simple && (!cact || !gmin_t)))
+    return fail(VCB_ERR_INVALID, "vcb_pgd_screen: NULL pointer");
+  ScreenArgs a{N, n_out, ldy, ldg, ncon, D, n_act, per_restart_disj ? 1 : 0, R, t,
+               simple ? 1 : 0, hinge, confirm_thr, y, C, cb, cdis, cact, best, gmin_t, g};
+  pgd_screen_kernel<<<(N + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("vcb_pgd_screen");
+}
+
+extern "C" int vcb_pgd_step(int32_t N, int32_t R, int32_t n_in, float* x, const float* lo,
+                            const float* hi, const float* g, int32_t ldg, int32_t mode,
+                            int32_t optim, int32_t t, const float* step0, int32_t step_rows,
+                            float* cur, float* m1, float* m2, float sc1, float sc2,
+                            float decay, float lr, void* stream) {
+  using namespace vcb;
+  if (N < 0 || R <= 0 || n_in <= 0 || ldg < n_in || mode < 0 || mode > 2 || optim < 0 ||
+      optim > 2 || (mode != 2 && step_rows != 1 && step_rows != R))
+    return fail(VCB_ERR_INVALID, "vcb_pgd_step: N=%d R=%d n_in=%d mode=%d", N, R, n_in, mode);
+  if (N == 0) return VCB_OK;
+  if (!x || !lo || !hi || !g || (mode == 1 && !step0) ||
+      (mode == 0 && (!cur || (optim > 0 && (!m1 || !m2)))))
+    return fail(VCB_ERR_INVALID, "vcb_pgd_step: NULL pointer");
+  StepArgs a{N, R, n_in, ldg, step_rows, mode, optim, t, decay, lr,
+             static_cast<float>(0.9), static_cast<float>(0.999),
+             static_cast<float>(1.0 - 0.9), static_cast<float>(1.0 - 0.999), 1e-8f, sc1, sc2,
+             x, lo, hi, g, step0, cur, m1, m2};
+  const long long n = (long long)N * n_in;
+  pgd_step_kernel<<<(unsigned)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("vcb_pgd_step");
 }

@@ -25,17 +25,29 @@ def _pad4(n):
 
 
 class GraphNet:
-    """Device-side layers of a gg chain of fc / conv / relu / reshape ops."""
+    """Device-side layers of a gg chain of fc / conv / relu / reshape ops; a
+    single-input ``add`` / ``sub`` of a bias right after an fc or conv is
+    folded into that layer's bias.  ``names[i]`` lists the op names whose
+    output is layer i's output (reshapes alias the previous value; ``-1`` is
+    the network input); ``stale`` holds fc / conv names whose own output no
+    longer exists because a later bias was folded in."""
 
     def __init__(self, gg, device):
         self.layers = []
         self.relu_widths = []
+        self.names = {-1: [gg['input_name']]}
+        self.stale = set()
         cur = gg['input_name']
         n = int(gg.get('input_n') or 0)
         for op in gg['ops']:
             t = op['type']
             if op['inputs'][0] != cur:
                 raise NotImplementedError(f'vibecheck_nn_b200: non-chain graph at {op["name"]!r}')
+            if t in ('add', 'sub') and not op.get('is_merge') and op.get('bias') is not None \
+                    and self.layers and self.layers[-1]['type'] in ('fc', 'conv'):
+                self._fold_bias(op, t, device)
+                cur = op['name']
+                continue
             if t == 'fc':
                 W = torch.as_tensor(_as_np(op['W']), dtype=F32, device=device).contiguous()
                 b = torch.as_tensor(_as_np(op['bias']), dtype=F32, device=device).flatten()
@@ -68,11 +80,51 @@ class GraphNet:
                 self.layers.append({'type': 'relu', 'L': op['layer_idx'], 'n': n})
                 self.relu_widths.append(n)
             elif t == 'reshape':
-                pass
+                self.names.setdefault(len(self.layers) - 1, []).append(op['name'])
+                cur = op['name']
+                continue
             else:
                 raise NotImplementedError(f'vibecheck_nn_b200: unsupported op {t!r}')
+            self.names[len(self.layers) - 1] = [op['name']]
             cur = op['name']
         self.n_out = n
+
+    def _fold_bias(self, op, t, device):
+        """Bias add / sub after an fc or conv (the reference broadcasts it as
+        _point_bcast_bias, verify_zono_bnb.py:525-551): a scalar, an fc's
+        full-width vector or a conv's per-channel (Co, 1, 1) block folds into
+        the layer bias; other broadcasts are not supported."""
+        layer = self.layers[-1]
+        raw = np.asarray(_as_np(op['bias']))
+        shape = tuple(int(d) for d in raw.shape)
+        while shape and shape[0] == 1 and len(shape) > 1:
+            shape = shape[1:]
+        if raw.size == 1:
+            n_ch = layer['nout'] if layer['type'] == 'fc' else layer['Co']
+            vec = np.full(n_ch, float(raw.reshape(-1)[0]))
+        elif layer['type'] == 'fc' and raw.size == layer['nout']:
+            vec = raw.reshape(-1)
+        elif layer['type'] == 'conv' and shape == (layer['Co'], 1, 1):
+            vec = raw.reshape(-1)
+        else:
+            raise NotImplementedError('vibecheck_nn_b200: broadcast bias')
+        bias = torch.as_tensor(vec, dtype=F32, device=device)
+        layer['b'] = (layer['b'] + bias if t == 'add' else layer['b'] - bias).contiguous()
+        if layer['type'] == 'fc':
+            layer['Waug'][:, layer['nin']] = layer['b']
+        idx = len(self.layers) - 1
+        self.stale.update(self.names.get(idx, []))
+        self.names[idx] = [op['name']]
+
+    def layer_of(self, name):
+        """Index of the layer whose output is op ``name`` (-1: the input)."""
+        if name in self.stale:
+            raise NotImplementedError(
+                f'vibecheck_nn_b200: {name!r} has a bias folded into it; capture the add')
+        for idx, names in self.names.items():
+            if name in names:
+                return idx
+        raise KeyError(name)
 
 
 def graph_net(gg, device):
@@ -214,3 +266,73 @@ def graph_crown(G, xl, xh, sb, W_q, b_q, alpha=None, beta=None, want_A=False):
     if want_A:
         out['A'] = A.view(D, Q, n0)
     return out
+
+
+def graph_forward(G, x, upto=None, keep=False):
+    """Concrete forward of N points x (N, n0) through the chain (the
+    fc / conv / relu branches of _forward_batch_graph,
+    verify_zono_bnb.py:554-596).  Returns the output of layer ``upto``
+    (default: the last) and, with ``keep``, the pre-activation of every layer
+    that feeds a ReLU {layer index: (N, n)} for graph_vjp."""
+    dev = x.device
+    N = x.shape[0]
+    st = _lib.stream_of(dev)
+    L_ = _lib.lib()
+    layers = G.layers
+    last = len(layers) - 1 if upto is None else upto
+    cur = x.contiguous()
+    pre = {}
+    for idx in range(last + 1):
+        layer = layers[idx]
+        t = layer['type']
+        if t == 'relu':
+            continue  # written by the producer's epilogue
+        nxt_relu = idx + 1 < len(layers) and layers[idx + 1]['type'] == 'relu'
+        want_a = nxt_relu and idx + 1 <= last
+        want_z = keep or not want_a
+        z = torch.empty((N, layer['nout']), dtype=F32, device=dev) if want_z else None
+        a = torch.empty((N, layer['nout']), dtype=F32, device=dev) if want_a else None
+        if t == 'fc':
+            rc = L_.vcb_fc_forward(N, layer['nin'], layer['nout'], P(cur), cur.shape[1],
+                                   P(layer['W']), P(layer['b']), P(z), layer['nout'], P(a),
+                                   layer['nout'], st)
+            _lib.check(rc, 'vcb_fc_forward')
+        else:
+            rc = L_.vcb_conv_forward(N, _geom_ptr(layer['geom']), P(cur), P(layer['K']),
+                                     P(layer['b']), P(z), P(a), st)
+            _lib.check(rc, 'vcb_conv_forward')
+        if keep and nxt_relu:
+            pre[idx] = z
+        cur = a if want_a else z
+    return (cur, pre) if keep else cur
+
+
+def graph_vjp(G, pre, g):
+    """d(g . f(x))/dx for the points whose pre-activations ``pre`` came from
+    graph_forward(keep=True): the transposed layers, each masked by the ReLU
+    in front of it (F.relu passes the gradient where z > 0)."""
+    dev = g.device
+    N = g.shape[0]
+    st = _lib.stream_of(dev)
+    L_ = _lib.lib()
+    layers = G.layers
+    if layers[-1]['type'] == 'relu':
+        raise NotImplementedError('vibecheck_nn_b200: network output after a relu')
+    cur = g.contiguous()
+    for idx in range(len(layers) - 1, -1, -1):
+        layer = layers[idx]
+        if layer['type'] == 'relu':
+            continue
+        mask = pre.get(idx - 2) if idx >= 1 and layers[idx - 1]['type'] == 'relu' else None
+        out = torch.empty((N, layer['nin']), dtype=F32, device=dev)
+        if layer['type'] == 'fc':
+            rc = L_.vcb_fc_backward(N, layer['nin'], layer['nout'], P(cur), cur.shape[1],
+                                    P(layer['W']), P(mask), layer['nin'], P(out),
+                                    layer['nin'], st)
+            _lib.check(rc, 'vcb_fc_backward')
+        else:
+            rc = L_.vcb_conv_backward(N, _geom_ptr(layer['geom']), P(cur), P(layer['K']),
+                                      P(mask), P(out), st)
+            _lib.check(rc, 'vcb_conv_backward')
+        cur = out
+    return cur

@@ -19,6 +19,7 @@ BINDINGS = {
         '_forward_zonotope_graph_batched': ('interm', '_forward_zonotope_graph_batched'),
         '_crown_intermediate_batched': ('interm', '_crown_intermediate_batched'),
         '_run_alpha_crown_inputsplit_batched': ('alpha', '_run_alpha_crown_inputsplit_batched'),
+        '_forward_batch_graph': ('forward', '_forward_batch_graph', 'delegate'),
     },
     'vibecheck.verify_graph': {
         '_input_split_batched': ('bab', '_input_split_batched'),
@@ -26,6 +27,7 @@ BINDINGS = {
     'vibecheck.verify_hybrid_acasxu': {
         '_simple_pgd': ('pgd', '_simple_pgd'),
         '_simple_pgd_batched': ('pgd', '_simple_pgd_batched'),
+        '_forward_batch_graph': ('forward', '_forward_batch_graph', 'delegate'),
     },
     # verify_milp._pgd_attack_general (verify_milp.py:111-124), which every
     # caller uses, looks this attribute up at call time
@@ -33,6 +35,24 @@ BINDINGS = {
         'pgd_attack_general': ('pgd', 'pgd_attack_general'),
     },
 }
+
+
+def _delegating(impl, original):
+    """``impl`` for the inputs it supports; the reference's own function for
+    the rest.  Used for the concrete forward, which the reference also calls
+    off the hot path (CPU / float64 tensors, merge graphs, ND fc ops) where no
+    caller catches NotImplementedError."""
+    if original is None:
+        return impl
+
+    def fn(*args, **kwargs):
+        try:
+            return impl(*args, **kwargs)
+        except (NotImplementedError, RuntimeError):
+            return original(*args, **kwargs)
+    fn.__wrapped__ = impl
+    fn.__name__ = getattr(impl, '__name__', 'fn')
+    return fn
 
 
 def install(modules=None):
@@ -44,8 +64,11 @@ def install(modules=None):
         mod = (modules or {}).get(mod_name)
         if mod is None:
             mod = importlib.import_module(mod_name)
-        for attr, (sub, fn) in names.items():
+        for attr, spec in names.items():
+            sub, fn = spec[0], spec[1]
             impl = getattr(importlib.import_module(f'{__package__}.{sub}'), fn)
+            if len(spec) > 2 and spec[2] == 'delegate':
+                impl = _delegating(impl, getattr(mod, attr, None))
             setattr(mod, attr, impl)
             done.setdefault(mod_name, []).append(attr)
     return done

@@ -17,7 +17,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .netdesc import mlp_desc
+from .netdesc import MlpDesc, mlp_desc
 from .ops import F32, _dev
 
 NO_SAT = 0xFFFFFFFFFFFFFFFF
@@ -91,6 +91,66 @@ def pgd_run(desc, x, lo, hi, R, C, cb, cdis, D, n_iter, lr):
     return key, x
 
 
+def _graph(gg, device):
+    from .graph import graph_net
+    return graph_net(gg, device)
+
+
+def _screen(G_out, t, y, rows, R, simple, best, gmin_t, g, hinge=0.0, bloat=0.0,
+            prd=False, n_act=1):
+    C, cb, cdis, cact, D = rows
+    rc = _lib.lib().vcb_pgd_screen(
+        y.shape[0], G_out, _lib.ptr(y), y.shape[1], C.shape[0], _lib.ptr(C), _lib.ptr(cb),
+        _lib.ptr(cdis), _lib.ptr(cact), D, n_act, int(prd), R, int(simple), float(hinge),
+        float(bloat), t, best, gmin_t, _lib.ptr(g), g.shape[1], _lib.stream_of(y.device))
+    _lib.check(rc, 'vcb_pgd_screen')
+
+
+def _step(x, lo, hi, R, g, mode, optim=0, t=0, step0=None, cur=None, m1=None, m2=None,
+          sc1=1.0, sc2=1.0, decay=1.0, lr=0.0):
+    N, n_in = x.shape
+    rc = _lib.lib().vcb_pgd_step(
+        N, R, n_in, _lib.ptr(x), _lib.ptr(lo), _lib.ptr(hi), _lib.ptr(g), g.shape[1], mode,
+        optim, t, _lib.ptr(step0), 1 if step0 is None else step0.shape[0], _lib.ptr(cur),
+        _lib.ptr(m1), _lib.ptr(m2), float(sc1), float(sc2), float(decay), float(lr),
+        _lib.stream_of(x.device))
+    _lib.check(rc, 'vcb_pgd_step')
+
+
+def simple_layerwise(G, x, lo, hi, R, C, cb, cdis, D, n_iter, lr):
+    """_simple_pgd's loop on the layer kernels for networks outside the
+    shared-memory kernel: per iteration forward, screen (SAT at loss
+    <= 1e-6), backward, sign step.  x (N, n_in) is updated in place; returns
+    the first SAT sample's index or None."""
+    from .graph import graph_forward, graph_vjp
+    dev = x.device
+    best = torch.full((1,), -1, dtype=torch.int64, device=dev)
+    g = torch.empty((x.shape[0], G.n_out), dtype=F32, device=dev)
+    rows = (C, cb, cdis, None, D)
+    for it in range(n_iter):
+        y, pre = graph_forward(G, x, keep=True)
+        _screen(G.n_out, it, y, rows, R, True, best.data_ptr(), None, g)
+        key = int(best.item()) & NO_SAT  # the reference checks sat_mask.any() here too
+        if key != NO_SAT:
+            return key & 0xFFFFFFFF
+        gx = graph_vjp(G, pre, g)
+        _step(x, lo, hi, R, gx, 2, lr=lr)
+    return None
+
+
+def _simple_run(gg, x, lo, hi, R, C, cb, cdis, D, n_iter, lr):
+    """One simple-PGD attack: the fused kernel for MLPs that fit it, the
+    layer kernels otherwise.  Returns the witness row index or None."""
+    dev = x.device
+    try:
+        desc = mlp_desc(gg, dev)
+        key, _ = pgd_run(desc, x, lo, hi, R, C, cb, cdis, D, n_iter, lr)
+        return None if key == NO_SAT else key & 0xFFFFFFFF
+    except NotImplementedError:
+        pass
+    return simple_layerwise(_graph(gg, dev), x, lo, hi, R, C, cb, cdis, D, n_iter, lr)
+
+
 def _simple_pgd_batched(xl, xh, spec, gg, n_output, device, dtype,
                         n_restarts=128, n_iter=50, lr=0.1, seed=0, box_expand=0.0):
     """Sign-gradient PGD over many boxes at once (verify_hybrid_acasxu.py:103).
@@ -106,18 +166,16 @@ def _simple_pgd_batched(xl, xh, spec, gg, n_output, device, dtype,
     if rows is None or B == 0:
         return False, None
     C, cb, cdis, D = rows
-    desc = mlp_desc(gg, device)
     torch.manual_seed(seed)
     R = n_restarts
     lo = xl.unsqueeze(1).expand(B, R, n_in).reshape(B * R, n_in)
     hi = xh.unsqueeze(1).expand(B, R, n_in).reshape(B * R, n_in)
     x = (lo + (hi - lo) * torch.rand(B * R, n_in, device=device, dtype=F32)).contiguous()
-    key, x = pgd_run(desc, x, xl.contiguous(), xh.contiguous(), R,
-                     torch.as_tensor(C, device=device), torch.as_tensor(cb, device=device),
-                     torch.as_tensor(cdis, device=device), D, n_iter, lr)
-    if key == NO_SAT:
+    idx = _simple_run(gg, x, xl.contiguous(), xh.contiguous(), R,
+                      torch.as_tensor(C, device=device), torch.as_tensor(cb, device=device),
+                      torch.as_tensor(cdis, device=device), D, n_iter, lr)
+    if idx is None:
         return False, None
-    idx = key & 0xFFFFFFFF
     return True, x[idx].detach().cpu().numpy()
 
 
@@ -133,21 +191,21 @@ def _simple_pgd(xl, xh, spec, gg, n_output, device, dtype, n_restarts=10000,
     if rows is None:
         return False, None
     C, cb, cdis, D = rows
-    desc = mlp_desc(gg, device)
     cur = n_restarts
     while cur >= min_restarts:
         try:
             torch.manual_seed(seed)
             x = (xl0 + (xh0 - xl0) * torch.rand(cur, n_in, device=device, dtype=F32)).contiguous()
-            key, x = pgd_run(desc, x, xl0.reshape(1, -1).contiguous(),
-                             xh0.reshape(1, -1).contiguous(), cur,
-                             torch.as_tensor(C, device=device),
-                             torch.as_tensor(cb, device=device),
-                             torch.as_tensor(cdis, device=device), D, n_iter, lr)
-            if key == NO_SAT:
+            idx = _simple_run(gg, x, xl0.reshape(1, -1).contiguous(),
+                              xh0.reshape(1, -1).contiguous(), cur,
+                              torch.as_tensor(C, device=device),
+                              torch.as_tensor(cb, device=device),
+                              torch.as_tensor(cdis, device=device), D, n_iter, lr)
+            if idx is None:
                 return False, None
-            return True, x[key & 0xFFFFFFFF].detach().cpu().numpy()
+            return True, x[idx].detach().cpu().numpy()
         except torch.cuda.OutOfMemoryError:
+            torch.cuda.empty_cache()
             cur //= 2
     return False, None
 
@@ -202,8 +260,10 @@ def pgd_attack_general(xl, xh, spec, gg, settings, restrict_disj=None,
     """PGD counterexample search for a DNF spec (pgd.py:233-524): restarts
     drawn uniformly in the box, optional OSI initialisation, hinge loss over
     the attacked disjuncts, sign_sgd / adam_sign / adam_clipping steps with
-    step decay, plateau give-up and wall-time budget.  One kernel launch runs
-    every restart and iteration.  Returns (is_sat, witness ndarray or None).
+    step decay, plateau give-up and wall-time budget.  For MLPs that fit the
+    shared-memory kernel one launch runs every restart and iteration; other
+    networks run the same loop on the layer kernels.  Returns (is_sat,
+    witness ndarray or None).
     """
     t_start = time.perf_counter()
     xl, xh = expand_search_box(xl, xh, settings)
@@ -248,24 +308,35 @@ def pgd_attack_general(xl, xh, spec, gg, settings, restrict_disj=None,
     prd = bool(per_restart_disj) and len(act) > 1
     init_mode = str(_num(settings, 'pgd_init_mode', 'uniform'))
     x = xl + (xh - xl) * torch.rand(n_restarts, *xl.shape, dtype=dt, device=dev)
-    desc = mlp_desc(gg, dev)
-    n_out = desc.n_out
-    n_in = desc.dims[0]
+    try:
+        net = mlp_desc(gg, dev)
+        n_out, n_in = net.n_out, net.dims[0]
+    except NotImplementedError:
+        net = _graph(gg, dev)
+        n_out, n_in = net.n_out, x[0].numel()
     w_d = None
     n_osi = 0
     if init_mode == 'osi':
         w_d = ((torch.rand(n_restarts, n_out, dtype=dt, device=dev) - 0.5) * 2.0).contiguous()
         n_osi = int(_num(settings, 'pgd_osi_iters', 50))
     plateau = int(_num(settings, 'pgd_plateau_iters', 100))
-    budget_ns = 0
-    if time_budget is not None:
-        left = time_budget - (time.perf_counter() - t_start)
-        budget_ns = max(1, int(left * 1e9))
+    bloat = float(getattr(spec, 'unsat_margin_bloat', 0.0) or 0.0)
     x = x.reshape(n_restarts, n_in).contiguous()
-    idx = pgd_general_run(desc, x, xl.reshape(1, n_in), xh.reshape(1, n_in),
-                          step.reshape(-1, n_in), w_d, n_osi, n_iter, optim, lr_decay,
-                          hinge_thr, plateau, disjuncts, act, prd,
-                          float(getattr(spec, 'unsat_margin_bloat', 0.0) or 0.0), budget_ns)
+    args = (x, xl.reshape(1, n_in), xh.reshape(1, n_in), step.reshape(-1, n_in), w_d, n_osi,
+            n_iter, optim, lr_decay, hinge_thr, plateau, disjuncts, act, prd, bloat)
+    idx = -1
+    if isinstance(net, MlpDesc):
+        budget_ns = 0
+        if time_budget is not None:
+            left = time_budget - (time.perf_counter() - t_start)
+            budget_ns = max(1, int(left * 1e9))
+        try:
+            idx = pgd_general_run(net, *args, budget_ns)
+        except NotImplementedError:  # wider than the shared-memory kernel
+            net = _graph(gg, dev)
+    if idx == -1:
+        deadline = None if time_budget is None else t_start + time_budget
+        idx = general_layerwise(net, *args, deadline)
     if idx is None:
         return False, None
     return True, x[idx].reshape(xl.shape).detach().cpu().numpy()
@@ -330,6 +401,72 @@ def pgd_general_run(desc, x, lo, hi, step, w_d, n_osi, n_iter, optim, lr_decay, 
             nimp = 0
     if t_w == final:
         return key & 0xFFFFFFFF
+    return None
+
+
+def general_layerwise(G, x, lo, hi, step, w_d, n_osi, n_iter, optim, lr_decay, hinge_thr,
+                      plateau, disjuncts, act, prd, bloat=0.0, deadline=None):
+    """pgd_attack_general's loop on the layer kernels (networks outside the
+    shared-memory kernel): OSI steps, then per iteration forward, screen,
+    host check (the reference's ``cand.any()`` sync), plateau / deadline,
+    backward and the optimiser step.  x (R, n_in) is updated in place;
+    returns the witness row or None."""
+    from .graph import graph_forward, graph_vjp
+    dev = x.device
+    R, n_in = x.shape
+    n_out = G.n_out
+    lo = lo.to(F32).contiguous()
+    hi = hi.to(F32).contiguous()
+    step = step.to(F32).contiguous()
+    for _ in range(n_osi if w_d is not None else 0):
+        _, pre = graph_forward(G, x, keep=True)
+        gx = graph_vjp(G, pre, w_d)
+        _step(x, lo, hi, R, gx, 1, step0=step)
+    rows_np, bs, dis = _rows_of(disjuncts, n_out)
+    ordinal = {d: i for i, d in enumerate(act)}
+    rows = (torch.as_tensor(np.stack(rows_np), dtype=F32, device=dev),
+            torch.as_tensor(np.asarray(bs, np.float32), device=dev),
+            torch.as_tensor(np.asarray(dis, np.int32), device=dev),
+            torch.as_tensor(np.asarray([ordinal.get(d, -1) for d in dis], np.int32),
+                            device=dev),
+            len(disjuncts))
+    t_ = np.arange(1, max(n_iter, 1) + 1, dtype=np.float64)
+    sc1 = np.float32(1.0) / (1.0 - 0.9 ** t_).astype(np.float32)
+    sc2 = np.float32(1.0) / ((1.0 - 0.999 ** t_) ** 0.5).astype(np.float32)
+    cur = step.expand(R, n_in).contiguous().clone()
+    m1 = torch.zeros_like(x)
+    m2 = torch.zeros_like(x)
+    g = torch.empty((R, n_out), dtype=F32, device=dev)
+    state = torch.full((4,), -1, dtype=torch.int32, device=dev)  # best (2) | gmin | pad
+    base = state.data_ptr()
+    best_min = float('inf')
+    nimp = 0
+    for t in range(1, n_iter + 2):
+        final = t == n_iter + 1 or (deadline is not None and time.perf_counter() > deadline)
+        state[2] = -1
+        y, pre = graph_forward(G, x, keep=True)
+        _screen(n_out, t, y, rows, R, False, base, base + 8, g, hinge_thr, bloat, prd,
+                len(act))
+        host = state.cpu().numpy().view(np.uint32)
+        key = int(host[0]) | (int(host[1]) << 32)
+        if key != NO_SAT:
+            return key & 0xFFFFFFFF
+        if final:
+            return None
+        curr_min = _decode_min(int(host[2]))
+        if curr_min > hinge_thr:
+            if curr_min < best_min - 1e-6:
+                best_min = curr_min
+                nimp = 0
+            else:
+                nimp += 1
+            if nimp >= plateau:
+                return None
+        else:
+            nimp = 0
+        gx = graph_vjp(G, pre, g)
+        _step(x, lo, hi, R, gx, 0, _OPTIM[optim], t, cur=cur, m1=m1, m2=m2,
+              sc1=sc1[t - 1], sc2=sc2[t - 1], decay=lr_decay)
     return None
 
 
