@@ -112,6 +112,12 @@ class Worklist:
         self.xh = [xh0.reshape(1, -1)]
         self.sizes = [1]
 
+    @classmethod
+    def empty(cls, n_in=None, device=None):
+        wl = cls.__new__(cls)
+        wl.xl, wl.xh, wl.sizes = [], [], []
+        return wl
+
     def size(self):
         return sum(self.sizes)
 
@@ -177,99 +183,164 @@ def bab_step(xl, xh, lb, A, acc, qd, D, clip, branch_sb, q_sens=None):
     return lo_xl, lo_xh, hi_xl, hi_xh, cnt
 
 
+class BabConfig:
+    """The driver's settings keys with the reference's default_settings
+    values (settings.py)."""
+
+    def __init__(self, settings):
+        g = lambda k, d: _setting(settings, k, d)  # noqa: E731
+        self.total_budget = float(g('total_timeout', 120.0))
+        self.batch_size = int(g('input_split_batch_size', 4096))
+        self.max_worklist = int(g('input_split_batched_max_worklist', 200_000))
+        self.clip = bool(g('input_split_batched_clip_enabled', True))
+        self.crown_intermediate = bool(g('input_split_crown_intermediate', False))
+        self.branch_sb = bool(g('input_split_batched_branch_sb', False))
+        self.alpha_eps = float(g('input_split_batched_alpha_boundary_eps', 0.0))
+        self.alpha_iters = int(g('input_split_batched_alpha_iters', 0))
+        self.alpha_all = bool(g('input_split_batched_alpha_all_leaves', False))
+        self.alpha_max_leaves = int(g('input_split_batched_alpha_max_leaves', 200))
+        self.leaf_pgd_every = int(g('input_split_leaf_pgd_every', 0))
+        self.sat_finding = not bool(g('disable_sat_finding', False))
+        self.pgd_phase0 = bool(g('pgd_phase0_enabled', True))
+        self.raise_on_oom = bool(g('raise_on_oom', True))
+
+
+class StepResult:
+    """One bounded-and-split batch: the two child blocks (low half, high
+    half), the degenerate count and a witness if leaf PGD found one."""
+    __slots__ = ('lo', 'hi', 'n_split', 'n_degen', 'witness')
+
+    def __init__(self, lo, hi, n_split, n_degen, witness=None):
+        self.lo, self.hi = lo, hi
+        self.n_split, self.n_degen, self.witness = n_split, n_degen, witness
+
+
+class BoundEngine:
+    """Bounds and splits one popped batch on the GPU (steps 2-4 above)."""
+
+    def __init__(self, spec, gg, settings, device):
+        self.cfg = BabConfig(settings)
+        self.spec, self.gg, self.settings = spec, gg, settings
+        self.device = device
+        self.desc = mlp_desc(gg, device)
+        self.n_output = self.desc.n_out
+        self.n_in = self.desc.n_in
+        self.queries = spec.as_linear_queries(self.n_output)
+        if self.queries:
+            (self.W_q, self.b_q, self.qd, self.D,
+             self.q_sens) = dedup_queries(self.queries, device)
+
+    def root(self):
+        xl0 = torch.as_tensor(np.asarray(self.spec.x_lo), dtype=F32, device=self.device).flatten()
+        xh0 = torch.as_tensor(np.asarray(self.spec.x_hi), dtype=F32, device=self.device).flatten()
+        return xl0, xh0
+
+    def process(self, xl_b, xh_b, n_iter):
+        c = self.cfg
+        lb, A, acc = bound_batch(self.desc, xl_b, xh_b, self.W_q, self.b_q,
+                                 c.crown_intermediate, c.clip or c.branch_sb)
+        if c.alpha_iters > 0 and (c.alpha_all or c.alpha_eps > 0):
+            from .alpha import alpha_boundary_refine
+            lb = alpha_boundary_refine(self.desc, xl_b, xh_b, lb, self.W_q, self.b_q, self.qd,
+                                       self.D, c.alpha_eps, c.alpha_iters, c.alpha_max_leaves,
+                                       c.alpha_all)
+        if c.leaf_pgd_every > 0 and c.sat_finding and n_iter % c.leaf_pgd_every == 0:
+            from .pgd import leaf_pgd
+            sat, wit = leaf_pgd(xl_b, xh_b, lb, self.qd, self.D, self.spec, self.gg,
+                                self.n_output, self.device, self.settings)
+            if sat:
+                return StepResult(None, None, 0, 0, wit)
+        lo_xl, lo_xh, hi_xl, hi_xh, cnt = bab_step(
+            xl_b, xh_b, lb, A, acc, self.qd, self.D, c.clip, c.branch_sb, self.q_sens)
+        cnt = cnt.tolist()  # host sync: chunk sizes
+        n_split, n_degen = int(cnt[2]), int(cnt[3])
+        return StepResult((lo_xl[:n_split], lo_xh[:n_split]), (hi_xl[:n_split], hi_xh[:n_split]),
+                          n_split, n_degen)
+
+
+class LocalState:
+    """Per-process BaB state: the worklist and its counters."""
+
+    def __init__(self, wl, batch_size):
+        self.wl = wl
+        self.batch_size = batch_size
+        self.n_leaves = 0
+        self.n_iters = 0
+        self.n_open = 0
+        self.witness = None
+        self.oom = False
+
+
+def local_iteration(engine, st):
+    """Pop a batch, bound and split it, push the children (LIFO: low block,
+    then high block) -- one iteration of verify_graph.py:12840-13429.  On a
+    bound failure the batch goes back and the batch size halves
+    (:12872-12897); ``st.oom`` is set when it cannot halve further."""
+    wl = st.wl
+    B = min(st.batch_size, wl.size())
+    xl_b, xh_b = wl.pop(B)
+    try:
+        res = engine.process(xl_b, xh_b, st.n_iters)
+    except (torch.cuda.OutOfMemoryError, RuntimeError) as e:
+        new_bs = max(1, st.batch_size // 2)
+        wl.push(xl_b, xh_b)
+        if new_bs == st.batch_size:
+            if isinstance(e, torch.cuda.OutOfMemoryError) and engine.cfg.raise_on_oom:
+                raise
+            st.oom = True
+            return
+        st.batch_size = new_bs
+        return
+    if res.witness is not None:
+        st.witness = res.witness
+        return
+    st.n_leaves += B
+    st.n_open += res.n_degen
+    if res.n_split > 0:
+        wl.push(*res.lo)
+        wl.push(*res.hi)
+    st.n_iters += 1
+
+
 def _input_split_batched(graph, spec, settings, gg, device, dtype):
     """Worklist-based input-split BaB with batched leaf evaluation
     (verify_graph.py:12466).  Returns (verdict, details) with verdict in
     {'verified', 'unknown', 'sat'}."""
     device = _dev(device)
     t_start = time.perf_counter()
-    # defaults are the reference's default_settings values (settings.py)
-    total_budget = float(_setting(settings, 'total_timeout', 120.0))
-    batch_size = int(_setting(settings, 'input_split_batch_size', 4096))
-    max_worklist = int(_setting(settings, 'input_split_batched_max_worklist', 200_000))
-    clip_enabled = bool(_setting(settings, 'input_split_batched_clip_enabled', True))
-    crown_intermediate = bool(_setting(settings, 'input_split_crown_intermediate', False))
-    branch_sb = bool(_setting(settings, 'input_split_batched_branch_sb', False))
-    alpha_eps = float(_setting(settings, 'input_split_batched_alpha_boundary_eps', 0.0))
-    alpha_iters = int(_setting(settings, 'input_split_batched_alpha_iters', 0))
-    alpha_all = bool(_setting(settings, 'input_split_batched_alpha_all_leaves', False))
-    alpha_max_leaves = int(_setting(settings, 'input_split_batched_alpha_max_leaves', 200))
-    leaf_pgd_every = int(_setting(settings, 'input_split_leaf_pgd_every', 0))
-    sat_finding = not bool(_setting(settings, 'disable_sat_finding', False))
-    desc = mlp_desc(gg, device)
-    n_output = desc.n_out
-
-    if sat_finding and bool(_setting(settings, 'pgd_phase0_enabled', True)):
+    engine = BoundEngine(spec, gg, settings, device)
+    cfg = engine.cfg
+    if cfg.sat_finding and cfg.pgd_phase0:
         from .pgd import root_pgd
-        sat, wit, phase = root_pgd(spec, gg, n_output, device, settings)
+        sat, wit, phase = root_pgd(spec, gg, engine.n_output, device, settings)
         if sat:
             return 'sat', {'phase': phase, 'witness': wit}
-
-    queries = spec.as_linear_queries(n_output)
-    if not queries:
+    if not engine.queries:
         return 'verified', {'phase': 'batched_no_queries'}
-    W_q, b_q, qd, D, q_sens = dedup_queries(queries, device)
-    xl0 = torch.as_tensor(np.asarray(spec.x_lo), dtype=F32, device=device).flatten()
-    xh0 = torch.as_tensor(np.asarray(spec.x_hi), dtype=F32, device=device).flatten()
-    wl = Worklist(xl0, xh0)
-    n_leaves = 0
-    n_iters = 0
-    n_open = 0
-    want_A = clip_enabled or branch_sb
+    st = LocalState(Worklist(*engine.root()), cfg.batch_size)
+    wl = st.wl
     while wl:
-        wl_n = wl.size()
-        if time.perf_counter() - t_start > total_budget - 0.5:
-            n_open = wl_n
+        if time.perf_counter() - t_start > cfg.total_budget - 0.5:
+            st.n_open = wl.size()
             break
-        B = min(batch_size, wl_n)
-        xl_b, xh_b = wl.pop(B)
-        try:
-            lb, A, acc = bound_batch(desc, xl_b, xh_b, W_q, b_q,
-                                     crown_intermediate, want_A)
-        except (torch.cuda.OutOfMemoryError, RuntimeError) as e:
-            new_bs = max(1, batch_size // 2)
-            if new_bs == batch_size:
-                if isinstance(e, torch.cuda.OutOfMemoryError) and bool(
-                        _setting(settings, 'raise_on_oom', True)):
-                    raise
-                return 'unknown', {'phase': 'batched_oom', 'batch_size': batch_size}
-            wl.push(xl_b, xh_b)
-            batch_size = new_bs
-            continue
-        if alpha_iters > 0 and (alpha_all or alpha_eps > 0):
-            from .alpha import alpha_boundary_refine
-            lb = alpha_boundary_refine(desc, xl_b, xh_b, lb, W_q, b_q, qd, D,
-                                       alpha_eps, alpha_iters, alpha_max_leaves,
-                                       alpha_all)
-        if (leaf_pgd_every > 0 and sat_finding and n_iters % leaf_pgd_every == 0):
-            from .pgd import leaf_pgd
-            sat, wit = leaf_pgd(xl_b, xh_b, lb, qd, D, spec, gg, n_output,
-                                device, settings)
-            if sat:
-                return 'sat', {'phase': 'batched_leaf_pgd', 'witness': wit}
-        lo_xl, lo_xh, hi_xl, hi_xh, cnt = bab_step(
-            xl_b, xh_b, lb, A, acc, qd, D, clip_enabled, branch_sb, q_sens)
-        c = cnt.tolist()  # host sync: chunk sizes
-        n_leaves += B
-        n_split, n_degen = int(c[2]), int(c[3])
-        n_open += n_degen
-        if n_split > 0:
-            wl.push(lo_xl[:n_split], lo_xh[:n_split])
-            wl.push(hi_xl[:n_split], hi_xh[:n_split])
-        if n_split + n_degen > 0 and wl.size() > max_worklist:
+        local_iteration(engine, st)
+        if st.oom:
+            return 'unknown', {'phase': 'batched_oom', 'batch_size': st.batch_size}
+        if st.witness is not None:
+            return 'sat', {'phase': 'batched_leaf_pgd', 'witness': st.witness}
+        if wl.size() > cfg.max_worklist:
             return 'unknown', {'phase': 'batched_worklist_overflow',
-                               'batched_n_leaves': n_leaves,
-                               'batched_n_iters': n_iters,
+                               'batched_n_leaves': st.n_leaves,
+                               'batched_n_iters': st.n_iters,
                                'worklist_size': wl.size()}
-        n_iters += 1
-    if not wl and n_open == 0:
+    if not wl and st.n_open == 0:
         return 'verified', {'phase': 'batched_verified',
-                            'batched_n_leaves': n_leaves,
-                            'batched_n_iters': n_iters,
-                            'batched_batch_size': batch_size}
+                            'batched_n_leaves': st.n_leaves,
+                            'batched_n_iters': st.n_iters,
+                            'batched_batch_size': st.batch_size}
     return 'unknown', {'phase': 'batched_timeout',
-                       'batched_n_leaves': n_leaves,
-                       'batched_n_iters': n_iters,
+                       'batched_n_leaves': st.n_leaves,
+                       'batched_n_iters': st.n_iters,
                        'batched_worklist_left': wl.size(),
-                       'batched_open_degenerate': n_open,
-                       'batched_batch_size': batch_size}
+                       'batched_open_degenerate': st.n_open,
+                       'batched_batch_size': st.batch_size}
