@@ -8,6 +8,12 @@ coefficients in {-1,0,1}; one step = IBP intermediate bounds + CROWN
 back-substitution for every box (one fused kernel launch, vcb_mlp_crown).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config cfg2|cfg1|cfg3|cfg4]
+
+``--config`` selects another BASELINE config on its own metric: cfg1 the
+input-split BaB time-to-verdict (N > 1: the sharded driver, strong scaling),
+cfg3 alpha-CROWN over 1,024 ReLU-split domains, cfg4 conv CROWN over 256
+domains.
 
 N > 1 runs under torchrun, one rank per GPU; every rank bounds its own
 65,536 boxes (weak scaling, no data-path collective); the time is the max
@@ -43,6 +49,9 @@ def parse():
     ap.add_argument('--warmup', type=int, default=10)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--config', default='cfg2', choices=['cfg2', 'cfg1', 'cfg3', 'cfg4'],
+                    help='cfg2 (default) is the headline; the others time the '
+                         'remaining BASELINE configs on their own metrics')
     return ap.parse_args()
 
 
@@ -365,10 +374,233 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# other BASELINE configs (cfg1, cfg3, cfg4)
+# ---------------------------------------------------------------------------
+
+def _setup_dist():
+    import torch
+    import torch.distributed as dist
+    rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    dev = torch.device(f'cuda:{local}')
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', timeout=timedelta(seconds=300), device_id=dev)
+    return rank, world, local, dev
+
+
+def _time_steps(dev, step, args, world, flush):
+    """W warm-up steps, then K timed steps (CUDA events, L2 flushed before
+    each); returns (per-step ms, clocks summary, max-over-ranks total ms)."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    props = torch.cuda.get_device_properties(dev)
+    gid = getattr(props, 'uuid', None)
+    gid = f'GPU-{gid}' if gid is not None else dev.index
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(gid) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    per = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    tot = torch.tensor([sum(per)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    return per, clk.summary(), float(tot.item())
+
+
+def _cpu_cfg1(budget_s=15.0):
+    from oracle import bab as obab
+    from vibecheck_nn_b200 import workloads as wk
+    w = wk.cfg1(0)
+    t0 = time.perf_counter()
+    _, det = obab.input_split_bab(wk.mlp_gg(w['layers']), w['xl'], w['xh'], w['spec_W'],
+                                  w['spec_b'], batch_size=2048, crown_intermediate=True,
+                                  timeout=budget_s)
+    return det['batched_n_leaves'] / (time.perf_counter() - t0)
+
+
+def run_cfg1(args):
+    import torch
+    import torch.distributed as dist
+    import types
+    rank, world, _, dev = _setup_dist()
+    from vibecheck_nn_b200 import bab, shard, workloads as wk
+    w = wk.cfg1(0)
+    gg = wk.mlp_gg(w['layers'], dev)
+    spec = bab.LinearSpec(w['xl'], w['xh'], [[('pair', 1, 0)]])
+    st = types.SimpleNamespace(input_split_batch_size=2048, input_split_crown_intermediate=True,
+                               total_timeout=600.0)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    res = {}
+
+    def step():
+        if world > 1:
+            res['v'] = shard._input_split_batched_sharded(None, spec, st, gg, dev, torch.float32)
+        else:
+            res['v'] = bab._input_split_batched(None, spec, st, gg, dev, torch.float32)
+
+    per, clocks, t_max = _time_steps(dev, step, args, world, flush)
+    verdict, det = res['v']
+    n_leaves = det['batched_n_leaves']
+    ms = t_max / args.steps
+    if rank == 0:
+        line = {
+            'metric': 'BaB time-to-verdict (cfg1, input-split, CROWN intermediates)',
+            'value': ms / 1e3, 'unit': 's', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': False,
+            'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic (seeded numpy rng)',
+            'config': {'workload': 'cfg1: 5x[50]x6x5 MLP, y0 - y1 <= d, input-split BaB, '
+                                   'leaf batch 2048, root PGD included',
+                       'verdict': verdict, 'leaves': n_leaves,
+                       'leaves_per_s': n_leaves / (ms / 1e3),
+                       'l2': 'flushed (256 MiB write) before each verdict',
+                       'parallelism': f'{world} GPU(s), leaves sharded' if world > 1
+                       else '1 GPU'},
+            'clocks': clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            rate = _cpu_cfg1()
+            line['cpu_baseline'] = {
+                'value': n_leaves / rate, 'unit': 's', 'cores': 1, 'kind': 'port',
+                'sample': f'oracle/bab.py input-split BaB for 15 s ({rate:.0f} leaves/s, '
+                          f'numpy), extrapolated to the {n_leaves} leaves of the verdict'}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _domains(xl1, xh1, root_lo, root_hi, n_split):
+    import numpy as np
+    from vibecheck_nn_b200 import workloads as wk
+    picked, clamps = wk.split_domains(root_lo, root_hi, n_split)
+    Dn = 1 << len(picked)
+    xl = np.broadcast_to(xl1, (Dn, xl1.size)).copy()
+    xh = np.broadcast_to(xh1, (Dn, xh1.size)).copy()
+    return xl, xh, clamps
+
+
+def run_cfg34(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    rank, world, _, dev = _setup_dist()
+    from vibecheck_nn_b200 import graph, ops, wide, workloads as wk
+    from oracle import bounds as ob
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    T = lambda a: torch.as_tensor(a, device=dev)  # noqa: E731
+    if args.config == 'cfg3':
+        w = wk.cfg3(0)
+        gg = wk.mlp_gg(w['layers'], dev)
+        wn = wide.wide_net(gg, dev)
+        root = wide.wide_ibp(wn, T(w['xl'][None]), T(w['xh'][None]))
+        xl, xh, clamps = _domains(w['xl'], w['xh'], {L: v[0][0].cpu().numpy() for L, v in root.items()},
+                                  {L: v[1][0].cpu().numpy() for L, v in root.items()}, 10)
+        Dn = xl.shape[0]
+        dims = wk.CFG3_DIMS
+        sw = sum(a * b for a, b in zip(dims[:-1], dims[1:]))
+        Q = w['spec_W'].shape[0]
+        flop = 20 * Dn * 4 * Q * sw + 4 * sw * Dn
+        tcl = {L: (T(c[0]), T(c[1])) for L, c in clamps.items()}
+
+        def step():
+            return wide.alpha_crown_domains(xl, xh, gg, w['spec_W'], w['spec_b'], tcl, dev,
+                                            n_iters=20, lr=0.1)
+
+        def cpu():
+            ggc = wk.mlp_gg(w['layers'])
+            n = 16
+            cc = {L: (c[0][:n], c[1][:n]) for L, c in clamps.items()}
+            t0 = time.perf_counter()
+            ob.alpha_beta_crown_domains(xl[:n], xh[:n], ggc, w['spec_W'], w['spec_b'], cc,
+                                        n_iters=20, lr=0.1)
+            return n / (time.perf_counter() - t0), f'{n} domains x 20 iterations, numpy oracle'
+        metric = 'alpha-CROWN domains/s (cfg3: 20 Adam iterations, 9 spec rows)'
+        workload = ('cfg3: 784x[256]x6x10 MLP, 1024 ReLU-split domains (10 widest unstable '
+                    'neurons), IBP intermediates, min-area alpha init, Adam lr 0.1 x 20')
+    else:
+        w = wk.cfg4(0)
+        gg = wk.cnn_gg(w['params'], dev)
+        G = graph.graph_net(gg, dev)
+        root = graph.graph_ibp(G, T(w['xl'][None]), T(w['xh'][None]))
+        xl, xh, clamps = _domains(w['xl'], w['xh'], {L: v[0][0].cpu().numpy() for L, v in root.items()},
+                                  {L: v[1][0].cpu().numpy() for L, v in root.items()}, 8)
+        Dn = xl.shape[0]
+        SW, Sb = wk.margin_rows(10, 3)
+        flop = Dn * (4 * 926_696 + 2 * 9 * 926_696)
+        tcl = {L: (T(c[0]), T(c[1])) for L, c in clamps.items()}
+        xlt, xht = T(xl), T(xh)
+        spec_ew = wk.spec_ew_from(SW, Sb, dev)
+
+        def step():
+            sb = ops._ibp_forward_graph_batched(xlt, xht, gg, dev, torch.float32,
+                                                relu_clamps=tcl)
+            return ops._spec_backward_graph_batched(sb, xlt, xht, gg, spec_ew, dev,
+                                                    torch.float32)
+
+        def cpu():
+            ggc = wk.cnn_gg(w['params'])
+            n = 16
+            cc = {L: (c[0][:n], c[1][:n]) for L, c in clamps.items()}
+            t0 = time.perf_counter()
+            sbr = ob.ibp_forward_batched(xl[:n], xh[:n], ggc, relu_clamps=cc)
+            ob.spec_backward_batched(sbr, xl[:n], xh[:n], ggc, SW, Sb)
+            return n / (time.perf_counter() - t0), f'{n} domains, numpy oracle'
+        metric = 'conv CROWN domains/s (cfg4: IBP intermediates + CROWN through conv-transpose)'
+        workload = ('cfg4: CNN 3x32x32 -> conv16 4x4 s2 -> conv32 4x4 s2 -> fc100 -> fc10, '
+                    '256 ReLU-split domains, 9 margin rows')
+    per, clocks, t_max = _time_steps(dev, step, args, world, flush)
+    ms = t_max / args.steps
+    peak = measured_fp32_peak(dev)
+    achieved = flop / (statistics.mean(per) * 1e-3) / 1e12
+    if rank == 0:
+        line = {
+            'metric': metric, 'value': world * Dn / (ms / 1e3), 'unit': 'domains/s',
+            'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic (seeded numpy rng)',
+            'config': {'workload': workload, 'domains_per_gpu': Dn,
+                       'l2': 'flushed (256 MiB write) between timed steps',
+                       'parallelism': f'{world} GPU(s), domains sharded'},
+            'roofline': {'bound': 'fp32_simt', 'achieved': achieved, 'peak': peak,
+                         'unit': 'TFLOP/s', 'frac': achieved / peak if peak else None,
+                         'traffic': None, 'flop_per_step': flop,
+                         'peak_source': 'measured live: vcb_probe_ffma'},
+            'clocks': clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            rate, sample = cpu()
+            line['cpu_baseline'] = {'value': rate, 'unit': 'domains/s',
+                                    'cores': os.cpu_count(), 'kind': 'port',
+                                    'sample': sample + ' (numpy BLAS threads)'}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == 'reference':
         run_reference(args)
+    elif args.config == 'cfg1':
+        run_cfg1(args)
+    elif args.config in ('cfg3', 'cfg4'):
+        run_cfg34(args)
     else:
         run_ours(args)
 
