@@ -345,9 +345,15 @@ int vcb_conv_ibp(int32_t D, const int32_t* geometry, const float* mid,
                  const float* b, float* lo, float* hi, void* stream);
 
 /* CROWN conv step: e_in (R x C x H x W) = conv_transpose(e (R x C_out x H_out
- * x W_out), K) -- the adjoint of the convolution. */
+ * x W_out), K) -- the adjoint of the convolution.  workspace: device scratch
+ * of at least vcb_conv_back_workspace(R, geometry) bytes (the per-tap
+ * products, R Ho Wo C kh kw floats). */
 int vcb_conv_back(int32_t R, const int32_t* geometry, const float* e,
-                  const float* K, float* e_in, void* stream);
+                  const float* K, float* e_in, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* Scratch bytes vcb_conv_back / vcb_conv_backward need for R rows. */
+size_t vcb_conv_back_workspace(int32_t R, const int32_t* geometry);
 
 /* bd[r] = sum_{c, p} e[r][c][p] b[c] (conv bias dot, e: R x Co x hw). */
 int vcb_conv_bias_dot(int32_t R, int32_t Co, int32_t hw, const float* e,
@@ -392,10 +398,11 @@ int vcb_conv_forward(int32_t N, const int32_t* geometry, const float* x,
                      void* stream);
 
 /* Conv vector-Jacobian product: g_in (N x C x H x W) = conv_transpose(g, K),
- * zeroed where mask (same shape as g_in, or NULL) is <= 0. */
+ * zeroed where mask (same shape as g_in, or NULL) is <= 0; workspace as for
+ * vcb_conv_back. */
 int vcb_conv_backward(int32_t N, const int32_t* geometry, const float* g,
                       const float* K, const float* mask, float* g_in,
-                      void* stream);
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* Diagnostic: FP32 FFMA throughput probe (no reference counterpart).  Runs
  * `blocks` CTAs of 256 threads, each thread `iters` x 64 dependent-chain FMAs

@@ -67,13 +67,14 @@ SIGNATURES = {
     'vcb_wide_alpha_adam': [_I, _I, _I, _I, _P, _P, _P, _P, ctypes.c_float, _I,
                             _P],
     'vcb_conv_ibp': [_I, _P, _P, _P, _P, _P, _P, _P, _P, _P],
-    'vcb_conv_back': [_I, _P, _P, _P, _P, _P],
+    'vcb_conv_back': [_I, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
+    'vcb_conv_back_workspace': [_I, _P],
     'vcb_pgd_screen': [_I, _I, _P, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I,
                        ctypes.c_float, ctypes.c_double, _I, _P, _P, _P, _I, _P],
     'vcb_pgd_step': [_I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _P, _I, _P, _P, _P,
                      ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P],
     'vcb_conv_forward': [_I, _P, _P, _P, _P, _P, _P, _P],
-    'vcb_conv_backward': [_I, _P, _P, _P, _P, _P, _P],
+    'vcb_conv_backward': [_I, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     'vcb_fc_forward': [_I, _I, _I, _P, _I, _P, _P, _P, _I, _P, _I, _P],
     'vcb_fc_backward': [_I, _I, _I, _P, _I, _P, _P, _I, _P, _I, _P],
     'vcb_conv_bias_dot': [_I, _I, _I, _P, _P, _P, _P],
@@ -84,7 +85,8 @@ SIGNATURES = {
 }
 RESTYPES = {'vcb_last_error': ctypes.c_char_p,
             'vcb_mlp_crown_workspace': ctypes.c_size_t,
-            'vcb_mlp_crown_noalloc_capacity': ctypes.c_size_t}
+            'vcb_mlp_crown_noalloc_capacity': ctypes.c_size_t,
+            'vcb_conv_back_workspace': ctypes.c_size_t}
 
 _lib = None
 

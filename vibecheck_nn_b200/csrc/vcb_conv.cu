@@ -5,11 +5,12 @@
 //   A operand is an im2col gather of the NCHW input), giving the
 //   pre-activation lo/hi.
 // * conv back-substitution (verify_zono_bnb.py:4568-4593, the
-//   conv_transpose2d of the coefficients): implicit GEMM over input pixels
-//   (M = rows x H x W, N = C_in, K = C_out kh kw) whose A operand gathers the
-//   output-pixel coefficient that each kernel tap of a stride-s convolution
-//   maps onto the input pixel (zero where no output pixel does), so every sum
-//   has a fixed order and no atomics are needed.
+//   conv_transpose2d of the coefficients) in two steps: a dense GEMM of the
+//   coefficients with the kernel gives every (output pixel, input channel,
+//   tap) product (M = rows x Ho x Wo, N = C_in kh kw, K = C_out -- no
+//   structural zeros), then a gather sums, for every input pixel, the taps
+//   that land on it in a fixed (ki, kj) order: no atomics, deterministic, and
+//   both passes read and write contiguously.
 // * concrete conv forward (the conv branch of _forward_batch_graph,
 //   verify_zono_bnb.py:569-575) as the same implicit GEMM with a bias +
 //   optional ReLU epilogue, and its vector-Jacobian product (the transposed
@@ -35,6 +36,7 @@ struct ConvGeom {
 struct Im2col {
   const float* x;  // boxes x C x H x W
   ConvGeom g;
+  static constexpr bool kFastA = true;  // consecutive m = neighbouring output pixels
   __device__ __forceinline__ float a(int m, int k) const {
     const int hw = g.Ho * g.Wo;
     const int d = m / hw, pix = m - d * hw;
@@ -48,36 +50,15 @@ struct Im2col {
   }
 };
 
-// Transposed-convolution gather: row m = (row r, input pixel h, w), col
-// k = (co, ki, kj); the output pixel (oh, ow) with oh*sh - ph + ki == h.
-struct Col2im {
-  const float* e;  // rows x Co x Ho x Wo
-  ConvGeom g;
+// A(m, k) of the per-tap product: m = (row r, output pixel), k = output
+// channel co; e is rows x Co x Ho x Wo, so consecutive m are contiguous.
+struct EPix {
+  const float* e;
+  int Co, hw;
+  static constexpr bool kFastA = true;
   __device__ __forceinline__ float a(int m, int k) const {
-    const int hw = g.H * g.W;
     const int r = m / hw, pix = m - r * hw;
-    const int h = pix / g.W, w = pix - h * g.W;
-    const int kk = g.kh * g.kw;
-    const int co = k / kk, t = k - co * kk;
-    const int ki = t / g.kw, kj = t - ki * g.kw;
-    const int nh = h + g.ph - ki, nw = w + g.pw - kj;
-    if (nh < 0 || nw < 0) return 0.f;
-    const int oh = nh / g.sh, ow = nw / g.sw;
-    if (oh * g.sh != nh || ow * g.sw != nw || oh >= g.Ho || ow >= g.Wo) return 0.f;
-    return __ldg(e + (((long long)r * g.Co + co) * g.Ho + oh) * g.Wo + ow);
-  }
-};
-
-// B(k, n) = K[co][n][ki][kj] for k = (co, ki, kj): the conv weight read as
-// the (C_out kh kw) x C_in operand of the transposed convolution.
-struct KernT {
-  const float* K;
-  ConvGeom g;
-  static constexpr bool kFastB = false;
-  __device__ __forceinline__ float b(int k, int n) const {
-    const int kk = g.kh * g.kw;
-    const int co = k / kk, t = k - co * kk;
-    return __ldg(K + ((long long)co * g.C + n) * kk + t);
+    return __ldg(e + ((long long)r * Co + k) * hw + pix);
   }
 };
 
@@ -150,37 +131,79 @@ __global__ void __launch_bounds__(GT) conv_fwd_kernel(const ConvFwdArgs a) {
   }
 }
 
-struct ConvBackArgs {
+// Transposed convolution, step 1: cols^T (C kh kw) x (R Ho Wo) = (e^T K)^T,
+// the contribution of every output pixel to every kernel tap of every input
+// channel (M = R Ho Wo, N = C kh kw, K = Co).
+struct ConvColsArgs {
   int R;
   ConvGeom g;
   const float *e, *K;
-  float* e_in;        // R x C x H x W
-  const float* mask;  // R x C x H x W pre-activations: keep e_in where > 0; or NULL
+  float* cols;  // (C kh kw) x (R Ho Wo)
 };
 
-__global__ void __launch_bounds__(GT) conv_back_kernel(const ConvBackArgs a) {
+constexpr int kColsPad = TM + 1;  // smem row of the transposed epilogue tile
+
+__global__ void __launch_bounds__(GT) conv_cols_kernel(const ConvColsArgs a) {
   extern __shared__ __align__(16) float smem[];
   float acc[8][4], acc2[8][4];
-  const int KD = a.g.Co * a.g.kh * a.g.kw;
-  const int M = a.R * a.g.H * a.g.W;
-  mainloop<false>(M, a.g.C, KD, Col2im{a.e, a.g}, KernT{a.K, a.g}, Col2im{nullptr, a.g},
-                  KernT{nullptr, a.g}, acc, acc2, smem);
+  const int hw = a.g.Ho * a.g.Wo;
+  const int M = a.R * hw;
+  const int N = a.g.C * a.g.kh * a.g.kw;
+  mainloop<false>(M, N, a.g.Co, EPix{a.e, a.g.Co, hw}, ColLoad{a.K, N}, EPix{nullptr, 0, 1},
+                  ColLoad{nullptr, 0}, acc, acc2, smem);
+  // transpose the 128 x 64 tile through shared memory so that each column n
+  // of cols^T is written as 128 consecutive floats
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-  const int m0 = blockIdx.x * TM + ty * 8, n0 = blockIdx.y * TN + tx * 4;
-  const int hw = a.g.H * a.g.W;
+  const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int m = m0 + i;
-    if (m >= M) continue;
-    const int r = m / hw, pix = m - r * hw;
+  for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + j;
-      if (n >= a.g.C) continue;
-      const long long o = ((long long)r * a.g.C + n) * hw + pix;
-      a.e_in[o] = (a.mask && !(a.mask[o] > 0.f)) ? 0.f : acc[i][j];
+    for (int j = 0; j < 4; ++j) smem[(tx * 4 + j) * kColsPad + ty * 8 + i] = acc[i][j];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int nn = warp; nn < TN; nn += GT / 32) {
+    const int n = n0 + nn;
+    if (n >= N) break;
+    for (int mm = lane; mm < TM; mm += 32) {
+      const int m = m0 + mm;
+      if (m < M) a.cols[(long long)n * M + m] = smem[nn * kColsPad + mm];
     }
   }
+}
+
+// Step 2: e_in[r][c][h][w] = sum over the taps (ki, kj) whose output pixel
+// (oh, ow) = ((h + ph - ki) / sh, (w + pw - kj) / sw) exists, in (ki, kj)
+// order; zeroed where mask (the ReLU pre-activation in front, or NULL) <= 0.
+// Grid: x over the H W pixels of one (row, channel) plane, y = row C + c.
+__global__ void col2im_kernel(int R, ConvGeom g, const float* __restrict__ cols,
+                              const float* __restrict__ mask, float* __restrict__ e_in) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= g.H * g.W) return;
+  const int rc = blockIdx.y;
+  const int c = rc % g.C, r = rc / g.C;
+  const int h = p / g.W, w = p - h * g.W;
+  const long long M = (long long)R * g.Ho * g.Wo;
+  const long long rowbase = (long long)r * g.Ho;
+  const int kk = g.kh * g.kw;
+  float acc = 0.f;
+  // the taps that reach (h, w) are ki = (h + ph) mod sh + sh t
+  const int hp = h + g.ph, wp = w + g.pw;
+  for (int ki = hp % g.sh; ki < g.kh; ki += g.sh) {
+    const int nh = hp - ki;
+    if (nh < 0) break;
+    const int oh = nh / g.sh;
+    if (oh >= g.Ho) continue;
+    for (int kj = wp % g.sw; kj < g.kw; kj += g.sw) {
+      const int nw = wp - kj;
+      if (nw < 0) break;
+      const int ow = nw / g.sw;
+      if (ow >= g.Wo) continue;
+      const long long col = (long long)c * kk + ki * g.kw + kj;
+      acc += __ldg(cols + col * M + (rowbase + oh) * g.Wo + ow);
+    }
+  }
+  const long long idx = ((long long)rc * g.H + h) * g.W + w;
+  e_in[idx] = (mask && !(mask[idx] > 0.f)) ? 0.f : acc;
 }
 
 // bd[r] = sum_{c, pix} e[r][c][pix] * b[c]  (one warp per row)
@@ -289,18 +312,41 @@ extern "C" int vcb_conv_ibp(int32_t D, const int32_t* geometry, const float* mid
   return check_launch("vcb_conv_ibp");
 }
 
-extern "C" int vcb_conv_back(int32_t R, const int32_t* geometry, const float* e,
-                             const float* K, float* e_in, void* stream) {
-  if (R < 0 || !geometry) return fail(VCB_ERR_INVALID, "vcb_conv_back: bad arguments");
+static int conv_transpose(const char* who, int32_t R, const int32_t* geometry, const float* g,
+                          const float* K, const float* mask, float* g_in, void* workspace,
+                          size_t ws_bytes, void* stream) {
+  if (R < 0 || !geometry) return fail(VCB_ERR_INVALID, "%s: bad arguments", who);
   if (R == 0) return VCB_OK;
-  if (!e || !K || !e_in) return fail(VCB_ERR_INVALID, "vcb_conv_back: NULL pointer");
-  ConvBackArgs a{R, geom(geometry), e, K, e_in, nullptr};
-  const int sm = gemm_smem_bytes(false);
-  int rc = ensure_smem(reinterpret_cast<const void*>(conv_back_kernel), sm);
+  if (!g || !K || !g_in) return fail(VCB_ERR_INVALID, "%s: NULL pointer", who);
+  ConvColsArgs a{R, geom(geometry), g, K, static_cast<float*>(workspace)};
+  const size_t need = (size_t)R * a.g.Ho * a.g.Wo * a.g.C * a.g.kh * a.g.kw * sizeof(float);
+  if (!workspace || ws_bytes < need)
+    return fail(VCB_ERR_INVALID, "%s: workspace of %zu bytes, need %zu", who, ws_bytes, need);
+  if ((long long)R * a.g.C > 65535)
+    return fail(VCB_ERR_UNSUPPORTED, "%s: %d rows x %d channels", who, R, a.g.C);
+  const int sm = std::max(gemm_smem_bytes(false), TN * kColsPad * 4);
+  int rc = ensure_smem(reinterpret_cast<const void*>(conv_cols_kernel), sm);
   if (rc) return rc;
-  conv_back_kernel<<<gemm_grid(R * a.g.H * a.g.W, a.g.C), GT, sm,
-                     static_cast<cudaStream_t>(stream)>>>(a);
-  return check_launch("vcb_conv_back");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  conv_cols_kernel<<<gemm_grid(R * a.g.Ho * a.g.Wo, a.g.C * a.g.kh * a.g.kw), GT, sm, st>>>(a);
+  rc = check_launch(who);
+  if (rc) return rc;
+  const dim3 grid((a.g.H * a.g.W + 255) / 256, R * a.g.C);
+  col2im_kernel<<<grid, 256, 0, st>>>(R, a.g, a.cols, mask, g_in);
+  return check_launch(who);
+}
+
+extern "C" size_t vcb_conv_back_workspace(int32_t R, const int32_t* geometry) {
+  if (R <= 0 || !geometry) return 0;
+  const ConvGeom g = geom(geometry);
+  return (size_t)R * g.Ho * g.Wo * g.C * g.kh * g.kw * sizeof(float);
+}
+
+extern "C" int vcb_conv_back(int32_t R, const int32_t* geometry, const float* e,
+                             const float* K, float* e_in, void* workspace, size_t ws_bytes,
+                             void* stream) {
+  return conv_transpose("vcb_conv_back", R, geometry, e, K, nullptr, e_in, workspace, ws_bytes,
+                        stream);
 }
 
 extern "C" int vcb_conv_forward(int32_t N, const int32_t* geometry, const float* x,
@@ -320,17 +366,9 @@ extern "C" int vcb_conv_forward(int32_t N, const int32_t* geometry, const float*
 
 extern "C" int vcb_conv_backward(int32_t N, const int32_t* geometry, const float* g,
                                  const float* K, const float* mask, float* g_in,
-                                 void* stream) {
-  if (N < 0 || !geometry) return fail(VCB_ERR_INVALID, "vcb_conv_backward: bad arguments");
-  if (N == 0) return VCB_OK;
-  if (!g || !K || !g_in) return fail(VCB_ERR_INVALID, "vcb_conv_backward: NULL pointer");
-  ConvBackArgs a{N, geom(geometry), g, K, g_in, mask};
-  const int sm = gemm_smem_bytes(false);
-  int rc = ensure_smem(reinterpret_cast<const void*>(conv_back_kernel), sm);
-  if (rc) return rc;
-  conv_back_kernel<<<gemm_grid(N * a.g.H * a.g.W, a.g.C), GT, sm,
-                     static_cast<cudaStream_t>(stream)>>>(a);
-  return check_launch("vcb_conv_backward");
+                                 void* workspace, size_t ws_bytes, void* stream) {
+  return conv_transpose("vcb_conv_backward", N, geometry, g, K, mask, g_in, workspace, ws_bytes,
+                        stream);
 }
 
 extern "C" int vcb_conv_bias_dot(int32_t R, int32_t Co, int32_t hw, const float* e,

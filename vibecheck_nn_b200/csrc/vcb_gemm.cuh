@@ -5,7 +5,9 @@
 // tile; 256 threads; 16-deep k-slices double-buffered in shared memory.
 // Operands come through loader functors:  a(m, k) and b(k, n) return the
 // element or 0 outside the matrix, so plain row-major matrices, transposed
-// weights and implicit-GEMM convolution gathers share one mainloop.  DUAL
+// weights and implicit-GEMM convolution gathers share one mainloop.  A
+// loader's kFastA / kFastB says which index consecutive threads should walk
+// for coalesced loads (m / n when true, k otherwise).  DUAL
 // also accumulates A2 * B2 into acc2 (IBP's mid @ W and rad @ |W| together).
 #pragma once
 
@@ -22,7 +24,8 @@ struct RowLoad {
   int ld;
   __device__ __forceinline__ float a(int m, int k) const { return __ldg(p + (long long)m * ld + k); }
   __device__ __forceinline__ float b(int k, int n) const { return __ldg(p + (long long)n * ld + k); }
-  static constexpr bool kFastB = true;  // consecutive threads walk k
+  static constexpr bool kFastA = false;  // consecutive threads walk k
+  static constexpr bool kFastB = true;   // consecutive threads walk k
 };
 
 // B (K x N) row-major with leading dimension ld.
@@ -53,7 +56,8 @@ __device__ __forceinline__ void mainloop(int M, int N, int K, const AL& A, const
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int idx = tid + u * GT;  // 0..2047: 128 rows x 16 k
-      const int mm = idx >> 4, kk = idx & 15;
+      int mm, kk;
+      if (AL::kFastA) { mm = idx & 127; kk = idx >> 7; } else { mm = idx >> 4; kk = idx & 15; }
       const int gm = m0 + mm, gk = k0 + kk;
       const bool ok = gm < M && gk < K;
       ra[u] = ok ? A.a(gm, gk) : 0.f;
@@ -76,8 +80,10 @@ __device__ __forceinline__ void mainloop(int M, int N, int K, const AL& A, const
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int idx = tid + u * GT;
-      as[(idx & 15) * (TM + 4) + (idx >> 4)] = ra[u];
-      if (DUAL) As2[buf * TK * (TM + 4) + (idx & 15) * (TM + 4) + (idx >> 4)] = ra2[u];
+      int mm, kk;
+      if (AL::kFastA) { mm = idx & 127; kk = idx >> 7; } else { mm = idx >> 4; kk = idx & 15; }
+      as[kk * (TM + 4) + mm] = ra[u];
+      if (DUAL) As2[buf * TK * (TM + 4) + kk * (TM + 4) + mm] = ra2[u];
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {

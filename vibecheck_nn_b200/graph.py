@@ -234,8 +234,10 @@ def graph_crown(G, xl, xh, sb, W_q, b_q, alpha=None, beta=None, want_A=False):
                                       P(bd), st)
             _lib.check(rc, 'vcb_conv_bias_dot')
             e_in = torch.empty((R, layer['nin']), dtype=F32, device=dev)
+            ws_n = L_.vcb_conv_back_workspace(R, _geom_ptr(layer['geom']))
+            ws = _lib.workspace(ws_n, dev)
             rc = L_.vcb_conv_back(R, _geom_ptr(layer['geom']), P(coef), P(layer['K']),
-                                  P(e_in), st)
+                                  P(e_in), P(ws), ws_n, st)
             _lib.check(rc, 'vcb_conv_back')
             rc = L_.vcb_wide_rowsum(R, 1, 0, P(bd), P(bd), P(acc), st)
             _lib.check(rc, 'vcb_wide_rowsum')
@@ -331,8 +333,10 @@ def graph_vjp(G, pre, g):
                                     layer['nin'], st)
             _lib.check(rc, 'vcb_fc_backward')
         else:
+            ws_n = L_.vcb_conv_back_workspace(N, _geom_ptr(layer['geom']))
+            ws = _lib.workspace(ws_n, dev)
             rc = L_.vcb_conv_backward(N, _geom_ptr(layer['geom']), P(cur), P(layer['K']),
-                                      P(mask), P(out), st)
+                                      P(mask), P(out), P(ws), ws_n, st)
             _lib.check(rc, 'vcb_conv_backward')
         cur = out
     return cur
