@@ -404,6 +404,23 @@ int vcb_conv_backward(int32_t N, const int32_t* geometry, const float* g,
                       const float* K, const float* mask, float* g_in,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- fp32 GEMM on the tcgen05 tensor cores with error-compensated 3xTF32
+ * (the contraction of the wide layers; no single reference counterpart --
+ * it replaces the fp32 matmuls / einsums inside the functions above). ---- */
+
+/* hi = x rounded to TF32 (nearest), lo = x - hi, elementwise over n floats. */
+int vcb_tf32_split(int64_t n, const float* x, float* hi, float* lo,
+                   void* stream);
+
+/* C (M x N, ld ldc) = A B^T (+ bias[n]) with A (M x K, ld lda) and B (N x K,
+ * ld ldb) given as split pairs (vcb_tf32_split); every operand 16-byte
+ * aligned with ld % 4 == 0.  err: device int32, 0 on entry; set to 1 when a
+ * bounded pipeline wait expired (then C is not valid). */
+int vcb_tc_gemm(int32_t M, int32_t N, int32_t K, const float* A_hi,
+                const float* A_lo, int32_t lda, const float* B_hi,
+                const float* B_lo, int32_t ldb, const float* bias, float* C,
+                int32_t ldc, int32_t* err, void* stream);
+
 /* Diagnostic: FP32 FFMA throughput probe (no reference counterpart).  Runs
  * `blocks` CTAs of 256 threads, each thread `iters` x 64 dependent-chain FMAs
  * (8 independent chains); FLOPs = blocks * 256 * iters * 128.  `out` must

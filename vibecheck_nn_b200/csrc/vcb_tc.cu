@@ -1,0 +1,347 @@
+// fp32 GEMM on the 5th-generation tensor cores with error-compensated
+// 3xTF32 (the contraction behind the wide layers' bound propagation).
+//
+// C (M x N) = A (M x K) B^T, A and B both K-major (row-major M x K and
+// N x K -- activations x weights).  Each operand is pre-split into a TF32
+// "hi" part (round to nearest at 10 mantissa bits) and the exact fp32
+// remainder "lo" (vcb_tf32_split); the tensor cores then accumulate
+//   lo_A hi_B + hi_A lo_B + hi_A hi_B
+// in fp32 in tensor memory, which keeps the product within ~2^-22 of the
+// fp32 product (the dropped lo_A lo_B term) -- fp32-level accuracy at
+// tensor-core rate.
+//
+// Kernel structure (one 128 x 128 output tile per CTA, 4 warps):
+//   warp 0 / one thread : TMA producer -- per 32-wide K chunk, four 128 x 32
+//                         fp32 tiles (A hi/lo, B hi/lo) land in a 3-stage
+//                         ring of shared memory with 128-byte swizzle, each
+//                         stage signalled by an mbarrier (complete_tx);
+//   warp 1 / one thread : MMA issuer -- tcgen05.mma kind::tf32, M = 128,
+//                         N = 128, K = 8, three per K step; K chunk kb
+//                         accumulates in TMEM columns 128 (kb % 4) (four
+//                         accumulators); tcgen05.commit frees a stage when
+//                         its MMAs have read it;
+//   all 4 warps         : epilogue -- tcgen05.ld of the accumulator rows
+//                         (warp w owns TMEM lanes 32w..32w+31), the four
+//                         accumulators summed in fp32, optional bias, store.
+// Every mbarrier wait is bounded: on expiry the kernel records an error
+// flag, drains its MMAs through the final commit, frees its TMEM and
+// returns, and the host reports VCB_ERR_TIMEOUT.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "vcb_common.cuh"
+
+namespace vcb {
+namespace {
+
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
+// K chunks go round-robin to NACC accumulators (NACC x 128 TMEM columns),
+// summed in fp32 by the epilogue: the tensor cores' fp32 accumulation drops
+// low-order bits at every step, so shorter chains keep the sum accurate.
+constexpr int NACC = 4;
+constexpr int TMEM_COLS = NACC * TC_BN;  // 512: the whole tensor memory
+constexpr int TC_THREADS = 128;
+constexpr int TILE_A_BYTES = TC_BM * TC_BK * 4;  // 16 KB
+constexpr int TILE_B_BYTES = TC_BN * TC_BK * 4;  // 16 KB
+constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;
+constexpr int TC_SMEM = TC_STAGES * STAGE_BYTES + 1024;  // + alignment slack
+constexpr unsigned kSpinLimit = 1u << 22;      // pipeline waits (a stage is microseconds)
+constexpr unsigned kDoneSpinLimit = 1u << 27;  // the epilogue waits out the whole mainloop
+
+// instruction descriptor: D f32, A/B tf32, both K-major, N = 128, M = 128
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) |
+                            ((uint32_t)(TC_BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Wait for the phase with the given parity to complete; false on expiry.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity,
+                                          unsigned limit = kSpinLimit) {
+  const uint32_t a = smem_u32(bar);
+  for (unsigned i = 0; i < limit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// K-major operand tile with 128-byte swizzle: rows of 128 B, 8-row groups
+// 1024 B apart (SBO), leading offset unused, descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct TcArgs {
+  int M, N, K, ldc;
+  float* C;
+  const float* bias;  // (N) added to every row, or NULL
+  int* err;           // set to 1 when a bounded wait expired
+};
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
+                   const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
+                   const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int failed;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * TC_BM, n0 = blockIdx.y * TC_BN;
+  const int nk = (a.K + TC_BK - 1) / TC_BK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0 && lane == 0) {  // TMA producer
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % TC_STAGES;
+      const unsigned round = kb / TC_STAGES;
+      if (kb >= TC_STAGES && !mbar_wait(&empty[s], (round - 1) & 1)) {
+        failed = 1;
+        break;
+      }
+      uint8_t* st = smem + s * STAGE_BYTES;
+      mbar_expect_tx(&full[s], STAGE_BYTES);
+      tma_load_2d(st, &mAh, &full[s], kb * TC_BK, m0);
+      tma_load_2d(st + TILE_A_BYTES, &mAl, &full[s], kb * TC_BK, m0);
+      tma_load_2d(st + 2 * TILE_A_BYTES, &mBh, &full[s], kb * TC_BK, n0);
+      tma_load_2d(st + 2 * TILE_A_BYTES + TILE_B_BYTES, &mBl, &full[s], kb * TC_BK, n0);
+    }
+  } else if (warp == 1 && lane == 0) {  // MMA issuer
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % TC_STAGES;
+      const unsigned round = kb / TC_STAGES;
+      if (!mbar_wait(&full[s], round & 1)) {
+        failed = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+      const uint32_t ah = base, al = base + TILE_A_BYTES;
+      const uint32_t bh = base + 2 * TILE_A_BYTES, bl = bh + TILE_B_BYTES;
+      const uint32_t dst = tmem + (uint32_t)((kb % NACC) * TC_BN);
+#pragma unroll
+      for (int j = 0; j < TC_BK / 8; ++j) {
+        const uint32_t off = j * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
+        const uint32_t acc = (kb >= NACC || j > 0) ? 1u : 0u;
+        mma_tf32(dst, sw128_desc(al + off), sw128_desc(bh + off), acc);
+        mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bl + off), 1u);
+        mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bh + off), 1u);
+      }
+      mma_commit(&empty[s]);
+    }
+    mma_commit(&done);  // arrives once every MMA issued above has completed
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(&done, 0, kDoneSpinLimit);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const int row = m0 + warp * 32 + lane;
+  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  const int nacc = nk < NACC ? nk : NACC;
+#pragma unroll 1
+  for (int c0 = 0; c0 < TC_BN; c0 += 16) {
+    float v[16];
+    tmem_ld16(lane_addr + c0, v);
+    for (int q = 1; q < nacc; ++q) {
+      float w[16];
+      tmem_ld16(lane_addr + q * TC_BN + c0, w);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], w[j]);
+    }
+    if (row < a.M && ok) {
+      float* crow = a.C + (long long)row * a.ldc;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + c0 + j;
+        if (n < a.N) crow[n] = a.bias ? __fadd_rn(v[j], a.bias[n]) : v[j];
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TMEM_COLS));
+  if (threadIdx.x == 0 && (failed || !ok)) atomicExch(a.err, 1);
+}
+
+// hi = x rounded to nearest at TF32 precision (10 explicit mantissa bits),
+// lo = x - hi (exact in fp32).
+__global__ void tf32_split_kernel(long long n, const float* __restrict__ x, float* __restrict__ hi,
+                                  float* __restrict__ lo) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const uint32_t u = __float_as_uint(v);
+    const bool finite = (u & 0x7F800000u) != 0x7F800000u;
+    const float h = finite ? __uint_as_float((u + 0x1000u) & 0xFFFFE000u) : v;
+    hi[i] = h;
+    lo[i] = finite ? __fsub_rn(v, h) : 0.f;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Row-major (rows x cols, leading dimension ld) fp32 matrix as 128 x 32 tiles
+// with 128-byte swizzle; out-of-range reads fill zeros.
+int make_map(CUtensorMap* map, const float* p, int rows, int cols, int ld, const char* who) {
+  auto fn = encode_fn();
+  if (!fn) return fail(VCB_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", who);
+  if ((reinterpret_cast<uintptr_t>(p) & 15) || (ld % 4) || ld < cols)
+    return fail(VCB_ERR_INVALID, "%s: operand must be 16-byte aligned with ld %% 4 == 0", who);
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {TC_BK, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VCB_ERR_CUDA, "%s: tensor map encode failed (%d)", who, (int)r);
+  return VCB_OK;
+}
+
+}  // namespace
+
+// C = A B^T with 3xTF32 on tcgen05 (see the file comment); err: device int,
+// zero on entry, set on a bounded-wait expiry.
+int tc_gemm_3xtf32(int M, int N, int K, const float* Ah, const float* Al, int lda,
+                   const float* Bh, const float* Bl, int ldb, float* C, int ldc,
+                   const float* bias, int* err, cudaStream_t st, const char* who) {
+  if (M == 0 || N == 0) return VCB_OK;
+  CUtensorMap mAh, mAl, mBh, mBl;
+  int rc = make_map(&mAh, Ah, M, K, lda, who);
+  if (!rc) rc = make_map(&mAl, Al, M, K, lda, who);
+  if (!rc) rc = make_map(&mBh, Bh, N, K, ldb, who);
+  if (!rc) rc = make_map(&mBl, Bl, N, K, ldb, who);
+  if (rc) return rc;
+  rc = ensure_smem(reinterpret_cast<const void*>(tc_gemm_kernel), TC_SMEM);
+  if (rc) return rc;
+  TcArgs args{M, N, K, ldc, C, bias, err};
+  dim3 grid((M + TC_BM - 1) / TC_BM, (N + TC_BN - 1) / TC_BN);
+  tc_gemm_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(mAh, mAl, mBh, mBl, args);
+  return check_launch(who);
+}
+
+int tf32_split(long long n, const float* x, float* hi, float* lo, cudaStream_t st) {
+  if (n <= 0) return VCB_OK;
+  const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 32);
+  tf32_split_kernel<<<blocks, 256, 0, st>>>(n, x, hi, lo);
+  return check_launch("vcb_tf32_split");
+}
+
+}  // namespace vcb
+
+extern "C" int vcb_tf32_split(int64_t n, const float* x, float* hi, float* lo, void* stream) {
+  using namespace vcb;
+  if (n < 0 || (n > 0 && (!x || !hi || !lo))) return fail(VCB_ERR_INVALID, "vcb_tf32_split: bad arguments");
+  return tf32_split(n, x, hi, lo, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int vcb_tc_gemm(int32_t M, int32_t N, int32_t K, const float* A_hi, const float* A_lo,
+                           int32_t lda, const float* B_hi, const float* B_lo, int32_t ldb,
+                           const float* bias, float* C, int32_t ldc, int32_t* err,
+                           void* stream) {
+  using namespace vcb;
+  if (M < 0 || N < 0 || K <= 0 || ldc < N)
+    return fail(VCB_ERR_INVALID, "vcb_tc_gemm: M=%d N=%d K=%d ldc=%d", M, N, K, ldc);
+  if (M == 0 || N == 0) return VCB_OK;
+  if (!A_hi || !A_lo || !B_hi || !B_lo || !C || !err)
+    return fail(VCB_ERR_INVALID, "vcb_tc_gemm: NULL pointer");
+  return tc_gemm_3xtf32(M, N, K, A_hi, A_lo, lda, B_hi, B_lo, ldb, C, ldc, bias, err,
+                        static_cast<cudaStream_t>(stream), "vcb_tc_gemm");
+}
