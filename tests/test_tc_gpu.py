@@ -67,3 +67,43 @@ def test_tc_gemm_matches_fp64(M, N, K):
     print(f'M={M} N={N} K={K}: 3xtf32 {rel:.3e}  cuBLAS fp32 {rel32:.3e} of sum|a||b|')
     # 3xTF32 drops lo_a lo_b (~2^-22 |ab|); fp32 accumulation adds ~sqrt(K) ulps
     assert rel < 2e-6 * max(1.0, K / 1024) ** 0.5, rel
+
+
+def test_tc_gemm_throughput_vs_cublas_fp32():
+    """Timing line for profiles/tc_gemm_3xtf32.md (CUDA events, 3 warm-up +
+    10 launches); the tensor-core path must beat cuBLAS fp32 on a large shape."""
+    M = N = K = 4096
+    A = torch.randn(M, K, device=DEV)
+    B = torch.randn(N, K, device=DEV)
+    Ah, Al = split(A)
+    Bh, Bl = split(B)
+    C = torch.empty(M, N, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+
+    def tc():
+        _lib.check(_lib.lib().vcb_tc_gemm(M, N, K, P(Ah), P(Al), K, P(Bh), P(Bl), K, None, P(C),
+                                          N, P(err), _lib.stream_of(DEV)))
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 10
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        t_tc = timed(tc)
+        t_32 = timed(lambda: A @ B.T)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    fl = 2.0 * M * N * K
+    print(f'{M}x{N}x{K}: tcgen05 3xTF32 {t_tc:.3f} ms = {fl / t_tc / 1e9:.1f} TFLOP/s; '
+          f'cuBLAS fp32 {t_32:.3f} ms = {fl / t_32 / 1e9:.1f} TFLOP/s')
+    assert int(err.item()) == 0
+    assert t_tc < t_32
