@@ -421,6 +421,37 @@ int vcb_tc_gemm(int32_t M, int32_t N, int32_t K, const float* A_hi,
                 const float* B_lo, int32_t ldb, const float* bias, float* C,
                 int32_t ldc, int32_t* err, void* stream);
 
+/* ---- DeepZ zonotope for wide MLPs (_forward_zonotope_graph_batched,
+ * src/vibecheck/verify_zono_bnb.py:3079-4074, layer by layer).  Generators
+ * are generator-major rows: leaf b owns rows [off[b], off[b+1]) of one
+ * (rows x ld) matrix, the first k[b] meaningful, the rest zero; one fc layer
+ * of the whole batch is then one vcb_tc_gemm. ---- */
+
+/* ReLU transformer per leaf (B x n): lambda, mu (:3175-3211), c_out = lambda c
+ * + mu, cnt[b] = unstable count, idx_of_rank (B x n): leaf b's unstable
+ * neurons in index order (first cnt[b] entries). */
+int vcb_zw_relu(int32_t B, int32_t n, const float* c, const float* lo,
+                const float* hi, float* lam, float* mu, float* c_out,
+                int32_t* cnt, int32_t* idx_of_rank, void* stream);
+
+/* Next layer's A operand (TF32 hi / lo, ld ld): leaf b's k_in[b] generator
+ * rows scaled column-wise by lambda -- from C (ld ldc) at in_off[b], or, when
+ * C is NULL (layer 0), r[b][k] W0T[k] (W0T: n0 x n, the first fc transposed)
+ * -- then one row mu_j e_j per unstable neuron, zero rows up to out_off[b+1].
+ * rows_hint: out_off[B] (sizes the grid). */
+int vcb_zw_build(int32_t B, int32_t n, int32_t ld, const int64_t* in_off,
+                 const int32_t* k_in, const float* C, int32_t ldc,
+                 const float* r, int32_t n0, const float* W0T,
+                 const float* lam, const float* mu, const int32_t* cnt,
+                 const int32_t* idx_of_rank, const int64_t* out_off,
+                 int64_t rows_hint, float* A_hi, float* A_lo, void* stream);
+
+/* lo / hi (B x n) = c -+ sum over leaf b's first k[b] rows of |C| (row
+ * order). */
+int vcb_zw_colsum(int32_t B, int32_t n, const int64_t* off, const int32_t* k,
+                  const float* C, int32_t ldc, const float* c, float* lo,
+                  float* hi, void* stream);
+
 /* Diagnostic: FP32 FFMA throughput probe (no reference counterpart).  Runs
  * `blocks` CTAs of 256 threads, each thread `iters` x 64 dependent-chain FMAs
  * (8 independent chains); FLOPs = blocks * 256 * iters * 128.  `out` must

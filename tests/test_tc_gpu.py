@@ -65,8 +65,8 @@ def test_tc_gemm_matches_fp64(M, N, K):
     fp32 = (A @ B.T + bias).double()
     rel32 = ((fp32 - ref).abs() / scale).max().item()
     print(f'M={M} N={N} K={K}: 3xtf32 {rel:.3e}  cuBLAS fp32 {rel32:.3e} of sum|a||b|')
-    # 3xTF32 drops lo_a lo_b (~2^-22 |ab|); fp32 accumulation adds ~sqrt(K) ulps
-    assert rel < 2e-6 * max(1.0, K / 1024) ** 0.5, rel
+    # 3xTF32 drops lo_a lo_b (~2^-22 |ab|); chunk partials are summed in fp32
+    assert rel < max(4e-7, 2.0 * rel32), (rel, rel32)
 
 
 def test_tc_gemm_throughput_vs_cublas_fp32():

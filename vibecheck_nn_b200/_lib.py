@@ -75,6 +75,10 @@ SIGNATURES = {
                      ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P],
     'vcb_tf32_split': [ctypes.c_int64, _P, _P, _P, _P],
     'vcb_tc_gemm': [_I, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _I, _P, _P],
+    'vcb_zw_relu': [_I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    'vcb_zw_build': [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P,
+                     ctypes.c_int64, _P, _P, _P],
+    'vcb_zw_colsum': [_I, _I, _P, _P, _P, _I, _P, _P, _P, _P],
     'vcb_conv_forward': [_I, _P, _P, _P, _P, _P, _P, _P],
     'vcb_conv_backward': [_I, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     'vcb_fc_forward': [_I, _I, _I, _P, _I, _P, _P, _P, _I, _P, _I, _P],

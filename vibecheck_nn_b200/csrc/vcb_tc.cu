@@ -4,25 +4,27 @@
 // C (M x N) = A (M x K) B^T, A and B both K-major (row-major M x K and
 // N x K -- activations x weights).  Each operand is pre-split into a TF32
 // "hi" part (round to nearest at 10 mantissa bits) and the exact fp32
-// remainder "lo" (vcb_tf32_split); the tensor cores then accumulate
+// remainder "lo" (vcb_tf32_split); the tensor cores form
 //   lo_A hi_B + hi_A lo_B + hi_A hi_B
-// in fp32 in tensor memory, which keeps the product within ~2^-22 of the
-// fp32 product (the dropped lo_A lo_B term) -- fp32-level accuracy at
-// tensor-core rate.
+// which is within ~2^-22 of the fp32 product (the dropped lo_A lo_B term).
+// The tensor cores' own fp32 accumulation drops low-order bits at every MMA,
+// so each 32-wide K chunk accumulates in a fresh TMEM buffer (12 MMAs) and
+// the epilogue warps add the chunk partials into fp32 registers with
+// round-to-nearest adds: the long sum over K is an ordinary fp32 sum.
 //
-// Kernel structure (one 128 x 128 output tile per CTA, 4 warps):
-//   warp 0 / one thread : TMA producer -- per 32-wide K chunk, four 128 x 32
-//                         fp32 tiles (A hi/lo, B hi/lo) land in a 3-stage
-//                         ring of shared memory with 128-byte swizzle, each
-//                         stage signalled by an mbarrier (complete_tx);
-//   warp 1 / one thread : MMA issuer -- tcgen05.mma kind::tf32, M = 128,
-//                         N = 128, K = 8, three per K step; K chunk kb
-//                         accumulates in TMEM columns 128 (kb % 4) (four
-//                         accumulators); tcgen05.commit frees a stage when
-//                         its MMAs have read it;
-//   all 4 warps         : epilogue -- tcgen05.ld of the accumulator rows
-//                         (warp w owns TMEM lanes 32w..32w+31), the four
-//                         accumulators summed in fp32, optional bias, store.
+// Kernel structure (one 128 x 128 output tile per CTA, 6 warps):
+//   warp 4 / one thread : TMA producer -- per K chunk, four 128 x 32 fp32
+//                         tiles (A hi/lo, B hi/lo) into a 3-stage ring of
+//                         shared memory with 128-byte swizzle, each stage
+//                         signalled by an mbarrier (complete_tx);
+//   warp 5 / one thread : MMA issuer -- tcgen05.mma kind::tf32, M = 128,
+//                         N = 128, K = 8, three per K step, chunk kb into TMEM
+//                         buffer kb % 4 (4 x 128 columns); tcgen05.commit
+//                         frees the smem stage and publishes the buffer;
+//   warps 0-3           : accumulators -- warp w owns TMEM lanes 32w..32w+31
+//                         (tile rows); per chunk tcgen05.ld of its 128
+//                         columns, fp32 adds into registers, then the buffer
+//                         is released to the MMA issuer; finally bias + store.
 // Every mbarrier wait is bounded: on expiry the kernel records an error
 // flag, drains its MMAs through the final commit, frees its TMEM and
 // returns, and the host reports VCB_ERR_TIMEOUT.
@@ -32,17 +34,15 @@
 #include <algorithm>
 
 #include "vcb_common.cuh"
+#include "vcb_tc.cuh"
 
 namespace vcb {
 namespace {
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
-// K chunks go round-robin to NACC accumulators (NACC x 128 TMEM columns),
-// summed in fp32 by the epilogue: the tensor cores' fp32 accumulation drops
-// low-order bits at every step, so shorter chains keep the sum accurate.
-constexpr int NACC = 4;
-constexpr int TMEM_COLS = NACC * TC_BN;  // 512: the whole tensor memory
-constexpr int TC_THREADS = 128;
+constexpr int NBUF = 4;                  // TMEM chunk buffers
+constexpr int TMEM_COLS = NBUF * TC_BN;  // 512: the whole tensor memory
+constexpr int TC_THREADS = 192;          // 4 accumulator warps + producer + MMA
 constexpr int TILE_A_BYTES = TC_BM * TC_BK * 4;  // 16 KB
 constexpr int TILE_B_BYTES = TC_BN * TC_BK * 4;  // 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;
@@ -150,7 +150,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], done;
+  __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES];
+  __shared__ __align__(8) uint64_t acc_full[NBUF], acc_free[NBUF], done;
   __shared__ uint32_t tmem_slot;
   __shared__ int failed;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -160,6 +161,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int s = 0; s < TC_STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int q = 0; q < NBUF; ++q) {
+      mbar_init(&acc_full[q], 1);
+      mbar_init(&acc_free[q], 4);  // one arrival per accumulator warp
     }
     mbar_init(&done, 1);
     failed = 0;
@@ -176,68 +181,82 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_slot;
 
-  if (warp == 0 && lane == 0) {  // TMA producer
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % TC_STAGES;
-      const unsigned round = kb / TC_STAGES;
-      if (kb >= TC_STAGES && !mbar_wait(&empty[s], (round - 1) & 1)) {
-        failed = 1;
-        break;
+  if (warp == 4) {
+    if (lane == 0) {  // TMA producer
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % TC_STAGES;
+        const unsigned round = kb / TC_STAGES;
+        if (kb >= TC_STAGES && !mbar_wait(&empty[s], (round - 1) & 1)) {
+          failed = 1;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        mbar_expect_tx(&full[s], STAGE_BYTES);
+        tma_load_2d(st, &mAh, &full[s], kb * TC_BK, m0);
+        tma_load_2d(st + TILE_A_BYTES, &mAl, &full[s], kb * TC_BK, m0);
+        tma_load_2d(st + 2 * TILE_A_BYTES, &mBh, &full[s], kb * TC_BK, n0);
+        tma_load_2d(st + 2 * TILE_A_BYTES + TILE_B_BYTES, &mBl, &full[s], kb * TC_BK, n0);
       }
-      uint8_t* st = smem + s * STAGE_BYTES;
-      mbar_expect_tx(&full[s], STAGE_BYTES);
-      tma_load_2d(st, &mAh, &full[s], kb * TC_BK, m0);
-      tma_load_2d(st + TILE_A_BYTES, &mAl, &full[s], kb * TC_BK, m0);
-      tma_load_2d(st + 2 * TILE_A_BYTES, &mBh, &full[s], kb * TC_BK, n0);
-      tma_load_2d(st + 2 * TILE_A_BYTES + TILE_B_BYTES, &mBl, &full[s], kb * TC_BK, n0);
     }
-  } else if (warp == 1 && lane == 0) {  // MMA issuer
+  } else if (warp == 5) {
+    if (lane == 0) {  // MMA issuer
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % TC_STAGES;
+        const int q = kb % NBUF;
+        if (!mbar_wait(&full[s], (kb / TC_STAGES) & 1) ||
+            (kb >= NBUF && !mbar_wait(&acc_free[q], ((kb / NBUF) - 1) & 1))) {
+          failed = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t ah = base, al = base + TILE_A_BYTES;
+        const uint32_t bh = base + 2 * TILE_A_BYTES, bl = bh + TILE_B_BYTES;
+        const uint32_t dst = tmem + (uint32_t)(q * TC_BN);
+#pragma unroll
+        for (int j = 0; j < TC_BK / 8; ++j) {
+          const uint32_t off = j * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
+          mma_tf32(dst, sw128_desc(al + off), sw128_desc(bh + off), j > 0 ? 1u : 0u);
+          mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bl + off), 1u);
+          mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bh + off), 1u);
+        }
+        mma_commit(&empty[s]);
+        mma_commit(&acc_full[q]);
+      }
+      // every MMA issued above has finished before TMEM can be freed
+      mma_commit(&done);
+      if (!mbar_wait(&done, 0, kDoneSpinLimit)) failed = 1;
+    }
+  } else {  // accumulator warps 0-3: row m0 + 32 warp + lane
+    float acc[TC_BN];
+#pragma unroll
+    for (int j = 0; j < TC_BN; ++j) acc[j] = 0.f;
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
     for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % TC_STAGES;
-      const unsigned round = kb / TC_STAGES;
-      if (!mbar_wait(&full[s], round & 1)) {
+      const int q = kb % NBUF;
+      if (!mbar_wait(&acc_full[q], (kb / NBUF) & 1, kDoneSpinLimit)) {
         failed = 1;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-      const uint32_t ah = base, al = base + TILE_A_BYTES;
-      const uint32_t bh = base + 2 * TILE_A_BYTES, bl = bh + TILE_B_BYTES;
-      const uint32_t dst = tmem + (uint32_t)((kb % NACC) * TC_BN);
 #pragma unroll
-      for (int j = 0; j < TC_BK / 8; ++j) {
-        const uint32_t off = j * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
-        const uint32_t acc = (kb >= NACC || j > 0) ? 1u : 0u;
-        mma_tf32(dst, sw128_desc(al + off), sw128_desc(bh + off), acc);
-        mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bl + off), 1u);
-        mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bh + off), 1u);
+      for (int c0 = 0; c0 < TC_BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(lane_addr + q * TC_BN + c0, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], v[j]);
       }
-      mma_commit(&empty[s]);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_free[q])) : "memory");
     }
-    mma_commit(&done);  // arrives once every MMA issued above has completed
-  }
-  __syncwarp();
-  const bool ok = mbar_wait(&done, 0, kDoneSpinLimit);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const int row = m0 + warp * 32 + lane;
-  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-  const int nacc = nk < NACC ? nk : NACC;
-#pragma unroll 1
-  for (int c0 = 0; c0 < TC_BN; c0 += 16) {
-    float v[16];
-    tmem_ld16(lane_addr + c0, v);
-    for (int q = 1; q < nacc; ++q) {
-      float w[16];
-      tmem_ld16(lane_addr + q * TC_BN + c0, w);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], w[j]);
-    }
-    if (row < a.M && ok) {
+    const int row = m0 + warp * 32 + lane;
+    if (row < a.M && !failed) {
       float* crow = a.C + (long long)row * a.ldc;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = n0 + c0 + j;
-        if (n < a.N) crow[n] = a.bias ? __fadd_rn(v[j], a.bias[n]) : v[j];
+      for (int j = 0; j < TC_BN; ++j) {
+        const int n = n0 + j;
+        if (n < a.N) crow[n] = a.bias ? __fadd_rn(acc[j], a.bias[n]) : acc[j];
       }
     }
   }
@@ -246,7 +265,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(TMEM_COLS));
-  if (threadIdx.x == 0 && (failed || !ok)) atomicExch(a.err, 1);
+  if (threadIdx.x == 0 && failed) atomicExch(a.err, 1);
 }
 
 // hi = x rounded to nearest at TF32 precision (10 explicit mantissa bits),

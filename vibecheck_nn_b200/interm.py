@@ -86,7 +86,14 @@ def _forward_zonotope_graph_batched(xl, xh, gg, device, dtype):
     xh = _f32(xh, device)
     desc = mlp_desc(gg, device)
     B = xl.shape[0]
-    sb_lo, sb_hi, _, (c, G, K) = mlp_zono(desc, xl, xh, full=True)
+    try:
+        sb_lo, sb_hi, _, (c, G, K) = mlp_zono(desc, xl, xh, full=True)
+    except NotImplementedError:  # too wide for the shared-memory kernel
+        from .wide import wide_net
+        from .zono_wide import wide_zono
+        sb, (c, G) = wide_zono(wide_net(gg, device), xl, xh, want_output=True)
+        _forward_zonotope_graph_batched.last_bilinear_op_bounds = {}
+        return sb, (c, G)
     kmax = int(K.max().item()) if B > 0 else 0
     G = G[:, :, :kmax]
     lo = _unpack_layers(desc, B, sb_lo)
