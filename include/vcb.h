@@ -173,6 +173,20 @@ int vcb_bab_step(int32_t B, int32_t n_in, int32_t Q, int32_t D,
                  float* lo_xl, float* lo_xh, float* hi_xl, float* hi_xh,
                  int64_t* counters, void* stream);
 
+/* vcb_bab_step for any input width (n_in > 64 included, e.g. 3072): one CTA
+ * per leaf with fixed-order block reductions, then a scan and the child
+ * writes -- the same decisions, counters and child order.  workspace: at
+ * least vcb_bab_step_wide_workspace(B, n_in) bytes of device memory. */
+int vcb_bab_step_wide(int32_t B, int32_t n_in, int32_t Q, int32_t D,
+                      int32_t q_sens, const int32_t* query_disjunct,
+                      const float* xl, const float* xh, const float* lb,
+                      const float* A, const float* acc, int32_t clip,
+                      int32_t branch_sb, float* lo_xl, float* lo_xh,
+                      float* hi_xl, float* hi_xh, int64_t* counters,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+size_t vcb_bab_step_wide_workspace(int32_t B, int32_t n_in);
+
 /* Batched sign-gradient PGD for ReLU MLPs (widths <= 128); replaces the loop
  * of _simple_pgd / _simple_pgd_batched (src/vibecheck/verify_hybrid_acasxu.py:
  * 39, 103).

@@ -29,7 +29,13 @@ def _sb_dict(desc, B, lo, hi):
 
 
 def zonotope_sb(desc, xl, xh):
-    lo, hi, _, _ = mlp_zono(desc, xl, xh)
+    try:
+        lo, hi, _, _ = mlp_zono(desc, xl, xh)
+    except NotImplementedError:  # too wide for the shared-memory kernel
+        from .zono_wide import wide_zono
+        wn = desc.__dict__.get('_wide') or wide.WideNet(desc)
+        desc.__dict__['_wide'] = wn
+        return wide_zono(wn, xl, xh)
     return _sb_dict(desc, xl.shape[0], lo, hi)
 
 

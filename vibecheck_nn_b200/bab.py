@@ -31,6 +31,9 @@ from .netdesc import mlp_desc
 from .ops import F32, _dev, mlp_crown
 
 
+WIDE_IN = 64  # input widths above this take the one-CTA-per-leaf step kernel
+
+
 class LinearSpec:
     """Minimal stand-in for the reference ``VNNSpec``: input box plus a DNF of
     output constraints.  ``disjuncts`` is a list of lists of
@@ -174,12 +177,21 @@ def bab_step(xl, xh, lb, A, acc, qd, D, clip, branch_sb, q_sens=None):
     hi_xh = torch.empty_like(lo_xl)
     cnt = torch.zeros(4, dtype=torch.int64, device=dev)
     P = _lib.ptr
-    rc = _lib.lib().vcb_bab_step(B, n, Q, D, Q if q_sens is None else q_sens,
-                                 P(qd), P(xl), P(xh), P(lb), P(A),
-                                 P(acc), int(bool(clip)), int(bool(branch_sb)),
-                                 P(lo_xl), P(lo_xh), P(hi_xl), P(hi_xh), P(cnt),
-                                 _lib.stream_of(dev))
-    _lib.check(rc, 'vcb_bab_step')
+    L_ = _lib.lib()
+    qs = Q if q_sens is None else q_sens
+    if n <= WIDE_IN:
+        rc = L_.vcb_bab_step(B, n, Q, D, qs, P(qd), P(xl), P(xh), P(lb), P(A),
+                             P(acc), int(bool(clip)), int(bool(branch_sb)),
+                             P(lo_xl), P(lo_xh), P(hi_xl), P(hi_xh), P(cnt),
+                             _lib.stream_of(dev))
+        _lib.check(rc, 'vcb_bab_step')
+    else:
+        ws_n = L_.vcb_bab_step_wide_workspace(B, n)
+        ws = _lib.workspace(ws_n, dev)
+        rc = L_.vcb_bab_step_wide(B, n, Q, D, qs, P(qd), P(xl), P(xh), P(lb), P(A), P(acc),
+                                  int(bool(clip)), int(bool(branch_sb)), P(lo_xl), P(lo_xh),
+                                  P(hi_xl), P(hi_xh), P(cnt), P(ws), ws_n, _lib.stream_of(dev))
+        _lib.check(rc, 'vcb_bab_step_wide')
     return lo_xl, lo_xh, hi_xl, hi_xh, cnt
 
 
@@ -235,10 +247,13 @@ class BoundEngine:
         xh0 = torch.as_tensor(np.asarray(self.spec.x_hi), dtype=F32, device=self.device).flatten()
         return xl0, xh0
 
+    def bounds(self, xl_b, xh_b, want_A):
+        return bound_batch(self.desc, xl_b, xh_b, self.W_q, self.b_q,
+                           self.cfg.crown_intermediate, want_A)
+
     def process(self, xl_b, xh_b, n_iter):
         c = self.cfg
-        lb, A, acc = bound_batch(self.desc, xl_b, xh_b, self.W_q, self.b_q,
-                                 c.crown_intermediate, c.clip or c.branch_sb)
+        lb, A, acc = self.bounds(xl_b, xh_b, c.clip or c.branch_sb)
         if c.alpha_iters > 0 and (c.alpha_all or c.alpha_eps > 0):
             from .alpha import alpha_boundary_refine
             lb = alpha_boundary_refine(self.desc, xl_b, xh_b, lb, self.W_q, self.b_q, self.qd,
@@ -256,6 +271,46 @@ class BoundEngine:
         n_split, n_degen = int(cnt[2]), int(cnt[3])
         return StepResult((lo_xl[:n_split], lo_xh[:n_split]), (hi_xl[:n_split], hi_xh[:n_split]),
                           n_split, n_degen)
+
+
+class WideBoundEngine(BoundEngine):
+    """BoundEngine for MLPs outside the shared-memory kernels (the cfg5 shape):
+    zonotope intermediates on the tcgen05 GEMM (``zono_wide.wide_zono``),
+    then the layer-wise CROWN back-substitution with the input-space linear
+    form (``wide.wide_crown``); the split runs on the wide step kernel."""
+
+    def __init__(self, spec, gg, settings, device):
+        super().__init__(spec, gg, settings, device)
+        if self.cfg.crown_intermediate:
+            raise NotImplementedError(
+                'vibecheck_nn_b200: CROWN intermediates for networks outside the '
+                'shared-memory kernels')
+        from .wide import wide_net
+        self.wn = wide_net(gg, device)
+
+    def bounds(self, xl_b, xh_b, want_A):
+        from .wide import wide_crown
+        from .zono_wide import wide_zono
+        sb = wide_zono(self.wn, xl_b, xh_b)
+        out = wide_crown(self.wn, xl_b, xh_b, sb, self.W_q, self.b_q, want_A=want_A)
+        return out['lb'], out.get('A'), out.get('acc')
+
+
+def make_engine(spec, gg, settings, device):
+    """The fused shared-memory engine when the network fits its kernels, the
+    wide engine otherwise."""
+    eng = BoundEngine(spec, gg, settings, device)
+    if not eng.queries:
+        return eng
+    from .ops import fits_smem
+    fused = fits_smem(eng.desc, eng.W_q.shape[0])
+    if fused:
+        try:  # the zonotope kernel has its own limits
+            xl0, xh0 = eng.root()
+            mlp_zono(eng.desc, xl0.reshape(1, -1), xh0.reshape(1, -1))
+        except NotImplementedError:
+            fused = False
+    return eng if fused else WideBoundEngine(spec, gg, settings, device)
 
 
 class LocalState:
@@ -308,7 +363,7 @@ def _input_split_batched(graph, spec, settings, gg, device, dtype):
     {'verified', 'unknown', 'sat'}."""
     device = _dev(device)
     t_start = time.perf_counter()
-    engine = BoundEngine(spec, gg, settings, device)
+    engine = make_engine(spec, gg, settings, device)
     cfg = engine.cfg
     if cfg.sat_finding and cfg.pgd_phase0:
         from .pgd import root_pgd

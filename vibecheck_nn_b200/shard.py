@@ -194,11 +194,11 @@ def _input_split_batched_sharded(graph, spec, settings, gg, device, dtype, group
     """``_input_split_batched`` (verify_graph.py:12466) over the ranks of
     ``group`` (default: the world), one GPU per rank: the same verdict and,
     with alpha-CROWN and leaf PGD off, the same leaf count as one GPU."""
-    from .bab import BoundEngine
+    from .bab import make_engine
     from .ops import _dev
     device = _dev(device)
     t_start = time.perf_counter()
-    engine = BoundEngine(spec, gg, settings, device)
+    engine = make_engine(spec, gg, settings, device)
     cfg = engine.cfg
     if cfg.sat_finding and cfg.pgd_phase0:
         from .pgd import root_pgd
