@@ -13,7 +13,8 @@ back-substitution for every box (one fused kernel launch, vcb_mlp_crown).
 ``--config`` selects another BASELINE config on its own metric: cfg1 the
 input-split BaB time-to-verdict (N > 1: the sharded driver, strong scaling),
 cfg3 alpha-CROWN over 1,024 ReLU-split domains, cfg4 conv CROWN over 256
-domains.
+domains, cfg5 one BaB iteration (tcgen05 zonotope + CROWN + split) over
+leaves of the depth-18 input-split tree of the 3072->[1024]x8->10 MLP.
 
 N > 1 runs under torchrun, one rank per GPU; every rank bounds its own
 65,536 boxes (weak scaling, no data-path collective); the time is the max
@@ -49,7 +50,7 @@ def parse():
     ap.add_argument('--warmup', type=int, default=10)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--config', default='cfg2', choices=['cfg2', 'cfg1', 'cfg3', 'cfg4'],
+    ap.add_argument('--config', default='cfg2', choices=['cfg2', 'cfg1', 'cfg3', 'cfg4', 'cfg5'],
                     help='cfg2 (default) is the headline; the others time the '
                          'remaining BASELINE configs on their own metrics')
     return ap.parse_args()
@@ -392,12 +393,12 @@ def _setup_dist():
     return rank, world, local, dev
 
 
-def _time_steps(dev, step, args, world, flush):
+def _time_steps(dev, step, args, world, flush, min_warmup=3):
     """W warm-up steps, then K timed steps (CUDA events, L2 flushed before
     each); returns (per-step ms, clocks summary, max-over-ranks total ms)."""
     import torch
     import torch.distributed as dist
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(min_warmup, args.warmup)):
         step()
     torch.cuda.synchronize(dev)
     stream = torch.cuda.current_stream(dev)
@@ -593,6 +594,92 @@ def run_cfg34(args):
         dist.destroy_process_group()
 
 
+def run_cfg5(args, per_step=64):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import types
+    rank, world, _, dev = _setup_dist()
+    from vibecheck_nn_b200 import bab, workloads as wk
+    from oracle import bounds as ob
+    w = wk.cfg5(0)
+    gg = wk.mlp_gg(w['layers'], dev)
+    t = w['true_label']
+    spec = bab.LinearSpec(w['xl'], w['xh'], wk.robustness_disjuncts(10, t))
+    st = types.SimpleNamespace(input_split_batch_size=per_step, disable_sat_finding=True)
+    eng = bab.make_engine(spec, gg, st, dev)
+    assert isinstance(eng, bab.WideBoundEngine)
+    n_batches = max(3, args.warmup) + args.steps
+    base = rank * n_batches * per_step
+    batches = []
+    for i in range(n_batches):
+        lo, hi = wk.cfg5_leaves(w['xl'], w['xh'], base + i * per_step, per_step)
+        batches.append((torch.as_tensor(lo, device=dev), torch.as_tensor(hi, device=dev)))
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    it = {'i': 0}
+
+    def step():
+        xl_b, xh_b = batches[it['i'] % n_batches]
+        it['i'] += 1
+        return eng.process(xl_b, xh_b, 0)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    eng.stats = {}
+    per, clocks, t_max = _time_steps(dev, step, types.SimpleNamespace(warmup=0, steps=args.steps),
+                                     world, flush, min_warmup=0)
+    torch.cuda.synchronize(dev)
+    stats = eng.stats
+    gemm_ms = sum(a.elapsed_time(b) for a, b in stats['gemm_events'])
+    achieved = stats['gemm_flop'] / (gemm_ms * 1e-3) / 1e12
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, 'MEASURED_PEAKS.json')))
+    except (OSError, ValueError):
+        pass
+    bf16 = peaks.get('bf16_tflops')
+    peak = bf16 / 6.0 if bf16 else 1590.0 / 6.0
+    ms = t_max / args.steps
+    if rank == 0:
+        line = {
+            'metric': 'cfg5 leaves/s (zonotope + CROWN spec bound + split, one BaB iteration)',
+            'value': world * per_step / (ms / 1e3), 'unit': 'leaves/s', 'n_gpus': world,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic (seeded numpy rng)',
+            'config': {'workload': 'cfg5: 3072x[1024]x8x10 MLP, eps 1/255 box, leaves of the '
+                                   'depth-18 input-split tree, 9 robustness disjuncts',
+                       'leaves_per_step_per_gpu': per_step,
+                       'l2': 'inputs and generator matrices far larger than L2; flushed too',
+                       'parallelism': f'{world} GPU(s), leaves sharded'},
+            'roofline': {'bound': 'tensor', 'achieved': achieved, 'peak': peak,
+                         'unit': 'TFLOP/s (fp32-equivalent, 3xTF32)',
+                         'frac': achieved / peak, 'traffic': None,
+                         'kernel': 'vcb_tc_gemm (tc_gemm_kernel), zonotope generator GEMMs',
+                         'gemm_share_of_step': gemm_ms / sum(per),
+                         'peak_source': 'MEASURED_PEAKS.json bf16_tflops / 2 (TF32 rate) / 3 '
+                                        '(three MMAs per fp32 product)' if bf16 else
+                                        'fallback 1590 / 6'},
+            'clocks': clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            ggc = wk.mlp_gg(w['layers'])
+            n = 2
+            lo, hi = wk.cfg5_leaves(w['xl'], w['xh'], 0, n)
+            W_q, b_q = wk.margin_rows(10, t)
+            t0 = time.perf_counter()
+            sb, _ = ob.forward_zonotope_batched(lo, hi, ggc)
+            ob.spec_backward_batched(sb, lo, hi, ggc, W_q, b_q)
+            rate = n / (time.perf_counter() - t0)
+            line['cpu_baseline'] = {'value': rate, 'unit': 'leaves/s', 'cores': os.cpu_count(),
+                                    'kind': 'port',
+                                    'sample': f'{n} leaves: numpy oracle zonotope + CROWN '
+                                              '(BLAS threads)'}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == 'reference':
@@ -601,6 +688,8 @@ def main():
         run_cfg1(args)
     elif args.config in ('cfg3', 'cfg4'):
         run_cfg34(args)
+    elif args.config == 'cfg5':
+        run_cfg5(args)
     else:
         run_ours(args)
 

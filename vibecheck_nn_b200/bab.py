@@ -288,10 +288,12 @@ class WideBoundEngine(BoundEngine):
         from .wide import wide_net
         self.wn = wide_net(gg, device)
 
+    stats = None  # a dict here collects the zonotope GEMMs' FLOPs and timing
+
     def bounds(self, xl_b, xh_b, want_A):
         from .wide import wide_crown
         from .zono_wide import wide_zono
-        sb = wide_zono(self.wn, xl_b, xh_b)
+        sb = wide_zono(self.wn, xl_b, xh_b, stats=self.stats)
         out = wide_crown(self.wn, xl_b, xh_b, sb, self.W_q, self.b_q, want_A=want_A)
         return out['lb'], out.get('A'), out.get('acc')
 

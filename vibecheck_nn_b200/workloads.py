@@ -353,3 +353,40 @@ def split_domains(sb_lo, sb_hi, n_split):
         clamps[L][0][on, j] = 0.0
         clamps[L][1][~on, j] = 0.0
     return picked, clamps
+
+
+def cfg5_split_dims(xl, xh, depth=18):
+    """The dimensions the first ``depth`` widest-axis bisections of the box
+    split, in order (ties -> lowest index, as torch.argmax): each split halves
+    one dimension, so while at least ``depth`` dimensions share the largest
+    width the splits walk them in index order."""
+    width = (np.asarray(xh, np.float64) - np.asarray(xl, np.float64)).copy()
+    dims = []
+    for _ in range(depth):
+        d = int(np.argmax(width))
+        dims.append(d)
+        width[d] *= 0.5
+    return dims
+
+
+def cfg5_leaves(xl, xh, start, count, depth=18):
+    """Leaves start .. start+count-1 of the depth-``depth`` input-split tree
+    of the box: bit t of the leaf index picks the lower (0) or upper (1) half
+    along the t-th split dimension.  Returns (count, n) float32 arrays."""
+    xl = np.asarray(xl, np.float32)
+    xh = np.asarray(xh, np.float32)
+    dims = cfg5_split_dims(xl, xh, depth)
+    lo = np.repeat(xl[None], count, 0)
+    hi = np.repeat(xh[None], count, 0)
+    idx = np.arange(start, start + count)
+    for t, d in enumerate(dims):
+        upper = (idx >> t) & 1
+        mid = ((lo[:, d].astype(np.float32) + hi[:, d]) * np.float32(0.5)).astype(np.float32)
+        lo[:, d] = np.where(upper == 1, mid, lo[:, d])
+        hi[:, d] = np.where(upper == 1, hi[:, d], mid)
+    return lo, hi
+
+
+def robustness_disjuncts(n_out, true_label):
+    """Unsafe iff some y_j >= y_true: one pairwise disjunct per j != true."""
+    return [[('pair', true_label, j)] for j in range(n_out) if j != true_label]

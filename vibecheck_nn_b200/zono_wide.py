@@ -78,11 +78,12 @@ def _fc(x, W, b):
     return z
 
 
-def wide_zono(wn, xl, xh, want_output=False):
+def wide_zono(wn, xl, xh, want_output=False, stats=None):
     """Zonotope bounds of B boxes.  Returns sb {L: (lo, hi) (B, n_L)} and,
     with ``want_output``, (c_out (B, n_out), G (B, n_out, K)) as the
     reference returns them (generator columns in its order, zero-padded to
-    the batch maximum)."""
+    the batch maximum).  ``stats`` (a dict) collects the generator GEMMs'
+    algorithmic FLOPs (unpadded rows) and CUDA events around each launch."""
     z = zono_net(wn)
     dev = xl.device
     st = _lib.stream_of(dev)
@@ -104,6 +105,8 @@ def wide_zono(wn, xl, xh, want_output=False):
     ldc = 0
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     for l in range(1, nfc):
+        if l == nfc - 1 and not want_output:
+            break  # the output layer's generators are not needed for the bounds
         n = wn.dims[l]
         ld = _pad4(n)
         lam = torch.empty((B, n), dtype=F32, device=dev)
@@ -129,9 +132,17 @@ def wide_zono(wn, xl, xh, want_output=False):
         ldc = _pad4(nout)
         C = torch.empty((M, ldc), dtype=F32, device=dev)
         W_hi, W_lo = z.split[l]
+        if stats is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
         rc = L_.vcb_tc_gemm(M, nout, n, P(A_hi), P(A_lo), ld, P(W_hi), P(W_lo), ld, None, P(C),
                             ldc, P(err), st)
         _lib.check(rc, 'vcb_tc_gemm')
+        if stats is not None:
+            ev[1].record()
+            stats.setdefault('gemm_events', []).append(ev)
+            stats['gemm_flop'] = stats.get('gemm_flop', 0) + 2.0 * float(k_out.sum()) * nout * n
+            stats['gemm_launches'] = stats.get('gemm_launches', 0) + 1
         del A_hi, A_lo
         cur_c = _fc(c_relu, z.W[l], z.b[l])
         k_host = k_out
