@@ -460,11 +460,17 @@ int vcb_zw_build(int32_t B, int32_t n, int32_t ld, const int64_t* in_off,
                  const int32_t* idx_of_rank, const int64_t* out_off,
                  int64_t rows_hint, float* A_hi, float* A_lo, void* stream);
 
-/* lo / hi (B x n) = c -+ sum over leaf b's first k[b] rows of |C| (row
- * order). */
+/* lo / hi (B x n) = c -+ sum over leaf b's first k[b] rows of |C|:
+ * compensated sums over 128-row chunks (chunk_off (B+1): prefix of the
+ * per-leaf chunk counts ceil(k[b] / 128), max_chunks their maximum), then over
+ * a leaf's chunks in order.  workspace: vcb_zw_colsum_workspace(chunk_off[B],
+ * n) bytes. */
 int vcb_zw_colsum(int32_t B, int32_t n, const int64_t* off, const int32_t* k,
-                  const float* C, int32_t ldc, const float* c, float* lo,
-                  float* hi, void* stream);
+                  const int64_t* chunk_off, int32_t max_chunks, const float* C,
+                  int32_t ldc, const float* c, float* lo, float* hi,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+size_t vcb_zw_colsum_workspace(int64_t total_chunks, int32_t n);
 
 /* Diagnostic: FP32 FFMA throughput probe (no reference counterpart).  Runs
  * `blocks` CTAs of 256 threads, each thread `iters` x 64 dependent-chain FMAs

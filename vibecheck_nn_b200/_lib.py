@@ -78,7 +78,8 @@ SIGNATURES = {
     'vcb_zw_relu': [_I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     'vcb_zw_build': [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P,
                      ctypes.c_int64, _P, _P, _P],
-    'vcb_zw_colsum': [_I, _I, _P, _P, _P, _I, _P, _P, _P, _P],
+    'vcb_zw_colsum': [_I, _I, _P, _P, _P, _I, _P, _I, _P, _P, _P, _P, ctypes.c_size_t, _P],
+    'vcb_zw_colsum_workspace': [ctypes.c_int64, _I],
     'vcb_bab_step_wide': [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P,
                           _P, _P, ctypes.c_size_t, _P],
     'vcb_bab_step_wide_workspace': [_I, _I],
@@ -96,7 +97,8 @@ RESTYPES = {'vcb_last_error': ctypes.c_char_p,
             'vcb_mlp_crown_workspace': ctypes.c_size_t,
             'vcb_mlp_crown_noalloc_capacity': ctypes.c_size_t,
             'vcb_conv_back_workspace': ctypes.c_size_t,
-            'vcb_bab_step_wide_workspace': ctypes.c_size_t}
+            'vcb_bab_step_wide_workspace': ctypes.c_size_t,
+            'vcb_zw_colsum_workspace': ctypes.c_size_t}
 
 _lib = None
 

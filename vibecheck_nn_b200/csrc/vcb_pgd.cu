@@ -36,7 +36,7 @@
 namespace vcb {
 namespace {
 
-constexpr int kPT = 256;   // threads per CTA
+constexpr int kPT = 1024;  // threads per CTA (16 per sample: the iterations are latency-bound)
 constexpr int kPS = 64;    // samples per tile
 constexpr int kPMaxW = 128;
 constexpr int kStep = kPT / kPS;

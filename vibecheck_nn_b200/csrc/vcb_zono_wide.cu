@@ -15,7 +15,8 @@
 //     scaled column-wise by lambda, then one new row mu_j e_j per unstable
 //     neuron j in index order, then zero padding;
 //   * vcb_zw_colsum: per leaf and neuron the fixed-order compensated sum of
-//     |G| over the leaf's rows -> lo / hi = c -+ that radius.
+//     |G| over the leaf's rows (per 128-row chunk, then over the chunks)
+//     -> lo / hi = c -+ that radius.
 // Layer 0 needs no GEMM: its generators are r_i W0[:, i] (one per input
 // dimension; zero rows where the radius is 0), built straight from W0^T.
 #include <algorithm>
@@ -81,72 +82,147 @@ __global__ void __launch_bounds__(ZW_T) zw_relu_kernel(int n, const float* __res
   if (tid == 0) cnt[b] = carry;
 }
 
-__device__ __forceinline__ void split_store(float v, float* hi, float* lo, long long i) {
+__device__ __forceinline__ void split1(float v, float& h, float& l) {
   const uint32_t u = __float_as_uint(v);
   const bool finite = (u & 0x7F800000u) != 0x7F800000u;
-  const float h = finite ? __uint_as_float((u + 0x1000u) & 0xFFFFE000u) : v;
-  hi[i] = h;
-  lo[i] = finite ? __fsub_rn(v, h) : 0.f;
+  h = finite ? __uint_as_float((u + 0x1000u) & 0xFFFFE000u) : v;
+  l = finite ? __fsub_rn(v, h) : 0.f;
 }
 
-// A rows of leaf b (blockIdx.y): [0, k_in) scaled rows, [k_in, k_in + cnt)
-// new generators, then zeros up to the next leaf's offset.  Source rows come
-// from C (ld ldc) at in_off[b], or -- layer 0 (C == NULL) -- are r_b[k] W0T[k].
-__global__ void zw_build_kernel(int n, int ld, const long long* __restrict__ in_off,
-                                const int* __restrict__ k_in, const float* __restrict__ C,
-                                int ldc, const float* __restrict__ r, int n0,
-                                const float* __restrict__ W0T, const float* __restrict__ lam,
-                                const float* __restrict__ mu, const int* __restrict__ cnt,
-                                const int* __restrict__ idx_of_rank,
-                                const long long* __restrict__ out_off, float* __restrict__ Ah,
-                                float* __restrict__ Al) {
-  const int b = blockIdx.y;
-  const long long o0 = out_off[b], rows = out_off[b + 1] - o0;
-  const int kin = k_in[b], u = cnt[b];
-  const float* lam_b = lam + (long long)b * n;
-  const long long total = rows * ld;
-  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total;
-       e += (long long)gridDim.x * blockDim.x) {
-    const long long row = e / ld;
-    const int j = (int)(e - row * ld);
-    float v = 0.f;
-    if (j < n) {
-      if (row < kin) {
-        float g;
-        if (C) {
-          g = C[(in_off[b] + row) * ldc + j];
+__device__ __forceinline__ void split4(const float (&e)[4], float4& h, float4& l) {
+  split1(e[0], h.x, l.x);
+  split1(e[1], h.y, l.y);
+  split1(e[2], h.z, l.z);
+  split1(e[3], h.w, l.w);
+}
+
+// A rows of leaf b: [0, k_in) scaled rows, [k_in, k_in + cnt) new
+// generators, then zeros up to the next leaf's offset.  Source rows come from
+// C (ld ldc) at in_off[b], or -- layer 0 (C == NULL) -- are r_b[k] W0T[k].
+// One warp per output row, float4 across the row (ld % 4 == 0).
+__global__ void __launch_bounds__(256) zw_build_kernel(
+    int B, int n, int ld, const long long* __restrict__ in_off, const int* __restrict__ k_in,
+    const float* __restrict__ C, int ldc, const float* __restrict__ r, int n0,
+    const float* __restrict__ W0T, const float* __restrict__ lam, const float* __restrict__ mu,
+    const int* __restrict__ cnt, const int* __restrict__ idx_of_rank,
+    const long long* __restrict__ out_off, long long total_rows, float* __restrict__ Ah,
+    float* __restrict__ Al) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const int nv = ld >> 2;
+  for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       row < total_rows; row += warps) {
+    // leaf of this row: binary search of out_off (B + 1 offsets)
+    int lo = 0, hi = B;
+    while (hi - lo > 1) {
+      const int m = (lo + hi) >> 1;
+      if (out_off[m] <= row) lo = m; else hi = m;
+    }
+    const int b = lo;
+    const long long rr = row - out_off[b];
+    const int kin = k_in[b], u = cnt[b];
+    const float4* lam4 = reinterpret_cast<const float4*>(lam + (long long)b * n);
+    float4* dh = reinterpret_cast<float4*>(Ah + row * ld);
+    float4* dl = reinterpret_cast<float4*>(Al + row * ld);
+    if (rr < kin) {
+      const float* src;
+      float rk = 1.f;
+      if (C) {
+        src = C + (in_off[b] + rr) * ldc;
+      } else {
+        src = W0T + rr * (long long)n;
+        rk = r[(long long)b * n0 + rr];
+      }
+      for (int v = lane; v < nv; v += 32) {
+        const int j = 4 * v;
+        float e[4] = {0.f, 0.f, 0.f, 0.f};
+        if (j + 3 < n && (n & 3) == 0 && (C ? (ldc & 3) == 0 : true)) {
+          const float4 g = *reinterpret_cast<const float4*>(src + j);
+          const float4 lv = lam4[v];
+          e[0] = C ? g.x : __fmul_rn(g.x, rk);
+          e[1] = C ? g.y : __fmul_rn(g.y, rk);
+          e[2] = C ? g.z : __fmul_rn(g.z, rk);
+          e[3] = C ? g.w : __fmul_rn(g.w, rk);
+          e[0] = __fmul_rn(e[0], lv.x);
+          e[1] = __fmul_rn(e[1], lv.y);
+          e[2] = __fmul_rn(e[2], lv.z);
+          e[3] = __fmul_rn(e[3], lv.w);
         } else {
-          g = __fmul_rn(W0T[row * (long long)n + j], r[(long long)b * n0 + row]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int jj = j + t;
+            if (jj < n) {
+              const float g = C ? src[jj] : __fmul_rn(src[jj], rk);
+              e[t] = __fmul_rn(g, lam[(long long)b * n + jj]);
+            }
+          }
         }
-        v = __fmul_rn(g, lam_b[j]);
-      } else if (row < kin + u) {
-        const int jj = idx_of_rank[(long long)b * n + (row - kin)];
-        v = (j == jj) ? mu[(long long)b * n + j] : 0.f;
+        float4 h, l;
+        split4(e, h, l);
+        dh[v] = h;
+        dl[v] = l;
+      }
+    } else {
+      const int jj = (rr < kin + u) ? idx_of_rank[(long long)b * n + (rr - kin)] : -1;
+      const float m = jj >= 0 ? mu[(long long)b * n + jj] : 0.f;
+      for (int v = lane; v < nv; v += 32) {
+        float e[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) e[t] = (4 * v + t == jj) ? m : 0.f;
+        float4 h, l;
+        split4(e, h, l);
+        dh[v] = h;
+        dl[v] = l;
       }
     }
-    split_store(v, Ah, Al, (o0 + row) * ld + j);
   }
 }
 
-// rad[b][j] = sum over the leaf's k rows of |C[row][j]| in row order with
-// Neumaier's compensated summation (the radius sums thousands of terms; the
-// compensation keeps it at fp32 rounding of the exact sum); lo = c - rad,
-// hi = c + rad.
-__global__ void zw_colsum_kernel(int n, const long long* __restrict__ off,
-                                 const int* __restrict__ k, const float* __restrict__ C, int ldc,
-                                 const float* __restrict__ c, float* __restrict__ lo,
-                                 float* __restrict__ hi) {
+// rad[b][j] = sum over the leaf's k rows of |C[row][j]| with Neumaier's
+// compensated summation in a fixed order: chunks of kChunk rows (one thread
+// per (chunk, column)) give (sum, compensation) partials, then the chunks of
+// a leaf are combined in order.  lo = c - rad, hi = c + rad.
+constexpr int kChunk = 128;
+
+__device__ __forceinline__ void neumaier(float& s, float& comp, float v) {
+  const float t = __fadd_rn(s, v);
+  comp = __fadd_rn(comp, (fabsf(s) >= fabsf(v)) ? __fadd_rn(__fsub_rn(s, t), v)
+                                                 : __fadd_rn(__fsub_rn(v, t), s));
+  s = t;
+}
+
+__global__ void __launch_bounds__(256) zw_colsum_part_kernel(
+    int n, const long long* __restrict__ off, const int* __restrict__ k,
+    const long long* __restrict__ chunk_off, const float* __restrict__ C, int ldc,
+    float2* __restrict__ part) {
+  const int b = blockIdx.z;
+  const int ch = blockIdx.y;  // chunk index inside the leaf
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const long long nch = chunk_off[b + 1] - chunk_off[b];
+  if (ch >= nch || j >= n) return;
+  const int kb = k[b];
+  const int r0 = ch * kChunk, r1 = min(kb, r0 + kChunk);
+  const float* p = C + (off[b] + r0) * ldc + j;
+  float s = 0.f, comp = 0.f;
+#pragma unroll 4
+  for (int row = r0; row < r1; ++row) {
+    neumaier(s, comp, fabsf(*p));
+    p += ldc;
+  }
+  part[(chunk_off[b] + ch) * n + j] = make_float2(s, comp);
+}
+
+__global__ void __launch_bounds__(256) zw_colsum_combine_kernel(
+    int n, const long long* __restrict__ chunk_off, const float2* __restrict__ part,
+    const float* __restrict__ c, float* __restrict__ lo, float* __restrict__ hi) {
   const int b = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= n) return;
-  const float* p = C + off[b] * ldc + j;
-  const int kb = k[b];
   float s = 0.f, comp = 0.f;
-  for (int row = 0; row < kb; ++row) {
-    const float v = fabsf(p[(long long)row * ldc]);
-    const float t = __fadd_rn(s, v);
-    comp = __fadd_rn(comp, (s >= v) ? __fadd_rn(__fsub_rn(s, t), v) : __fadd_rn(__fsub_rn(v, t), s));
-    s = t;
+  for (long long ch = chunk_off[b]; ch < chunk_off[b + 1]; ++ch) {
+    const float2 v = part[ch * n + j];
+    neumaier(s, comp, v.x);
+    comp = __fadd_rn(comp, v.y);
   }
   s = __fadd_rn(s, comp);
   const long long i = (long long)b * n + j;
@@ -179,25 +255,43 @@ extern "C" int vcb_zw_build(int32_t B, int32_t n, int32_t ld, const int64_t* in_
                             void* stream) {
   if (B < 0 || n <= 0 || ld < n || ld % 4 || rows_hint < 0)
     return fail(VCB_ERR_INVALID, "vcb_zw_build: B=%d n=%d ld=%d", B, n, ld);
-  if (B == 0) return VCB_OK;
+  if (B == 0 || rows_hint == 0) return VCB_OK;
   if (!k_in || !lam || !mu || !cnt || !idx_of_rank || !out_off || !A_hi || !A_lo ||
       (C && !in_off) || (!C && (!r || !W0T)))
     return fail(VCB_ERR_INVALID, "vcb_zw_build: NULL pointer");
-  const long long per_leaf = (rows_hint / std::max(1, B) + 1) * ld;
-  const int bx = (int)std::max<long long>(1, std::min<long long>((per_leaf + 255) / 256, 1024));
-  zw_build_kernel<<<dim3(bx, B), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      n, ld, reinterpret_cast<const long long*>(in_off), k_in, C, ldc, r, n0, W0T, lam, mu, cnt,
-      idx_of_rank, reinterpret_cast<const long long*>(out_off), A_hi, A_lo);
+  const long long blocks = std::min<long long>((rows_hint + 7) / 8, 148LL * 64);
+  zw_build_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      B, n, ld, reinterpret_cast<const long long*>(in_off), k_in, C, ldc, r, n0, W0T, lam, mu,
+      cnt, idx_of_rank, reinterpret_cast<const long long*>(out_off), rows_hint, A_hi, A_lo);
   return check_launch("vcb_zw_build");
 }
 
+extern "C" size_t vcb_zw_colsum_workspace(int64_t total_chunks, int32_t n) {
+  if (total_chunks <= 0 || n <= 0) return 0;
+  return (size_t)total_chunks * n * sizeof(float2);
+}
+
 extern "C" int vcb_zw_colsum(int32_t B, int32_t n, const int64_t* off, const int32_t* k,
-                             const float* C, int32_t ldc, const float* c, float* lo, float* hi,
-                             void* stream) {
-  if (B < 0 || n <= 0 || ldc < n) return fail(VCB_ERR_INVALID, "vcb_zw_colsum: B=%d n=%d", B, n);
+                             const int64_t* chunk_off, int32_t max_chunks, const float* C,
+                             int32_t ldc, const float* c, float* lo, float* hi, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (B < 0 || n <= 0 || ldc < n || max_chunks < 0)
+    return fail(VCB_ERR_INVALID, "vcb_zw_colsum: B=%d n=%d", B, n);
   if (B == 0) return VCB_OK;
-  if (!off || !k || !C || !c || !lo || !hi) return fail(VCB_ERR_INVALID, "vcb_zw_colsum: NULL pointer");
-  zw_colsum_kernel<<<dim3((n + 255) / 256, B), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      n, reinterpret_cast<const long long*>(off), k, C, ldc, c, lo, hi);
+  if (!off || !k || !chunk_off || !C || !c || !lo || !hi || (max_chunks > 0 && !workspace))
+    return fail(VCB_ERR_INVALID, "vcb_zw_colsum: NULL pointer");
+  if (B > 65535 || max_chunks > 65535)
+    return fail(VCB_ERR_UNSUPPORTED, "vcb_zw_colsum: %d leaves, %d chunks", B, max_chunks);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float2* part = static_cast<float2*>(workspace);
+  if (max_chunks > 0) {
+    zw_colsum_part_kernel<<<dim3((n + 255) / 256, max_chunks, B), 256, 0, st>>>(
+        n, reinterpret_cast<const long long*>(off), k,
+        reinterpret_cast<const long long*>(chunk_off), C, ldc, part);
+    const int rc = check_launch("vcb_zw_colsum: parts");
+    if (rc) return rc;
+  }
+  zw_colsum_combine_kernel<<<dim3((n + 255) / 256, B), 256, 0, st>>>(
+      n, reinterpret_cast<const long long*>(chunk_off), part, c, lo, hi);
   return check_launch("vcb_zw_colsum");
 }

@@ -27,6 +27,7 @@ from .ops import F32
 
 P = _lib.ptr
 ROW_TILE = 128
+COL_CHUNK = 128  # rows per partial radius sum (vcb_zw_colsum)
 
 
 def _pad4(n):
@@ -151,8 +152,14 @@ def wide_zono(wn, xl, xh, want_output=False, stats=None):
         if l < nfc - 1 or want_output:
             lo = torch.empty((B, nout), dtype=F32, device=dev)
             hi = torch.empty_like(lo)
-            rc = L_.vcb_zw_colsum(B, nout, P(in_off), P(k_in), P(C), ldc, P(cur_c), P(lo), P(hi),
-                                  st)
+            nch = (k_out + COL_CHUNK - 1) // COL_CHUNK
+            ch_off = np.zeros(B + 1, dtype=np.int64)
+            ch_off[1:] = np.cumsum(nch)
+            ws_n = L_.vcb_zw_colsum_workspace(int(ch_off[-1]), nout)
+            ws = _lib.workspace(ws_n, dev)
+            rc = L_.vcb_zw_colsum(B, nout, P(in_off), P(k_in),
+                                  P(torch.as_tensor(ch_off, device=dev)), int(nch.max()), P(C),
+                                  ldc, P(cur_c), P(lo), P(hi), P(ws), ws_n, st)
             _lib.check(rc, 'vcb_zw_colsum')
             if l < nfc - 1:
                 sb[l] = (lo, hi)
