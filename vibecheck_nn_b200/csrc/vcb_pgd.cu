@@ -42,6 +42,8 @@ constexpr int kPMaxW = 128;
 constexpr int kStep = kPT / kPS;
 
 // Shared-memory layout of the network and one sample tile (offsets in floats).
+// The activation rows need no padding beyond n: every loop over inputs stops
+// at the layer width.
 struct PgdNet {
   int n_fc;
   int dims[VCB_MAX_FC + 1];
@@ -49,11 +51,10 @@ struct PgdNet {
   const float* b;
   long long w_goff[VCB_MAX_FC];
   int b_goff[VCB_MAX_FC];
-  int w_soff[VCB_MAX_FC];
-  int pw[VCB_MAX_FC];
-  int wrows[VCB_MAX_FC];
-  int pa;                 // activation row stride (multiple of 4)
-  int pz;                 // pre-activation / gradient row stride (odd)
+  int wt_soff[VCB_MAX_FC];  // [W^T; b] ((n_in + 1) rows x pwt floats, zero-padded)
+  int pwt[VCB_MAX_FC];
+  int pa;                 // activation row stride (odd)
+  int pz;                 // pre-activation / gradient row stride (4 x odd)
   int act_soff;           // 2 ping-pong activation buffers, kPS x pa
   int z_soff;             // n_fc pre-activation buffers, kPS x pz
   int g_soff, x_soff, c_soff;
@@ -109,61 +110,63 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Weights (+ bias column) of every fc layer into shared memory.
+// Every fc layer as [W^T; b] in shared memory: row i < n_in holds W[:, i],
+// row n_in the bias, columns zero-padded to pwt (a multiple of 4).
 __device__ void load_net(const PgdNet& n, float* sm, int tid) {
   for (int l = 0; l < n.n_fc; ++l) {
-    const int nin = n.dims[l], nout = n.dims[l + 1], pw = n.pw[l];
-    float* dst = sm + n.w_soff[l];
+    const int nin = n.dims[l], nout = n.dims[l + 1], pwt = n.pwt[l];
+    float* dt = sm + n.wt_soff[l];
     const float* Wg = n.W + n.w_goff[l];
     const float* bg = n.b + n.b_goff[l];
-    for (int o = tid >> 5; o < n.wrows[l]; o += kPT / 32)
-      for (int i = tid & 31; i < pw; i += 32) {
-        float v = 0.f;
-        if (o < nout) v = (i < nin) ? Wg[(long long)o * nin + i] : (i == nin ? bg[o] : 0.f);
-        dst[o * pw + i] = v;
-      }
+    for (int i = tid >> 5; i <= nin; i += kPT / 32)
+      for (int o = tid & 31; o < pwt; o += 32)
+        dt[i * pwt + o] = (o < nout) ? (i < nin ? Wg[(long long)o * nin + i] : bg[o]) : 0.f;
   }
 }
 
 // Forward pass of the tile's samples xs (kPS x n0): z_l kept for the masks,
-// a_{l+1} = relu(z_l); the network output is z_{n_fc-1}.
+// a_{l+1} = relu(z_l); the network output is z_{n_fc-1}.  A thread computes
+// 4 consecutive outputs of one sample: z[o] = sum_i a[i] W[o][i] in ascending
+// i, then + b[o].
 __device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int tid) {
   const int n0 = n.dims[0], pa = n.pa, pz = n.pz;
   float* a_cur = sm + n.act_soff;
-  const int n0p = pad4(n0);
-  for (int idx = tid; idx < kPS * n0p; idx += kPT) {
-    const int s = idx / n0p, i = idx - s * n0p;
-    a_cur[s * pa + i] = i < n0 ? xs[s * n0 + i] : 0.f;
+  for (int idx = tid; idx < kPS * n0; idx += kPT) {
+    const int s = idx / n0, i = idx - s * n0;
+    a_cur[s * pa + i] = xs[idx];
   }
   __syncthreads();
   for (int l = 0; l < n.n_fc; ++l) {
-    const int nin = n.dims[l], nout = n.dims[l + 1], pw = n.pw[l];
-    const float* sW = sm + n.w_soff[l];
+    const int nin = n.dims[l], nout = n.dims[l + 1], pwt = n.pwt[l];
+    const float* sWT = sm + n.wt_soff[l];
     const float* ain = sm + n.act_soff + (l & 1) * kPS * pa;
     float* aout = sm + n.act_soff + ((l + 1) & 1) * kPS * pa;
     float* z = sm + n.z_soff + l * kPS * pz;
-    const int kend = pad4(nin);
-    const int noutp = pad4(nout);
-    for (int idx = tid; idx < kPS * noutp; idx += kPT) {
-      const int o = idx / kPS, s = idx - o * kPS;
-      if (o >= nout) {
-        aout[s * pa + o] = 0.f;
-        continue;
-      }
-      float acc = 0.f;
+    const int nob = pwt >> 2;
+    for (int idx = tid; idx < kPS * nob; idx += kPT) {
+      const int ob = idx / kPS, s = idx - ob * kPS;
+      const int o4 = 4 * ob;
       const float* ar = ain + s * pa;
-      const float* wr = sW + o * pw;
-      for (int k = 0; k < kend; k += 4) {
-        const float4 av = *reinterpret_cast<const float4*>(ar + k);
-        const float4 wv = *reinterpret_cast<const float4*>(wr + k);
-        acc = fmaf(av.x, wv.x, acc);
-        acc = fmaf(av.y, wv.y, acc);
-        acc = fmaf(av.z, wv.z, acc);
-        acc = fmaf(av.w, wv.w, acc);
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (int i = 0; i < nin; ++i) {
+        const float av = ar[i];
+        const float4 wv = *reinterpret_cast<const float4*>(sWT + i * pwt + o4);
+        a0 = fmaf(av, wv.x, a0);
+        a1 = fmaf(av, wv.y, a1);
+        a2 = fmaf(av, wv.z, a2);
+        a3 = fmaf(av, wv.w, a3);
       }
-      const float zz = __fadd_rn(acc, wr[nin]);
-      z[s * pz + o] = zz;
-      aout[s * pa + o] = fmaxf(zz, 0.f);
+      const float4 bv = *reinterpret_cast<const float4*>(sWT + nin * pwt + o4);
+      const float zz[4] = {__fadd_rn(a0, bv.x), __fadd_rn(a1, bv.y), __fadd_rn(a2, bv.z),
+                           __fadd_rn(a3, bv.w)};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int o = o4 + j;
+        if (o < nout) {
+          z[s * pz + o] = zz[j];
+          aout[s * pa + o] = fmaxf(zz[j], 0.f);
+        }
+      }
     }
     __syncthreads();
   }
@@ -175,15 +178,27 @@ __device__ void tile_backward(const PgdNet& n, float* sm, int tid) {
   const int pz = n.pz;
   float* g = sm + n.g_soff;
   for (int l = n.n_fc - 1; l >= 0; --l) {
-    const int nin = n.dims[l], nout = n.dims[l + 1], pw = n.pw[l];
-    const float* sW = sm + n.w_soff[l];
+    const int nin = n.dims[l], nout = n.dims[l + 1], pwt = n.pwt[l];
+    const float* sWT = sm + n.wt_soff[l];
     const float* zprev = (l > 0) ? sm + n.z_soff + (l - 1) * kPS * pz : nullptr;
     float vals[(kPMaxW + kStep - 1) / kStep];
     const int sl = tid % kPS, i0 = tid / kPS;
+    const float* grow = g + sl * pz;
+    const int kend = pad4(nout);
     int cnt = 0;
     for (int i = i0; i < nin; i += kStep) {
+      // sum over o in fixed ascending order, 4 at a time (g and W^T rows are
+      // zero past n_out)
+      const float* wt = sWT + i * pwt;
       float acc = 0.f;
-      for (int o = 0; o < nout; ++o) acc = fmaf(g[sl * pz + o], sW[o * pw + i], acc);
+      for (int o = 0; o < kend; o += 4) {
+        const float4 gv = *reinterpret_cast<const float4*>(grow + o);
+        const float4 wv = *reinterpret_cast<const float4*>(wt + o);
+        acc = fmaf(gv.x, wv.x, acc);
+        acc = fmaf(gv.y, wv.y, acc);
+        acc = fmaf(gv.z, wv.z, acc);
+        acc = fmaf(gv.w, wv.w, acc);
+      }
       if (zprev && !(zprev[sl * pz + i] > 0.f)) acc = 0.f;
       vals[cnt++] = acc;
     }
@@ -633,14 +648,12 @@ int plan_net(const vcb_mlp* net, int ncon, PgdNet& n, const char* who) {
     n.b_goff[l] = boff;
     woff += (long long)net->dims[l] * net->dims[l + 1];
     boff += net->dims[l + 1];
-    n.pw[l] = pad4odd(net->dims[l] + 1);
-    n.wrows[l] = pad4(net->dims[l + 1]);
-    n.w_soff[l] = off;
-    off += n.wrows[l] * n.pw[l];
+    n.pwt[l] = pad4(net->dims[l + 1]);
+    n.wt_soff[l] = off;
+    off += pad4((net->dims[l] + 1) * n.pwt[l]);
   }
-  off = pad4(off + 8);
-  n.pa = pad4odd(maxw);
-  n.pz = pad4(maxw) + 1;
+  n.pa = maxw | 1;         // odd: scalar loads of 32 samples' rows hit 32 banks
+  n.pz = pad4odd(maxw);    // 4 x odd: float4 loads of 8 samples' rows hit 32 banks
   n.act_soff = off;
   off += 2 * kPS * n.pa;
   n.z_soff = off;
