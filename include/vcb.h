@@ -334,14 +334,15 @@ int vcb_wide_concretize(int32_t R, int32_t Q, int32_t n0, int32_t lde,
 
 /* alpha adjoint fc step: ga = g (R x nin, ld ldg) W^T + b; with rec (R x
  * nout, ld ldo), the raw coefficients entering relu layer L's relaxation,
- * writes g_o (the adjoint before that relu) and dcontrib (per-row alpha
- * gradient, [unstable] max(e,0) ga). */
+ * writes g_o (the adjoint before that relu), dcontrib (per-row alpha
+ * gradient, [unstable] max(e,0) ga) and, if non-NULL, dbeta (per-row gradient
+ * with respect to the split multiplier beta added after the relaxation: ga). */
 int vcb_wide_adjoint_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
                            const float* g, int32_t ldg, const float* W,
                            const float* b, const float* rec,
                            const float* sb_lo, const float* sb_hi,
                            const float* alpha, float* g_o, float* dcontrib,
-                           int32_t ldo, void* stream);
+                           float* dbeta, int32_t ldo, void* stream);
 
 /* Adam (betas 0.9/0.999, eps 1e-8, as torch.optim.Adam) step `step` on the
  * loss -sum(lb): gradient = -sum over the Q rows of each domain of dcontrib;

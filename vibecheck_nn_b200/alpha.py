@@ -8,9 +8,11 @@
 * ``alpha_boundary_refine`` -- the BaB's selective alpha-CROWN on boundary
   leaves (verify_graph.py:12927-12975).
 * ``spec_backward_with_grad`` -- ``_spec_backward_graph_batched`` with alpha
-  (and beta) tensors that require grad: a ``torch.autograd.Function`` whose
-  backward is the hand-written adjoint kernel, so the reference's own
-  ``(-lbs.sum()).backward()`` loops work unchanged.
+  and beta tensors that require grad: a ``torch.autograd.Function`` whose
+  backward is the hand-written adjoint kernel (beta, added after each
+  relaxation, gets the adjoint itself as its gradient), so the reference's
+  own ``(-lbs.sum()).backward()`` loops work unchanged -- the alpha-beta loop
+  of ``_ibp_crown_bab`` (verify_milp.py:2762-2807) included.
 """
 from __future__ import annotations
 
@@ -93,17 +95,20 @@ def alpha_boundary_refine(desc, xl, xh, lb, W_q, b_q, qd, D, eps, iters,
 
 
 class _SpecBackwardAlpha(torch.autograd.Function):
-    """lb = CROWN(alpha); backward by the hand-written adjoint."""
+    """lb = CROWN(alpha, beta); backward by the hand-written adjoint."""
 
     @staticmethod
-    def forward(ctx, wn, xl, xh, sb, W_q, b_q, Ls, *alphas):
-        alpha = {L: a.detach().contiguous() for L, a in zip(Ls, alphas)}
+    def forward(ctx, wn, xl, xh, sb, W_q, b_q, Ls, Lb, *params):
+        alpha = {L: a.detach().contiguous() for L, a in zip(Ls, params[:len(Ls)])}
+        beta = {L: b.detach().contiguous() for L, b in zip(Lb, params[len(Ls):])}
         with torch.no_grad():
-            lb, contrib = wide.wide_alpha_grad(wn, xl, xh, sb, W_q, b_q, alpha)
+            lb, contrib, bcontrib = wide.wide_alpha_grad(
+                wn, xl, xh, sb, W_q, b_q, alpha, beta=beta or None, beta_grad=True)
         ctx.Q = W_q.shape[0]
-        ctx.Ls = Ls
+        ctx.Ls, ctx.Lb = Ls, Lb
         ctx.widths = [alpha[L].shape[1] for L in Ls]
-        ctx.contrib = contrib
+        ctx.bwidths = [beta[L].shape[1] for L in Lb]
+        ctx.contrib, ctx.bcontrib = contrib, bcontrib
         return lb
 
     @staticmethod
@@ -111,27 +116,25 @@ class _SpecBackwardAlpha(torch.autograd.Function):
         w = grad.flatten()
         if not bool((w == w[0]).all()):
             raise NotImplementedError(
-                'vibecheck_nn_b200: alpha gradient only for a uniform weighting '
+                'vibecheck_nn_b200: alpha / beta gradients only for a uniform weighting '
                 'of the spec lower bounds (the loss -sum(lb) the reference uses)')
         scale = w[0]
-        outs = []
-        for L, n in zip(ctx.Ls, ctx.widths):
-            dc, ldo = ctx.contrib[L]
+
+        def per_domain(store, L, n):
+            dc, ldo = store[L]
             D = dc.shape[0] // ctx.Q
-            outs.append(dc.view(D, ctx.Q, ldo).sum(dim=1)[:, :n] * scale)
-        res = [None] * 7
-        for L, g in zip(ctx.Ls, outs):
-            res.append(g)
+            return dc.view(D, ctx.Q, ldo).sum(dim=1)[:, :n] * scale
+
+        res = [None] * 8
+        res += [per_domain(ctx.contrib, L, n) for L, n in zip(ctx.Ls, ctx.widths)]
+        res += [per_domain(ctx.bcontrib, L, n) for L, n in zip(ctx.Lb, ctx.bwidths)]
         return tuple(res)
 
 
 def spec_backward_with_grad(desc, lo, hi, xl, xh, spec, alpha_at_layer,
                             relu_split_beta, return_input_linear):
-    if relu_split_beta is not None and any(
-            bool(b.requires_grad) for b in relu_split_beta.values()):
-        raise NotImplementedError('vibecheck_nn_b200: gradients with respect to beta')
-    if relu_split_beta is not None and any(bool((b != 0).any()) for b in relu_split_beta.values()):
-        raise NotImplementedError('vibecheck_nn_b200: non-zero beta with alpha gradients')
+    """_spec_backward_graph_batched with alpha (and beta) tensors that may
+    require grad: lb carries the hand-written adjoint as its backward."""
     if return_input_linear:
         raise NotImplementedError('vibecheck_nn_b200: return_input_linear with alpha gradients')
     B = xl.shape[0]
@@ -139,7 +142,8 @@ def spec_backward_with_grad(desc, lo, hi, xl, xh, spec, alpha_at_layer,
     wn = desc.__dict__.get('_wide') or wide.WideNet(desc)
     desc.__dict__['_wide'] = wn
     W_q, b_q = spec
-    Ls = sorted(alpha_at_layer)
-    out = _SpecBackwardAlpha.apply(wn, xl, xh, sb, W_q, b_q, Ls,
-                                   *[alpha_at_layer[L] for L in Ls])
-    return out
+    Ls = sorted(alpha_at_layer or {})
+    beta = relu_split_beta or {}
+    Lb = sorted(beta)
+    params = [alpha_at_layer[L] for L in Ls] + [beta[L].to(F32) for L in Lb]
+    return _SpecBackwardAlpha.apply(wn, xl, xh, sb, W_q, b_q, Ls, Lb, *params)

@@ -203,6 +203,7 @@ __global__ void concretize_kernel(int R, int Q, int n0, int lde, const float* e,
 // d(sum lb)/d(coefficient after relu L's relaxation); with rec (the raw
 // coefficient entering that relaxation) it gives
 //   dcontrib[r][j] = [unstable] * max(e, 0) * ga            (alpha gradient)
+//   dbeta[r][j]    = ga                                      (beta gradient)
 //   g_o[r][j] = [e >= 0] pos * ga + [e <= 0] (neg * ga + icp).
 // ---------------------------------------------------------------------------
 struct AdjArgs {
@@ -210,6 +211,7 @@ struct AdjArgs {
   const float *g, *W, *b;       // W: nout x nin (ld nin)
   const float *rec, *sblo, *sbhi, *alpha;  // rec: R x nout (ld ldo); sb/alpha (R/Q) x nout
   float *g_o, *dcontrib;        // R x nout (ld ldo)
+  float* dbeta;                 // R x nout (ld ldo): d lb / d beta = ga, or NULL
 };
 
 __global__ void __launch_bounds__(GT) alpha_adjoint_kernel(const AdjArgs a) {
@@ -236,6 +238,8 @@ __global__ void __launch_bounds__(GT) alpha_adjoint_kernel(const AdjArgs a) {
       const float e = a.rec[(long long)m * a.ldo + n];
       const Relax r = relax_of(a.sblo[gi], a.sbhi[gi], a.alpha ? a.alpha + gi : nullptr);
       a.dcontrib[(long long)m * a.ldo + n] = r.unstable ? __fmul_rn(fmaxf(e, 0.f), ga) : 0.f;
+      // beta is added after the relaxation, so its gradient is the adjoint itself
+      if (a.dbeta) a.dbeta[(long long)m * a.ldo + n] = ga;
       float go = 0.f;
       if (e >= 0.f) go = __fmul_rn(r.pos, ga);
       if (e <= 0.f) go = __fadd_rn(go, __fadd_rn(__fmul_rn(r.neg, ga), r.icp));
@@ -347,13 +351,14 @@ extern "C" int vcb_wide_adjoint_layer(int32_t R, int32_t Q, int32_t nin, int32_t
                                       const float* g, int32_t ldg, const float* W,
                                       const float* b, const float* rec, const float* sb_lo,
                                       const float* sb_hi, const float* alpha, float* g_o,
-                                      float* dcontrib, int32_t ldo, void* stream) {
+                                      float* dcontrib, float* dbeta, int32_t ldo,
+                                      void* stream) {
   if (R < 0 || Q <= 0 || nin <= 0 || nout <= 0)
     return fail(VCB_ERR_INVALID, "vcb_wide_adjoint_layer: shape");
   if (R == 0) return VCB_OK;
   if (!g || !W || !b || !rec || !sb_lo || !sb_hi || !g_o || !dcontrib || (ldg & 3) || (ldo & 3))
     return fail(VCB_ERR_INVALID, "vcb_wide_adjoint_layer: NULL pointer or bad ld");
-  AdjArgs a{R, Q, nin, nout, ldg, ldo, g, W, b, rec, sb_lo, sb_hi, alpha, g_o, dcontrib};
+  AdjArgs a{R, Q, nin, nout, ldg, ldo, g, W, b, rec, sb_lo, sb_hi, alpha, g_o, dcontrib, dbeta};
   const int sm = smem_bytes(false);
   int rc = ensure_smem(reinterpret_cast<const void*>(alpha_adjoint_kernel), sm);
   if (rc) return rc;

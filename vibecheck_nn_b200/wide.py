@@ -155,34 +155,42 @@ def wide_crown(wn, xl, xh, sb, W_q, b_q, alpha=None, beta=None, want_A=False,
     return out
 
 
-def wide_alpha_grad(wn, xl, xh, sb, W_q, b_q, alpha):
-    """lb (D, Q) and the per-row alpha-gradient contributions
-    {L: (R, ld)} of d(sum lb)/d(alpha) (summed over the Q rows of a domain
-    by the Adam kernel)."""
+def wide_alpha_grad(wn, xl, xh, sb, W_q, b_q, alpha, beta=None, beta_grad=False):
+    """lb (D, Q) and the per-row gradient contributions {L: (R, ld)} of
+    d(sum lb)/d(alpha) (summed over the Q rows of a domain by the Adam kernel);
+    with ``beta_grad`` also those of d(sum lb)/d(beta) for the split
+    multipliers ``beta`` {L: (D, n_L)} added after each relaxation."""
     dev = xl.device
     D, n0 = xl.shape
     Q = W_q.shape[0]
     R = D * Q
     st = _lib.stream_of(dev)
     L_ = _lib.lib()
-    res = wide_crown(wn, xl, xh, sb, W_q, b_q, alpha=alpha, record=True, want_g0=True)
+    res = wide_crown(wn, xl, xh, sb, W_q, b_q, alpha=alpha, beta=beta, record=True,
+                     want_g0=True)
     g, ldg = res['g0']
     contrib = {}
+    bcontrib = {}
     for l in range(len(wn.W) - 1):
         nout, nin = wn.W[l].shape
         rec = res['rec'][l]
         ldo = rec.shape[1]
         g_o = torch.empty((R, ldo), dtype=F32, device=dev)
         dc = torch.empty((R, ldo), dtype=F32, device=dev)
+        db = torch.empty((R, ldo), dtype=F32, device=dev) if beta_grad else None
         lo, hi = sb[l]
         al = alpha.get(l) if alpha is not None else None
         rc = L_.vcb_wide_adjoint_layer(R, Q, nin, nout, P(g), ldg, P(wn.W[l]), P(wn.b[l]),
                                        P(rec), P(lo.contiguous()), P(hi.contiguous()),
                                        P(None if al is None else al.contiguous()),
-                                       P(g_o), P(dc), ldo, st)
+                                       P(g_o), P(dc), P(db), ldo, st)
         _lib.check(rc, 'vcb_wide_adjoint_layer')
         contrib[l] = (dc, ldo)
+        if beta_grad:
+            bcontrib[l] = (db, ldo)
         g, ldg = g_o, ldo
+    if beta_grad:
+        return res['lb'], contrib, bcontrib
     return res['lb'], contrib
 
 
