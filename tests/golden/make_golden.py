@@ -64,7 +64,7 @@ def _net_arrays(layers):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--ref-src', required=True)
-    ap.add_argument('--only', default=None, choices=['pgd_general', 'forward'],
+    ap.add_argument('--only', default=None, choices=['pgd_general', 'forward', 'relu_bab'],
                     help='regenerate one fixture only')
     args = ap.parse_args()
     vz, vg, vh, vs, vspec = _import_reference(args.ref_src)
@@ -75,6 +75,9 @@ def main():
         return
     if args.only == 'forward':
         _golden_forward(vz, wk)
+        return
+    if args.only == 'relu_bab':
+        _golden_relu_bab(vz, wk)
         return
 
     # ------------------------------------------------------------------ slopes
@@ -435,6 +438,73 @@ def _golden_pgd_general(vspec, wk):
         out[p + 'x_last'] = _n(seen[-1])
     out['tags'] = np.array([c[0] for c in PGD_GENERAL_CASES])
     _save('pgd_general', **out)
+
+
+# ReLU-split BaB cases: (tag, seed, dims, eps, keyword settings)
+RELU_BAB_CASES = (
+    ('closed20', 0, (20, 32, 32, 32, 5), 0.005, {}),
+    ('exhausted', 0, (20, 32, 32, 32, 5), 0.01, {}),
+    ('closed229', 3, (12, 24, 24, 24, 4), 0.04, {}),
+    ('capped', 2, (10, 40, 40, 5), 0.05, {'max_domains': 400}),
+    ('deepest', 3, (12, 24, 24, 24, 4), 0.04, {'split_deepest': True}),
+    ('noreforward', 3, (12, 24, 24, 24, 4), 0.04, {'no_reforward': True}),
+    ('warm', 3, (12, 24, 24, 24, 4), 0.04, {'alpha_half': True, 'ew_ones': True}),
+    ('warm_noref', 3, (12, 24, 24, 24, 4), 0.04,
+     {'alpha_half': True, 'ew_ones': True, 'no_reforward': True}),
+)
+
+
+def relu_bab_kwargs(kw, root):
+    """Keyword arguments of a case: 'alpha_half' becomes alpha_init = 0.5
+    at every ReLU, 'ew_ones' a unit coefficient score ew_w at every ReLU."""
+    import torch
+    out = dict(time_left=lambda: 1e9, batch=16, alpha_iters=8, max_domains=3000)
+    for k, v in kw.items():
+        if k == 'alpha_half':
+            out['alpha_init'] = {L: torch.full_like(lo, 0.5) for L, (lo, _) in root.items()}
+        elif k == 'ew_ones':
+            out['ew_w'] = {L: torch.ones_like(lo) for L, (lo, _) in root.items()}
+        else:
+            out[k] = v
+    return out
+
+
+def relu_bab_problem(seed, dims, eps):
+    """Network, box and margin query (y_top - y_second > 0 at the centre) of
+    a ReLU-split BaB case."""
+    from vibecheck_nn_b200 import workloads as wk
+    rng = np.random.default_rng(seed)
+    layers = wk.mlp_params(dims, rng)
+    x0 = rng.uniform(0, 1, dims[0])
+    y = wk._mlp_forward64(layers, x0[None])[0]
+    t, j = int(np.argmax(y)), int(np.argsort(y)[-2])
+    w = np.zeros(dims[-1])
+    w[t], w[j] = 1.0, -1.0
+    return layers, (x0 - eps).astype(np.float32), (x0 + eps).astype(np.float32), w
+
+
+def _golden_relu_bab(vz, wk):
+    """_ibp_crown_bab (verify_milp.py:2658-2960) in float32 on CPU: closed
+    flag, domain count and reason per case (batch 16, 8 alpha-beta Adam
+    iterations)."""
+    import torch
+    import vibecheck.verify_milp as vm
+    out = {}
+    for tag, seed, dims, eps, kw in RELU_BAB_CASES:
+        layers, xl, xh, w = relu_bab_problem(seed, dims, eps)
+        dt = torch.float32
+        gg = wk.mlp_gg(layers, 'cpu', dt)
+        xlt, xht = torch.as_tensor(xl), torch.as_tensor(xh)
+        sb = vz._ibp_forward_graph_batched(xlt[None], xht[None], gg, 'cpu', dt)
+        root = {L: (lo[0], hi[0]) for L, (lo, hi) in sb.items()}
+        closed, n, reason = vm._ibp_crown_bab(gg, xlt, xht, root, w, 0.0, 'cpu', dt,
+                                              **relu_bab_kwargs(kw, root))
+        print('relu_bab', tag, closed, n, reason)
+        out[f'{tag}_closed'] = np.array(bool(closed))
+        out[f'{tag}_n'] = np.array(int(n))
+        out[f'{tag}_reason'] = np.array(reason)
+    out['tags'] = np.array([c[0] for c in RELU_BAB_CASES])
+    _save('relu_bab', **out)
 
 
 def forward_cnn_gg(k1, b1, cb, W2, b2, W3, b3, fb, ins, dt):

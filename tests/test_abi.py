@@ -113,7 +113,24 @@ def test_install_rebinds_reference_functions():
     assert mods['vibecheck.verify_graph']._input_split_batched is bab._input_split_batched
     assert mods['vibecheck.verify_hybrid_acasxu']._simple_pgd_batched is pgd._simple_pgd_batched
     assert mods['vibecheck.pgd'].pgd_attack_general is pgd.pgd_attack_general
-    assert sum(len(v) for v in done.values()) == 11
+    assert sum(len(v) for v in done.values()) == 12
+
+
+def test_install_relu_bab_delegates_and_is_optional():
+    import types
+    from vibecheck_nn_b200 import install, relu_bab
+    mods = {name: types.ModuleType(name) for name in install.BINDINGS}
+    mods['vibecheck.verify_milp']._ibp_crown_bab = lambda *a, **k: 'reference'
+    install.install(mods)
+    fn = mods['vibecheck.verify_milp']._ibp_crown_bab
+    assert fn.__wrapped__ is relu_bab._ibp_crown_bab
+    # CPU and float64 calls are the reference's
+    assert fn(None, None, None, {}, None, 0.0, 'cpu', torch.float32, time_left=None) == 'reference'
+    assert fn(None, None, None, {}, None, 0.0, 'cuda', torch.float64, time_left=None) == 'reference'
+    # without the optional module (it needs a MILP solver) the rest still binds
+    del mods['vibecheck.verify_milp']
+    done = install.install(mods)
+    assert 'vibecheck.verify_milp' not in done and len(done) == len(install.BINDINGS) - 1
 
 
 def test_install_forward_delegates_outside_the_kernels():

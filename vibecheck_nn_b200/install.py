@@ -6,7 +6,9 @@ module attributes before ``verify_graph`` runs routes the input-split BaB
 through this package.  ``verify_hybrid_acasxu`` binds its PGD helpers at
 import (verify_hybrid_acasxu.py:31-34), so they are rebound there too; the
 general PGD attack is rebound in ``vibecheck.pgd``, which the reference's
-``_pgd_attack_general`` wrapper imports at call time.
+``_pgd_attack_general`` wrapper imports at call time; the MILP phase's
+ReLU-split BaB is rebound in ``vibecheck.verify_milp`` when that module
+imports (it needs gurobipy).
 """
 from __future__ import annotations
 
@@ -34,7 +36,15 @@ BINDINGS = {
     'vibecheck.pgd': {
         'pgd_attack_general': ('pgd', 'pgd_attack_general'),
     },
+    # the MILP phase calls its ReLU-split BaB through the module global
+    # (verify_milp.py:3874); float64 or CPU calls go to the reference's own
+    'vibecheck.verify_milp': {
+        '_ibp_crown_bab': ('relu_bab', '_ibp_crown_bab', 'delegate'),
+    },
 }
+# modules whose import needs an optional solver (verify_milp imports
+# gurobipy): without it the phase that would call the binding cannot run
+OPTIONAL = {'vibecheck.verify_milp'}
 
 
 def _delegating(impl, original):
@@ -63,7 +73,12 @@ def install(modules=None):
     for mod_name, names in BINDINGS.items():
         mod = (modules or {}).get(mod_name)
         if mod is None:
-            mod = importlib.import_module(mod_name)
+            try:
+                mod = importlib.import_module(mod_name)
+            except ImportError:
+                if mod_name in OPTIONAL:
+                    continue
+                raise
         for attr, spec in names.items():
             sub, fn = spec[0], spec[1]
             impl = getattr(importlib.import_module(f'{__package__}.{sub}'), fn)
