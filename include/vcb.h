@@ -95,6 +95,18 @@ int vcb_mlp_crown(const vcb_mlp* net, int32_t B,
  * (vcb_mlp_crown then reports the error). */
 size_t vcb_mlp_crown_workspace(const vcb_mlp* net, int32_t B, int32_t Q);
 
+/* Routing threshold of vcb_mlp_crown (no counterpart in the reference, which
+ * has one implementation): networks with input and hidden widths <= 63 and
+ * Q <= 16 are bounded by the tensor-core (tcgen05, 3xTF32) kernel when
+ * B >= the threshold, else by the fp32 SIMT kernel; results agree to fp32
+ * rounding.  Sets the threshold when value >= 0 and returns the previous
+ * one (process-wide). */
+int32_t vcb_mlp_crown_tc_min_batch(int32_t value);
+
+/* Which kernel vcb_mlp_crown runs for (net, B, Q) under the current
+ * threshold: 1 = tensor-core, 0 = SIMT. */
+int32_t vcb_mlp_crown_path(const vcb_mlp* net, int32_t B, int32_t Q);
+
 /* Allocation-free variant of vcb_mlp_crown (no counterpart in the
  * reference).  For callers that cannot allocate device memory while they
  * bound boxes -- a host application whose memory pool already owns the GPU,

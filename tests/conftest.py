@@ -38,6 +38,21 @@ def max_excess(a, b, rtol=1e-5, atol=1e-6):
     return float(np.max(np.abs(a - b) - (atol + rtol * np.abs(b)), initial=-1))
 
 
+def fp32_equivalent(ours, ref32, ref64, rtol=1e-5, atol=1e-6, slack=2.0):
+    """fp32-equivalence against exact (float64) arithmetic: every element of
+    ``ours`` within the parity tolerance of the float64 result plus ``slack``
+    times the float32 reference's own worst error on the same output.
+    Returns (ok, worst excess, worst error of ours, worst error of ref32)."""
+    ours = np.asarray(ours, np.float64)
+    ref32 = np.asarray(ref32, np.float64)
+    ref64 = np.asarray(ref64, np.float64)
+    ref_err = float(np.abs(ref32 - ref64).max(initial=0.0))
+    err = np.abs(ours - ref64)
+    excess = err - (atol + rtol * np.abs(ref64) + slack * ref_err)
+    worst = float(excess.max(initial=-1.0))
+    return worst <= 0, worst, float(err.max(initial=0.0)), ref_err
+
+
 @pytest.fixture(scope='session')
 def cuda_available():
     import torch

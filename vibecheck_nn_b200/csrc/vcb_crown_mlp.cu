@@ -24,6 +24,8 @@
 #include <mutex>
 
 #include "vcb_common.cuh"
+#include "vcb_crown_tc.cuh"
+#include "vcb_relu.cuh"
 
 namespace vcb {
 namespace {
@@ -65,39 +67,6 @@ __device__ __forceinline__ float4 ld4(const float* p) {
 // groups hit distinct bank groups.
 __device__ __forceinline__ int swz(int r, int k) {
   return ((((k >> 2) ^ ((r >> 2) & 7))) << 2) | (k & 3);
-}
-
-// CROWN slope rule (verify_zono_bnb.py:511-521), sign-encoded:
-//   x = dead ? -up_s : up_s,   y = active ? -0.0f : up_t.
-// The division only runs where lo < 0 < hi or in the dead corner where
-// lo + 1e-8 > 0 (elsewhere up_s is exactly 1 or 0).
-__device__ __forceinline__ float2 encode_slope(float lo, float hi) {
-  if (lo >= 0.f) return make_float2(1.f, -0.0f);  // active
-  const bool dead = hi <= 0.f;
-  const float ub_r = fmaxf(fmaxf(hi, 0.f), __fadd_rn(lo, 1e-8f));
-  if (ub_r == 0.f) return make_float2(-0.0f, 0.0f);  // dead, up_s = 0
-  const float up_s = __fdiv_rn(ub_r, __fsub_rn(ub_r, lo));
-  const float up_t = __fmul_rn(-lo, up_s);
-  return make_float2(dead ? -up_s : up_s, up_t);
-}
-
-struct Slope {
-  float pos, neg, icp;  // multiplier for e >= 0, for e < 0, intercept factor
-};
-
-// Decoded relaxation of one neuron; alpha (may be NULL) replaces the
-// min-area lower slope of unstable neurons (verify_zono_bnb.py:4420-4433).
-__device__ __forceinline__ Slope decode_slope(float2 v, const float* alpha) {
-  Slope s;
-  if (signbit(v.y)) {  // active: identity, no intercept
-    s.pos = 1.f; s.neg = 1.f; s.icp = 0.f;
-  } else if (signbit(v.x)) {  // dead (lower slope 0)
-    s.pos = 0.f; s.neg = -v.x; s.icp = v.y;
-  } else {  // unstable
-    s.pos = alpha ? __ldg(alpha) : (v.x > 0.5f ? 1.f : 0.f);
-    s.neg = v.x; s.icp = v.y;
-  }
-  return s;
 }
 
 __global__ void __launch_bounds__(kNT, 2)
@@ -599,12 +568,14 @@ extern "C" size_t vcb_mlp_crown_workspace(const vcb_mlp* net, int32_t B,
   using namespace vcb;
   if (!net || B <= 0) return 0;
   // Large enough for either mode (the caller-supplied-bounds mode may use a
-  // different tile size).
+  // different tile size) and, for networks the tensor-core kernel takes,
+  // for that kernel too (its routing threshold may change between calls).
   size_t bytes = 0;
   for (bool ibp : {true, false}) {
     Plan plan;
     if (plan_crown(net, B, Q, ibp, &plan) == VCB_OK) bytes = std::max(bytes, plan.ws_bytes);
   }
+  if (crown_tc_eligible(net, Q)) bytes = std::max(bytes, crown_tc_workspace(net, B));
   return bytes;
 }
 
@@ -634,6 +605,10 @@ int launch_crown(const vcb_mlp* net, int32_t B, const float* xl, const float* xh
     return fail(VCB_ERR_INVALID, "%s: Q>0 needs spec_W, spec_b and lb", who);
   if (sb_in_lo && (clamp_lo || sb_out_lo))
     return fail(VCB_ERR_INVALID, "%s: sb_in excludes clamps and sb_out", who);
+  if (!cap_grid && crown_tc_route(net, B, Q))
+    return crown_tc_launch(net, B, xl, xh, clamp_lo, clamp_hi, sb_in_lo, sb_in_hi, alpha, beta,
+                           Q, spec_W, spec_b, lb, A, acc, sb_out_lo, sb_out_hi, slots,
+                           slots_bytes, static_cast<cudaStream_t>(stream), who);
   Plan plan;
   int rc = plan_crown(net, B, Q, /*ibp=*/sb_in_lo == nullptr, &plan);
   if (rc) return rc;

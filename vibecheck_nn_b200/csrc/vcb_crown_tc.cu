@@ -1,0 +1,749 @@
+// Fused IBP forward + CROWN back-substitution on the 5th-generation tensor
+// cores, for ReLU MLPs whose input and hidden widths are at most 63 (the
+// ACAS-Xu-sized networks of the batched BaB).  Same contract and results, to
+// fp32 rounding, as crown_mlp_kernel; vcb_mlp_crown routes large batches here.
+//
+// Every contraction is a 128-row tcgen05.mma (kind::tf32) with error-
+// compensated 3xTF32 operands: both operands split into TF32 hi and lo parts
+// (each rounded to nearest); hi_A hi_B goes to one tensor-memory accumulator
+// and the corrections lo_A hi_B + hi_A lo_B to a second, added by the
+// epilogue with a round-to-nearest fp32 add.  The tensor cores' fp32
+// accumulation truncates inside each K = 8 step, so results carry about twice
+// the rounding noise of an fp32 dot product (fp32-class, not bit-parity with
+// the SIMT kernel).
+//   * IBP forward (verify_zono_bnb.py:1066-1153), one tile = 128 boxes:
+//     per fc layer  mid' = mid W^T  and  rad' = rad |W|^T  with the boxes as
+//     rows; the epilogue adds the bias, applies the clamps / crossing repair,
+//     writes the CROWN slopes (verify_zono_bnb.py:503-522) and forms the
+//     next layer's operands.
+//   * CROWN back-substitution (verify_zono_bnb.py:4270-5134): one chain of
+//     GEMMs per spec row q, rows = the tile's 128 boxes, coefficients
+//     ew' = relax(ew) W with the layer bias as an extra column of W^T (its
+//     column of the product is the bias dot); two chains run interleaved, so
+//     the tensor cores work on one chain while the epilogue relaxes the
+//     other.  The first step, spec row times the last layer, is the same for
+//     every box and is computed once per CTA.
+//   * Concretisation against the input box; optional A / acc outputs.
+//
+// Operands: the activations / coefficients (A) live in tensor memory, written
+// by the epilogue with tcgen05.st as tf32 hi / lo parts, in two slots (slot 0
+// = chain 0 / forward mid, slot 1 = chain 1 / forward rad); the weights (B)
+// are pre-split, pre-swizzled 64 x 64 images (W, |W| and [W^T; b] per layer,
+// built by crown_tc_images into the workspace) streamed through a 4-stage
+// shared-memory ring by one bulk copy each.  Tensor memory (512 columns): A
+// of slot s at 128 s (hi) and 128 s + 64 (lo), its accumulators at
+// 256 + 128 s (hi_A hi_B) and 256 + 128 s + 64 (corrections).
+//
+// Warps: 0-11 epilogue (warp w reads tensor-memory lanes 32 (w % 4) ..
+// 32 (w % 4) + 31, i.e. boxes of the tile, and 16-column chunks {0, 3}, {1}
+// or {2} for w / 4 = 0, 1, 2), warp 12 loads the weights and issues the MMAs
+// (13 warps leave 128 registers per thread).  The ReLU slopes of a tile go
+// to the CTA's workspace slot in neuron-major order ([layer][neuron][box],
+// coalesced across a warp) and are read back by the thread that wrote them.
+// Every wait is bounded; on expiry the kernel stops, writes NaN to the lower
+// bounds (and A / acc / sb outputs) of every box it had not finished -- a NaN
+// bound proves nothing -- and sets the workspace error word.
+#include <algorithm>
+#include <atomic>
+#include <type_traits>
+
+#include "vcb_common.cuh"
+#include "vcb_crown_tc.cuh"
+#include "vcb_relu.cuh"
+#include "vcb_tcgen05.cuh"
+
+namespace vcb {
+namespace {
+
+using namespace tc5;
+
+constexpr int kTB = 128;                   // boxes per tile (MMA rows)
+constexpr int kEpi = 12;                   // epilogue warps
+constexpr int kCtlWarp = kEpi;             // weight loads + MMA issue
+constexpr int kThreads = (kEpi + 1) * 32;  // 416: at most 4 warps per SM sub-partition
+constexpr int kW = 64;                     // padded operand width
+constexpr int kMaxWidth = 63;              // widest hidden / input layer
+constexpr int kBlk = kW * 128;             // 8 KB: 64 rows x 32 tf32 (one swizzle column)
+constexpr int kHalf = 2 * kBlk;            // 16 KB: one tf32 part of a 64 x 64 image
+constexpr int kImg = 2 * kHalf;            // hi + lo
+constexpr int kStages = 4;
+constexpr int kMaxQ = 16;
+constexpr unsigned kSpin = 1u << 24;
+constexpr unsigned kSpinSleep = 1u << 20;  // polls of at most ~1 us each
+constexpr int kSmem = 1024 + kStages * kImg + (kMaxQ * kW + VCB_MAX_FC * kW + 2 * 2 * 4 * kTB) * 4;
+
+// Batches of the input-split BaB (<= 4096 boxes) stay on the SIMT kernel, whose
+// rounding the leaf-count parity of the BaB tests is pinned to.
+std::atomic<int> g_min_batch{16384};
+
+struct TcParams {
+  int n_fc;
+  int dims[VCB_MAX_FC + 1];
+  const float* W;
+  const float* b;
+  long long w_goff[VCB_MAX_FC];
+  int b_goff[VCB_MAX_FC];
+  long long relu_goff[VCB_MAX_FC];
+  int sl_off[VCB_MAX_FC];  // float2 offset of relu layer L in a slot
+  long long slot_f2;       // float2 per CTA slot
+  const uint8_t* img;      // (n_fc - 1) x 3 images of kImg bytes
+  int B, Q, ntiles, npass;
+  const float *xl, *xh, *clo, *chi, *sblo, *sbhi, *alpha, *beta, *specW, *specb;
+  float *lb, *A, *accout, *sbolo, *sbohi;
+  float2* slopes;
+  int* err;
+};
+
+__host__ __device__ inline int pad16(int n) { return (n + 15) & ~15; }
+
+// Weight images, one thread per (image, row, k).  Image 3 l + 0: W_l
+// (rows = outputs, K = inputs), + 1: |W_l|, + 2: [W_l^T; b_l] (rows = inputs
+// then the bias row, K = outputs).  Each is split into tf32 hi (first 16 KB)
+// and lo, laid out as two 64-row x 32-column blocks with the 128-byte swizzle
+// of a K-major tcgen05 operand.
+__global__ void crown_tc_images(const TcParams p) {
+  const int nimg = 3 * (p.n_fc - 1);
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= nimg * kW * kW) return;
+  const int im = idx / (kW * kW), n = (idx / kW) % kW, k = idx % kW;
+  const int l = im / 3, use = im % 3;
+  const int nin = p.dims[l], nout = p.dims[l + 1];
+  const float* Wl = p.W + p.w_goff[l];
+  float v = 0.f;
+  if (use < 2) {
+    if (n < nout && k < nin) v = Wl[(long long)n * nin + k];
+    if (use == 1) v = fabsf(v);
+  } else if (k < nout) {
+    if (n < nin) v = Wl[(long long)k * nin + n];
+    else if (n == nin) v = p.b[p.b_goff[l] + k];
+  }
+  uint32_t h, lo;
+  tf32_split_rn(v, h, lo);
+  const int off = (k >> 5) * kBlk + (n >> 3) * 1024 + (n & 7) * 128 +
+                  ((((k & 31) >> 2) ^ (n & 7)) << 4) + (k & 3) * 4;
+  uint8_t* base = const_cast<uint8_t*>(p.img) + (long long)im * kImg;
+  *reinterpret_cast<uint32_t*>(base + off) = h;
+  *reinterpret_cast<uint32_t*>(base + kHalf + off) = lo;
+}
+
+// A B^T over `ksteps` K steps of 8 with 3xTF32: A in tensor memory (hi at
+// column a, lo at a + 64), B a weight image in shared memory (hi at b, lo at
+// b + kHalf, 8 KB per 32-column block); hi_A hi_B into accumulator d,
+// lo_A hi_B + hi_A lo_B into d + 64.
+__device__ __forceinline__ void gemm_ts(uint32_t d, uint32_t a, uint32_t b, int ksteps,
+                                        uint32_t idesc) {
+  for (int j = 0; j < ksteps; ++j) {
+    const uint32_t bo = (uint32_t)((j >> 2) * kBlk + (j & 3) * 32);
+    const uint64_t bh = sw128_desc(b + bo), bl = sw128_desc(b + kHalf + bo);
+    mma_tf32_ts(d + kW, a + kW + 8 * j, bh, idesc, j > 0 ? 1u : 0u);
+    mma_tf32_ts(d + kW, a + 8 * j, bl, idesc, 1u);
+    mma_tf32_ts(d, a + 8 * j, bh, idesc, j > 0 ? 1u : 0u);
+  }
+}
+
+// Publish this warp's tensor-memory stores and completed accumulator loads
+// to the MMA issuer.
+__device__ __forceinline__ void publish(uint64_t* bar) {
+  tmem_wait_st();
+  fence_before_sync();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
+__device__ __forceinline__ float2* slot_base(const TcParams& p) {
+  return p.slopes + (long long)blockIdx.x * p.slot_f2;
+}
+
+// Split NC (8 or 16) finite values and store the hi / lo parts at
+// tensor-memory columns taddr and taddr + 64 of this warp's lanes.
+template <int NC>
+__device__ __forceinline__ void store_operand(uint32_t taddr, const float (&v)[NC]) {
+  uint32_t h[NC], l[NC];
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    const uint32_t u = (__float_as_uint(v[j]) + 0x1000u) & 0xFFFFE000u;
+    const float r = __fsub_rn(v[j], __uint_as_float(u));
+    h[j] = u;
+    l[j] = (__float_as_uint(r) + 0x1000u) & 0xFFFFE000u;
+  }
+  if constexpr (NC == 16) {
+    tmem_st16(taddr, h);
+    tmem_st16(taddr + kW, l);
+  } else {
+    tmem_st8(taddr, h);
+    tmem_st8(taddr + kW, l);
+  }
+}
+
+// Sum of the two accumulators (hi_A hi_B and corrections) at tensor-memory
+// column taddr and taddr + 64, NC columns.
+template <int NC>
+__device__ __forceinline__ void load_acc(uint32_t taddr, float (&v)[NC]) {
+  uint32_t a[NC], e[NC];
+  if constexpr (NC == 16) {
+    tmem_ld16(taddr, a);
+    tmem_ld16(taddr + kW, e);
+  } else {
+    tmem_ld8(taddr, a);
+    tmem_ld8(taddr + kW, e);
+  }
+  tmem_wait_ld(a, e);
+#pragma unroll
+  for (int j = 0; j < NC; ++j) v[j] = __fadd_rn(__uint_as_float(a[j]), __uint_as_float(e[j]));
+}
+
+using C8 = std::integral_constant<int, 8>;
+using C16 = std::integral_constant<int, 16>;
+
+// The 12 epilogue warps: warp w owns the tile's boxes 32 (w % 4) + lane
+// (tensor-memory lanes) and the 16-column operand chunks {0, 3}, {1} or {2}
+// (w / 4 = 0, 1, 2; the light fourth chunk shares a warp, which balances
+// 50-wide layers).  kPlain: no alpha, beta, clamps or sb outputs (the common
+// case, without their guards).  Returns false when a wait expired or another
+// role failed; then every box of this CTA from the unfinished tile on gets
+// NaN outputs.
+template <bool kPlain>
+__device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float2* slot,
+                                      const float* sV, const float* sBias,
+                                      float* sRow, uint64_t* a_ready, uint64_t* acc_ready,
+                                      uint64_t* rows_ready, const volatile int* vfailed) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qd = warp & 3, gi = warp >> 2;
+  const int row = 32 * qd + lane;
+  const uint32_t tl = tmem + ((uint32_t)(32 * qd) << 16);
+  const int nck = gi == 0 ? 2 : 1;  // chunks of this warp
+  auto chunk_c0 = [&](int k) { return gi == 0 ? 48 * k : 16 * gi; };
+  const int nfc = p.n_fc, Q = p.Q, n0 = p.dims[0];
+  const bool fwd = p.sblo == nullptr;
+  unsigned uacc[2] = {0, 0}, urows = 0;
+  bool ok = true;
+  auto wait_acc = [&](int c) {
+    if (!mbar_wait_sleep(&acc_ready[c], uacc[c] & 1, kSpinSleep, vfailed)) return false;
+    ++uacc[c];
+    fence_after_sync();
+    return true;
+  };
+  int tile = blockIdx.x;
+  for (; tile < p.ntiles; tile += gridDim.x) {
+    const int box = tile * kTB + row;
+    const bool valid = box < p.B;
+    const bool full = (tile + 1) * kTB <= p.B;  // every row of the tile is a box
+    if (fwd) {
+      // ---- layer-0 operands: centre and radius of the box
+      for (int k = 0; k < nck; ++k) {
+        const int c0 = chunk_c0(k);
+        if (c0 >= n0) continue;
+        float m[16], r[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int i = c0 + j;
+          m[j] = r[j] = 0.f;
+          if (i < n0 && valid) {
+            const float lo = __ldg(p.xl + (long long)box * n0 + i);
+            const float hi = __ldg(p.xh + (long long)box * n0 + i);
+            m[j] = __fmul_rn(__fadd_rn(lo, hi), 0.5f);
+            r[j] = __fmul_rn(__fsub_rn(hi, lo), 0.5f);
+          }
+        }
+        store_operand<16>(tl + c0, m);
+        store_operand<16>(tl + 128 + c0, r);
+      }
+      publish(&a_ready[0]);
+      // ---- fc layers 0 .. nfc-2: bounds and slopes of relu layer l
+      for (int l = 0; l < nfc - 1; ++l) {
+        if (!(ok = wait_acc(0))) break;
+        const int nout = p.dims[l + 1];
+        const bool last = l == nfc - 2;
+        const long long gi0 = p.relu_goff[l] + (long long)box * nout;
+        float2* sl = slot + p.sl_off[l] + row;
+        // one chunk of NC output columns starting at c0
+        auto chunk = [&](auto nc, int c0) {
+          constexpr int NC = decltype(nc)::value;
+          float mc[NC], rc[NC];
+          load_acc<NC>(tl + 256 + c0, mc);
+          load_acc<NC>(tl + 384 + c0, rc);
+          const float* bias = sBias + l * kW + c0;
+#pragma unroll
+          for (int j = 0; j < NC; ++j) {
+            const int o = c0 + j;
+            const float mid = __fadd_rn(mc[j], bias[j]);
+            float lo = __fsub_rn(mid, rc[j]);
+            float hi = __fadd_rn(mid, rc[j]);
+            if (!kPlain && p.clo && valid && o < nout) {
+              lo = fmaxf(lo, __ldg(p.clo + gi0 + o));
+              hi = fminf(hi, __ldg(p.chi + gi0 + o));
+            }
+            hi = fmaxf(hi, lo);
+            if (!kPlain && p.sbolo && valid && o < nout) {
+              p.sbolo[gi0 + o] = lo;
+              p.sbohi[gi0 + o] = hi;
+            }
+            if (o < nout) sl[o * kTB] = encode_slope(lo, hi);
+            const float lc = fmaxf(lo, 0.f), hc = fmaxf(hi, 0.f);
+            mc[j] = o < nout ? __fmul_rn(__fadd_rn(lc, hc), 0.5f) : 0.f;
+            rc[j] = o < nout ? __fmul_rn(__fsub_rn(hc, lc), 0.5f) : 0.f;
+          }
+          if (!last) {
+            store_operand<NC>(tl + c0, mc);
+            store_operand<NC>(tl + 128 + c0, rc);
+          }
+        };
+        for (int k = 0; k < nck; ++k) {
+          const int c0 = chunk_c0(k);
+          if (c0 >= nout) continue;
+          if (nout - c0 <= 8)
+            chunk(C8{}, c0);
+          else
+            chunk(C16{}, c0);
+        }
+        if (!last) publish(&a_ready[0]);
+      }
+      if (!ok) break;
+    } else {
+      // ---- caller-supplied intermediate bounds: slopes only
+      for (int L = 0; L < nfc - 1; ++L) {
+        const int n = p.dims[L + 1];
+        const long long gi0 = p.relu_goff[L] + (long long)box * n;
+        float2* sl = slot + p.sl_off[L] + row;
+        for (int k = 0; k < nck; ++k) {
+          const int c0 = chunk_c0(k);
+          for (int i = c0; i < min(n, c0 + 16); ++i)
+            sl[i * kTB] = valid ? encode_slope(__ldg(p.sblo + gi0 + i), __ldg(p.sbhi + gi0 + i))
+                                : make_float2(1.f, -0.0f);
+        }
+      }
+    }
+    // ---- CROWN back-substitution, spec rows in pairs
+    for (int pass = 0; ok && pass < p.npass; ++pass) {
+      const int nch = min(2, Q - 2 * pass);
+      float racc[2] = {0.f, 0.f}, conc[2] = {0.f, 0.f};
+      // step l relaxes the product of fc layer l with relu layer l - 1; the
+      // first step (l = nfc - 1) takes its product from the spec table
+      for (int l = nfc - 1; l >= 0; --l) {
+        const int nin = p.dims[l];
+        const int L = l - 1;
+        const float2* sl = slot + (L >= 0 ? p.sl_off[L] : 0) + row;
+        const long long ri = L >= 0 ? p.relu_goff[L] + (long long)box * nin : 0;
+        const float* arow = (!kPlain && L >= 0 && p.alpha && valid) ? p.alpha + ri : nullptr;
+        const float* brow = (!kPlain && L >= 0 && p.beta && valid) ? p.beta + ri : nullptr;
+        for (int c = 0; c < nch; ++c) {
+          const int q = 2 * pass + c;
+          if (l < nfc - 1 && !(ok = wait_acc(c))) break;
+          // one chunk of NC columns starting at c0 (neurons and / or the bias column)
+          auto chunk = [&](auto nc, int c0) {
+            constexpr int NC = decltype(nc)::value;
+            float v[NC];
+            if (l == nfc - 1) {
+#pragma unroll
+              for (int j = 0; j < NC; ++j) v[j] = sV[q * kW + c0 + j];
+            } else {
+              load_acc<NC>(tl + 256 + 128 * c + c0, v);
+            }
+            if (!full && !valid) {
+#pragma unroll
+              for (int j = 0; j < NC; ++j) v[j] = 0.f;
+            }
+            const int bc = nin - c0;  // bias column within the chunk
+            float bj = 0.f;
+            if (bc < NC) {
+#pragma unroll
+              for (int j = 0; j < NC; ++j)
+                if (j == bc) bj = v[j];
+            }
+            if (L >= 0) {
+              float2 sv[NC];  // slopes, zero beyond the layer width
+#pragma unroll
+              for (int j = 0; j < NC; ++j)
+                sv[j] = c0 + j < nin ? sl[(c0 + j) * kTB] : make_float2(0.f, 0.f);
+              float pj = 0.f;
+#pragma unroll
+              for (int j = 0; j < NC; ++j) {
+                const float x = v[j];
+                if (kPlain) {
+                  // slope (0, 0) beyond the layer width gives 0 and no intercept
+                  const float pos = sv[j].x > 0.5f ? 1.f : 0.f;
+                  const float mlt = x < 0.f ? fabsf(sv[j].x) : pos;
+                  v[j] = __fmul_rn(x, mlt);
+                  pj = fmaf(fminf(x, 0.f), sv[j].y, pj);
+                } else {
+                  const int i = c0 + j;
+                  v[j] = 0.f;
+                  if (i < nin) {
+                    const Slope s = decode_slope(sv[j], arow ? arow + i : nullptr);
+                    const float mlt = x < 0.f ? s.neg : s.pos;
+                    pj = fmaf(fminf(x, 0.f), s.icp, pj);
+                    v[j] = __fmul_rn(x, mlt);
+                    if (brow) v[j] = __fadd_rn(v[j], __ldg(brow + i));
+                  }
+                }
+              }
+              store_operand<NC>(tl + 128 * c + c0, v);
+              racc[c] = __fadd_rn(racc[c], __fadd_rn(bj, pj));
+            } else {
+              // input layer: concretise against the box
+              float s1 = 0.f, s2 = 0.f;
+              if (valid) {
+                for (int i = c0; i < min(nin, c0 + NC); ++i) {
+                  float x = 0.f;
+#pragma unroll
+                  for (int j = 0; j < NC; ++j)
+                    if (c0 + j == i) x = v[j];
+                  s1 = fmaf(fmaxf(x, 0.f), __ldg(p.xl + (long long)box * n0 + i), s1);
+                  s2 = fmaf(fminf(x, 0.f), __ldg(p.xh + (long long)box * n0 + i), s2);
+                  if (p.A) p.A[((long long)box * Q + q) * n0 + i] = x;
+                }
+              }
+              racc[c] = __fadd_rn(racc[c], bj);
+              conc[c] = __fadd_rn(conc[c], __fadd_rn(s1, s2));
+            }
+          };
+          for (int k = 0; k < nck; ++k) {
+            const int c0 = chunk_c0(k);
+            if (c0 > nin) continue;  // no neurons and no bias column here
+            if (nin + 1 - c0 <= 8)
+              chunk(C8{}, c0);
+            else
+              chunk(C16{}, c0);
+          }
+          if (L >= 0) publish(&a_ready[c]);
+        }
+        if (!ok) break;
+      }
+      if (!ok) break;
+      // ---- combine the three column warps of every box
+      for (int c = 0; c < nch; ++c) {
+        sRow[((c * 2 + 0) * 4 + gi) * kTB + row] = racc[c];
+        sRow[((c * 2 + 1) * 4 + gi) * kTB + row] = conc[c];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(rows_ready);
+      if (gi == 0) {
+        if (!(ok = mbar_wait_sleep(rows_ready, urows & 1, kSpinSleep, vfailed))) break;
+        for (int c = 0; c < nch && valid; ++c) {
+          const int q = 2 * pass + c;
+          const float* ra = sRow + (c * 2 + 0) * 4 * kTB + row;
+          const float* co = sRow + (c * 2 + 1) * 4 * kTB + row;
+          float a = __ldg(p.specb + q);
+          float t = 0.f;
+#pragma unroll
+          for (int g = 0; g < kEpi / 4; ++g) {
+            a = __fadd_rn(a, ra[g * kTB]);
+            t = __fadd_rn(t, co[g * kTB]);
+          }
+          const long long go = (long long)box * Q + q;
+          p.lb[go] = __fadd_rn(a, t);
+          if (p.accout) p.accout[go] = a;
+        }
+      }
+      ++urows;
+    }
+    if (!ok) break;
+  }
+  if (ok) return true;
+  // NaN for every box of this CTA from the unfinished tile on
+  const float nan = __int_as_float(0x7fffffff);
+  for (; tile < p.ntiles; tile += gridDim.x) {
+    const int box = tile * kTB + row;
+    if (box >= p.B || gi != 0) continue;
+    for (int q = 0; q < Q; ++q) {
+      p.lb[(long long)box * Q + q] = nan;
+      if (p.accout) p.accout[(long long)box * Q + q] = nan;
+      if (p.A)
+        for (int i = 0; i < n0; ++i) p.A[((long long)box * Q + q) * n0 + i] = nan;
+    }
+    if (p.sbolo)
+      for (int L = 0; L < nfc - 1; ++L) {
+        const int n = p.dims[L + 1];
+        for (int i = 0; i < n; ++i) {
+          p.sbolo[p.relu_goff[L] + (long long)box * n + i] = nan;
+          p.sbohi[p.relu_goff[L] + (long long)box * n + i] = nan;
+        }
+      }
+  }
+  return false;
+}
+
+template <bool kPlain>
+__global__ void __launch_bounds__(kThreads, 1) crown_tc_kernel(const __grid_constant__ TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* sV = reinterpret_cast<float*>(ring + kStages * kImg);  // kMaxQ x kW
+  float* sBias = sV + kMaxQ * kW;                               // VCB_MAX_FC x kW
+  float* sRow = sBias + VCB_MAX_FC * kW;                        // [chain][kind][chunk][box]
+  __shared__ __align__(8) uint64_t w_full[kStages], w_empty[kStages];
+  __shared__ __align__(8) uint64_t a_ready[2], acc_ready[2], rows_ready, done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int failed;
+  volatile int* vfailed = &failed;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nfc = p.n_fc;
+  const int Q = p.Q;
+  const bool fwd = p.sblo == nullptr;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 1);
+    }
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(&a_ready[c], kEpi);
+      mbar_init(&acc_ready[c], 1);
+    }
+    mbar_init(&rows_ready, kEpi);
+    mbar_init(&done, 1);
+    failed = 0;
+    mbar_fence_init();
+  }
+  for (int idx = threadIdx.x; idx < (nfc - 1) * kW; idx += kThreads) {
+    const int l = idx / kW, o = idx % kW;
+    sBias[idx] = o < p.dims[l + 1] ? __ldg(p.b + p.b_goff[l] + o) : 0.f;
+  }
+  {  // spec rows times the last fc layer, bias dot in column dims[nfc - 1]
+    const int nprev = p.dims[nfc - 1], nL = p.dims[nfc];
+    const float* Wg = p.W + p.w_goff[nfc - 1];
+    const float* bg = p.b + p.b_goff[nfc - 1];
+    for (int idx = threadIdx.x; idx < Q * kW; idx += kThreads) {
+      const int q = idx / kW, c = idx % kW;
+      float s = 0.f;
+      if (c <= nprev)
+        for (int o = 0; o < nL; ++o)
+          s = fmaf(__ldg(p.specW + q * nL + o),
+                   c < nprev ? __ldg(Wg + (long long)o * nprev + c) : __ldg(bg + o), s);
+      sV[idx] = s;
+    }
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == kCtlWarp) {
+    // ----------------------- control: weight loads and MMA issue (lane 0)
+    if (lane == 0) {
+      // image sequence of one tile: forward (W_l, |W_l|) for l = 0 .. nfc-2,
+      // then per pass [W_l^T; b_l] for l = nfc-2 .. 0
+      const unsigned nl = (unsigned)(nfc - 1);
+      const unsigned fwdlen = fwd ? 2 * nl : 0;
+      const unsigned T = fwdlen + (unsigned)p.npass * nl;
+      const unsigned ntl =
+          blockIdx.x < (unsigned)p.ntiles ? (p.ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+      const unsigned total = ntl * T;
+      unsigned issued = 0, used = 0, ua[2] = {0, 0};
+      bool ok = true;
+      auto image_of = [&](unsigned n) {
+        const unsigned t = n % T;
+        if (t < fwdlen) return 3 * (t >> 1) + (t & 1);
+        return 3 * (nl - 1 - (t - fwdlen) % nl) + 2;
+      };
+      // keep the ring full; a stage is reloaded once the MMAs reading it completed
+      auto refill = [&]() {
+        while (issued < total && issued < used + kStages) {
+          const int s = issued % kStages;
+          if (issued >= kStages &&
+              !mbar_wait(&w_empty[s], ((issued / kStages) - 1) & 1, kSpin, vfailed))
+            return false;
+          mbar_expect_tx(&w_full[s], kImg);
+          bulk_load(ring + s * kImg, p.img + (long long)image_of(issued) * kImg, kImg, &w_full[s]);
+          ++issued;
+        }
+        return true;
+      };
+      auto take = [&](int& s) {
+        s = used % kStages;
+        if (!mbar_wait(&w_full[s], (used / kStages) & 1, kSpin, vfailed)) return false;
+        ++used;
+        return true;
+      };
+      auto wait_a = [&](int c) {
+        if (!mbar_wait_sleep(&a_ready[c], ua[c] & 1, kSpinSleep, vfailed)) return false;
+        ++ua[c];
+        fence_after_sync();
+        return true;
+      };
+      ok = refill();
+      for (int tile = blockIdx.x; ok && tile < p.ntiles; tile += gridDim.x) {
+        if (fwd) {
+          for (int l = 0; ok && l < nfc - 1; ++l) {
+            int sw, sa;
+            if (!(ok = wait_a(0) && take(sw) && take(sa))) break;
+            const int ks = (p.dims[l] + 7) >> 3;
+            const uint32_t id = idesc_tf32(kTB, pad16(p.dims[l + 1]));
+            gemm_ts(tmem + 256, tmem, smem_u32(ring + sw * kImg), ks, id);
+            gemm_ts(tmem + 384, tmem + 128, smem_u32(ring + sa * kImg), ks, id);
+            mma_commit(&w_empty[sw]);
+            mma_commit(&w_empty[sa]);
+            mma_commit(&acc_ready[0]);
+            ok = refill();
+          }
+        }
+        for (int pass = 0; ok && pass < p.npass; ++pass) {
+          for (int l = nfc - 2; ok && l >= 0; --l) {
+            int st;
+            if (!(ok = take(st))) break;
+            const int ks = (p.dims[l + 1] + 7) >> 3;
+            const uint32_t id = idesc_tf32(kTB, pad16(p.dims[l] + 1));
+            for (int c = 0; c < 2 && 2 * pass + c < Q; ++c) {
+              if (!(ok = wait_a(c))) break;
+              gemm_ts(tmem + 256 + 128 * c, tmem + 128 * c, smem_u32(ring + st * kImg), ks, id);
+              mma_commit(&acc_ready[c]);
+            }
+            mma_commit(&w_empty[st]);
+            if (ok) ok = refill();
+          }
+        }
+      }
+      if (!ok) failed = 1;
+      // every MMA issued above completes before tensor memory is freed, and
+      // every copy issued lands before the CTA exits
+      mma_commit(&done);
+      if (!mbar_wait(&done, 0, kSpin)) failed = 1;
+      for (unsigned k = used; k < issued; ++k)
+        if (!mbar_wait(&w_full[k % kStages], (k / kStages) & 1, kSpin)) failed = 1;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    if (!epilogue<kPlain>(p, tmem, slot_base(p), sV, sBias, sRow, a_ready, acc_ready,
+                          &rows_ready, vfailed))
+      failed = 1;
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  if (threadIdx.x == 0 && failed) atomicExch(p.err, 1);
+}
+
+bool eligible_dims(const vcb_mlp* net) {
+  const int nfc = net->n_fc;
+  if (nfc < 2 || nfc > VCB_MAX_FC) return false;
+  for (int l = 0; l < nfc; ++l)
+    if (net->dims[l] < 1 || net->dims[l] > kMaxWidth) return false;
+  return net->dims[nfc] >= 1;
+}
+
+struct TcPlan {
+  int grid;
+  long long slot_f2;
+  size_t img_bytes, ws_bytes;
+};
+
+TcPlan plan_tc(const vcb_mlp* net, int B) {
+  TcPlan t;
+  const int ntiles = (B + kTB - 1) / kTB;
+  t.grid = std::max(1, std::min(ntiles, sm_count()));
+  long long slot = 0;
+  for (int L = 0; L < net->n_fc - 1; ++L) slot += (long long)net->dims[L + 1] * kTB;
+  t.slot_f2 = slot;
+  t.img_bytes = (size_t)3 * (net->n_fc - 1) * kImg;
+  // error word, then the images, then the slope slots
+  t.ws_bytes = 256 + t.img_bytes + (size_t)t.grid * slot * sizeof(float2);
+  return t;
+}
+
+}  // namespace
+
+bool crown_tc_eligible(const vcb_mlp* net, int Q) {
+  return net && eligible_dims(net) && Q >= 0 && Q <= kMaxQ;
+}
+
+bool crown_tc_route(const vcb_mlp* net, int B, int Q) {
+  return crown_tc_eligible(net, Q) && B >= g_min_batch.load(std::memory_order_relaxed);
+}
+
+size_t crown_tc_workspace(const vcb_mlp* net, int B) {
+  if (!net || B <= 0 || !eligible_dims(net)) return 0;
+  return plan_tc(net, B).ws_bytes;
+}
+
+int crown_tc_launch(const vcb_mlp* net, int32_t B, const float* xl, const float* xh,
+                    const float* clamp_lo, const float* clamp_hi, const float* sb_in_lo,
+                    const float* sb_in_hi, const float* alpha, const float* beta, int32_t Q,
+                    const float* spec_W, const float* spec_b, float* lb, float* A, float* acc,
+                    float* sb_out_lo, float* sb_out_hi, void* ws, size_t ws_bytes,
+                    cudaStream_t st, const char* who) {
+  const TcPlan plan = plan_tc(net, B);
+  if (!ws || ws_bytes < plan.ws_bytes)
+    return fail(VCB_ERR_INVALID, "%s: workspace of %zu bytes needed (got %zu)", who,
+                plan.ws_bytes, ws_bytes);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0)
+    return fail(VCB_ERR_INVALID, "%s: workspace must be 256-byte aligned", who);
+  TcParams p{};
+  const int nfc = net->n_fc;
+  p.n_fc = nfc;
+  long long woff = 0, roff = 0;
+  int boff = 0, soff = 0;
+  for (int l = 0; l <= nfc; ++l) p.dims[l] = net->dims[l];
+  for (int l = 0; l < nfc; ++l) {
+    p.w_goff[l] = woff;
+    p.b_goff[l] = boff;
+    woff += (long long)net->dims[l] * net->dims[l + 1];
+    boff += net->dims[l + 1];
+    if (l < nfc - 1) {
+      p.relu_goff[l] = roff;
+      roff += (long long)B * net->dims[l + 1];
+      p.sl_off[l] = soff;
+      soff += net->dims[l + 1] * kTB;
+    }
+  }
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  p.W = net->W;
+  p.b = net->b;
+  p.err = reinterpret_cast<int*>(base);
+  p.img = base + 256;
+  p.slopes = reinterpret_cast<float2*>(base + 256 + plan.img_bytes);
+  p.slot_f2 = plan.slot_f2;
+  p.B = B;
+  p.Q = Q;
+  p.ntiles = (B + kTB - 1) / kTB;
+  p.npass = (Q + 1) / 2;
+  p.xl = xl;
+  p.xh = xh;
+  p.clo = clamp_lo;
+  p.chi = clamp_hi;
+  p.sblo = sb_in_lo;
+  p.sbhi = sb_in_hi;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.specW = spec_W;
+  p.specb = spec_b;
+  p.lb = lb;
+  p.A = A;
+  p.accout = acc;
+  p.sbolo = sb_out_lo;
+  p.sbohi = sb_out_hi;
+  cudaError_t e = cudaMemsetAsync(p.err, 0, sizeof(int), st);
+  if (e != cudaSuccess) return cuda_fail(e, who);
+  const int nimg = 3 * (nfc - 1) * kW * kW;
+  crown_tc_images<<<(nimg + 255) / 256, 256, 0, st>>>(p);
+  int rc = check_launch(who);
+  if (rc) return rc;
+  const bool plain = !alpha && !beta && !clamp_lo && !sb_out_lo;
+  const void* fn = plain ? reinterpret_cast<const void*>(crown_tc_kernel<true>)
+                         : reinterpret_cast<const void*>(crown_tc_kernel<false>);
+  rc = ensure_smem(fn, kSmem);
+  if (rc) return rc;
+  if (plain)
+    crown_tc_kernel<true><<<plan.grid, kThreads, kSmem, st>>>(p);
+  else
+    crown_tc_kernel<false><<<plan.grid, kThreads, kSmem, st>>>(p);
+  return check_launch(who);
+}
+
+}  // namespace vcb
+
+extern "C" int32_t vcb_mlp_crown_path(const vcb_mlp* net, int32_t B, int32_t Q) {
+  return vcb::crown_tc_route(net, B, Q) ? 1 : 0;
+}
+
+extern "C" int32_t vcb_mlp_crown_tc_min_batch(int32_t value) {
+  const int32_t prev = vcb::g_min_batch.load();
+  if (value >= 0) vcb::g_min_batch.store(value);
+  return prev;
+}

@@ -35,6 +35,7 @@
 
 #include "vcb_common.cuh"
 #include "vcb_tc.cuh"
+#include "vcb_tcgen05.cuh"
 
 namespace vcb {
 namespace {
@@ -51,40 +52,9 @@ constexpr unsigned kSpinLimit = 1u << 22;      // pipeline waits (a stage is mic
 constexpr unsigned kDoneSpinLimit = 1u << 27;  // the epilogue waits out the whole mainloop
 
 // instruction descriptor: D f32, A/B tf32, both K-major, N = 128, M = 128
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) |
-                            ((uint32_t)(TC_BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+constexpr uint32_t kIdesc = tc5::idesc_tf32(TC_BM, TC_BN);
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-// Wait for the phase with the given parity to complete; false on expiry.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity,
-                                          unsigned limit = kSpinLimit) {
-  const uint32_t a = smem_u32(bar);
-  for (unsigned i = 0; i < limit; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
-}
+using namespace tc5;
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y) {
@@ -95,45 +65,10 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// K-major operand tile with 128-byte swizzle: rows of 128 B, 8-row groups
-// 1024 B apart (SBO), leading offset unused, descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;
-  d |= (uint64_t)(1024 >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
+// D (tensor memory) (+)= A B^T for one K step of the 128 x 128 tile.
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db,
                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  mma_tf32_ss(tmem_d, da, db, kIdesc, accumulate);
 }
 
 struct TcArgs {
@@ -168,7 +103,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     mbar_init(&done, 1);
     failed = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_fence_init();
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -186,7 +121,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % TC_STAGES;
         const unsigned round = kb / TC_STAGES;
-        if (kb >= TC_STAGES && !mbar_wait(&empty[s], (round - 1) & 1)) {
+        if (kb >= TC_STAGES && !mbar_wait(&empty[s], (round - 1) & 1, kSpinLimit)) {
           failed = 1;
           break;
         }
@@ -203,8 +138,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % TC_STAGES;
         const int q = kb % NBUF;
-        if (!mbar_wait(&full[s], (kb / TC_STAGES) & 1) ||
-            (kb >= NBUF && !mbar_wait(&acc_free[q], ((kb / NBUF) - 1) & 1))) {
+        if (!mbar_wait(&full[s], (kb / TC_STAGES) & 1, kSpinLimit) ||
+            (kb >= NBUF && !mbar_wait(&acc_free[q], ((kb / NBUF) - 1) & 1, kSpinLimit))) {
           failed = 1;
           break;
         }
@@ -241,14 +176,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
       for (int c0 = 0; c0 < TC_BN; c0 += 16) {
-        float v[16];
+        uint32_t v[16];
         tmem_ld16(lane_addr + q * TC_BN + c0, v);
+        tmem_wait_ld(v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], v[j]);
+        for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], __uint_as_float(v[j]));
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_free[q])) : "memory");
+      if (lane == 0) mbar_arrive(&acc_free[q]);
     }
     const int row = m0 + warp * 32 + lane;
     if (row < a.M && !failed) {
@@ -274,12 +210,10 @@ __global__ void tf32_split_kernel(long long n, const float* __restrict__ x, floa
                                   float* __restrict__ lo) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
-    const float v = x[i];
-    const uint32_t u = __float_as_uint(v);
-    const bool finite = (u & 0x7F800000u) != 0x7F800000u;
-    const float h = finite ? __uint_as_float((u + 0x1000u) & 0xFFFFE000u) : v;
-    hi[i] = h;
-    lo[i] = finite ? __fsub_rn(v, h) : 0.f;
+    uint32_t h, l;
+    tf32_split(x[i], h, l);
+    hi[i] = __uint_as_float(h);
+    lo[i] = __uint_as_float(l);
   }
 }
 
