@@ -214,10 +214,10 @@ class ClockSampler:
 # GPU leg
 # ---------------------------------------------------------------------------
 
-def read_traffic():
-    """Per-launch DRAM bytes of vcb_mlp_crown on cfg2 from the committed ncu
-    summary (profiles/crown_mlp_cfg2.md, line 'traffic_bytes_per_launch: N')."""
-    path = os.path.join(ROOT, 'profiles', 'crown_mlp_cfg2.md')
+def read_traffic(name='crown_mlp_cfg2.md'):
+    """Per-launch DRAM bytes of a cfg2 kernel from its committed ncu summary
+    (profiles/<name>, line 'traffic_bytes_per_launch: N')."""
+    path = os.path.join(ROOT, 'profiles', name)
     try:
         for ln in open(path):
             if ln.startswith('traffic_bytes_per_launch:'):
@@ -247,6 +247,42 @@ def measured_fp32_peak(dev):
         ms = e0.elapsed_time(e1)
         best = max(best, blocks * 256.0 * iters * 128 / (ms * 1e-3) / 1e12)
     return best
+
+
+def _lib_path(desc, B, Q):
+    """1 when vcb_mlp_crown runs the tensor-core kernel for (B, Q)."""
+    from vibecheck_nn_b200 import _lib
+    return _lib.lib().vcb_mlp_crown_path(desc.struct, B, Q)
+
+
+def roofline_cfg2(tc_path, achieved, ffma_peak, flop_per_box):
+    """Roofline of the cfg2 step's kernel.  The tensor-core kernel is judged
+    against the 3xTF32 rate the tensor cores can deliver (measured bf16 dense
+    peak / 2 for TF32 / 3 products); the SIMT kernel against the FFMA peak
+    measured live."""
+    if not tc_path:
+        return {'bound': 'fp32_simt', 'achieved': achieved, 'peak': ffma_peak,
+                'unit': 'TFLOP/s', 'frac': achieved / ffma_peak if ffma_peak else None,
+                'traffic': read_traffic('crown_mlp_cfg2.md'),
+                'kernel': 'vcb_mlp_crown (crown_mlp_kernel)', 'flop_per_box': flop_per_box,
+                'peak_source': 'measured live: vcb_probe_ffma FFMA loop (MEASURED_PEAKS.json '
+                               'has no FP32 SIMT figure)'}
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, 'MEASURED_PEAKS.json')))
+    except (OSError, ValueError):
+        pass
+    bf16 = peaks.get('bf16_tflops')
+    peak = (bf16 if bf16 else 1590.0) / 6.0
+    return {'bound': 'tensor', 'achieved': achieved, 'peak': peak, 'unit': 'TFLOP/s',
+            'frac': achieved / peak, 'traffic': read_traffic('crown_tc_cfg2.md'),
+            'kernel': 'vcb_mlp_crown (crown_tc_kernel, tcgen05 3xTF32; the step also runs '
+                      'crown_tc_images, <1% of its time)',
+            'flop_per_box': flop_per_box,
+            'frac_of_ffma_peak': achieved / ffma_peak if ffma_peak else None,
+            'peak_source': ('of measured: MEASURED_PEAKS.json bf16_tflops / 2 (TF32 rate) / 3 '
+                            '(3xTF32 products)') if bf16 else
+                           'of fallback: 1590 TFLOP/s bf16 / 2 / 3'}
 
 
 def run_ours(args):
@@ -340,6 +376,8 @@ def run_ours(args):
     flop_per_box = (4 + 2 * N_Q) * sum_w
     mean_ms = t_ms / args.steps
     achieved = N_BOXES * flop_per_box / (mean_ms * 1e-3) / 1e12
+    desc = ops.mlp_desc(gg, dev)
+    tc_path = bool(_lib_path(desc, N_BOXES, N_Q))
     cpu = None
     if pool is not None:
         cpu = cpu_baseline(pool, cores)
@@ -355,16 +393,8 @@ def run_ours(args):
             'e2e': {'value': e2e_value, 'unit': UNIT,
                     'h2d_bytes_per_step': int(xl_h.numel() * 4 * 2),
                     'd2h_bytes_per_step': int(lb_h.numel() * 4)},
-            'gpu_launches': args.steps,
-            'roofline': {'bound': 'fp32_simt', 'achieved': achieved,
-                         'peak': peak, 'unit': 'TFLOP/s',
-                         'frac': achieved / peak if peak else None,
-                         'traffic': read_traffic(),
-                         'kernel': 'vcb_mlp_crown (crown_mlp_kernel)',
-                         'flop_per_box': flop_per_box,
-                         'peak_source': 'measured live: vcb_probe_ffma FFMA '
-                                        'loop (MEASURED_PEAKS.json has no '
-                                        'FP32 SIMT figure)'},
+            'gpu_launches': (2 if tc_path else 1) * args.steps,
+            'roofline': roofline_cfg2(tc_path, achieved, peak, flop_per_box),
             'clocks': clk.summary(),
             'wall_s_timed_region': t_wall,
         }

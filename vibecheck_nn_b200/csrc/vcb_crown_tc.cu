@@ -96,7 +96,8 @@ struct TcParams {
 
 __host__ __device__ inline int pad16(int n) { return (n + 15) & ~15; }
 
-// Weight images, one thread per (image, row, k).  Image 3 l + 0: W_l
+// Weight images, one thread per (image, row, k); thread 0 also clears the
+// error word.  Image 3 l + 0: W_l
 // (rows = outputs, K = inputs), + 1: |W_l|, + 2: [W_l^T; b_l] (rows = inputs
 // then the bias row, K = outputs).  Each is split into tf32 hi (first 16 KB)
 // and lo, laid out as two 64-row x 32-column blocks with the 128-byte swizzle
@@ -104,6 +105,7 @@ __host__ __device__ inline int pad16(int n) { return (n + 15) & ~15; }
 __global__ void crown_tc_images(const TcParams p) {
   const int nimg = 3 * (p.n_fc - 1);
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx == 0) *p.err = 0;  // the error word of the launch that follows
   if (idx >= nimg * kW * kW) return;
   const int im = idx / (kW * kW), n = (idx / kW) % kW, k = idx % kW;
   const int l = im / 3, use = im % 3;
@@ -718,8 +720,6 @@ int crown_tc_launch(const vcb_mlp* net, int32_t B, const float* xl, const float*
   p.accout = acc;
   p.sbolo = sb_out_lo;
   p.sbohi = sb_out_hi;
-  cudaError_t e = cudaMemsetAsync(p.err, 0, sizeof(int), st);
-  if (e != cudaSuccess) return cuda_fail(e, who);
   const int nimg = 3 * (nfc - 1) * kW * kW;
   crown_tc_images<<<(nimg + 255) / 256, 256, 0, st>>>(p);
   int rc = check_launch(who);
