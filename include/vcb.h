@@ -320,15 +320,17 @@ int vcb_wide_ibp_layer(int32_t D, int32_t nin, int32_t nout, const float* mid,
 /* CROWN fc step: coef (R x nout, ld ldc) times Waug = [W | b] (nout x
  * (nin+1), ld ldw) -> coef_o (R x nin, ld ldo >= nin+1) and the bias dot bd
  * (R).  With sb_lo/hi ((R/Q) x nin, the bounds of the relu feeding this fc)
- * the relu relaxation (alpha / beta optional, (R/Q) x nin) is applied, the
- * raw coefficients are written to rec (R x ldo) when non-NULL and intercept
- * partial sums to part (R x vcb_wide_back_parts(R, nin)). */
+ * the relu relaxation (alpha / beta optional, (R/Q) x nin; with alpha_rows
+ * alpha is R x nin, one per spec row: the reference's (B, Q, n) form,
+ * verify_zono_bnb.py:4423) is applied, the raw coefficients are written to
+ * rec (R x ldo) when non-NULL and intercept partial sums to part (R x
+ * vcb_wide_back_parts(R, nin)). */
 int vcb_wide_back_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
                         const float* coef, int32_t ldc, const float* Waug,
                         int32_t ldw, const float* sb_lo, const float* sb_hi,
-                        const float* alpha, const float* beta, float* coef_o,
-                        float* rec, int32_t ldo, float* bd, float* part,
-                        void* stream);
+                        const float* alpha, int32_t alpha_rows, const float* beta,
+                        float* coef_o, float* rec, int32_t ldo, float* bd,
+                        float* part, void* stream);
 int vcb_wide_back_parts(int32_t R, int32_t nin);
 
 /* acc[r] = (acc[r] + bd[r]) + sum_t part[r][t] (if with_part), fixed order. */
@@ -353,8 +355,8 @@ int vcb_wide_adjoint_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
                            const float* g, int32_t ldg, const float* W,
                            const float* b, const float* rec,
                            const float* sb_lo, const float* sb_hi,
-                           const float* alpha, float* g_o, float* dcontrib,
-                           float* dbeta, int32_t ldo, void* stream);
+                           const float* alpha, int32_t alpha_rows, float* g_o,
+                           float* dcontrib, float* dbeta, int32_t ldo, void* stream);
 
 /* Adam (betas 0.9/0.999, eps 1e-8, as torch.optim.Adam) step `step` on the
  * loss -sum(lb): gradient = -sum over the Q rows of each domain of dcontrib;

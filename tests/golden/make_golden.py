@@ -64,7 +64,8 @@ def _net_arrays(layers):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--ref-src', required=True)
-    ap.add_argument('--only', default=None, choices=['pgd_general', 'forward', 'relu_bab'],
+    ap.add_argument('--only', default=None,
+                    choices=['pgd_general', 'forward', 'relu_bab', 'hybrid'],
                     help='regenerate one fixture only')
     args = ap.parse_args()
     vz, vg, vh, vs, vspec = _import_reference(args.ref_src)
@@ -78,6 +79,9 @@ def main():
         return
     if args.only == 'relu_bab':
         _golden_relu_bab(vz, wk)
+        return
+    if args.only == 'hybrid':
+        _golden_hybrid(wk)
         return
 
     # ------------------------------------------------------------------ slopes
@@ -505,6 +509,52 @@ def _golden_relu_bab(vz, wk):
         out[f'{tag}_reason'] = np.array(reason)
     out['tags'] = np.array([c[0] for c in RELU_BAB_CASES])
     _save('relu_bab', **out)
+
+
+# freeze-replay hybrid cases: (tag, cfg1 seed, offset added to the property
+# threshold d, settings)
+HYBRID_CASES = (
+    ('unsat0', 0, 0.0, {}),
+    ('unsat1', 1, 0.0, {}),
+    ('unsat0_short', 0, 0.0, {'hybrid_freeze_iters': 20, 'hybrid_pgd_between_every': 3}),
+    ('sat0', 0, -2.0, {}),
+)
+
+
+def hybrid_problem(seed, offset):
+    """cfg1 network with the property y0 - y1 <= d + offset folded into the
+    last bias (unsafe iff Y1' >= Y0' after the fold)."""
+    from vibecheck_nn_b200 import workloads as wk
+    w = wk.cfg1(seed)
+    layers = [(np.array(W), np.array(b)) for W, b in w['layers']]
+    layers[-1][1][0] -= np.float32(offset) if offset else 0
+    return layers, w['xl'], w['xh']
+
+
+def _golden_hybrid(wk):
+    """verify_hybrid (verify_hybrid_acasxu.py:321-539) on CPU in float32:
+    verdict, phase and the BaB counters per case."""
+    import types as _types
+    import torch
+    import vibecheck.spec as vspec
+    import vibecheck.verify_hybrid_acasxu as vhy
+    out = {}
+    for tag, seed, offset, st in HYBRID_CASES:
+        layers, xl, xh = hybrid_problem(seed, offset)
+        gg = wk.mlp_gg(layers, 'cpu', torch.float32)
+        graph = _types.SimpleNamespace(gpu_graph=lambda device, dtype, gg=gg: gg)
+        spec = vspec.VNNSpec(x_lo=np.asarray(xl, np.float64), x_hi=np.asarray(xh, np.float64),
+                             disjuncts=[vspec.Conjunct([vspec.PairwiseConstraint(pred=1,
+                                                                                 comp=0)])])
+        settings = _types.SimpleNamespace(**st)
+        res = vhy.verify_hybrid(graph, spec, settings, timeout=1e6)
+        print('hybrid', tag, {k: v for k, v in res.items() if k != 'witness'})
+        out[f'{tag}_verdict'] = np.array(res['verdict'])
+        out[f'{tag}_phase'] = np.array(res.get('phase', ''))
+        for k in ('evaluated', 'closed', 'bab_iters'):
+            out[f'{tag}_{k}'] = np.array(int(res.get(k, -1)))
+    out['tags'] = np.array([c[0] for c in HYBRID_CASES])
+    _save('hybrid', **out)
 
 
 def forward_cnn_gg(k1, b1, cb, W2, b2, W3, b3, fb, ins, dt):

@@ -59,13 +59,13 @@ SIGNATURES = {
                             _P, _P, _P],
     'vcb_wide_ibp_layer': [_I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P,
                            _P, _P, _I, _P],
-    'vcb_wide_back_layer': [_I, _I, _I, _I, _P, _I, _P, _I, _P, _P, _P, _P, _P,
+    'vcb_wide_back_layer': [_I, _I, _I, _I, _P, _I, _P, _I, _P, _P, _P, _I, _P, _P,
                             _P, _I, _P, _P, _P],
     'vcb_wide_back_parts': [_I, _I],
     'vcb_wide_rowsum': [_I, _I, _I, _P, _P, _P, _P],
     'vcb_wide_concretize': [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P],
-    'vcb_wide_adjoint_layer': [_I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                               _I, _P],
+    'vcb_wide_adjoint_layer': [_I, _I, _I, _I, _P, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P,
+                               _P, _I, _P],
     'vcb_wide_alpha_adam': [_I, _I, _I, _I, _P, _P, _P, _P, ctypes.c_float, _I,
                             _P],
     'vcb_conv_ibp': [_I, _P, _P, _P, _P, _P, _P, _P, _P, _P],

@@ -95,24 +95,31 @@ def alpha_boundary_refine(desc, xl, xh, lb, W_q, b_q, qd, D, eps, iters,
 
 
 class _SpecBackwardAlpha(torch.autograd.Function):
-    """lb = CROWN(alpha, beta); backward by the hand-written adjoint."""
+    """lb = CROWN(alpha, beta); backward by the hand-written adjoint.  alpha
+    per layer is (D, n) (one slope per domain) or (D, Q, n) (one per spec
+    row); with ``want_A`` the input-space linear bound (A, acc) is returned
+    too, without gradient."""
 
     @staticmethod
-    def forward(ctx, wn, xl, xh, sb, W_q, b_q, Ls, Lb, *params):
+    def forward(ctx, wn, xl, xh, sb, W_q, b_q, Ls, Lb, want_A, *params):
         alpha = {L: a.detach().contiguous() for L, a in zip(Ls, params[:len(Ls)])}
         beta = {L: b.detach().contiguous() for L, b in zip(Lb, params[len(Ls):])}
         with torch.no_grad():
-            lb, contrib, bcontrib = wide.wide_alpha_grad(
-                wn, xl, xh, sb, W_q, b_q, alpha, beta=beta or None, beta_grad=True)
+            lb, contrib, bcontrib, A, acc = wide.wide_alpha_grad(
+                wn, xl, xh, sb, W_q, b_q, alpha, beta=beta or None, beta_grad=True,
+                want_A=True)
         ctx.Q = W_q.shape[0]
         ctx.Ls, ctx.Lb = Ls, Lb
-        ctx.widths = [alpha[L].shape[1] for L in Ls]
+        ctx.shapes = [tuple(alpha[L].shape) for L in Ls]
         ctx.bwidths = [beta[L].shape[1] for L in Lb]
         ctx.contrib, ctx.bcontrib = contrib, bcontrib
+        if want_A:
+            ctx.mark_non_differentiable(A, acc)
+            return lb, A, acc
         return lb
 
     @staticmethod
-    def backward(ctx, grad):
+    def backward(ctx, grad, *unused):
         w = grad.flatten()
         if not bool((w == w[0]).all()):
             raise NotImplementedError(
@@ -125,8 +132,14 @@ class _SpecBackwardAlpha(torch.autograd.Function):
             D = dc.shape[0] // ctx.Q
             return dc.view(D, ctx.Q, ldo).sum(dim=1)[:, :n] * scale
 
-        res = [None] * 8
-        res += [per_domain(ctx.contrib, L, n) for L, n in zip(ctx.Ls, ctx.widths)]
+        def per_row(store, L, shape):
+            dc, ldo = store[L]
+            D, Q, n = shape
+            return dc.view(D, Q, ldo)[:, :, :n] * scale
+
+        res = [None] * 9
+        res += [per_row(ctx.contrib, L, sh) if len(sh) == 3 else per_domain(ctx.contrib, L, sh[1])
+                for L, sh in zip(ctx.Ls, ctx.shapes)]
         res += [per_domain(ctx.bcontrib, L, n) for L, n in zip(ctx.Lb, ctx.bwidths)]
         return tuple(res)
 
@@ -134,9 +147,9 @@ class _SpecBackwardAlpha(torch.autograd.Function):
 def spec_backward_with_grad(desc, lo, hi, xl, xh, spec, alpha_at_layer,
                             relu_split_beta, return_input_linear):
     """_spec_backward_graph_batched with alpha (and beta) tensors that may
-    require grad: lb carries the hand-written adjoint as its backward."""
-    if return_input_linear:
-        raise NotImplementedError('vibecheck_nn_b200: return_input_linear with alpha gradients')
+    require grad: lb carries the hand-written adjoint as its backward;
+    with ``return_input_linear`` also A (B, Q, n_in) and acc (B, Q), which
+    carry no gradient."""
     B = xl.shape[0]
     sb = _sb_dict(desc, B, lo, hi)
     wn = desc.__dict__.get('_wide') or wide.WideNet(desc)
@@ -146,4 +159,5 @@ def spec_backward_with_grad(desc, lo, hi, xl, xh, spec, alpha_at_layer,
     beta = relu_split_beta or {}
     Lb = sorted(beta)
     params = [alpha_at_layer[L] for L in Ls] + [beta[L].to(F32) for L in Lb]
-    return _SpecBackwardAlpha.apply(wn, xl, xh, sb, W_q, b_q, Ls, Lb, *params)
+    return _SpecBackwardAlpha.apply(wn, xl, xh, sb, W_q, b_q, Ls, Lb,
+                                    bool(return_input_linear), *params)

@@ -110,6 +110,7 @@ struct BackArgs {
   int ldw;
   const float *sblo, *sbhi, *alpha, *beta;  // (R / Q) x nin, or NULL (no relu)
   float *coef_o, *rec, *bd, *part;
+  int alpha_rows;             // alpha is R x nin (one per spec row) instead
 };
 
 __global__ void __launch_bounds__(GT) crown_back_kernel(const BackArgs a) {
@@ -133,7 +134,8 @@ __global__ void __launch_bounds__(GT) crown_back_kernel(const BackArgs a) {
           float o = v;
           if (a.sblo) {
             const long long gi = (long long)box * a.nin + n;
-            const Relax r = relax_of(a.sblo[gi], a.sbhi[gi], a.alpha ? a.alpha + gi : nullptr);
+            const long long ai = a.alpha_rows ? (long long)m * a.nin + n : gi;
+            const Relax r = relax_of(a.sblo[gi], a.sbhi[gi], a.alpha ? a.alpha + ai : nullptr);
             if (a.rec) a.rec[(long long)m * a.ldo + n] = v;
             if (v < 0.f) {
               pt = fmaf(v, r.icp, pt);
@@ -212,6 +214,7 @@ struct AdjArgs {
   const float *rec, *sblo, *sbhi, *alpha;  // rec: R x nout (ld ldo); sb/alpha (R/Q) x nout
   float *g_o, *dcontrib;        // R x nout (ld ldo)
   float* dbeta;                 // R x nout (ld ldo): d lb / d beta = ga, or NULL
+  int alpha_rows;               // alpha is R x nout (one per spec row) instead
 };
 
 __global__ void __launch_bounds__(GT) alpha_adjoint_kernel(const AdjArgs a) {
@@ -236,7 +239,8 @@ __global__ void __launch_bounds__(GT) alpha_adjoint_kernel(const AdjArgs a) {
       const float ga = __fadd_rn(acc[i][j], a.b[n]);
       const long long gi = (long long)box * a.nout + n;
       const float e = a.rec[(long long)m * a.ldo + n];
-      const Relax r = relax_of(a.sblo[gi], a.sbhi[gi], a.alpha ? a.alpha + gi : nullptr);
+      const long long ai = a.alpha_rows ? (long long)m * a.nout + n : gi;
+      const Relax r = relax_of(a.sblo[gi], a.sbhi[gi], a.alpha ? a.alpha + ai : nullptr);
       a.dcontrib[(long long)m * a.ldo + n] = r.unstable ? __fmul_rn(fmaxf(e, 0.f), ga) : 0.f;
       // beta is added after the relaxation, so its gradient is the adjoint itself
       if (a.dbeta) a.dbeta[(long long)m * a.ldo + n] = ga;
@@ -304,9 +308,9 @@ extern "C" int vcb_wide_ibp_layer(int32_t D, int32_t nin, int32_t nout, const fl
 extern "C" int vcb_wide_back_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
                                    const float* coef, int32_t ldc, const float* Waug,
                                    int32_t ldw, const float* sb_lo, const float* sb_hi,
-                                   const float* alpha, const float* beta, float* coef_o,
-                                   float* rec, int32_t ldo, float* bd, float* part,
-                                   void* stream) {
+                                   const float* alpha, int32_t alpha_rows, const float* beta,
+                                   float* coef_o, float* rec, int32_t ldo, float* bd,
+                                   float* part, void* stream) {
   if (R < 0 || Q <= 0 || nin <= 0 || nout <= 0)
     return fail(VCB_ERR_INVALID, "vcb_wide_back_layer: shape");
   if (R == 0) return VCB_OK;
@@ -314,7 +318,7 @@ extern "C" int vcb_wide_back_layer(int32_t R, int32_t Q, int32_t nin, int32_t no
       ldo < nin + 1)
     return fail(VCB_ERR_INVALID, "vcb_wide_back_layer: NULL pointer or bad leading dimension");
   BackArgs a{R, Q, nin, nout, ldc, ldo, coef, Waug, ldw, sb_lo, sb_hi, alpha, beta,
-             coef_o, rec, bd, part};
+             coef_o, rec, bd, part, alpha_rows};
   const int sm = smem_bytes(false);
   int rc = ensure_smem(reinterpret_cast<const void*>(crown_back_kernel), sm);
   if (rc) return rc;
@@ -350,15 +354,16 @@ extern "C" int vcb_wide_concretize(int32_t R, int32_t Q, int32_t n0, int32_t lde
 extern "C" int vcb_wide_adjoint_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
                                       const float* g, int32_t ldg, const float* W,
                                       const float* b, const float* rec, const float* sb_lo,
-                                      const float* sb_hi, const float* alpha, float* g_o,
-                                      float* dcontrib, float* dbeta, int32_t ldo,
-                                      void* stream) {
+                                      const float* sb_hi, const float* alpha,
+                                      int32_t alpha_rows, float* g_o, float* dcontrib,
+                                      float* dbeta, int32_t ldo, void* stream) {
   if (R < 0 || Q <= 0 || nin <= 0 || nout <= 0)
     return fail(VCB_ERR_INVALID, "vcb_wide_adjoint_layer: shape");
   if (R == 0) return VCB_OK;
   if (!g || !W || !b || !rec || !sb_lo || !sb_hi || !g_o || !dcontrib || (ldg & 3) || (ldo & 3))
     return fail(VCB_ERR_INVALID, "vcb_wide_adjoint_layer: NULL pointer or bad ld");
-  AdjArgs a{R, Q, nin, nout, ldg, ldo, g, W, b, rec, sb_lo, sb_hi, alpha, g_o, dcontrib, dbeta};
+  AdjArgs a{R, Q, nin, nout, ldg, ldo, g, W, b, rec, sb_lo, sb_hi, alpha, g_o, dcontrib, dbeta,
+            alpha_rows};
   const int sm = smem_bytes(false);
   int rc = ensure_smem(reinterpret_cast<const void*>(alpha_adjoint_kernel), sm);
   if (rc) return rc;

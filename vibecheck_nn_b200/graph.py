@@ -219,7 +219,7 @@ def graph_crown(G, xl, xh, sb, W_q, b_q, alpha=None, beta=None, want_A=False):
             nparts = L_.vcb_wide_back_parts(R, nin)
             part = torch.empty((R, nparts), dtype=F32, device=dev)
             rc = L_.vcb_wide_back_layer(R, Q, nin, layer['nout'], P(coef), ldc, P(layer['Waug']),
-                                        layer['Waug'].shape[1], None, None, None, None,
+                                        layer['Waug'].shape[1], None, None, None, 0, None,
                                         P(coef_o), None, ldo, P(bd), P(part), st)
             _lib.check(rc, 'vcb_wide_back_layer')
             rc = L_.vcb_wide_rowsum(R, nparts, 0, P(bd), P(part), P(acc), st)

@@ -144,10 +144,14 @@ def _crown_intermediate_batched(gg, xl, xh, device, dtype, chunk=2048):
     return {L: (lo_d[L], hi_d[L]) for L in lo_d}
 
 
-def spec_backward_seeded(tight, xl, xh, gg, seed_ew_at, seed_acc, device):
+def spec_backward_seeded(tight, xl, xh, gg, seed_ew_at, seed_acc, device, alpha_at_layer=None):
     """``_spec_backward_graph_batched(..., seed_ew_at=..., seed_acc=...)`` for
     a seed at the output of one fc layer that is identical across the batch
-    (the form ``_crown_intermediate_batched`` uses, verify_zono_bnb.py:4131-4139)."""
+    (the form ``_crown_intermediate_batched`` uses, verify_zono_bnb.py:4131-4139,
+    and the per-layer alpha freeze of verify_hybrid_acasxu.py:186-215).  With
+    ``alpha_at_layer`` ({L: (B, n_L) or (B, Q, n_L)} for the relu layers below
+    the seed, possibly requiring grad) the layer-wise kernels run the
+    relaxation with those slopes."""
     device = _dev(device)
     if len(seed_ew_at) != 1:
         raise NotImplementedError('vibecheck_nn_b200: one seed op supported')
@@ -175,5 +179,17 @@ def spec_backward_seeded(tight, xl, xh, gg, seed_ew_at, seed_acc, device):
         else torch.zeros(1, dtype=F32, device=device)
     hi = _packed_layers(sub, B, {l: tight[l][1] for l in range(L)}, device) if L > 0 \
         else torch.zeros(1, dtype=F32, device=device)
-    return mlp_crown(sub, xl, xh, sb_in=(lo, hi),
-                     spec=(_f32(s0, device), _f32(acc0, device)))['lb']
+    spec = (_f32(s0, device), _f32(acc0, device))
+    alpha = {k: a for k, a in (alpha_at_layer or {}).items() if k < L}
+    if alpha:
+        if any(bool(a.requires_grad) for a in alpha.values()) and torch.is_grad_enabled():
+            from .alpha import spec_backward_with_grad
+            return spec_backward_with_grad(sub, lo, hi, xl, xh, spec, alpha, None, False)
+        from . import wide
+        from .alpha import _sb_dict
+        wn = sub.__dict__.get('_wide') or wide.WideNet(sub)
+        sub.__dict__['_wide'] = wn
+        return wide.wide_crown(wn, xl, xh, _sb_dict(sub, B, lo, hi), spec[0], spec[1],
+                               alpha={k: a.detach().to(F32).contiguous()
+                                      for k, a in alpha.items()})['lb']
+    return mlp_crown(sub, xl, xh, sb_in=(lo, hi), spec=spec)['lb']

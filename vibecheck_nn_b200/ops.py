@@ -238,7 +238,7 @@ def _spec_backward_graph_batched(tight, xl, xh, gg, spec_ew, device, dtype,
     if seed_ew_at is not None:
         from .interm import spec_backward_seeded
         return spec_backward_seeded(tight, xl, xh, gg, seed_ew_at, seed_acc,
-                                    device)
+                                    device, alpha_at_layer=alpha_at_layer)
     if alpha_mccormick or alpha_recip:
         raise NotImplementedError('vibecheck_nn_b200: bilinear alpha terms')
     xl = _f32(xl, device)
@@ -265,10 +265,12 @@ def _spec_backward_graph_batched(tight, xl, xh, gg, spec_ew, device, dtype,
     hi = _packed_layers(desc, B, {L: v[1] for L, v in tight.items()}, device)
     spec = spec_matrix(spec_ew, device)
     needs_grad = False
+    per_query = False  # alpha (B, Q, n): one slope per spec row (verify_zono_bnb.py:4423)
     if alpha_at_layer is not None:
         for a in alpha_at_layer.values():
-            if a.dim() != 2:
-                raise NotImplementedError('vibecheck_nn_b200: per-query alpha')
+            if a.dim() not in (2, 3):
+                raise NotImplementedError('vibecheck_nn_b200: alpha must be (B, n) or (B, Q, n)')
+            per_query |= a.dim() == 3
             needs_grad |= bool(a.requires_grad)
     if relu_split_beta is not None:
         needs_grad |= any(bool(b.requires_grad) for b in relu_split_beta.values())
@@ -277,7 +279,7 @@ def _spec_backward_graph_batched(tight, xl, xh, gg, spec_ew, device, dtype,
         return spec_backward_with_grad(desc, lo, hi, xl, xh, spec,
                                        alpha_at_layer, relu_split_beta,
                                        return_input_linear)
-    if not fits_smem(desc, spec[0].shape[0]):
+    if per_query or not fits_smem(desc, spec[0].shape[0]):
         from . import wide
         sb = {L: (tight[L][0].to(F32).contiguous(), tight[L][1].to(F32).contiguous())
               for L in range(len(desc.relu_widths))}

@@ -94,7 +94,9 @@ def wide_crown(wn, xl, xh, sb, W_q, b_q, alpha=None, beta=None, want_A=False,
                record=False, want_g0=False):
     """CROWN back-substitution for D boxes x Q spec rows.
 
-    sb {L: (lo, hi)} (D, n_L); alpha/beta {L: (D, n_L)} or None.
+    sb {L: (lo, hi)} (D, n_L); alpha {L: (D, n_L) or (D, Q, n_L), the latter
+    one slope per spec row (verify_zono_bnb.py:4423)}, beta {L: (D, n_L)} or
+    None.
     Returns dict(lb (D, Q), acc (D, Q), A (D, Q, n0) if want_A, rec {L: (R, ld)}
     if record, g0 (R, ld0) if want_g0)."""
     dev = xl.device
@@ -132,6 +134,7 @@ def wide_crown(wn, xl, xh, sb, W_q, b_q, alpha=None, beta=None, want_A=False,
         rc = L_.vcb_wide_back_layer(R, Q, nin, nout, P(coef), ldc, P(wn.Waug[l]),
                                     wn.Waug[l].shape[1], P(lo), P(hi),
                                     P(None if al is None else al.contiguous()),
+                                    int(al is not None and al.dim() == 3),
                                     P(None if be is None else be.contiguous()),
                                     P(coef_o), P(r_buf), ldo, P(bd), P(part), st)
         _lib.check(rc, 'vcb_wide_back_layer')
@@ -155,11 +158,13 @@ def wide_crown(wn, xl, xh, sb, W_q, b_q, alpha=None, beta=None, want_A=False,
     return out
 
 
-def wide_alpha_grad(wn, xl, xh, sb, W_q, b_q, alpha, beta=None, beta_grad=False):
+def wide_alpha_grad(wn, xl, xh, sb, W_q, b_q, alpha, beta=None, beta_grad=False,
+                    want_A=False):
     """lb (D, Q) and the per-row gradient contributions {L: (R, ld)} of
-    d(sum lb)/d(alpha) (summed over the Q rows of a domain by the Adam kernel);
-    with ``beta_grad`` also those of d(sum lb)/d(beta) for the split
-    multipliers ``beta`` {L: (D, n_L)} added after each relaxation."""
+    d(sum lb)/d(alpha) (summed over the Q rows of a domain for per-domain
+    alpha); with ``beta_grad`` also those of d(sum lb)/d(beta) for the split
+    multipliers ``beta`` {L: (D, n_L)} added after each relaxation; with
+    ``want_A`` also A (D, Q, n0) and acc (D, Q) (appended to the tuple)."""
     dev = xl.device
     D, n0 = xl.shape
     Q = W_q.shape[0]
@@ -167,7 +172,7 @@ def wide_alpha_grad(wn, xl, xh, sb, W_q, b_q, alpha, beta=None, beta_grad=False)
     st = _lib.stream_of(dev)
     L_ = _lib.lib()
     res = wide_crown(wn, xl, xh, sb, W_q, b_q, alpha=alpha, beta=beta, record=True,
-                     want_g0=True)
+                     want_g0=True, want_A=want_A)
     g, ldg = res['g0']
     contrib = {}
     bcontrib = {}
@@ -183,15 +188,17 @@ def wide_alpha_grad(wn, xl, xh, sb, W_q, b_q, alpha, beta=None, beta_grad=False)
         rc = L_.vcb_wide_adjoint_layer(R, Q, nin, nout, P(g), ldg, P(wn.W[l]), P(wn.b[l]),
                                        P(rec), P(lo.contiguous()), P(hi.contiguous()),
                                        P(None if al is None else al.contiguous()),
+                                       int(al is not None and al.dim() == 3),
                                        P(g_o), P(dc), P(db), ldo, st)
         _lib.check(rc, 'vcb_wide_adjoint_layer')
         contrib[l] = (dc, ldo)
         if beta_grad:
             bcontrib[l] = (db, ldo)
         g, ldg = g_o, ldo
-    if beta_grad:
-        return res['lb'], contrib, bcontrib
-    return res['lb'], contrib
+    out = (res['lb'], contrib) + ((bcontrib,) if beta_grad else ())
+    if want_A:
+        out += (res['A'], res['acc'])
+    return out
 
 
 def min_area_alpha(sb):
