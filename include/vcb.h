@@ -107,6 +107,21 @@ int32_t vcb_mlp_crown_tc_min_batch(int32_t value);
  * threshold: 1 = tensor-core, 0 = SIMT. */
 int32_t vcb_mlp_crown_path(const vcb_mlp* net, int32_t B, int32_t Q);
 
+/* Batched forward linear bounds (forward LiRPA, the default bound of the
+ * multi-subbox input-split BaB: chunked_batched_forward_linear_bounds,
+ * forward_lirpa.py:1391, fc / relu ops :580-687) of B boxes xl/xh (B x
+ * dims[0]) over the K varying input dimensions var_idx (int32[K]), then the
+ * spec rows spec_W (Q x dims[n_fc]) as in verify_graph.py:11522-11560:
+ * spec_A (B x Q x K, may be NULL) = w+ A_lo + w- A_up, spec_b (B x Q, may be
+ * NULL) likewise, lb (B x Q) = spec_A+ xl + spec_A- xh + spec_b over the
+ * varying dimensions.  A_lo/A_up (B x n_out x K) and b_lo/b_up (B x n_out),
+ * the output bounds, are written when non-NULL.  Widths <= 64, 1 <= K <= 31,
+ * Q <= 64. */
+int vcb_mlp_flirpa(const vcb_mlp* net, int32_t B, int32_t K, const float* xl,
+                   const float* xh, const int32_t* var_idx, int32_t Q,
+                   const float* spec_W, float* spec_A, float* spec_b, float* lb,
+                   float* A_lo, float* A_up, float* b_lo, float* b_up, void* stream);
+
 /* Allocation-free variant of vcb_mlp_crown (no counterpart in the
  * reference).  For callers that cannot allocate device memory while they
  * bound boxes -- a host application whose memory pool already owns the GPU,

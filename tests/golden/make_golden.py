@@ -65,7 +65,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--ref-src', required=True)
     ap.add_argument('--only', default=None,
-                    choices=['pgd_general', 'forward', 'relu_bab', 'hybrid'],
+                    choices=['pgd_general', 'forward', 'relu_bab', 'hybrid', 'multisub'],
                     help='regenerate one fixture only')
     args = ap.parse_args()
     vz, vg, vh, vs, vspec = _import_reference(args.ref_src)
@@ -82,6 +82,9 @@ def main():
         return
     if args.only == 'hybrid':
         _golden_hybrid(wk)
+        return
+    if args.only == 'multisub':
+        _golden_multisub(wk)
         return
 
     # ------------------------------------------------------------------ slopes
@@ -555,6 +558,88 @@ def _golden_hybrid(wk):
             out[f'{tag}_{k}'] = np.array(int(res.get(k, -1)))
     out['tags'] = np.array([c[0] for c in HYBRID_CASES])
     _save('hybrid', **out)
+
+
+# multi-subbox BaB cases: (tag, net seed, sub-boxes, margins (lo, hi),
+# half-widths of the varying dimensions (lo, hi), batch, split depth, budget);
+# 'unsafe' has one sub-box whose property fails (only its closed set is
+# deterministic: the loop runs until the budget)
+MULTISUB_CASES = (
+    ('mixed', 5, 16, (0.01, 0.05), (0.1, 0.3), 1024, 4, 1e6),
+    ('small_batch', 6, 12, (0.005, 0.03), (0.1, 0.3), 64, 2, 1e6),
+    ('wide', 7, 16, (0.01, 0.1), (0.3, 0.5), 1024, 4, 1e6),
+    ('unsafe', 5, 1, (-0.3, -0.3), (0.1, 0.3), 1024, 4, 3.0),
+)
+
+
+def multisub_problem(seed, n_sub, margins, half=(0.1, 0.3)):
+    """A 6 -> [24] x 3 -> 2 MLP and sub-boxes whose dimensions 0-3 are fixed
+    and 4-5 vary.  Sub-box k is unsafe iff y0 >= t0_k and y1 <= t1_k, with
+    t0_k = max y0 + m_k and t1_k = min y1 - m_k over samples (the property
+    holds when m_k > 0 and the sampled extremes are the true ones).  Returns
+    (layers, [(x_lo, x_hi, [[('ge', 0, t0), ('le', 1, t1)]])])."""
+    from vibecheck_nn_b200 import workloads as wk
+    rng = np.random.default_rng(seed)
+    layers = wk.mlp_params((6, 24, 24, 24, 2), rng)
+    subs = []
+    for k in range(n_sub):
+        fixed = rng.uniform(0, 1, 4)
+        c = rng.uniform(0.2, 0.8, 2)
+        h = rng.uniform(half[0], half[1], 2)
+        lo = np.concatenate([fixed, c - h]).astype(np.float32)
+        hi = np.concatenate([fixed, c + h]).astype(np.float32)
+        pts = lo + (hi - lo) * rng.random((4096, 6))
+        y = wk._mlp_forward64(layers, pts.astype(np.float64))
+        m = margins[0] + (margins[1] - margins[0]) * (k / max(1, n_sub - 1))
+        t0 = float(y[:, 0].max() + m)
+        t1 = float(y[:, 1].min() - m)
+        subs.append((lo, hi, [[('ge', 0, t0), ('le', 1, t1)]]))
+    return layers, subs
+
+
+def _golden_multisub(wk):
+    """_multi_sub_input_split_bab (verify_graph.py:11180) on CPU in float32:
+    closed sub-boxes, iterations and visited leaves per case."""
+    import contextlib
+    import io
+    import re
+    import types as _types
+    import torch
+    import vibecheck.spec as vspec
+    import vibecheck.verify_graph as vg
+    out = {}
+    for tag, seed, n_sub, margins, half, batch, depth, budget in MULTISUB_CASES:
+        layers, subs = multisub_problem(seed, n_sub, margins, half)
+        gg = wk.mlp_gg(layers, 'cpu', torch.float32)
+        groups = []
+        for lo, hi, conj in subs:
+            cons = [vspec.Constraint(i, '>=' if op == 'ge' else '<=', v) for op, i, v in conj[0]]
+            groups.append((lo.astype(np.float64), hi.astype(np.float64), [vspec.Conjunct(cons)]))
+        order = list(range(len(groups)))
+        st = _types.SimpleNamespace(input_split_batch_size=batch, bab_split_depth=depth,
+                                    print_progress=True)
+        buf = io.StringIO()
+        with contextlib.redirect_stdout(buf):
+            closed = vg._multi_sub_input_split_bab(list(range(len(groups))), groups, order, gg,
+                                                   torch.device('cpu'), torch.float32, budget,
+                                                   2, st)
+        mt = re.search(r'(\d+) iters, (\d+) leaves', buf.getvalue())
+        print('multisub', tag, sorted(closed), mt.group(0) if mt else buf.getvalue()[-200:])
+        out[f'{tag}_closed'] = np.array(sorted(closed), np.int64)
+        out[f'{tag}_iters'] = np.array(int(mt.group(1)) if mt else -1)
+        out[f'{tag}_leaves'] = np.array(int(mt.group(2)) if mt else -1)
+    # forward linear bounds of the first net on its sub-boxes (varying dims 4, 5)
+    import vibecheck.forward_lirpa as fl
+    layers, subs = multisub_problem(*MULTISUB_CASES[0][1:5])
+    gg = wk.mlp_gg(layers, 'cpu', torch.float32)
+    xl = torch.as_tensor(np.stack([sb[0] for sb in subs]))
+    xh = torch.as_tensor(np.stack([sb[1] for sb in subs]))
+    bb = fl.chunked_batched_forward_linear_bounds(gg, xl, xh, torch.device('cpu'), torch.float32)
+    for k in ('A_lo', 'A_up', 'b_lo', 'b_up', 'lo_box', 'hi_box'):
+        out[f'flirpa_{k}'] = getattr(bb, k).numpy()
+    out['flirpa_mask'] = fl.chunked_batched_forward_linear_bounds.last_varying_mask.numpy()
+    out['tags'] = np.array([c[0] for c in MULTISUB_CASES])
+    _save('multisub', **out)
 
 
 def forward_cnn_gg(k1, b1, cb, W2, b2, W3, b3, fb, ins, dt):

@@ -113,7 +113,7 @@ def test_install_rebinds_reference_functions():
     assert mods['vibecheck.verify_graph']._input_split_batched is bab._input_split_batched
     assert mods['vibecheck.verify_hybrid_acasxu']._simple_pgd_batched is pgd._simple_pgd_batched
     assert mods['vibecheck.pgd'].pgd_attack_general is pgd.pgd_attack_general
-    assert sum(len(v) for v in done.values()) == 15
+    assert sum(len(v) for v in done.values()) == 16
 
 
 def test_install_relu_bab_delegates_and_is_optional():

@@ -43,6 +43,8 @@ SIGNATURES = {
     'vcb_mlp_crown_workspace': [ctypes.POINTER(VcbMlp), _I, _I],
     'vcb_mlp_crown_tc_min_batch': [_I],
     'vcb_mlp_crown_path': [ctypes.POINTER(VcbMlp), _I, _I],
+    'vcb_mlp_flirpa': [ctypes.POINTER(VcbMlp), _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P,
+                       _P, _P, _P, _P],
     'vcb_mlp_crown_noalloc': [ctypes.POINTER(VcbMlp), _I, _P, _P, _P, _P, _P,
                               _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P],
     'vcb_mlp_crown_noalloc_capacity': [],

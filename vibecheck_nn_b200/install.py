@@ -25,6 +25,9 @@ BINDINGS = {
     },
     'vibecheck.verify_graph': {
         '_input_split_batched': ('bab', '_input_split_batched'),
+        # per-disjunct sub-box verification calls it as a module global
+        # (verify_graph.py:9337); CPU calls go to the reference's own
+        '_multi_sub_input_split_bab': ('multisub', '_multi_sub_input_split_bab', 'delegate'),
     },
     'vibecheck.verify_hybrid_acasxu': {
         '_simple_pgd': ('pgd', '_simple_pgd'),
