@@ -12,7 +12,8 @@
 // the epilogue warps add the chunk partials into fp32 registers with
 // round-to-nearest adds: the long sum over K is an ordinary fp32 sum.
 //
-// Kernel structure (one 128 x 128 output tile per CTA, 6 warps):
+// Kernel structure (one 128 x 128 output tile per CTA, N tile fastest in the
+// 1-D grid so the CTAs reading the same A rows are resident together; 6 warps):
 //   warp 4 / one thread : TMA producer -- per K chunk, four 128 x 32 fp32
 //                         tiles (A hi/lo, B hi/lo) into a 3-stage ring of
 //                         shared memory with 128-byte swizzle, each stage
@@ -90,7 +91,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __shared__ uint32_t tmem_slot;
   __shared__ int failed;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * TC_BM, n0 = blockIdx.y * TC_BN;
+  // N tile fastest: the CTAs that share an A row tile run together, so the
+  // (large) A operand streams from HBM once and the other N tiles hit L2
+  const int n_tiles = (a.N + TC_BN - 1) / TC_BN;
+  const int m0 = (blockIdx.x / n_tiles) * TC_BM, n0 = (blockIdx.x % n_tiles) * TC_BN;
   const int nk = (a.K + TC_BK - 1) / TC_BK;
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -265,8 +269,9 @@ int tc_gemm_3xtf32(int M, int N, int K, const float* Ah, const float* Al, int ld
   rc = ensure_smem(reinterpret_cast<const void*>(tc_gemm_kernel), TC_SMEM);
   if (rc) return rc;
   TcArgs args{M, N, K, ldc, C, bias, err};
-  dim3 grid((M + TC_BM - 1) / TC_BM, (N + TC_BN - 1) / TC_BN);
-  tc_gemm_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(mAh, mAl, mBh, mBl, args);
+  const long long tiles = (long long)((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
+  if (tiles > 0x7fffffffLL) return fail(VCB_ERR_UNSUPPORTED, "%s: %lld output tiles", who, tiles);
+  tc_gemm_kernel<<<(unsigned)tiles, TC_THREADS, TC_SMEM, st>>>(mAh, mAl, mBh, mBl, args);
   return check_launch(who);
 }
 
