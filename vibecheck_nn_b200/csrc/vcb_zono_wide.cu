@@ -99,7 +99,12 @@ __device__ __forceinline__ void split4(const float (&e)[4], float4& h, float4& l
 // A rows of leaf b: [0, k_in) scaled rows, [k_in, k_in + cnt) new
 // generators, then zeros up to the next leaf's offset.  Source rows come from
 // C (ld ldc) at in_off[b], or -- layer 0 (C == NULL) -- are r_b[k] W0T[k].
-// One warp per output row, float4 across the row (ld % 4 == 0).
+// One warp per output row, float4 across the row (ld % 4 == 0); each warp
+// walks a contiguous range of rows (the leaf found once, then advanced), and
+// a row's loads are all issued before its arithmetic so that a warp keeps up
+// to kBuildVec float4 loads per lane in flight.
+constexpr int kBuildVec = 8;
+
 __global__ void __launch_bounds__(256) zw_build_kernel(
     int B, int n, int ld, const long long* __restrict__ in_off, const int* __restrict__ k_in,
     const float* __restrict__ C, int ldc, const float* __restrict__ r, int n0,
@@ -109,52 +114,73 @@ __global__ void __launch_bounds__(256) zw_build_kernel(
     float* __restrict__ Al) {
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long wid = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long per = (total_rows + warps - 1) / warps;
+  const long long r0 = wid * per, r1 = min(total_rows, r0 + per);
+  if (r0 >= r1) return;
   const int nv = ld >> 2;
-  for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       row < total_rows; row += warps) {
-    // leaf of this row: binary search of out_off (B + 1 offsets)
+  const bool vec = (n & 3) == 0 && (C == nullptr || (ldc & 3) == 0);
+  // leaf of the first row: binary search of out_off (B + 1 offsets)
+  int b;
+  {
     int lo = 0, hi = B;
     while (hi - lo > 1) {
       const int m = (lo + hi) >> 1;
-      if (out_off[m] <= row) lo = m; else hi = m;
+      if (out_off[m] <= r0) lo = m; else hi = m;
     }
-    const int b = lo;
+    b = lo;
+  }
+  long long leaf_end = out_off[b + 1];
+  for (long long row = r0; row < r1; ++row) {
+    while (row >= leaf_end) {
+      ++b;
+      leaf_end = out_off[b + 1];
+    }
     const long long rr = row - out_off[b];
     const int kin = k_in[b], u = cnt[b];
     const float4* lam4 = reinterpret_cast<const float4*>(lam + (long long)b * n);
     float4* dh = reinterpret_cast<float4*>(Ah + row * ld);
     float4* dl = reinterpret_cast<float4*>(Al + row * ld);
-    if (rr < kin) {
-      const float* src;
-      float rk = 1.f;
-      if (C) {
-        src = C + (in_off[b] + rr) * ldc;
-      } else {
-        src = W0T + rr * (long long)n;
-        rk = r[(long long)b * n0 + rr];
-      }
-      for (int v = lane; v < nv; v += 32) {
-        const int j = 4 * v;
-        float e[4] = {0.f, 0.f, 0.f, 0.f};
-        if (j + 3 < n && (n & 3) == 0 && (C ? (ldc & 3) == 0 : true)) {
-          const float4 g = *reinterpret_cast<const float4*>(src + j);
-          const float4 lv = lam4[v];
-          e[0] = C ? g.x : __fmul_rn(g.x, rk);
-          e[1] = C ? g.y : __fmul_rn(g.y, rk);
-          e[2] = C ? g.z : __fmul_rn(g.z, rk);
-          e[3] = C ? g.w : __fmul_rn(g.w, rk);
-          e[0] = __fmul_rn(e[0], lv.x);
-          e[1] = __fmul_rn(e[1], lv.y);
-          e[2] = __fmul_rn(e[2], lv.z);
-          e[3] = __fmul_rn(e[3], lv.w);
-        } else {
+    if (rr < kin && vec) {
+      const float* src = C ? C + (in_off[b] + rr) * ldc : W0T + rr * (long long)n;
+      const float rk = C ? 1.f : r[(long long)b * n0 + rr];
+      const float4* src4 = reinterpret_cast<const float4*>(src);
+      const int nvn = n >> 2;  // float4 of real columns
+      for (int v0 = 0; v0 < nv; v0 += 32 * kBuildVec) {
+        float4 g[kBuildVec], lv[kBuildVec];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int jj = j + t;
-            if (jj < n) {
-              const float g = C ? src[jj] : __fmul_rn(src[jj], rk);
-              e[t] = __fmul_rn(g, lam[(long long)b * n + jj]);
-            }
+        for (int t = 0; t < kBuildVec; ++t) {
+          const int v = v0 + 32 * t + lane;
+          g[t] = v < nvn ? src4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+          lv[t] = v < nvn ? lam4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int t = 0; t < kBuildVec; ++t) {
+          const int v = v0 + 32 * t + lane;
+          if (v >= nv) break;
+          float e[4] = {C ? g[t].x : __fmul_rn(g[t].x, rk), C ? g[t].y : __fmul_rn(g[t].y, rk),
+                        C ? g[t].z : __fmul_rn(g[t].z, rk), C ? g[t].w : __fmul_rn(g[t].w, rk)};
+          e[0] = __fmul_rn(e[0], lv[t].x);
+          e[1] = __fmul_rn(e[1], lv[t].y);
+          e[2] = __fmul_rn(e[2], lv[t].z);
+          e[3] = __fmul_rn(e[3], lv[t].w);
+          float4 h, l;
+          split4(e, h, l);
+          dh[v] = h;
+          dl[v] = l;
+        }
+      }
+    } else if (rr < kin) {
+      const float* src = C ? C + (in_off[b] + rr) * ldc : W0T + rr * (long long)n;
+      const float rk = C ? 1.f : r[(long long)b * n0 + rr];
+      for (int v = lane; v < nv; v += 32) {
+        float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int jj = 4 * v + t;
+          if (jj < n) {
+            const float gg = C ? src[jj] : __fmul_rn(src[jj], rk);
+            e[t] = __fmul_rn(gg, lam[(long long)b * n + jj]);
           }
         }
         float4 h, l;
@@ -204,8 +230,17 @@ __global__ void __launch_bounds__(256) zw_colsum_part_kernel(
   const int r0 = ch * kChunk, r1 = min(kb, r0 + kChunk);
   const float* p = C + (off[b] + r0) * ldc + j;
   float s = 0.f, comp = 0.f;
-#pragma unroll 4
-  for (int row = r0; row < r1; ++row) {
+  int row = r0;
+  // eight loads in flight per thread, then the fixed-order compensated sum
+  for (; row + 8 <= r1; row += 8) {
+    float v[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) v[t] = p[(long long)t * ldc];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) neumaier(s, comp, fabsf(v[t]));
+    p += 8LL * ldc;
+  }
+  for (; row < r1; ++row) {
     neumaier(s, comp, fabsf(*p));
     p += ldc;
   }
