@@ -12,8 +12,9 @@
 // the epilogue warps add the chunk partials into fp32 registers with
 // round-to-nearest adds: the long sum over K is an ordinary fp32 sum.
 //
-// Kernel structure (one 128 x 128 output tile per CTA, N tile fastest in the
-// 1-D grid so the CTAs reading the same A rows are resident together; 6 warps):
+// Kernel structure (persistent, one CTA per SM walking 128 x 128 output tiles
+// with the N tile fastest so the CTAs reading the same A rows run together;
+// 6 warps):
 //   warp 4 / one thread : TMA producer -- per K chunk, four 128 x 32 fp32
 //                         tiles (A hi/lo, B hi/lo) into a 3-stage ring of
 //                         shared memory with 128-byte swizzle, each stage
@@ -91,11 +92,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __shared__ uint32_t tmem_slot;
   __shared__ int failed;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // N tile fastest: the CTAs that share an A row tile run together, so the
-  // (large) A operand streams from HBM once and the other N tiles hit L2
+  // Persistent: the CTA walks tiles blockIdx.x, + gridDim.x, ... with the N
+  // tile fastest, so the CTAs that share an A row tile run together (the
+  // large A operand streams from HBM once, the other N tiles hit L2); stage,
+  // TMEM-buffer and phase counters run on across tiles, so the next tile's
+  // loads and MMAs overlap the previous tile's accumulation and stores.
   const int n_tiles = (a.N + TC_BN - 1) / TC_BN;
-  const int m0 = (blockIdx.x / n_tiles) * TC_BM, n0 = (blockIdx.x % n_tiles) * TC_BN;
+  const int tiles = ((a.M + TC_BM - 1) / TC_BM) * n_tiles;
   const int nk = (a.K + TC_BK - 1) / TC_BK;
+  const volatile int* vfailed = &failed;
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -122,83 +127,104 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (warp == 4) {
     if (lane == 0) {  // TMA producer
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % TC_STAGES;
-        const unsigned round = kb / TC_STAGES;
-        if (kb >= TC_STAGES && !mbar_wait(&empty[s], (round - 1) & 1, kSpinLimit)) {
-          failed = 1;
-          break;
+      unsigned g = 0;  // chunks loaded by this CTA
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * TC_BM, n0 = (tile % n_tiles) * TC_BN;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % TC_STAGES;
+          if (g >= TC_STAGES &&
+              !mbar_wait(&empty[s], ((g / TC_STAGES) - 1) & 1, kSpinLimit, vfailed)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * STAGE_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(st, &mAh, &full[s], kb * TC_BK, m0);
+          tma_load_2d(st + TILE_A_BYTES, &mAl, &full[s], kb * TC_BK, m0);
+          tma_load_2d(st + 2 * TILE_A_BYTES, &mBh, &full[s], kb * TC_BK, n0);
+          tma_load_2d(st + 2 * TILE_A_BYTES + TILE_B_BYTES, &mBl, &full[s], kb * TC_BK, n0);
         }
-        uint8_t* st = smem + s * STAGE_BYTES;
-        mbar_expect_tx(&full[s], STAGE_BYTES);
-        tma_load_2d(st, &mAh, &full[s], kb * TC_BK, m0);
-        tma_load_2d(st + TILE_A_BYTES, &mAl, &full[s], kb * TC_BK, m0);
-        tma_load_2d(st + 2 * TILE_A_BYTES, &mBh, &full[s], kb * TC_BK, n0);
-        tma_load_2d(st + 2 * TILE_A_BYTES + TILE_B_BYTES, &mBl, &full[s], kb * TC_BK, n0);
       }
+      if (!ok) failed = 1;
+      // the copies still in flight land before the CTA exits
+      for (unsigned k = g > TC_STAGES ? g - TC_STAGES : 0; k < g; ++k)
+        if (!mbar_wait(&full[k % TC_STAGES], (k / TC_STAGES) & 1, kSpinLimit)) failed = 1;
     }
   } else if (warp == 5) {
     if (lane == 0) {  // MMA issuer
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % TC_STAGES;
-        const int q = kb % NBUF;
-        if (!mbar_wait(&full[s], (kb / TC_STAGES) & 1, kSpinLimit) ||
-            (kb >= NBUF && !mbar_wait(&acc_free[q], ((kb / NBUF) - 1) & 1, kSpinLimit))) {
-          failed = 1;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-        const uint32_t ah = base, al = base + TILE_A_BYTES;
-        const uint32_t bh = base + 2 * TILE_A_BYTES, bl = bh + TILE_B_BYTES;
-        const uint32_t dst = tmem + (uint32_t)(q * TC_BN);
+      unsigned g = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % TC_STAGES;
+          const int q = g % NBUF;
+          if (!mbar_wait(&full[s], (g / TC_STAGES) & 1, kSpinLimit, vfailed) ||
+              (g >= NBUF && !mbar_wait(&acc_free[q], ((g / NBUF) - 1) & 1, kSpinLimit, vfailed))) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t ah = base, al = base + TILE_A_BYTES;
+          const uint32_t bh = base + 2 * TILE_A_BYTES, bl = bh + TILE_B_BYTES;
+          const uint32_t dst = tmem + (uint32_t)(q * TC_BN);
 #pragma unroll
-        for (int j = 0; j < TC_BK / 8; ++j) {
-          const uint32_t off = j * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
-          mma_tf32(dst, sw128_desc(al + off), sw128_desc(bh + off), j > 0 ? 1u : 0u);
-          mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bl + off), 1u);
-          mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bh + off), 1u);
+          for (int j = 0; j < TC_BK / 8; ++j) {
+            const uint32_t off = j * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
+            mma_tf32(dst, sw128_desc(al + off), sw128_desc(bh + off), j > 0 ? 1u : 0u);
+            mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bl + off), 1u);
+            mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bh + off), 1u);
+          }
+          mma_commit(&empty[s]);
+          mma_commit(&acc_full[q]);
         }
-        mma_commit(&empty[s]);
-        mma_commit(&acc_full[q]);
       }
+      if (!ok) failed = 1;
       // every MMA issued above has finished before TMEM can be freed
       mma_commit(&done);
       if (!mbar_wait(&done, 0, kDoneSpinLimit)) failed = 1;
     }
-  } else {  // accumulator warps 0-3: row m0 + 32 warp + lane
-    float acc[TC_BN];
-#pragma unroll
-    for (int j = 0; j < TC_BN; ++j) acc[j] = 0.f;
+  } else {  // accumulator warps 0-3: row m0 + 32 warp + lane of each tile
     const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-    for (int kb = 0; kb < nk; ++kb) {
-      const int q = kb % NBUF;
-      if (!mbar_wait(&acc_full[q], (kb / NBUF) & 1, kDoneSpinLimit)) {
-        failed = 1;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    unsigned g = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+      const int m0 = (tile / n_tiles) * TC_BM, n0 = (tile % n_tiles) * TC_BN;
+      float acc[TC_BN];
 #pragma unroll
-      for (int c0 = 0; c0 < TC_BN; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(lane_addr + q * TC_BN + c0, v);
-        tmem_wait_ld(v);
+      for (int j = 0; j < TC_BN; ++j) acc[j] = 0.f;
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int q = g % NBUF;
+        if (!mbar_wait(&acc_full[q], (g / NBUF) & 1, kDoneSpinLimit, vfailed)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], __uint_as_float(v[j]));
+        for (int c0 = 0; c0 < TC_BN; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(lane_addr + q * TC_BN + c0, v);
+          tmem_wait_ld(v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], __uint_as_float(v[j]));
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_free[q]);
       }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_free[q]);
+      if (!ok) break;
+      const int row = m0 + warp * 32 + lane;
+      if (row < a.M) {
+        float* crow = a.C + (long long)row * a.ldc;
+#pragma unroll
+        for (int j = 0; j < TC_BN; ++j) {
+          const int n = n0 + j;
+          if (n < a.N) crow[n] = a.bias ? __fadd_rn(acc[j], a.bias[n]) : acc[j];
+        }
+      }
     }
-    const int row = m0 + warp * 32 + lane;
-    if (row < a.M && !failed) {
-      float* crow = a.C + (long long)row * a.ldc;
-#pragma unroll
-      for (int j = 0; j < TC_BN; ++j) {
-        const int n = n0 + j;
-        if (n < a.N) crow[n] = a.bias ? __fadd_rn(acc[j], a.bias[n]) : acc[j];
-      }
-    }
+    if (!ok) failed = 1;
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -271,7 +297,8 @@ int tc_gemm_3xtf32(int M, int N, int K, const float* Ah, const float* Al, int ld
   TcArgs args{M, N, K, ldc, C, bias, err};
   const long long tiles = (long long)((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
   if (tiles > 0x7fffffffLL) return fail(VCB_ERR_UNSUPPORTED, "%s: %lld output tiles", who, tiles);
-  tc_gemm_kernel<<<(unsigned)tiles, TC_THREADS, TC_SMEM, st>>>(mAh, mAl, mBh, mBl, args);
+  const int grid = (int)std::min<long long>(tiles, sm_count());  // persistent: one CTA per SM
+  tc_gemm_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(mAh, mAl, mBh, mBl, args);
   return check_launch(who);
 }
 
