@@ -42,19 +42,27 @@
 namespace vcb {
 namespace {
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
-constexpr int NBUF = 4;                  // TMEM chunk buffers
-constexpr int TMEM_COLS = NBUF * TC_BN;  // 512: the whole tensor memory
-constexpr int TC_THREADS = 192;          // 4 accumulator warps + producer + MMA
+constexpr int TC_BM = 128, TC_BK = 32;
+constexpr int TMEM_COLS = 512;                   // the whole tensor memory
 constexpr int TILE_A_BYTES = TC_BM * TC_BK * 4;  // 16 KB
-constexpr int TILE_B_BYTES = TC_BN * TC_BK * 4;  // 16 KB
-constexpr int STAGE_BYTES = 2 * TILE_A_BYTES + 2 * TILE_B_BYTES;
-constexpr int TC_SMEM = TC_STAGES * STAGE_BYTES + 1024;  // + alignment slack
 constexpr unsigned kSpinLimit = 1u << 22;      // pipeline waits (a stage is microseconds)
 constexpr unsigned kDoneSpinLimit = 1u << 27;  // the epilogue waits out the whole mainloop
 
-// instruction descriptor: D f32, A/B tf32, both K-major, N = 128, M = 128
-constexpr uint32_t kIdesc = tc5::idesc_tf32(TC_BM, TC_BN);
+// Tile shapes: BN = 128 (3 smem stages, 4 TMEM chunk buffers, 4 accumulator
+// warps) or BN = 256 (2 stages, 2 buffers, 8 accumulator warps; per FLOP
+// half the A bytes from L2 into shared memory).
+template <int BN>
+struct TcCfg {
+  static constexpr int kStages = BN == 256 ? 2 : 3;
+  static constexpr int kNbuf = TMEM_COLS / BN;
+  static constexpr int kEpiWarps = BN / 32;  // warp w: TMEM lanes 32 (w % 4).., columns 128 (w / 4)..
+  static constexpr int kThreads = (kEpiWarps + 2) * 32;
+  static constexpr int kTileB = BN * TC_BK * 4;
+  static constexpr int kStage = 2 * TILE_A_BYTES + 2 * kTileB;
+  static constexpr int kSmem = kStages * kStage + 1024;  // + alignment slack
+  // instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = BN
+  static constexpr uint32_t kIdesc = tc5::idesc_tf32(TC_BM, BN);
+};
 
 using namespace tc5;
 
@@ -67,12 +75,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// D (tensor memory) (+)= A B^T for one K step of the 128 x 128 tile.
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db,
-                                         uint32_t accumulate) {
-  mma_tf32_ss(tmem_d, da, db, kIdesc, accumulate);
-}
-
 struct TcArgs {
   int M, N, K, ldc;
   float* C;
@@ -80,10 +82,15 @@ struct TcArgs {
   int* err;           // set to 1 when a bounded wait expired
 };
 
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <int BN>
+__global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
                    const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
                    const TcArgs a) {
+  using Cfg = TcCfg<BN>;
+  constexpr int TC_BN = BN, TC_STAGES = Cfg::kStages, NBUF = Cfg::kNbuf;
+  constexpr int TILE_B_BYTES = Cfg::kTileB, STAGE_BYTES = Cfg::kStage;
+  constexpr int EPI = Cfg::kEpiWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -108,7 +115,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int q = 0; q < NBUF; ++q) {
       mbar_init(&acc_full[q], 1);
-      mbar_init(&acc_free[q], 4);  // one arrival per accumulator warp
+      mbar_init(&acc_free[q], EPI);  // one arrival per accumulator warp
     }
     mbar_init(&done, 1);
     failed = 0;
@@ -125,7 +132,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_slot;
 
-  if (warp == 4) {
+  if (warp == EPI) {
     if (lane == 0) {  // TMA producer
       unsigned g = 0;  // chunks loaded by this CTA
       bool ok = true;
@@ -151,7 +158,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (unsigned k = g > TC_STAGES ? g - TC_STAGES : 0; k < g; ++k)
         if (!mbar_wait(&full[k % TC_STAGES], (k / TC_STAGES) & 1, kSpinLimit)) failed = 1;
     }
-  } else if (warp == 5) {
+  } else if (warp == EPI + 1) {
     if (lane == 0) {  // MMA issuer
       unsigned g = 0;
       bool ok = true;
@@ -172,9 +179,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < TC_BK / 8; ++j) {
             const uint32_t off = j * 32;  // 8 tf32 = 32 bytes along K inside the swizzle atom
-            mma_tf32(dst, sw128_desc(al + off), sw128_desc(bh + off), j > 0 ? 1u : 0u);
-            mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bl + off), 1u);
-            mma_tf32(dst, sw128_desc(ah + off), sw128_desc(bh + off), 1u);
+            mma_tf32_ss(dst, sw128_desc(al + off), sw128_desc(bh + off), Cfg::kIdesc,
+                        j > 0 ? 1u : 0u);
+            mma_tf32_ss(dst, sw128_desc(ah + off), sw128_desc(bl + off), Cfg::kIdesc, 1u);
+            mma_tf32_ss(dst, sw128_desc(ah + off), sw128_desc(bh + off), Cfg::kIdesc, 1u);
           }
           mma_commit(&empty[s]);
           mma_commit(&acc_full[q]);
@@ -185,15 +193,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mma_commit(&done);
       if (!mbar_wait(&done, 0, kDoneSpinLimit)) failed = 1;
     }
-  } else {  // accumulator warps 0-3: row m0 + 32 warp + lane of each tile
-    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  } else {  // accumulator warps: row m0 + 32 (warp % 4) + lane, columns 128 (warp / 4)..
+    const int cg = 128 * (warp >> 2);
+    const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + cg;
     unsigned g = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
       const int m0 = (tile / n_tiles) * TC_BM, n0 = (tile % n_tiles) * TC_BN;
-      float acc[TC_BN];
+      float acc[128];
 #pragma unroll
-      for (int j = 0; j < TC_BN; ++j) acc[j] = 0.f;
+      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
       for (int kb = 0; kb < nk; ++kb, ++g) {
         const int q = g % NBUF;
         if (!mbar_wait(&acc_full[q], (g / NBUF) & 1, kDoneSpinLimit, vfailed)) {
@@ -202,7 +211,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-        for (int c0 = 0; c0 < TC_BN; c0 += 16) {
+        for (int c0 = 0; c0 < 128; c0 += 16) {
           uint32_t v[16];
           tmem_ld16(lane_addr + q * TC_BN + c0, v);
           tmem_wait_ld(v);
@@ -214,12 +223,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) mbar_arrive(&acc_free[q]);
       }
       if (!ok) break;
-      const int row = m0 + warp * 32 + lane;
+      const int row = m0 + (warp & 3) * 32 + lane;
       if (row < a.M) {
         float* crow = a.C + (long long)row * a.ldc;
 #pragma unroll
-        for (int j = 0; j < TC_BN; ++j) {
-          const int n = n0 + j;
+        for (int j = 0; j < 128; ++j) {
+          const int n = n0 + cg + j;
           if (n < a.N) crow[n] = a.bias ? __fadd_rn(acc[j], a.bias[n]) : acc[j];
         }
       }
@@ -260,16 +269,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Row-major (rows x cols, leading dimension ld) fp32 matrix as 128 x 32 tiles
-// with 128-byte swizzle; out-of-range reads fill zeros.
-int make_map(CUtensorMap* map, const float* p, int rows, int cols, int ld, const char* who) {
+// Row-major (rows x cols, leading dimension ld) fp32 matrix as box_rows x 32
+// tiles with 128-byte swizzle; out-of-range reads fill zeros.
+int make_map(CUtensorMap* map, const float* p, int rows, int cols, int ld, int box_rows,
+             const char* who) {
   auto fn = encode_fn();
   if (!fn) return fail(VCB_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", who);
   if ((reinterpret_cast<uintptr_t>(p) & 15) || (ld % 4) || ld < cols)
     return fail(VCB_ERR_INVALID, "%s: operand must be 16-byte aligned with ld %% 4 == 0", who);
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {TC_BK, 128};
+  cuuint32_t box[2] = {TC_BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -286,19 +296,28 @@ int tc_gemm_3xtf32(int M, int N, int K, const float* Ah, const float* Al, int ld
                    const float* Bh, const float* Bl, int ldb, float* C, int ldc,
                    const float* bias, int* err, cudaStream_t st, const char* who) {
   if (M == 0 || N == 0) return VCB_OK;
+  const int bn = N > 128 ? 256 : 128;  // wide outputs: half the A traffic per FLOP
   CUtensorMap mAh, mAl, mBh, mBl;
-  int rc = make_map(&mAh, Ah, M, K, lda, who);
-  if (!rc) rc = make_map(&mAl, Al, M, K, lda, who);
-  if (!rc) rc = make_map(&mBh, Bh, N, K, ldb, who);
-  if (!rc) rc = make_map(&mBl, Bl, N, K, ldb, who);
-  if (rc) return rc;
-  rc = ensure_smem(reinterpret_cast<const void*>(tc_gemm_kernel), TC_SMEM);
+  int rc = make_map(&mAh, Ah, M, K, lda, TC_BM, who);
+  if (!rc) rc = make_map(&mAl, Al, M, K, lda, TC_BM, who);
+  if (!rc) rc = make_map(&mBh, Bh, N, K, ldb, bn, who);
+  if (!rc) rc = make_map(&mBl, Bl, N, K, ldb, bn, who);
   if (rc) return rc;
   TcArgs args{M, N, K, ldc, C, bias, err};
-  const long long tiles = (long long)((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
+  const long long tiles = (long long)((M + TC_BM - 1) / TC_BM) * ((N + bn - 1) / bn);
   if (tiles > 0x7fffffffLL) return fail(VCB_ERR_UNSUPPORTED, "%s: %lld output tiles", who, tiles);
   const int grid = (int)std::min<long long>(tiles, sm_count());  // persistent: one CTA per SM
-  tc_gemm_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(mAh, mAl, mBh, mBl, args);
+  if (bn == 256) {
+    rc = ensure_smem(reinterpret_cast<const void*>(tc_gemm_kernel<256>), TcCfg<256>::kSmem);
+    if (rc) return rc;
+    tc_gemm_kernel<256><<<grid, TcCfg<256>::kThreads, TcCfg<256>::kSmem, st>>>(mAh, mAl, mBh,
+                                                                            mBl, args);
+  } else {
+    rc = ensure_smem(reinterpret_cast<const void*>(tc_gemm_kernel<128>), TcCfg<128>::kSmem);
+    if (rc) return rc;
+    tc_gemm_kernel<128><<<grid, TcCfg<128>::kThreads, TcCfg<128>::kSmem, st>>>(mAh, mAl, mBh,
+                                                                            mBl, args);
+  }
   return check_launch(who);
 }
 
