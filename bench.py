@@ -267,22 +267,29 @@ def roofline_cfg2(tc_path, achieved, ffma_peak, flop_per_box):
                 'kernel': 'vcb_mlp_crown (crown_mlp_kernel)', 'flop_per_box': flop_per_box,
                 'peak_source': 'measured live: vcb_probe_ffma FFMA loop (MEASURED_PEAKS.json '
                                'has no FP32 SIMT figure)'}
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, 'MEASURED_PEAKS.json')))
-    except (OSError, ValueError):
-        pass
-    bf16 = peaks.get('bf16_tflops')
-    peak = (bf16 if bf16 else 1590.0) / 6.0
+    peak, source = tf32x3_peak()
     return {'bound': 'tensor', 'achieved': achieved, 'peak': peak, 'unit': 'TFLOP/s',
             'frac': achieved / peak, 'traffic': read_traffic('crown_tc_cfg2.md'),
             'kernel': 'vcb_mlp_crown (crown_tc_kernel, tcgen05 3xTF32; the step also runs '
                       'crown_tc_images, <1% of its time)',
             'flop_per_box': flop_per_box,
             'frac_of_ffma_peak': achieved / ffma_peak if ffma_peak else None,
-            'peak_source': ('of measured: MEASURED_PEAKS.json bf16_tflops / 2 (TF32 rate) / 3 '
-                            '(3xTF32 products)') if bf16 else
-                           'of fallback: 1590 TFLOP/s bf16 / 2 / 3'}
+            'peak_source': source}
+
+
+def tf32x3_peak():
+    """fp32-equivalent rate of 3xTF32 on the tensor cores: the measured bf16
+    dense peak / 2 (TF32 rate) / 3 (products per fp32 product)."""
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, 'MEASURED_PEAKS.json')))
+    except (OSError, ValueError):
+        pass
+    bf16 = peaks.get('bf16_tflops')
+    if bf16:
+        return bf16 / 6.0, ('of measured: MEASURED_PEAKS.json bf16_tflops / 2 (TF32 rate) / 3 '
+                            '(3xTF32 products)')
+    return 1590.0 / 6.0, 'of fallback: 1590 TFLOP/s bf16 / 2 / 3'
 
 
 def run_ours(args):
@@ -563,9 +570,11 @@ def run_cfg34(args):
         Q = w['spec_W'].shape[0]
         flop = 20 * Dn * 4 * Q * sw + 4 * sw * Dn
         tcl = {L: (T(c[0]), T(c[1])) for L, c in clamps.items()}
+        xld, xhd = T(xl).float(), T(xh).float()  # resident in HBM before the timed region
+        sWd, sbd = T(w['spec_W']).float(), T(w['spec_b']).float()
 
         def step():
-            return wide.alpha_crown_domains(xl, xh, gg, w['spec_W'], w['spec_b'], tcl, dev,
+            return wide.alpha_crown_domains(xld, xhd, gg, sWd, sbd, tcl, dev,
                                             n_iters=20, lr=0.1)
 
         def cpu():
@@ -629,6 +638,15 @@ def run_cfg34(args):
                          'peak_source': 'measured live: vcb_probe_ffma'},
             'clocks': clocks,
         }
+        if args.config == 'cfg3' and wide.last_stats.get('path') == 'tc':
+            tpk, src = tf32x3_peak()
+            line['roofline'] = {
+                'bound': 'tensor', 'achieved': achieved, 'peak': tpk, 'unit': 'TFLOP/s',
+                'frac': achieved / tpk, 'traffic': None, 'flop_per_step': flop,
+                'kernel': 'alpha loop on tcgen05 3xTF32 GEMMs with fused epilogues '
+                          '(vcb_wtc_*), one CUDA graph per call; the step also runs the '
+                          'SIMT wide IBP',
+                'frac_of_ffma_peak': achieved / peak if peak else None, 'peak_source': src}
         if world == 1 and not args.no_cpu_baseline:
             rate, sample = cpu()
             line['cpu_baseline'] = {'value': rate, 'unit': 'domains/s',

@@ -465,6 +465,82 @@ int vcb_tc_gemm(int32_t M, int32_t N, int32_t K, const float* A_hi,
                 const float* B_lo, int32_t ldb, const float* bias, float* C,
                 int32_t ldc, int32_t* err, void* stream);
 
+/* vcb_tc_gemm with a device gate: when *gate == 0 (gate non-NULL) the launch
+ * returns without touching C, so a host can queue work that the device
+ * decides to skip (the alpha-CROWN loop's stop test). */
+int vcb_tc_gemm_gated(int32_t M, int32_t N, int32_t K, const float* A_hi,
+                      const float* A_lo, int32_t lda, const float* B_hi,
+                      const float* B_lo, int32_t ldb, const float* bias, float* C,
+                      int32_t ldc, int32_t* err, const int32_t* gate, void* stream);
+
+/* ---- Tensor-core alpha-CROWN loop for wide MLPs (the Adam loop of
+ * _ibp_crown_bab, src/vibecheck/verify_milp.py:2762-2807, and
+ * _run_alpha_crown_inputsplit_batched, verify_zono_bnb.py:5248-5288).  Each
+ * layer is one 3xTF32 GEMM (operands as vcb_tf32_split pairs, 16-byte
+ * aligned, ld % 4 == 0) whose epilogue does the layer's bound arithmetic and
+ * writes the next GEMM's operand as a TF32 hi / lo pair.  R = D domains x Q
+ * spec rows; row r belongs to domain r / Q and per-domain arrays are D x N.
+ * Row sums leave as one partial per 64-column group, at part[r * ldpart +
+ * part0 + n / 64].  Every call takes an optional device gate and does
+ * nothing when *gate == 0; err as for vcb_tc_gemm. ---- */
+
+/* Relaxation records of one ReLU layer from its bounds (n = D x width
+ * neurons): rx (n x 2 floats, 8-byte aligned) = (upper slope, negated on
+ * stable neurons; intercept factor) and pos = the lower slope (1 active, 0
+ * dead, the min-area choice on unstable neurons: the alpha init, which the
+ * Adam steps then move on unstable neurons only). */
+int vcb_wtc_relax_init(int64_t n, const float* sb_lo, const float* sb_hi, float* rx,
+                       float* pos, const int32_t* gate, void* stream);
+
+/* Back-substitution through one layer: C = A B^T (R x N; A = coef (R x K),
+ * B = W^T (N x K)) kept as the record; coef_o = relaxation of the ReLU below
+ * (pos / rx from vcb_wtc_relax_init, D x N) + beta (or NULL), split into
+ * out_hi / out_lo; partials = intercept sum + coef_o . b_next (b_next (N) or
+ * NULL). */
+int vcb_wtc_back_gemm(int32_t R, int32_t Q, int32_t N, int32_t K, const float* A_hi,
+                      const float* A_lo, int32_t lda, const float* B_hi,
+                      const float* B_lo, int32_t ldb, float* C, int32_t ldc,
+                      const float* pos, const float* rx,
+                      const float* beta, const float* b_next, float* out_hi,
+                      float* out_lo, int32_t ldo, float* part, int32_t ldpart,
+                      int32_t part0, int32_t* err, const int32_t* gate, void* stream);
+
+/* Input layer: e = A B^T (R x N, N = input width) -> partials sum(e+ xl +
+ * e- xh) over the domain's box (xl, xh: D x N) and the adjoint seed xl [e >=
+ * 0] + xh [e <= 0] split into g_hi / g_lo. */
+int vcb_wtc_input_gemm(int32_t R, int32_t Q, int32_t N, int32_t K, const float* A_hi,
+                       const float* A_lo, int32_t lda, const float* B_hi,
+                       const float* B_lo, int32_t ldb, const float* xl, const float* xh,
+                       float* g_hi, float* g_lo, int32_t ldg, float* part,
+                       int32_t ldpart, int32_t part0, int32_t* err,
+                       const int32_t* gate, void* stream);
+
+/* Adjoint through one layer: ga = A B^T + bias (A = g (R x K), B = W (N x
+ * K)); with the record rec (R x N: the C that entered this ReLU's
+ * relaxation) and the relaxation pos / rx: dcontrib = [unstable] max(e, 0) ga (R x N, ld ldd) and the
+ * next adjoint [e >= 0] pos ga + [e <= 0] (neg ga + icp) split into g_hi /
+ * g_lo (or NULL). */
+int vcb_wtc_adj_gemm(int32_t R, int32_t Q, int32_t N, int32_t K, const float* A_hi,
+                     const float* A_lo, int32_t lda, const float* B_hi, const float* B_lo,
+                     int32_t ldb, const float* bias, const float* rec, int32_t ldrec,
+                     const float* pos, const float* rx,
+                     float* dcontrib, int32_t ldd, float* g_hi, float* g_lo, int32_t ldg,
+                     int32_t* err, const int32_t* gate, void* stream);
+
+/* lb[r] = acc0[r] + part[r][0] + ... + part[r][nparts - 1] (in order); best =
+ * lb (first) or the NaN-propagating max(best, lb) (best may be NULL);
+ * *open_flag = 1 when some best <= 0. */
+int vcb_wtc_finish(int32_t R, const float* acc0, const float* part, int32_t ldpart,
+                   int32_t nparts, float* lb, float* best, int32_t first,
+                   int32_t* open_flag, const int32_t* gate, void* stream);
+
+/* d(sum lb)/d(alpha) = sum over each domain's Q rows of dcontrib (rows in
+ * order), then one Adam step (torch defaults; step number `step`, learning
+ * rate lr) on -sum(lb) for alpha / m1 / m2 (D x n) and the clamp to [0, 1]. */
+int vcb_wtc_adam(int32_t D, int32_t Q, int32_t n, const float* dcontrib, int32_t ldd,
+                 float* alpha, float* m1, float* m2, float lr, int32_t step,
+                 const int32_t* gate, void* stream);
+
 /* ---- DeepZ zonotope for wide MLPs (_forward_zonotope_graph_batched,
  * src/vibecheck/verify_zono_bnb.py:3079-4074, layer by layer).  Generators
  * are generator-major rows: leaf b owns rows [off[b], off[b+1]) of one

@@ -239,3 +239,97 @@ def test_cfg4_cnn_against_oracle():
     assert close(N(lb), lb_ref), max_excess(N(lb), lb_ref)
     assert close(N(acc), acc_ref)
     _ = y0
+
+
+def _cfg3_domains(n_split, n_iters_unused=None):
+    w = wk.cfg3(seed=0)
+    ggc = wk.mlp_gg(w['layers'])
+    root = ob.ibp_forward_batched(w['xl'][None], w['xh'][None], ggc)
+    picked, clamps = wk.split_domains({L: v[0][0] for L, v in root.items()},
+                                      {L: v[1][0] for L, v in root.items()}, n_split)
+    Dn = 1 << len(picked)
+    xl = np.broadcast_to(w['xl'], (Dn, w['xl'].size)).copy()
+    xh = np.broadcast_to(w['xh'], (Dn, w['xh'].size)).copy()
+    return w, ggc, xl, xh, clamps
+
+
+def test_tc_alpha_loop_against_oracle():
+    """The tensor-core alpha loop (3xTF32 GEMMs, fused relaxation / adjoint /
+    Adam stages) on the cfg3 network against the numpy oracle."""
+    w, ggc, xl, xh, clamps = _cfg3_domains(5)
+    ref, _ = ob.alpha_beta_crown_domains(xl, xh, ggc, w['spec_W'], w['spec_b'], clamps,
+                                         n_iters=4, lr=0.1)
+    gg = wk.mlp_gg(w['layers'], DEV)
+    best, _ = wide.alpha_crown_domains(xl, xh, gg, w['spec_W'], w['spec_b'], clamps, DEV,
+                                       n_iters=4, lr=0.1, tc=True)
+    assert wide.last_stats['path'] == 'tc'
+    assert close(N(best), ref, rtol=5e-3, atol=1e-4), max_excess(N(best), ref, rtol=5e-3,
+                                                                 atol=1e-4)
+
+
+def test_tc_alpha_loop_matches_simt_at_cfg3_size():
+    """cfg3 itself (1,024 domains x 9 rows, 20 iterations): the size routing
+    picks the tensor cores, and they agree with the SIMT layer kernels."""
+    w, ggc, xl, xh, clamps = _cfg3_domains(10)
+    gg = wk.mlp_gg(w['layers'], DEV)
+    tcl = {L: (T(c[0]), T(c[1])) for L, c in clamps.items()}
+    best_tc, _ = wide.alpha_crown_domains(xl, xh, gg, w['spec_W'], w['spec_b'], tcl, DEV,
+                                          n_iters=20, lr=0.1)
+    assert wide.last_stats['path'] == 'tc'
+    best_s, _ = wide.alpha_crown_domains(xl, xh, gg, w['spec_W'], w['spec_b'], tcl, DEV,
+                                         n_iters=20, lr=0.1, tc=False)
+    assert close(N(best_tc), N(best_s), rtol=5e-3, atol=1e-4), max_excess(
+        N(best_tc), N(best_s), rtol=5e-3, atol=1e-4)
+
+
+@pytest.mark.parametrize('eps', [None, 1e-6])
+def test_tc_alpha_loop_stops_like_simt(eps):
+    """Stop rule (every best lb > 0, then the early-stop epsilon): shift the
+    spec offsets so that the batch closes after a few iterations; the device
+    gates must end the tensor-core loop at the same iteration as the SIMT loop
+    (lb is b_q + an alpha-dependent part, and alpha's trajectory does not
+    depend on b_q)."""
+    w, ggc, xl, xh, clamps = _cfg3_domains(5)
+    gg = wk.mlp_gg(w['layers'], DEV)
+    wn = wide.wide_net(gg, DEV)
+    xlt, xht = T(xl).float(), T(xh).float()
+    tcl = {L: (T(c[0]), T(c[1])) for L, c in clamps.items()}
+    sb = wide.wide_ibp(wn, xlt, xht, tcl)
+    W_q, b_q = T(w['spec_W']).float(), T(w['spec_b']).float()
+    mins = []
+    for k in range(1, 7):
+        b = wide.alpha_loop(wn, xlt, xht, sb, W_q, b_q, k, 0.1, tc=False)
+        mins.append(float(b.min()))
+    gaps = [mins[k] - mins[k - 1] for k in range(1, 6)]
+    k = max(range(1, 6), key=lambda i: gaps[i - 1])   # widest step: closes after k + 1 iterations
+    assert gaps[k - 1] > 1e-3
+    shift = -(mins[k - 1] + mins[k]) / 2
+    b_s = b_q + shift
+    out_s = wide.alpha_loop(wn, xlt, xht, sb, W_q, b_s, 10, 0.1, early_stop_eps=eps, tc=False)
+    it_s = wide.last_stats['iterations']
+    out_t = wide.alpha_loop(wn, xlt, xht, sb, W_q, b_s, 10, 0.1, early_stop_eps=eps, tc=True)
+    it_t = wide.last_stats['iterations']()
+    assert it_t == it_s and (eps is not None or it_s == k + 1), (it_t, it_s, k)
+    assert bool((out_t > 0).all()) == bool((out_s > 0).all())
+    assert close(N(out_t), N(out_s), rtol=5e-3, atol=1e-4)
+
+
+def test_tc_alpha_loop_graph_replay():
+    """Repeated calls with the same shapes replay the loop as a CUDA graph
+    from fixed buffers: each call's result follows its own inputs."""
+    w, ggc, xl, xh, clamps = _cfg3_domains(9)
+    gg = wk.mlp_gg(w['layers'], DEV)
+    wn = wide.wide_net(gg, DEV)
+    xlt, xht = T(xl).float(), T(xh).float()
+    tcl = {L: (T(c[0]), T(c[1])) for L, c in clamps.items()}
+    sb = wide.wide_ibp(wn, xlt, xht, tcl)
+    W_q, b_q = T(w['spec_W']).float(), T(w['spec_b']).float()
+    wide._tc_plan_cache.clear()
+    for k, shift in enumerate([0.0, 3.0, -2.0, 0.5]):
+        rng = np.random.default_rng(k)
+        W_k = W_q * T(rng.uniform(0.5, 1.5, W_q.shape)).float()
+        got = wide.alpha_loop(wn, xlt, xht, sb, W_k, b_q + shift, 6, 0.1, tc=True)
+        assert (wide._tc_plan_cache['plan'].graph is not None) == (k > 0)
+        ref = wide.alpha_loop(wn, xlt, xht, sb, W_k, b_q + shift, 6, 0.1, tc=False)
+        assert close(N(got), N(ref), rtol=5e-3, atol=1e-4), (k, max_excess(N(got), N(ref),
+                                                                           rtol=5e-3, atol=1e-4))

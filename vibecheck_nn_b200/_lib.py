@@ -79,6 +79,16 @@ SIGNATURES = {
                      ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, _P],
     'vcb_tf32_split': [ctypes.c_int64, _P, _P, _P, _P],
     'vcb_tc_gemm': [_I, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _I, _P, _P],
+    'vcb_tc_gemm_gated': [_I, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P],
+    'vcb_wtc_relax_init': [ctypes.c_int64, _P, _P, _P, _P, _P, _P],
+    'vcb_wtc_back_gemm': [_I, _I, _I, _I, _P, _P, _I, _P, _P, _I, _P, _I, _P, _P, _P, _P,
+                          _P, _P, _I, _P, _I, _I, _P, _P, _P],
+    'vcb_wtc_input_gemm': [_I, _I, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P, _P, _I, _P, _I,
+                           _I, _P, _P, _P],
+    'vcb_wtc_adj_gemm': [_I, _I, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _I, _P, _P, _P,
+                         _I, _P, _P, _I, _P, _P, _P],
+    'vcb_wtc_finish': [_I, _P, _P, _I, _I, _P, _P, _I, _P, _P, _P],
+    'vcb_wtc_adam': [_I, _I, _I, _P, _I, _P, _P, _P, ctypes.c_float, _I, _P, _P],
     'vcb_zw_relu': [_I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     'vcb_zw_build': [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P,
                      ctypes.c_int64, _P, _P, _P],

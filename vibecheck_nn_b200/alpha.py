@@ -86,7 +86,10 @@ def alpha_boundary_refine(desc, xl, xh, lb, W_q, b_q, qd, D, eps, iters,
     wn = desc.__dict__.get('_wide') or wide.WideNet(desc)
     desc.__dict__['_wide'] = wn
     try:
-        new = wide.alpha_loop(wn, xl_c, xh_c, sb, W_q, b_q, iters, 0.25, 0.98, 1e-6)
+        # SIMT layer kernels: the BaB engines' leaf counts are pinned to the
+        # reference's with this path's fp32 arithmetic
+        new = wide.alpha_loop(wn, xl_c, xh_c, sb, W_q, b_q, iters, 0.25, 0.98, 1e-6,
+                              tc=False)
     except (RuntimeError, torch.cuda.OutOfMemoryError):
         return lb  # opportunistic tightener, as in the reference
     lb = lb.clone()

@@ -40,4 +40,26 @@ __device__ __forceinline__ Slope decode_slope(float2 v, const float* alpha) {
   return s;
 }
 
+// Relaxation of one neuron from its pre-activation bounds as the wide
+// layer-wise passes apply it (verify_zono_bnb.py:511-521, 4413-4433): pos
+// multiplies e >= 0 (lower slope; alpha on unstable neurons when given), neg
+// multiplies e < 0 (upper slope), icp is the intercept factor of min(e, 0).
+struct RelaxTc {
+  float pos, neg, icp;
+  bool unstable;
+};
+
+__device__ __forceinline__ RelaxTc relax_tc(float lo, float hi, const float* alpha) {
+  RelaxTc r;
+  const float lb_r = fminf(lo, 0.f);
+  const float ub_r = fmaxf(fmaxf(hi, 0.f), __fadd_rn(lb_r, 1e-8f));
+  const float up_s = __fdiv_rn(ub_r, __fsub_rn(ub_r, lb_r));
+  const bool active = lo >= 0.f, dead = hi <= 0.f;
+  r.unstable = !active && !dead;
+  r.neg = up_s;
+  r.icp = __fmul_rn(-lb_r, up_s);
+  r.pos = active ? 1.f : (dead ? 0.f : (alpha ? *alpha : (up_s > 0.5f ? 1.f : 0.f)));
+  return r;
+}
+
 }  // namespace vcb

@@ -48,18 +48,21 @@ constexpr int TILE_A_BYTES = TC_BM * TC_BK * 4;  // 16 KB
 constexpr unsigned kSpinLimit = 1u << 22;      // pipeline waits (a stage is microseconds)
 constexpr unsigned kDoneSpinLimit = 1u << 27;  // the epilogue waits out the whole mainloop
 
-// Tile shapes: BN = 128 (3 smem stages, 4 TMEM chunk buffers, 4 accumulator
-// warps) or BN = 256 (2 stages, 2 buffers, 8 accumulator warps; per FLOP
-// half the A bytes from L2 into shared memory).
+// Tile shapes: BN = 128 (3 smem stages, 4 TMEM chunk buffers) or BN = 256
+// (2 stages, 2 buffers; per FLOP half the A bytes from L2 into shared
+// memory); 8 accumulator warps either way, warp w holding TMEM lanes
+// 32 (w % 4).. and kCols = BN / 2 columns from kCols (w / 4).
 template <int BN>
 struct TcCfg {
   static constexpr int kStages = BN == 256 ? 2 : 3;
   static constexpr int kNbuf = TMEM_COLS / BN;
-  static constexpr int kEpiWarps = BN / 32;  // warp w: TMEM lanes 32 (w % 4).., columns 128 (w / 4)..
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kCols = BN / 2;
   static constexpr int kThreads = (kEpiWarps + 2) * 32;
   static constexpr int kTileB = BN * TC_BK * 4;
   static constexpr int kStage = 2 * TILE_A_BYTES + 2 * kTileB;
-  static constexpr int kSmem = kStages * kStage + 1024;  // + alignment slack
+  // stages + the epilogue warps' staging blocks + alignment slack
+  static constexpr int kSmem = kStages * kStage + kEpiWarps * 32 * 33 * 4 + 1024;
   // instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = BN
   static constexpr uint32_t kIdesc = tc5::idesc_tf32(TC_BM, BN);
 };
@@ -80,9 +83,177 @@ struct TcArgs {
   float* C;
   const float* bias;  // (N) added to every row, or NULL
   int* err;           // set to 1 when a bounded wait expired
+  const int* gate;    // when non-NULL and *gate == 0 the launch does nothing
+  TcEpi ep;
 };
 
-template <int BN>
+// The epilogue stages 32 x 32 blocks (one warp's rows x 32 columns) through
+// shared memory so that every global access of a warp covers 128
+// contiguous bytes of one row; a pitch of 33 floats keeps both the row-wise
+// writes and the column-wise reads free of bank conflicts.
+constexpr int kStagePitch = 33;
+constexpr int kStageWarpBytes = 32 * kStagePitch * 4;
+
+// Rows of one warp go through the epilogue in batches: all global loads of
+// a batch are issued first (read-only path), then the arithmetic and the
+// stores, so a warp keeps a batch's worth of loads in flight.
+constexpr int kEpiBatch = 8;
+
+// Per-element inputs of one batch row (which of them are read depends on
+// the mode).
+struct EpiIn {
+  float x0, x1, x2, x3;
+};
+
+template <int MODE>
+__device__ __forceinline__ EpiIn epi_load(const TcArgs& a, int row, int box, int col) {
+  const TcEpi& e = a.ep;
+  EpiIn in{0.f, 0.f, 0.f, 0.f};
+  if (MODE == kEpiStore) return in;
+  const int bi = box * a.N + col;  // per-box arrays (the host checks 32-bit offsets)
+  if (MODE == kEpiConcretize) {
+    in.x0 = __ldg(e.xl + bi);
+    in.x1 = __ldg(e.xh + bi);
+    return in;
+  }
+  in.x0 = __ldg(e.pos + bi);
+  const float2 rx = __ldg(e.rx + bi);
+  in.x1 = rx.x;
+  in.x2 = rx.y;
+  if (MODE == kEpiRelax) {
+    if (e.beta) in.x3 = __ldg(e.beta + bi);
+  } else {
+    in.x3 = __ldg(e.rec + row * e.ldrec + col);
+  }
+  return in;
+}
+
+// Results of one element: o (the value whose split goes to out_hi /
+// out_lo), c (its share of the row's partial sum), d (the alpha-gradient
+// row entry).
+struct EpiOut {
+  float o, c, d;
+};
+
+// The arithmetic of one element with value v (see TcEpi); colv: bias[col]
+// (store / adjoint) or bnext[col] (relax).
+template <int MODE>
+__device__ __forceinline__ EpiOut epi_math(const TcArgs& a, float v, const EpiIn& in, float colv) {
+  EpiOut r{0.f, 0.f, 0.f};
+  if (MODE == kEpiStore) {
+    r.o = a.bias ? __fadd_rn(v, colv) : v;
+  } else if (MODE == kEpiConcretize) {
+    r.c = __fadd_rn(__fmul_rn(fmaxf(v, 0.f), in.x0), __fmul_rn(fminf(v, 0.f), in.x1));
+    r.o = (v >= 0.f ? in.x0 : 0.f) + (v <= 0.f ? in.x1 : 0.f);
+  } else {
+    const float pos = in.x0, neg = fabsf(in.x1), icp = in.x2;
+    if (MODE == kEpiRelax) {
+      float o;
+      if (v < 0.f) {
+        r.c = __fmul_rn(v, icp);
+        o = __fmul_rn(v, neg);
+      } else {
+        o = __fmul_rn(v, pos);
+      }
+      if (a.ep.beta) o = __fadd_rn(o, in.x3);
+      if (a.ep.bnext) r.c = fmaf(o, colv, r.c);
+      r.o = o;
+    } else {  // kEpiAdjoint
+      const float ga = __fadd_rn(v, colv);
+      const float ek = in.x3;
+      r.d = !signbit(in.x1) ? __fmul_rn(fmaxf(ek, 0.f), ga) : 0.f;  // unstable neurons only
+      float o = 0.f;
+      if (ek >= 0.f) o = __fmul_rn(pos, ga);
+      if (ek <= 0.f) o = __fadd_rn(o, __fadd_rn(__fmul_rn(neg, ga), icp));
+      r.o = o;
+    }
+  }
+  return r;
+}
+
+template <int MODE>
+__device__ __forceinline__ void epi_store(const TcArgs& a, int row, int col, float v,
+                                          const EpiOut& r) {
+  const TcEpi& e = a.ep;
+  if (MODE == kEpiStore) {
+    a.C[(long long)row * a.ldc + col] = r.o;
+    return;
+  }
+  if (MODE == kEpiRelax) a.C[row * a.ldc + col] = v;  // the record for the adjoint
+  if (MODE == kEpiAdjoint) e.dcontrib[row * e.ldd + col] = r.d;
+  if (e.out_hi) {
+    uint32_t h, l;
+    tc5::tf32_split(r.o, h, l);
+    const int oi = row * e.ldo + col;
+    e.out_hi[oi] = __uint_as_float(h);
+    e.out_lo[oi] = __uint_as_float(l);
+  }
+}
+
+// Epilogue of one warp's 32 rows (rowbase + lane holds acc) x the COLS-column
+// group starting at nb; sm: this warp's staging block.  Per batch of rows:
+// every load first (staged values, per-box inputs), then the arithmetic,
+// then every store, so the rows of a batch overlap.  Row sums leave as one
+// partial per 64 columns.
+template <int MODE, int COLS>
+__device__ __forceinline__ void tc_epilogue(const TcArgs& a, int rowbase, int nb,
+                                            const float (&acc)[COLS], float* sm) {
+  constexpr bool kSum = MODE == kEpiRelax || MODE == kEpiConcretize;
+  const int lane = threadIdx.x & 31;
+  const int rows = min(32, a.M - rowbase);
+  const int my_box = (rowbase + lane) / a.ep.Q;  // box of row rowbase + lane
+  float s = 0.f;  // partial sum of row rowbase + lane over the current 64 columns
+#pragma unroll
+  for (int c = 0; c < COLS / 32; ++c) {
+    if (nb + 32 * c < a.N) {  // warp-uniform
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sm[lane * kStagePitch + j] = acc[32 * c + j];
+      __syncwarp();
+      const int col = nb + 32 * c + lane;
+      const bool cv = col < a.N;
+      float colv = 0.f;
+      if (cv) {
+        if ((MODE == kEpiStore || MODE == kEpiAdjoint) && a.bias) colv = __ldg(a.bias + col);
+        if (MODE == kEpiRelax && a.ep.bnext) colv = __ldg(a.ep.bnext + col);
+      }
+      for (int r0 = 0; r0 < rows; r0 += kEpiBatch) {
+        float v[kEpiBatch];
+        EpiIn in[kEpiBatch];
+#pragma unroll
+        for (int u = 0; u < kEpiBatch; ++u) {
+          v[u] = sm[(r0 + u) * kStagePitch + lane];
+          const int box = __shfl_sync(0xffffffffu, my_box, r0 + u);
+          in[u] = (cv && r0 + u < rows) ? epi_load<MODE>(a, rowbase + r0 + u, box, col)
+                                        : EpiIn{0.f, 0.f, 0.f, 0.f};
+        }
+        EpiOut out[kEpiBatch];
+#pragma unroll
+        for (int u = 0; u < kEpiBatch; ++u) out[u] = epi_math<MODE>(a, v[u], in[u], colv);
+#pragma unroll
+        for (int u = 0; u < kEpiBatch; ++u) {
+          if (r0 + u < rows) {
+            if (cv) epi_store<MODE>(a, rowbase + r0 + u, col, v[u], out[u]);
+            if (kSum) sm[(r0 + u) * kStagePitch + lane] = cv ? out[u].c : 0.f;
+          }
+        }
+      }
+      if (kSum) {
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s = __fadd_rn(s, j < rows ? sm[lane * kStagePitch + j] : 0.f);
+      }
+    }
+    if (kSum && (c & 1) == 1) {  // a 64-column group is complete
+      const int g0 = nb + 32 * (c - 1);
+      if (lane < rows && g0 < a.N)
+        a.ep.part[(rowbase + lane) * a.ep.ldpart + a.ep.part0 + g0 / 64] = s;
+      s = 0.f;
+    }
+  }
+}
+
+template <int BN, int MODE>
 __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
                    const __grid_constant__ CUtensorMap mBh, const __grid_constant__ CUtensorMap mBl,
@@ -91,6 +262,7 @@ __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
   constexpr int TC_BN = BN, TC_STAGES = Cfg::kStages, NBUF = Cfg::kNbuf;
   constexpr int TILE_B_BYTES = Cfg::kTileB, STAGE_BYTES = Cfg::kStage;
   constexpr int EPI = Cfg::kEpiWarps;
+  if (a.gate && *a.gate == 0) return;  // uniform: before any barrier or TMEM use
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -193,16 +365,17 @@ __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
       mma_commit(&done);
       if (!mbar_wait(&done, 0, kDoneSpinLimit)) failed = 1;
     }
-  } else {  // accumulator warps: row m0 + 32 (warp % 4) + lane, columns 128 (warp / 4)..
-    const int cg = 128 * (warp >> 2);
+  } else {  // accumulator warps: row m0 + 32 (warp % 4) + lane, columns kCols (warp / 4)..
+    constexpr int kCols = Cfg::kCols;
+    const int cg = kCols * (warp >> 2);
     const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + cg;
     unsigned g = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
       const int m0 = (tile / n_tiles) * TC_BM, n0 = (tile % n_tiles) * TC_BN;
-      float acc[128];
+      float acc[kCols];
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      for (int j = 0; j < kCols; ++j) acc[j] = 0.f;
       for (int kb = 0; kb < nk; ++kb, ++g) {
         const int q = g % NBUF;
         if (!mbar_wait(&acc_full[q], (g / NBUF) & 1, kDoneSpinLimit, vfailed)) {
@@ -211,7 +384,7 @@ __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 16) {
+        for (int c0 = 0; c0 < kCols; c0 += 16) {
           uint32_t v[16];
           tmem_ld16(lane_addr + q * TC_BN + c0, v);
           tmem_wait_ld(v);
@@ -223,15 +396,10 @@ __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
         if (lane == 0) mbar_arrive(&acc_free[q]);
       }
       if (!ok) break;
-      const int row = m0 + (warp & 3) * 32 + lane;
-      if (row < a.M) {
-        float* crow = a.C + (long long)row * a.ldc;
-#pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          const int n = n0 + cg + j;
-          if (n < a.N) crow[n] = a.bias ? __fadd_rn(acc[j], a.bias[n]) : acc[j];
-        }
-      }
+      if (m0 + (warp & 3) * 32 < a.M)
+        tc_epilogue<MODE, kCols>(a, m0 + (warp & 3) * 32, n0 + cg, acc,
+                          reinterpret_cast<float*>(smem + TC_STAGES * STAGE_BYTES +
+                                                   warp * kStageWarpBytes));
     }
     if (!ok) failed = 1;
   }
@@ -290,35 +458,75 @@ int make_map(CUtensorMap* map, const float* p, int rows, int cols, int ld, int b
 
 }  // namespace
 
-// C = A B^T with 3xTF32 on tcgen05 (see the file comment); err: device int,
-// zero on entry, set on a bounded-wait expiry.
-int tc_gemm_3xtf32(int M, int N, int K, const float* Ah, const float* Al, int lda,
-                   const float* Bh, const float* Bl, int ldb, float* C, int ldc,
-                   const float* bias, int* err, cudaStream_t st, const char* who) {
+namespace {
+
+template <int BN, int EPI>
+int launch_tc(int grid, const CUtensorMap& mAh, const CUtensorMap& mAl, const CUtensorMap& mBh,
+              const CUtensorMap& mBl, const TcArgs& args, cudaStream_t st) {
+  const int rc = ensure_smem(reinterpret_cast<const void*>(tc_gemm_kernel<BN, EPI>),
+                             TcCfg<BN>::kSmem);
+  if (rc) return rc;
+  tc_gemm_kernel<BN, EPI><<<grid, TcCfg<BN>::kThreads, TcCfg<BN>::kSmem, st>>>(mAh, mAl, mBh,
+                                                                              mBl, args);
+  return VCB_OK;
+}
+
+template <int BN>
+int launch_mode(int grid, const CUtensorMap& mAh, const CUtensorMap& mAl,
+                const CUtensorMap& mBh, const CUtensorMap& mBl, const TcArgs& args,
+                cudaStream_t st) {
+  switch (args.ep.mode) {
+    case kEpiRelax: return launch_tc<BN, kEpiRelax>(grid, mAh, mAl, mBh, mBl, args, st);
+    case kEpiAdjoint: return launch_tc<BN, kEpiAdjoint>(grid, mAh, mAl, mBh, mBl, args, st);
+    case kEpiConcretize:
+      return launch_tc<BN, kEpiConcretize>(grid, mAh, mAl, mBh, mBl, args, st);
+    default: return launch_tc<BN, kEpiStore>(grid, mAh, mAl, mBh, mBl, args, st);
+  }
+}
+
+}  // namespace
+
+// C = A B^T with 3xTF32 on tcgen05 and the epilogue `ep` (see vcb_tc.cuh);
+// err: device int, zero on entry, set on a bounded-wait expiry.
+int tc_gemm_fused(int M, int N, int K, const float* Ah, const float* Al, int lda,
+                  const float* Bh, const float* Bl, int ldb, float* C, int ldc,
+                  const float* bias, int* err, cudaStream_t st, const char* who,
+                  const int* gate, const TcEpi& ep) {
   if (M == 0 || N == 0) return VCB_OK;
-  const int bn = N > 128 ? 256 : 128;  // wide outputs: half the A traffic per FLOP
+  // Wide outputs take 128 x 256 tiles (half the A traffic per FLOP) when
+  // that still gives every SM a tile; otherwise 128 x 128 tiles.
+  const long long m_tiles = (M + TC_BM - 1) / TC_BM;
+  const int bn = (N > 128 && m_tiles * ((N + 255) / 256) >= sm_count()) ? 256 : 128;
   CUtensorMap mAh, mAl, mBh, mBl;
   int rc = make_map(&mAh, Ah, M, K, lda, TC_BM, who);
   if (!rc) rc = make_map(&mAl, Al, M, K, lda, TC_BM, who);
   if (!rc) rc = make_map(&mBh, Bh, N, K, ldb, bn, who);
   if (!rc) rc = make_map(&mBl, Bl, N, K, ldb, bn, who);
   if (rc) return rc;
-  TcArgs args{M, N, K, ldc, C, bias, err};
-  const long long tiles = (long long)((M + TC_BM - 1) / TC_BM) * ((N + bn - 1) / bn);
+  if (ep.mode != kEpiStore) {
+    // fused epilogues index with 32-bit offsets
+    const long long boxes = M / std::max(ep.Q, 1) + 1;
+    const long long lim = 0x7fffffffLL;
+    if ((long long)M * std::max(std::max(ldc, ep.ldo), std::max(ep.ldrec, ep.ldd)) >= lim ||
+        boxes * N >= lim || (ep.part && (long long)M * ep.ldpart >= lim))
+      return fail(VCB_ERR_UNSUPPORTED, "%s: operands beyond 32-bit offsets", who);
+  }
+  TcArgs args{M, N, K, ldc, C, bias, err, gate, ep};
+  const long long tiles = m_tiles * ((N + bn - 1) / bn);
   if (tiles > 0x7fffffffLL) return fail(VCB_ERR_UNSUPPORTED, "%s: %lld output tiles", who, tiles);
   const int grid = (int)std::min<long long>(tiles, sm_count());  // persistent: one CTA per SM
-  if (bn == 256) {
-    rc = ensure_smem(reinterpret_cast<const void*>(tc_gemm_kernel<256>), TcCfg<256>::kSmem);
-    if (rc) return rc;
-    tc_gemm_kernel<256><<<grid, TcCfg<256>::kThreads, TcCfg<256>::kSmem, st>>>(mAh, mAl, mBh,
-                                                                            mBl, args);
-  } else {
-    rc = ensure_smem(reinterpret_cast<const void*>(tc_gemm_kernel<128>), TcCfg<128>::kSmem);
-    if (rc) return rc;
-    tc_gemm_kernel<128><<<grid, TcCfg<128>::kThreads, TcCfg<128>::kSmem, st>>>(mAh, mAl, mBh,
-                                                                            mBl, args);
-  }
+  rc = bn == 256 ? launch_mode<256>(grid, mAh, mAl, mBh, mBl, args, st)
+                 : launch_mode<128>(grid, mAh, mAl, mBh, mBl, args, st);
+  if (rc) return rc;
   return check_launch(who);
+}
+
+int tc_gemm_3xtf32(int M, int N, int K, const float* Ah, const float* Al, int lda,
+                   const float* Bh, const float* Bl, int ldb, float* C, int ldc,
+                   const float* bias, int* err, cudaStream_t st, const char* who,
+                   const int* gate) {
+  return tc_gemm_fused(M, N, K, Ah, Al, lda, Bh, Bl, ldb, C, ldc, bias, err, st, who, gate,
+                       TcEpi{});
 }
 
 int tf32_split(long long n, const float* x, float* hi, float* lo, cudaStream_t st) {
@@ -334,6 +542,20 @@ extern "C" int vcb_tf32_split(int64_t n, const float* x, float* hi, float* lo, v
   using namespace vcb;
   if (n < 0 || (n > 0 && (!x || !hi || !lo))) return fail(VCB_ERR_INVALID, "vcb_tf32_split: bad arguments");
   return tf32_split(n, x, hi, lo, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int vcb_tc_gemm_gated(int32_t M, int32_t N, int32_t K, const float* A_hi,
+                                 const float* A_lo, int32_t lda, const float* B_hi,
+                                 const float* B_lo, int32_t ldb, const float* bias, float* C,
+                                 int32_t ldc, int32_t* err, const int32_t* gate, void* stream) {
+  using namespace vcb;
+  if (M < 0 || N < 0 || K <= 0 || ldc < N)
+    return fail(VCB_ERR_INVALID, "vcb_tc_gemm_gated: M=%d N=%d K=%d ldc=%d", M, N, K, ldc);
+  if (M == 0 || N == 0) return VCB_OK;
+  if (!A_hi || !A_lo || !B_hi || !B_lo || !C || !err)
+    return fail(VCB_ERR_INVALID, "vcb_tc_gemm_gated: NULL pointer");
+  return tc_gemm_3xtf32(M, N, K, A_hi, A_lo, lda, B_hi, B_lo, ldb, C, ldc, bias, err,
+                        static_cast<cudaStream_t>(stream), "vcb_tc_gemm_gated", gate);
 }
 
 extern "C" int vcb_tc_gemm(int32_t M, int32_t N, int32_t K, const float* A_hi, const float* A_lo,

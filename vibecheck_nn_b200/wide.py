@@ -213,11 +213,247 @@ def min_area_alpha(sb):
     return out
 
 
+# Domains x spec rows from which alpha_loop runs on the tensor cores (3xTF32
+# GEMMs with fused relaxation / adjoint / Adam stages) instead of the SIMT
+# layer kernels; below it the GEMMs are too small to fill the SMs.
+_TC_MIN_ROWS = 4096
+
+# What the last alpha_loop ran: {'path': 'tc' | 'simt', 'iterations': k} (for
+# the tensor-core path 'iterations' is a callable, as reading the device
+# stop flags synchronises).
+last_stats = {}
+
+
+def _split_pad(t):
+    """(rows x cols) fp32 -> TF32 (hi, lo, ld) with ld = cols rounded up to 4
+    (the layout the tensor-core GEMM reads)."""
+    rows, cols = t.shape
+    ld = _pad4(cols)
+    buf = torch.zeros((rows, ld), dtype=F32, device=t.device)
+    buf[:, :cols] = t
+    hi, lo = torch.empty_like(buf), torch.empty_like(buf)
+    rc = _lib.lib().vcb_tf32_split(buf.numel(), P(buf), P(hi), P(lo), _lib.stream_of(t.device))
+    _lib.check(rc, 'vcb_tf32_split')
+    return hi, lo, ld
+
+
+def _tc_operands(wn):
+    """Per layer l the GEMM operands of W_l (n_out x n_in): W_l^T for the
+    back-substitution C = coef @ W_l and W_l for the adjoint g @ W_l^T."""
+    ops = wn.__dict__.get('_tc_ops')
+    if ops is None:
+        ops = ([_split_pad(W.t()) for W in wn.W], [_split_pad(W) for W in wn.W])
+        wn.__dict__['_tc_ops'] = ops
+    return ops
+
+
+def _tc_eligible(wn, D, Q):
+    return len(wn.W) >= 2 and D * Q >= _TC_MIN_ROWS
+
+
+class _TcAlphaPlan:
+    """Buffers and launch sequence of the tensor-core alpha loop for one
+    (net, D domains, Q spec rows, iterations, lr, decay).
+
+    Per Adam iteration, top layer down, one 3xTF32 GEMM per layer with the
+    bound arithmetic in its epilogue: vcb_wtc_back_gemm (C_l = coef @ W_l
+    kept as the record, the relaxation of ReLU l-1 written as the next coef's
+    TF32 split, intercept and next-bias partial sums), vcb_wtc_input_gemm
+    (the input box's partial sums, the adjoint seed), vcb_wtc_finish (lb,
+    best, stop flag); then bottom up vcb_wtc_adj_gemm (ga = g @ W_l^T + b_l,
+    alpha gradient rows, next adjoint) and vcb_wtc_adam.  Each iteration's
+    launches are gated on the previous iteration's "some best lb <= 0" flag,
+    so without an early-stop epsilon the whole loop is queued with no host
+    synchronisation -- and, replayed from fixed buffers, captured once as a
+    CUDA graph."""
+
+    def __init__(self, wn, D, n0, Q, dev, n_iters, lr, lr_decay):
+        self.wn, self.D, self.n0, self.Q, self.dev = wn, D, n0, Q, dev
+        self.n_it, self.lr, self.lr_decay = max(1, n_iters), lr, lr_decay
+        self.key = (id(wn), D, n0, Q, str(dev), self.n_it, lr, lr_decay)
+        nfc = len(wn.W)
+        self.dims = dims = [wn.W[0].shape[1]] + [W.shape[0] for W in wn.W]
+        R = D * Q
+        e = lambda *shape: torch.empty(shape, dtype=F32, device=dev)  # noqa: E731
+        # inputs (copied in by load)
+        self.xl, self.xh = e(D, n0), e(D, n0)
+        self.sb = {L: (e(D, dims[L + 1]), e(D, dims[L + 1])) for L in range(nfc - 1)}
+        self.W_q, self.b_q = e(Q, dims[nfc]), e(Q)
+        # working buffers: records C_l (l >= 1), two split operand pairs
+        # (a GEMM reads one and writes the other), alpha-gradient rows,
+        # per-row partial sums (one per 64 columns of every layer)
+        self.C = {l: e(R, _pad4(dims[l])) for l in range(1, nfc)}
+        ldmax = max(_pad4(d) for d in dims)
+        self.ops = [(e(R, ldmax), e(R, ldmax)) for _ in range(2)]
+        self.ldd = max(_pad4(d) for d in dims[1:nfc])
+        self.dcontrib = e(R, self.ldd)
+        self.part0 = {}
+        off = 0
+        for l in range(nfc - 1, -1, -1):
+            self.part0[l] = off
+            off += (dims[l] + 63) // 64
+        self.nparts = off
+        self.part = e(R, off)
+        self.lb, self.best = e(R), e(R)
+        self.opens = torch.zeros(self.n_it, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.graph = None
+        self.last_it = 0
+
+    def load(self, xl, xh, sb, W_q, b_q):
+        self.xl.copy_(xl)
+        self.xh.copy_(xh)
+        for L, (lo, hi) in sb.items():
+            self.sb[L][0].copy_(lo)
+            self.sb[L][1].copy_(hi)
+        self.W_q.copy_(W_q)
+        self.b_q.copy_(b_q)
+
+    def launch(self, early_stop_eps=None):
+        """Queue the loop on the current stream (one host synchronisation per
+        iteration only with ``early_stop_eps``)."""
+        wn, D, Q, dims = self.wn, self.D, self.Q, self.dims
+        R, n0, nfc = D * Q, self.n0, len(wn.W)
+        st = _lib.stream_of(self.dev)
+        L_ = _lib.lib()
+        fwd, adj = _tc_operands(wn)
+        err, C, part, ldp = self.err, self.C, self.part, self.part.shape[1]
+        self.opens.zero_()
+        # alpha-independent: the spec rows as the top layer's coef, and
+        # acc0 = b_q + W_q . b_last
+        wq = _split_pad(self.W_q.repeat(D, 1))
+        qh, ql, ldq = _split_pad(self.W_q)
+        bl = _split_pad(wn.b[-1][None, :])
+        wb = torch.empty((Q, 4), dtype=F32, device=self.dev)
+        rc = L_.vcb_tc_gemm(Q, 1, dims[nfc], P(qh), P(ql), ldq, P(bl[0]), P(bl[1]), bl[2], None,
+                            P(wb), 4, P(err), st)
+        _lib.check(rc, 'vcb_tc_gemm')
+        acc0 = (self.b_q + wb[:, 0]).repeat(D).contiguous()
+        # per ReLU layer: upper slope / intercept records and the lower
+        # slopes (alpha on unstable neurons, min-area init; 1 / 0 fixed on
+        # active / dead ones)
+        alpha, rx = {}, {}
+        for L, (s_lo, s_hi) in self.sb.items():
+            alpha[L] = torch.empty_like(s_lo)
+            rx[L] = torch.empty(s_lo.shape + (2,), dtype=F32, device=self.dev)
+            rc = L_.vcb_wtc_relax_init(s_lo.numel(), P(s_lo), P(s_hi), P(rx[L]), P(alpha[L]),
+                                       None, st)
+            _lib.check(rc, 'vcb_wtc_relax_init')
+        m1 = {L: torch.zeros_like(a) for L, a in alpha.items()}
+        m2 = {L: torch.zeros_like(a) for L, a in alpha.items()}
+        prev_max = -float('inf')
+        cur_lr = self.lr
+        for it in range(self.n_it):
+            self.last_it = it
+            gate_f = P(None if it == 0 else self.opens[it - 1:it])
+            gate_a = P(self.opens[it:it + 1])
+            src, ld_src = (wq[0], wq[1]), wq[2]
+            k = 0
+            for l in range(nfc - 1, 0, -1):
+                dst = self.ops[k]
+                n = dims[l]
+                rc = L_.vcb_wtc_back_gemm(R, Q, n, dims[l + 1], P(src[0]), P(src[1]), ld_src,
+                                          P(fwd[l][0]), P(fwd[l][1]), fwd[l][2], P(C[l]),
+                                          C[l].shape[1], P(alpha[l - 1]), P(rx[l - 1]),
+                                          None, P(wn.b[l - 1]), P(dst[0]), P(dst[1]), _pad4(n),
+                                          P(part), ldp, self.part0[l], P(err), gate_f, st)
+                _lib.check(rc, 'vcb_wtc_back_gemm')
+                src, ld_src, k = dst, _pad4(n), 1 - k
+            dst = self.ops[k]
+            rc = L_.vcb_wtc_input_gemm(R, Q, n0, dims[1], P(src[0]), P(src[1]), ld_src,
+                                       P(fwd[0][0]), P(fwd[0][1]), fwd[0][2], P(self.xl),
+                                       P(self.xh), P(dst[0]), P(dst[1]), _pad4(n0), P(part), ldp,
+                                       self.part0[0], P(err), gate_f, st)
+            _lib.check(rc, 'vcb_wtc_input_gemm')
+            rc = L_.vcb_wtc_finish(R, P(acc0), P(part), ldp, self.nparts, P(self.lb),
+                                   P(self.best), int(it == 0), gate_a, gate_f, st)
+            _lib.check(rc, 'vcb_wtc_finish')
+            src, k = dst, 1 - k
+            for l in range(nfc - 1):
+                nin, nout = dims[l], dims[l + 1]
+                dst = self.ops[k]
+                last = l == nfc - 2
+                rc = L_.vcb_wtc_adj_gemm(R, Q, nout, nin, P(src[0]), P(src[1]), _pad4(nin),
+                                         P(adj[l][0]), P(adj[l][1]), adj[l][2], P(wn.b[l]),
+                                         P(C[l + 1]), C[l + 1].shape[1], P(alpha[l]),
+                                         P(rx[l]), P(self.dcontrib), self.ldd,
+                                         None if last else P(dst[0]), None if last else P(dst[1]),
+                                         _pad4(nout), P(err), gate_a, st)
+                _lib.check(rc, 'vcb_wtc_adj_gemm')
+                rc = L_.vcb_wtc_adam(D, Q, nout, P(self.dcontrib), self.ldd, P(alpha[l]),
+                                     P(m1[l]), P(m2[l]), float(cur_lr), it + 1, gate_a, st)
+                _lib.check(rc, 'vcb_wtc_adam')
+                src, k = dst, 1 - k
+            if early_stop_eps is not None:
+                if not bool(self.opens[it].item()):
+                    break
+                curr_max = float(self.best.max().item())
+                if it > 0 and curr_max - prev_max < early_stop_eps:
+                    break
+                prev_max = curr_max
+            cur_lr *= self.lr_decay
+
+    def replay(self):
+        """Run the loop as one CUDA graph (captured on the first replay)."""
+        if self.graph is None:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.launch()
+            self.graph = g
+        self.graph.replay()
+
+    def finish(self):
+        if int(self.err.item()):
+            raise TimeoutError('vcb_tc_gemm_gated: a bounded pipeline wait expired')
+        opens, it = self.opens, self.last_it
+        last_stats.clear()
+        last_stats.update(path='tc', iterations=lambda: 1 + int(opens[:it].sum().item()))
+
+
+# The plan of the last graph-eligible call: a repeat with the same shapes and
+# settings replays it as a CUDA graph (one entry bounds the memory held).
+_tc_plan_cache = {}
+
+
+def _tc_alpha_loop(wn, xl, xh, sb, W_q, b_q, n_iters, lr, lr_decay, early_stop_eps):
+    """alpha_loop on the tensor cores (_TcAlphaPlan).  Without an early-stop
+    epsilon a repeated call with the same net, shapes and settings replays
+    the previous call's plan as a CUDA graph."""
+    dev = xl.device
+    D, n0 = xl.shape
+    Q = W_q.shape[0]
+    if early_stop_eps is not None:
+        plan = _TcAlphaPlan(wn, D, n0, Q, dev, n_iters, lr, lr_decay)
+        plan.load(xl, xh, sb, W_q, b_q)
+        plan.launch(early_stop_eps)
+        plan.finish()
+        return plan.best.view(D, Q)
+    key = (id(wn), D, n0, Q, str(dev), max(1, n_iters), lr, lr_decay)
+    plan = _tc_plan_cache.get('plan')
+    if plan is not None and plan.key == key and plan.wn is wn:
+        plan.load(xl, xh, sb, W_q, b_q)
+        plan.replay()
+    else:
+        _tc_plan_cache.clear()
+        plan = _TcAlphaPlan(wn, D, n0, Q, dev, n_iters, lr, lr_decay)
+        plan.load(xl, xh, sb, W_q, b_q)
+        plan.launch()
+        _tc_plan_cache['plan'] = plan
+    plan.finish()
+    return plan.best.view(D, Q).clone()
+
+
 def alpha_loop(wn, xl, xh, sb, W_q, b_q, n_iters, lr, lr_decay=1.0,
-               early_stop_eps=None):
+               early_stop_eps=None, tc=None):
     """Adam on -sum(lb) over alpha with clamp to [0,1] and best-of-iterations
     lb; stops when every best lb is > 0 (and, when early_stop_eps is given,
-    when the batch max improves by less than it -- verify_zono_bnb.py:5248-5288)."""
+    when the batch max improves by less than it -- verify_zono_bnb.py:5248-5288).
+    ``tc``: run on the tensor cores (True), on the SIMT layer kernels (False)
+    or by size (None: from _TC_MIN_ROWS domains x spec rows)."""
+    if tc is None:
+        tc = _tc_eligible(wn, xl.shape[0], W_q.shape[0])
+    if tc and len(wn.W) >= 2:
+        return _tc_alpha_loop(wn, xl, xh, sb, W_q, b_q, n_iters, lr, lr_decay, early_stop_eps)
     dev = xl.device
     D = xl.shape[0]
     Q = W_q.shape[0]
@@ -229,7 +465,10 @@ def alpha_loop(wn, xl, xh, sb, W_q, b_q, n_iters, lr, lr_decay=1.0,
     best = None
     prev_max = -float('inf')
     cur_lr = lr
+    last_stats.clear()
+    last_stats['path'] = 'simt'
     for it in range(max(1, n_iters)):
+        last_stats['iterations'] = it + 1
         lb, contrib = wide_alpha_grad(wn, xl, xh, sb, W_q, b_q, alpha)
         best = lb.clone() if best is None else torch.maximum(best, lb)
         curr_max = float(best.max().item()) if early_stop_eps is not None else 0.0
@@ -249,7 +488,7 @@ def alpha_loop(wn, xl, xh, sb, W_q, b_q, n_iters, lr, lr_decay=1.0,
 
 
 def alpha_crown_domains(xl, xh, gg, spec_W, spec_b, relu_clamps, device='cuda',
-                        n_iters=20, lr=0.1):
+                        n_iters=20, lr=0.1, tc=None):
     """alpha-CROWN over ReLU-split domains (cfg3; verify_milp.py:2762-2807
     with beta = 0).  xl, xh (D, n_in).  Returns (best lb (D, Q), sb)."""
     device = _dev(device)
@@ -263,5 +502,5 @@ def alpha_crown_domains(xl, xh, gg, spec_W, spec_b, relu_clamps, device='cuda',
         clamps = {L: (torch.as_tensor(c[0], device=device), torch.as_tensor(c[1], device=device))
                   for L, c in relu_clamps.items()}
     sb = wide_ibp(wn, xl, xh, clamps)
-    best = alpha_loop(wn, xl, xh, sb, W_q, b_q, n_iters, lr)
+    best = alpha_loop(wn, xl, xh, sb, W_q, b_q, n_iters, lr, tc=tc)
     return best, sb
