@@ -84,6 +84,7 @@ struct TcArgs {
   const float* bias;  // (N) added to every row, or NULL
   int* err;           // set to 1 when a bounded wait expired
   const int* gate;    // when non-NULL and *gate == 0 the launch does nothing
+  int vec;            // N % 4 == 0 and every row of every operand 16-byte aligned
   TcEpi ep;
 };
 
@@ -253,6 +254,137 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, int rowbase, int nb
   }
 }
 
+// Vectorised epilogue (TcArgs::vec): each lane takes 4 consecutive columns,
+// so a warp instruction covers 4 rows x 32 columns with 16-byte accesses.
+// The staging block is 32 rows x 32 floats with the 16-byte chunks of row r
+// XOR-swizzled by r % 8 (conflict-free for the row-wise writes and the
+// 4-row reads), followed by 32 per-row running sums.
+__device__ __forceinline__ float4 ldg4(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+
+__device__ __forceinline__ void stg4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+__device__ __forceinline__ float f4(const float4& v, int k) {
+  return k == 0 ? v.x : (k == 1 ? v.y : (k == 2 ? v.z : v.w));
+}
+
+template <int MODE, int COLS>
+__device__ __forceinline__ void tc_epilogue_vec(const TcArgs& a, int rowbase, int nb,
+                                                const float (&acc)[COLS], float* sm) {
+  constexpr bool kSum = MODE == kEpiRelax || MODE == kEpiConcretize;
+  constexpr int kRowsPerStep = 4, kSteps = 2;  // 8 rows of loads in flight per batch
+  const TcEpi& e = a.ep;
+  float* rs = sm + 32 * 32;  // per-row running sums
+  const int lane = threadIdx.x & 31;
+  const int rows = min(32, a.M - rowbase);
+  const int my_box = (rowbase + lane) / e.Q;
+  const int sub = lane >> 3, q4 = lane & 7;  // row within a step, 16-byte chunk within the row
+  if (kSum) rs[lane] = 0.f;
+#pragma unroll
+  for (int c = 0; c < COLS / 32; ++c) {
+    if (nb + 32 * c < a.N) {  // warp-uniform
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(sm + lane * 32 + 4 * (j ^ (lane & 7))) =
+            make_float4(acc[32 * c + 4 * j], acc[32 * c + 4 * j + 1], acc[32 * c + 4 * j + 2],
+                        acc[32 * c + 4 * j + 3]);
+      __syncwarp();
+      const int col = nb + 32 * c + 4 * q4;
+      const bool cv = col < a.N;
+      float4 colv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (cv) {
+        if ((MODE == kEpiStore || MODE == kEpiAdjoint) && a.bias) colv = ldg4(a.bias + col);
+        if (MODE == kEpiRelax && e.bnext) colv = ldg4(e.bnext + col);
+      }
+      for (int r0 = 0; r0 < rows; r0 += kRowsPerStep * kSteps) {
+        float4 v[kSteps], x0[kSteps], x1[kSteps], x2[kSteps], x3[kSteps];
+#pragma unroll
+        for (int u = 0; u < kSteps; ++u) {
+          const int r = r0 + kRowsPerStep * u + sub;  // <= 31
+          v[u] = *reinterpret_cast<const float4*>(sm + r * 32 + 4 * (q4 ^ (r & 7)));
+          const int box = __shfl_sync(0xffffffffu, my_box, r);
+          const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+          x0[u] = x1[u] = x2[u] = x3[u] = z;
+          if (cv && r < rows && MODE != kEpiStore) {
+            const int bi = box * a.N + col;
+            if (MODE == kEpiConcretize) {
+              x0[u] = ldg4(e.xl + bi);
+              x1[u] = ldg4(e.xh + bi);
+            } else {
+              x0[u] = ldg4(e.pos + bi);
+              x1[u] = ldg4(reinterpret_cast<const float*>(e.rx) + 2 * bi);      // cols 0, 1
+              x2[u] = ldg4(reinterpret_cast<const float*>(e.rx) + 2 * bi + 4);  // cols 2, 3
+              if (MODE == kEpiRelax && e.beta) x3[u] = ldg4(e.beta + bi);
+              if (MODE == kEpiAdjoint) x3[u] = ldg4(e.rec + (rowbase + r) * e.ldrec + col);
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kSteps; ++u) {
+          const int r = r0 + kRowsPerStep * u + sub;
+          const int row = rowbase + r;
+          float o[4], cs[4], d[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            EpiIn in{0.f, 0.f, 0.f, 0.f};
+            if (MODE == kEpiConcretize) {
+              in.x0 = f4(x0[u], k);
+              in.x1 = f4(x1[u], k);
+            } else if (MODE != kEpiStore) {
+              in.x0 = f4(x0[u], k);
+              in.x1 = k < 2 ? f4(x1[u], 2 * k) : f4(x2[u], 2 * k - 4);
+              in.x2 = k < 2 ? f4(x1[u], 2 * k + 1) : f4(x2[u], 2 * k - 3);
+              in.x3 = f4(x3[u], k);
+            }
+            const EpiOut out = epi_math<MODE>(a, f4(v[u], k), in, f4(colv, k));
+            o[k] = out.o;
+            cs[k] = out.c;
+            d[k] = out.d;
+          }
+          const bool live = cv && r < rows;
+          if (live) {
+            if (MODE == kEpiStore) {
+              stg4(a.C + (long long)row * a.ldc + col, make_float4(o[0], o[1], o[2], o[3]));
+            } else {
+              if (MODE == kEpiRelax) stg4(a.C + row * a.ldc + col, v[u]);
+              if (MODE == kEpiAdjoint)
+                stg4(e.dcontrib + row * e.ldd + col, make_float4(d[0], d[1], d[2], d[3]));
+              if (e.out_hi) {
+                uint32_t h[4], l[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) tc5::tf32_split(o[k], h[k], l[k]);
+                const int oi = row * e.ldo + col;
+                stg4(e.out_hi + oi, make_float4(__uint_as_float(h[0]), __uint_as_float(h[1]),
+                                                __uint_as_float(h[2]), __uint_as_float(h[3])));
+                stg4(e.out_lo + oi, make_float4(__uint_as_float(l[0]), __uint_as_float(l[1]),
+                                                __uint_as_float(l[2]), __uint_as_float(l[3])));
+              }
+            }
+          }
+          if (kSum) {
+            // row r's sum over this chunk: the lane's 4 columns, then its 8 lanes
+            float t = live ? __fadd_rn(__fadd_rn(cs[0], cs[1]), __fadd_rn(cs[2], cs[3])) : 0.f;
+            t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+            t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+            t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
+            if (q4 == 0 && r < rows) rs[r] = __fadd_rn(rs[r], t);
+          }
+        }
+      }
+    }
+    if (kSum && (c & 1) == 1) {  // a 64-column group is complete
+      __syncwarp();
+      const int g0 = nb + 32 * (c - 1);
+      if (lane < rows && g0 < a.N)
+        e.part[(rowbase + lane) * e.ldpart + e.part0 + g0 / 64] = rs[lane];
+      __syncwarp();
+      rs[lane] = 0.f;
+    }
+  }
+}
+
 template <int BN, int MODE>
 __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mAh, const __grid_constant__ CUtensorMap mAl,
@@ -396,10 +528,14 @@ __global__ void __launch_bounds__(TcCfg<BN>::kThreads, 1)
         if (lane == 0) mbar_arrive(&acc_free[q]);
       }
       if (!ok) break;
-      if (m0 + (warp & 3) * 32 < a.M)
-        tc_epilogue<MODE, kCols>(a, m0 + (warp & 3) * 32, n0 + cg, acc,
-                          reinterpret_cast<float*>(smem + TC_STAGES * STAGE_BYTES +
-                                                   warp * kStageWarpBytes));
+      if (m0 + (warp & 3) * 32 < a.M) {
+        float* sm = reinterpret_cast<float*>(smem + TC_STAGES * STAGE_BYTES +
+                                             warp * kStageWarpBytes);
+        if (a.vec)
+          tc_epilogue_vec<MODE, kCols>(a, m0 + (warp & 3) * 32, n0 + cg, acc, sm);
+        else
+          tc_epilogue<MODE, kCols>(a, m0 + (warp & 3) * 32, n0 + cg, acc, sm);
+      }
     }
     if (!ok) failed = 1;
   }
@@ -471,16 +607,15 @@ int launch_tc(int grid, const CUtensorMap& mAh, const CUtensorMap& mAl, const CU
   return VCB_OK;
 }
 
-template <int BN>
 int launch_mode(int grid, const CUtensorMap& mAh, const CUtensorMap& mAl,
                 const CUtensorMap& mBh, const CUtensorMap& mBl, const TcArgs& args,
                 cudaStream_t st) {
   switch (args.ep.mode) {
-    case kEpiRelax: return launch_tc<BN, kEpiRelax>(grid, mAh, mAl, mBh, mBl, args, st);
-    case kEpiAdjoint: return launch_tc<BN, kEpiAdjoint>(grid, mAh, mAl, mBh, mBl, args, st);
+    case kEpiRelax: return launch_tc<128, kEpiRelax>(grid, mAh, mAl, mBh, mBl, args, st);
+    case kEpiAdjoint: return launch_tc<128, kEpiAdjoint>(grid, mAh, mAl, mBh, mBl, args, st);
     case kEpiConcretize:
-      return launch_tc<BN, kEpiConcretize>(grid, mAh, mAl, mBh, mBl, args, st);
-    default: return launch_tc<BN, kEpiStore>(grid, mAh, mAl, mBh, mBl, args, st);
+      return launch_tc<128, kEpiConcretize>(grid, mAh, mAl, mBh, mBl, args, st);
+    default: return launch_tc<128, kEpiStore>(grid, mAh, mAl, mBh, mBl, args, st);
   }
 }
 
@@ -493,10 +628,13 @@ int tc_gemm_fused(int M, int N, int K, const float* Ah, const float* Al, int lda
                   const float* bias, int* err, cudaStream_t st, const char* who,
                   const int* gate, const TcEpi& ep) {
   if (M == 0 || N == 0) return VCB_OK;
-  // Wide outputs take 128 x 256 tiles (half the A traffic per FLOP) when
-  // that still gives every SM a tile; otherwise 128 x 128 tiles.
+  // Plain stores of wide outputs take 128 x 256 tiles (half the A traffic
+  // per FLOP) when that still gives every SM a tile; the fused epilogues and
+  // everything else take 128 x 128 tiles (twice the epilogue warps per
+  // output column, and more tiles per CTA to overlap them with the MMAs).
   const long long m_tiles = (M + TC_BM - 1) / TC_BM;
-  const int bn = (N > 128 && m_tiles * ((N + 255) / 256) >= sm_count()) ? 256 : 128;
+  const int bn = (ep.mode == kEpiStore && N > 128 && m_tiles * ((N + 255) / 256) >= sm_count())
+                     ? 256 : 128;
   CUtensorMap mAh, mAl, mBh, mBl;
   int rc = make_map(&mAh, Ah, M, K, lda, TC_BM, who);
   if (!rc) rc = make_map(&mAl, Al, M, K, lda, TC_BM, who);
@@ -511,12 +649,17 @@ int tc_gemm_fused(int M, int N, int K, const float* Ah, const float* Al, int lda
         boxes * N >= lim || (ep.part && (long long)M * ep.ldpart >= lim))
       return fail(VCB_ERR_UNSUPPORTED, "%s: operands beyond 32-bit offsets", who);
   }
-  TcArgs args{M, N, K, ldc, C, bias, err, gate, ep};
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec = N % 4 == 0 && ldc % 4 == 0 && al16(C) && al16(bias) && al16(ep.pos) &&
+                   al16(ep.rx) && al16(ep.beta) && al16(ep.bnext) && al16(ep.xl) &&
+                   al16(ep.xh) && al16(ep.rec) && al16(ep.out_hi) && al16(ep.out_lo) &&
+                   al16(ep.dcontrib) && ep.ldrec % 4 == 0 && ep.ldo % 4 == 0 && ep.ldd % 4 == 0;
+  TcArgs args{M, N, K, ldc, C, bias, err, gate, vec ? 1 : 0, ep};
   const long long tiles = m_tiles * ((N + bn - 1) / bn);
   if (tiles > 0x7fffffffLL) return fail(VCB_ERR_UNSUPPORTED, "%s: %lld output tiles", who, tiles);
   const int grid = (int)std::min<long long>(tiles, sm_count());  // persistent: one CTA per SM
-  rc = bn == 256 ? launch_mode<256>(grid, mAh, mAl, mBh, mBl, args, st)
-                 : launch_mode<128>(grid, mAh, mAl, mBh, mBl, args, st);
+  rc = bn == 256 ? launch_tc<256, kEpiStore>(grid, mAh, mAl, mBh, mBl, args, st)  // store only
+                 : launch_mode(grid, mAh, mAl, mBh, mBl, args, st);
   if (rc) return rc;
   return check_launch(who);
 }
