@@ -152,17 +152,60 @@ def config_dict(n):
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
+    """SM clock and clock-event reasons sampled while the timed region runs.
+
+    In-process NVML (read-only queries) polled every ~1 ms from a thread, so
+    even a timed region of a few milliseconds gets samples; `nvidia-smi -lms`
+    (which needs hundreds of milliseconds to start) is the fallback when NVML
+    is not importable.  The sampler starts before the region and has taken its
+    first sample before __enter__ returns."""
     FIELDS = ('clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,'
               'clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,'
               'clocks_event_reasons.sw_power_cap')
+    REASONS = (('hw_slowdown', 0x8), ('hw_thermal_slowdown', 0x40),
+               ('sw_thermal_slowdown', 0x20), ('sw_power_cap', 0x4))
 
-    def __init__(self, gpu_id):
+    def __init__(self, gpu_id, period_s=0.001):
         self.gpu_id = gpu_id
+        self.period = period_s
         self.proc = None
         self.lines = []
+        self.samples = []  # (sm MHz, max sm MHz, reason bits)
+        self._stop = threading.Event()
+        self._first = threading.Event()
+        self.t = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        gid = str(self.gpu_id)
+        if gid.startswith('GPU-'):
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(gid)
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(int(gid))
+
+    def _poll(self, nv, h):
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while True:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(sm), float(mx), int(rs)))
+            except Exception:  # noqa: BLE001 -- a failed read only loses a sample
+                pass
+            self._first.set()
+            if self._stop.wait(self.period):
+                break
 
     def __enter__(self):
+        try:
+            nv, h = self._nvml_handle()
+            self.t = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
+            self.t.start()
+            self._first.wait(5.0)
+            return self
+        except Exception:  # noqa: BLE001 -- no NVML: fall back to nvidia-smi
+            self.t = None
         try:
             self.proc = subprocess.Popen(
                 ['nvidia-smi', '-i', str(self.gpu_id),
@@ -180,17 +223,25 @@ class ClockSampler:
             self.lines.append(ln.strip())
 
     def __exit__(self, *a):
+        self._stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        elif self.t is not None:
+            self.t.join(timeout=5)
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown',
-                 'sw_power_cap']
+        for s_, m_, bits in self.samples:
+            sm.append(s_)
+            mx.append(m_)
+            for nm, bit in self.REASONS:
+                if bits & bit:
+                    reasons.add(nm)
+        names = [nm for nm, _ in self.REASONS]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(',')]
             if len(parts) != 6:
@@ -207,7 +258,8 @@ class ClockSampler:
             return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': [],
                     'samples': 0}
         return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(mx),
-                'reasons': sorted(reasons), 'samples': len(sm)}
+                'reasons': sorted(reasons), 'samples': len(sm),
+                'source': 'nvml' if self.samples else 'nvidia-smi'}
 
 
 # ---------------------------------------------------------------------------

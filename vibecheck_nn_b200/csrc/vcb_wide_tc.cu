@@ -54,6 +54,7 @@ __global__ void wtc_finish_kernel(int R, const float* acc0, const float* part, i
   for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < R; m += gridDim.x * blockDim.x) {
     float v = acc0[m];
     const float* p = part + (long long)m * ldpart;
+#pragma unroll 8
     for (int t = 0; t < nparts; ++t) v = __fadd_rn(v, p[t]);
     lb[m] = v;
     if (best) {
@@ -80,6 +81,7 @@ __global__ void wtc_adam_kernel(int D, int Q, int n, int ldd, const float* dcont
     const long long box = i / n;
     const int j = (int)(i - box * n);
     float gsum = 0.f;
+#pragma unroll 8
     for (int q = 0; q < Q; ++q) gsum = __fadd_rn(gsum, dcontrib[(box * Q + q) * ldd + j]);
     const float g = -gsum;
     const float mm = __fadd_rn(m1[i], __fmul_rn(0.1f, __fsub_rn(g, m1[i])));
