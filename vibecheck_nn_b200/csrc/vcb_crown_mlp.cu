@@ -116,20 +116,29 @@ __global__ void __launch_bounds__(kNT, 2)
   }
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
   if (tid < 8) sm[p.w_soff[nfc - 1] + p.wrows[nfc - 1] * p.pw[nfc - 1] + tid] = 0.f;
-  // ---- spec rows times the last fc layer (identical for every box)
+  // ---- spec rows times the last fc layer (identical for every box), from
+  // the resident weight rows [W[o, 0..nprev), b[o]]; each thread runs four
+  // spec rows' dot products side by side (each one in o order).
   if (Q > 0) {
+    __syncthreads();  // the zeroed pad above
     const int nprev = p.dims[nfc - 1];
-    const float* Wg = p.W + p.w_goff[nfc - 1];
-    const float* bg = p.b + p.b_goff[nfc - 1];
+    const int pwl = p.pw[nfc - 1];
+    const float* sWl = sm + p.w_soff[nfc - 1];
     float* V = sm + p.v_soff;
-    for (int q = tid >> 5; q < Q; q += kNT / 32) {
-      for (int c = tid & 31; c <= nprev; c += 32) {
-        float s = 0.f;
-        for (int o = 0; o < nL; ++o)
-          s = fmaf(__ldg(p.specW + q * nL + o),
-                   c < nprev ? __ldg(Wg + (long long)o * nprev + c) : __ldg(bg + o), s);
-        V[q * p.pv + c] = s;
+    const int ncol = nprev + 1, nqg = (Q + 3) >> 2;
+    for (int item = tid; item < nqg * ncol; item += kNT) {
+      const int qg = item / ncol, c = item - qg * ncol;
+      const int q0 = 4 * qg;
+      float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int o = 0; o < nL; ++o) {
+        const float w = sWl[o * pwl + c];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (q0 + j < Q) acc4[j] = fmaf(__ldg(p.specW + (q0 + j) * nL + o), w, acc4[j]);
       }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (q0 + j < Q) V[(q0 + j) * p.pv + c] = acc4[j];
     }
   }
   __syncthreads();
@@ -529,13 +538,20 @@ int plan_crown(const vcb_mlp* net, int B, int Q, bool ibp, Plan* plan) {
   // SM; otherwise one CTA per SM.
   const int two_cta = (233472 - 2 * 1024) / 2;
   const int one_cta = 232448;
-  // Small batches (a BaB iteration) use smaller tiles so every CTA slot gets
-  // work: the largest even TB <= 32 with at least two tiles per SM.
-  int tb_max = 32;
-  while (tb_max > 2 && (long long)B < (long long)tb_max * 2 * sm_count()) tb_max -= 2;
   // Without the IBP forward (caller-supplied bounds) a tile may hold a single
   // box, which many-row specs (the CROWN-intermediate seeds) need.
   const int tb_step = ibp ? 2 : 1;
+  // Small batches (a BaB iteration) use the smallest tile (a multiple of
+  // tb_step, <= 32) that still covers the batch in one wave of CTAs (two per
+  // SM): a tile's time is mostly its chain of dependent layer steps, so a
+  // second wave -- even a short one -- would double the launch time.  A
+  // box's arithmetic does not depend on the tile size.
+  int tb_max = 32;
+  const long long slots = 2LL * sm_count();
+  if (B > 0 && (long long)B <= 32 * slots) {
+    const int t = (int)((B + slots - 1) / slots);
+    tb_max = std::max(tb_step, std::min(32, (t + tb_step - 1) / tb_step * tb_step));
+  }
   bool found = false;
   for (int pass = 0; pass < 2 && !found; ++pass) {
     const int limit = pass == 0 ? two_cta : one_cta;
