@@ -119,3 +119,42 @@ def test_root_pgd_sequence_reports_phase():
     assert sat and phase == 'batched_pgd'
     y = wk._mlp_forward64(w['layers'], wit[None].astype(np.float64))[0]
     assert y[1] >= y[0] - 1e-5
+
+
+def _root_pgd_sequential(spec, gg, st):
+    """root_pgd's stages one after the other on one stream (the reference's
+    order), for comparison with the overlapped version."""
+    xl = torch.as_tensor(np.asarray(spec.x_lo), dtype=torch.float32, device=DEV)
+    xh = torch.as_tensor(np.asarray(spec.x_hi), dtype=torch.float32, device=DEV)
+    sat, wit = pgd.pgd_attack_general(xl, xh, spec, gg, st, time_budget=5.0)
+    if sat and wit is not None:
+        return True, wit, 'batched_pgd'
+    sat, wit = pgd._simple_pgd(xl.flatten().unsqueeze(0), xh.flatten().unsqueeze(0), spec,
+                               gg, 5, DEV, torch.float32, n_restarts=10000, n_iter=50)
+    return (True, wit, 'batched_simple_pgd') if sat else (False, None, None)
+
+
+@pytest.mark.parametrize('case', ['general_finds', 'none_finds', 'simple_finds'])
+def test_root_pgd_overlapped_stages_match_sequential(case):
+    """The general and simple stages overlap on two streams; verdict, phase,
+    witness and the generators' states afterwards equal the sequential run."""
+    w = wk.cfg1(0)
+    gg = wk.mlp_gg(w['layers'], DEV)
+    st = types.SimpleNamespace(pgd_restarts=10, pgd_iter=100, pgd_optim='adam_sign')
+    pair = (1, 0) if case == 'none_finds' else (0, 1)
+    spec = LinearSpec(w['xl'], w['xh'], [[('pair',) + pair]])
+    if case == 'simple_finds':
+        st.pgd_iter = 1  # one step from uniform draws: the general stage gives up
+        st.pgd_restarts = 1
+    outs = []
+    for fn in (lambda: pgd.root_pgd(spec, gg, 5, DEV, st),
+               lambda: _root_pgd_sequential(spec, gg, st)):
+        torch.manual_seed(1234)
+        outs.append((fn(), torch.get_rng_state(), torch.cuda.get_rng_state(DEV)))
+    (a, ca, ga), (b, cb_, gb) = outs
+    assert a[0] == b[0] and a[2] == b[2], (a[:1] + a[2:], b[:1] + b[2:])
+    if a[0]:
+        np.testing.assert_array_equal(a[1], b[1])
+    assert torch.equal(ca, cb_) and torch.equal(ga, gb)
+    if case == 'none_finds':
+        assert not a[0]

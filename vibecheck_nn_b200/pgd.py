@@ -256,14 +256,16 @@ def _bc_tables(n_iter, device):
 
 
 def pgd_attack_general(xl, xh, spec, gg, settings, restrict_disj=None,
-                       time_budget=None, per_restart_disj=None, seed=None):
+                       time_budget=None, per_restart_disj=None, seed=None, defer=False):
     """PGD counterexample search for a DNF spec (pgd.py:233-524): restarts
     drawn uniformly in the box, optional OSI initialisation, hinge loss over
     the attacked disjuncts, sign_sgd / adam_sign / adam_clipping steps with
     step decay, plateau give-up and wall-time budget.  For MLPs that fit the
     shared-memory kernel one launch runs every restart and iteration; other
     networks run the same loop on the layer kernels.  Returns (is_sat,
-    witness ndarray or None).
+    witness ndarray or None); with ``defer`` the launch is queued on the
+    current stream and a callable that waits for it and returns the same
+    pair comes back instead (or the pair itself when nothing was launched).
     """
     t_start = time.perf_counter()
     xl, xh = expand_search_box(xl, xh, settings)
@@ -324,6 +326,11 @@ def pgd_attack_general(xl, xh, spec, gg, settings, restrict_disj=None,
     x = x.reshape(n_restarts, n_in).contiguous()
     args = (x, xl.reshape(1, n_in), xh.reshape(1, n_in), step.reshape(-1, n_in), w_d, n_osi,
             n_iter, optim, lr_decay, hinge_thr, plateau, disjuncts, act, prd, bloat)
+    def result(idx):
+        if idx is None:
+            return False, None
+        return True, x[idx].reshape(xl.shape).detach().cpu().numpy()
+
     idx = -1
     if isinstance(net, MlpDesc):
         budget_ns = 0
@@ -331,15 +338,23 @@ def pgd_attack_general(xl, xh, spec, gg, settings, restrict_disj=None,
             left = time_budget - (time.perf_counter() - t_start)
             budget_ns = max(1, int(left * 1e9))
         try:
-            idx = pgd_general_run(net, *args, budget_ns)
+            fin = pgd_general_launch(net, *args, budget_ns)
+            if defer:
+                stream = torch.cuda.current_stream(dev)
+
+                def finish():
+                    i = fin()
+                    with torch.cuda.stream(stream):
+                        return result(i)
+                return finish
+            idx = fin()
         except NotImplementedError:  # wider than the shared-memory kernel
             net = _graph(gg, dev)
     if idx == -1:
         deadline = None if time_budget is None else t_start + time_budget
         idx = general_layerwise(net, *args, deadline)
-    if idx is None:
-        return False, None
-    return True, x[idx].reshape(xl.shape).detach().cpu().numpy()
+    out = result(idx)
+    return (lambda: out) if defer else out
 
 
 def pgd_general_run(desc, x, lo, hi, step, w_d, n_osi, n_iter, optim, lr_decay, hinge_thr,
@@ -347,6 +362,15 @@ def pgd_general_run(desc, x, lo, hi, step, w_d, n_osi, n_iter, optim, lr_decay, 
     """One ``vcb_mlp_pgd_general`` launch over the restarts x (R, n_in)
     (updated in place) and the host replay of the loop's give-up rules.
     Returns the restart index of the confirmed witness or None."""
+    return pgd_general_launch(desc, x, lo, hi, step, w_d, n_osi, n_iter, optim, lr_decay,
+                              hinge_thr, plateau, disjuncts, act, prd, bloat, budget_ns)()
+
+
+def pgd_general_launch(desc, x, lo, hi, step, w_d, n_osi, n_iter, optim, lr_decay, hinge_thr,
+                       plateau, disjuncts, act, prd, bloat=0.0, budget_ns=0):
+    """pgd_general_run up to its launch: returns ``finish()``, which waits
+    for the kernel (the one host synchronisation, on the stream current at
+    launch) and replays the give-up rules."""
     dev = x.device
     R, n_in = x.shape
     n_out = desc.n_out
@@ -373,7 +397,18 @@ def pgd_general_run(desc, x, lo, hi, step, w_d, n_osi, n_iter, optim, lr_decay, 
         len(act), int(prd), float(bloat), int(budget_ns), base, base + 8,
         base + 4 * (2 + n_iter + 2), _lib.stream_of(dev))
     _lib.check(rc, 'vcb_mlp_pgd_general')
-    host = state.cpu().numpy().view(np.uint32)  # the one host sync
+    stream = torch.cuda.current_stream(dev)
+
+    def finish():
+        with torch.cuda.stream(stream):
+            host = state.cpu().numpy().view(np.uint32)  # the one host sync
+        return _general_replay(host, n_iter, hinge_thr, plateau)
+    return finish
+
+
+def _general_replay(host, n_iter, hinge_thr, plateau):
+    """The host side of pgd_general_run: the witness key and the replay of
+    the loop's give-up rules from the kernel's per-iteration record."""
     key = int(host[0]) | (int(host[1]) << 32)
     t_w = (key >> 32) if key != NO_SAT else None
     t_stop = int(np.int32(host[-1]))
@@ -478,21 +513,45 @@ def root_pgd(spec, gg, n_output, device, settings):
     Returns (sat, witness, phase)."""
     xl = torch.as_tensor(np.asarray(spec.x_lo), dtype=F32, device=device)
     xh = torch.as_tensor(np.asarray(spec.x_hi), dtype=F32, device=device)
+    # The two stages are independent searches; the general one (a few
+    # restarts: one CTA) runs on a side stream while the simple one fills the
+    # other SMs.  Random draws happen on the host in the sequential order and
+    # the results are consulted in it (the simple stage's only when the
+    # general one found nothing), so the outcome is the sequential one.
+    dev = _dev(device)
+    main = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(main)
+    general = None
     try:
         budget = float(_num(settings, 'pgd_time_budget_phase0', 5.0))
-        sat, wit = pgd_attack_general(xl, xh, spec, gg, settings, time_budget=budget)
-        if sat and wit is not None:
-            return True, wit, 'batched_pgd'
+        with torch.cuda.stream(side):
+            r = pgd_attack_general(xl, xh, spec, gg, settings, time_budget=budget, defer=True)
+        general = r if callable(r) else (lambda: r)
     except (RuntimeError, torch.cuda.OutOfMemoryError):
         pass
+    # the simple stage reseeds torch's generators; when the general stage
+    # wins, the sequential order would not have run it, so its states return
+    rng = (torch.get_rng_state(), torch.cuda.get_rng_state(dev))
+    simple = (False, None)
     try:
-        sat, wit = _simple_pgd(xl.flatten().unsqueeze(0), xh.flatten().unsqueeze(0), spec,
-                               gg, n_output, device, torch.float32, n_restarts=10000,
-                               n_iter=50)
-        if sat:
-            return True, wit, 'batched_simple_pgd'
+        simple = _simple_pgd(xl.flatten().unsqueeze(0), xh.flatten().unsqueeze(0), spec,
+                             gg, n_output, device, torch.float32, n_restarts=10000, n_iter=50)
     except (RuntimeError, torch.cuda.OutOfMemoryError):
         pass
+    gen = (False, None)
+    if general is not None:
+        try:
+            gen = general()
+        except (RuntimeError, torch.cuda.OutOfMemoryError):
+            pass
+    main.wait_stream(side)
+    if gen[0] and gen[1] is not None:
+        torch.set_rng_state(rng[0])
+        torch.cuda.set_rng_state(rng[1], dev)
+        return True, gen[1], 'batched_pgd'
+    if simple[0]:
+        return True, simple[1], 'batched_simple_pgd'
     return False, None, None
 
 
