@@ -273,7 +273,7 @@ template <int MODE, int COLS>
 __device__ __forceinline__ void tc_epilogue_vec(const TcArgs& a, int rowbase, int nb,
                                                 const float (&acc)[COLS], float* sm) {
   constexpr bool kSum = MODE == kEpiRelax || MODE == kEpiConcretize;
-  constexpr int kRowsPerStep = 4, kSteps = 2;  // 8 rows of loads in flight per batch
+  constexpr int kRowsPerStep = 4, kSteps = 4;  // 16 rows of loads in flight per batch
   const TcEpi& e = a.ep;
   float* rs = sm + 32 * 32;  // per-row running sums
   const int lane = threadIdx.x & 31;
