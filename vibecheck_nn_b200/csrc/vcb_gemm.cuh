@@ -36,28 +36,54 @@ struct ColLoad {
   static constexpr bool kFastB = false;  // consecutive threads walk n
 };
 
-template <bool DUAL, class AL, class BL, class AL2, class BL2>
-__device__ __forceinline__ void mainloop(int M, int N, int K, const AL& A, const BL& B,
-                                         const AL2& A2, const BL2& B2, float (&acc)[8][4],
-                                         float (&acc2)[8][4], float* smem) {
+// RM consecutive staged A values of one k (16-byte loads where RM allows).
+template <int RM>
+__device__ __forceinline__ void tile_rows(const float* p, float (&v)[RM]) {
+  if constexpr (RM % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < RM; i += 4) {
+      const float4 t = *reinterpret_cast<const float4*>(p + i);
+      v[i] = t.x;
+      v[i + 1] = t.y;
+      v[i + 2] = t.z;
+      v[i + 3] = t.w;
+    }
+  } else if constexpr (RM == 2) {
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    v[0] = t.x;
+    v[1] = t.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < RM; ++i) v[i] = p[i];
+  }
+}
+
+// RM rows per thread: the CTA tile is (16 RM) x 64 (RM = 8: the 128 x 64 tile
+// above; smaller RM gives more CTAs for short operands).  Each output
+// accumulates over k in ascending order whatever RM is.
+template <bool DUAL, int RM, class AL, class BL, class AL2, class BL2>
+__device__ __forceinline__ void mainloop_rm(int M, int N, int K, const AL& A, const BL& B,
+                                            const AL2& A2, const BL2& B2, float (&acc)[RM][4],
+                                            float (&acc2)[RM][4], float* smem) {
+  constexpr int TMr = 16 * RM;
   const int tid = threadIdx.x;
   const int ty = tid >> 4, tx = tid & 15;
-  const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN;
+  const int m0 = blockIdx.x * TMr, n0 = blockIdx.y * TN;
   float* As = smem;                      // [2][TK][TM + 4]
-  float* Bs = As + 2 * TK * (TM + 4);    // [2][TK][TN + 4]
+  float* Bs = As + 2 * TK * (TMr + 4);    // [2][TK][TN + 4]
   float* As2 = Bs + 2 * TK * (TN + 4);
-  float* Bs2 = As2 + (DUAL ? 2 * TK * (TM + 4) : 0);
+  float* Bs2 = As2 + (DUAL ? 2 * TK * (TMr + 4) : 0);
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < RM; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = acc2[i][j] = 0.f;
-  float ra[8], rb[4], ra2[8], rb2[4];
+  float ra[RM], rb[4], ra2[RM], rb2[4];
   auto load = [&](int k0) {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int idx = tid + u * GT;  // 0..2047: 128 rows x 16 k
+    for (int u = 0; u < RM; ++u) {
+      const int idx = tid + u * GT;  // TMr rows x 16 k
       int mm, kk;
-      if (AL::kFastA) { mm = idx & 127; kk = idx >> 7; } else { mm = idx >> 4; kk = idx & 15; }
+      if (AL::kFastA) { mm = idx % TMr; kk = idx / TMr; } else { mm = idx >> 4; kk = idx & 15; }
       const int gm = m0 + mm, gk = k0 + kk;
       const bool ok = gm < M && gk < K;
       ra[u] = ok ? A.a(gm, gk) : 0.f;
@@ -75,15 +101,15 @@ __device__ __forceinline__ void mainloop(int M, int N, int K, const AL& A, const
     }
   };
   auto store = [&](int buf) {
-    float* as = As + buf * TK * (TM + 4);
+    float* as = As + buf * TK * (TMr + 4);
     float* bs = Bs + buf * TK * (TN + 4);
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < RM; ++u) {
       const int idx = tid + u * GT;
       int mm, kk;
-      if (AL::kFastA) { mm = idx & 127; kk = idx >> 7; } else { mm = idx >> 4; kk = idx & 15; }
-      as[kk * (TM + 4) + mm] = ra[u];
-      if (DUAL) As2[buf * TK * (TM + 4) + kk * (TM + 4) + mm] = ra2[u];
+      if (AL::kFastA) { mm = idx % TMr; kk = idx / TMr; } else { mm = idx >> 4; kk = idx & 15; }
+      as[kk * (TMr + 4) + mm] = ra[u];
+      if (DUAL) As2[buf * TK * (TMr + 4) + kk * (TMr + 4) + mm] = ra2[u];
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -101,29 +127,26 @@ __device__ __forceinline__ void mainloop(int M, int N, int K, const AL& A, const
   for (int t = 0; t < nk; ++t) {
     const int buf = t & 1;
     if (t + 1 < nk) load((t + 1) * TK);
-    const float* as = As + buf * TK * (TM + 4);
+    const float* as = As + buf * TK * (TMr + 4);
     const float* bs = Bs + buf * TK * (TN + 4);
-    const float* as2 = As2 + buf * TK * (TM + 4);
+    const float* as2 = As2 + buf * TK * (TMr + 4);
     const float* bs2 = Bs2 + buf * TK * (TN + 4);
 #pragma unroll
     for (int kk = 0; kk < TK; ++kk) {
-      const float4 a0 = *reinterpret_cast<const float4*>(as + kk * (TM + 4) + ty * 8);
-      const float4 a1 = *reinterpret_cast<const float4*>(as + kk * (TM + 4) + ty * 8 + 4);
+      float av[RM], cv[RM];
+      tile_rows<RM>(as + kk * (TMr + 4) + ty * RM, av);
       const float4 b0 = *reinterpret_cast<const float4*>(bs + kk * (TN + 4) + tx * 4);
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
       const float bv[4] = {b0.x, b0.y, b0.z, b0.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < RM; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
       if (DUAL) {
-        const float4 c0 = *reinterpret_cast<const float4*>(as2 + kk * (TM + 4) + ty * 8);
-        const float4 c1 = *reinterpret_cast<const float4*>(as2 + kk * (TM + 4) + ty * 8 + 4);
+        tile_rows<RM>(as2 + kk * (TMr + 4) + ty * RM, cv);
         const float4 d0 = *reinterpret_cast<const float4*>(bs2 + kk * (TN + 4) + tx * 4);
-        const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
         const float dv[4] = {d0.x, d0.y, d0.z, d0.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < RM; ++i)
 #pragma unroll
           for (int j = 0; j < 4; ++j) acc2[i][j] = fmaf(cv[i], dv[j], acc2[i][j]);
       }
@@ -133,10 +156,19 @@ __device__ __forceinline__ void mainloop(int M, int N, int K, const AL& A, const
   }
 }
 
-inline int gemm_smem_bytes(bool dual) {
-  return (2 * TK * (TM + 4) + 2 * TK * (TN + 4)) * (dual ? 2 : 1) * 4;
+template <bool DUAL, class AL, class BL, class AL2, class BL2>
+__device__ __forceinline__ void mainloop(int M, int N, int K, const AL& A, const BL& B,
+                                         const AL2& A2, const BL2& B2, float (&acc)[8][4],
+                                         float (&acc2)[8][4], float* smem) {
+  mainloop_rm<DUAL, 8>(M, N, K, A, B, A2, B2, acc, acc2, smem);
 }
 
-inline dim3 gemm_grid(int M, int N) { return dim3((M + TM - 1) / TM, (N + TN - 1) / TN); }
+inline int gemm_smem_bytes(bool dual, int rm = 8) {
+  return (2 * TK * (16 * rm + 4) + 2 * TK * (TN + 4)) * (dual ? 2 : 1) * 4;
+}
+
+inline dim3 gemm_grid(int M, int N, int rm = 8) {
+  return dim3((M + 16 * rm - 1) / (16 * rm), (N + TN - 1) / TN);
+}
 
 }  // namespace vcb

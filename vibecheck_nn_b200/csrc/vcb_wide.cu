@@ -61,15 +61,18 @@ struct IbpArgs {
   float *sblo, *sbhi, *mid_o, *rad_o;                 // sb: D x nout; mid_o/rad_o: D x ldo
 };
 
+// RM rows per thread ((16 RM) x 64 CTA tiles): the host takes the largest
+// RM whose grid still gives every SM a tile.
+template <int RM>
 __global__ void __launch_bounds__(GT) ibp_layer_kernel(const IbpArgs a) {
   extern __shared__ __align__(16) float smem[];
-  float acc[8][4], acc2[8][4];
-  mainloop<true>(a.D, a.nout, a.nin, RowLoad{a.mid, a.lda}, RowLoad{a.W, a.nin},
-                 RowLoad{a.rad, a.lda}, RowLoad{a.Wabs, a.nin}, acc, acc2, smem);
+  float acc[RM][4], acc2[RM][4];
+  mainloop_rm<true, RM>(a.D, a.nout, a.nin, RowLoad{a.mid, a.lda}, RowLoad{a.W, a.nin},
+                        RowLoad{a.rad, a.lda}, RowLoad{a.Wabs, a.nin}, acc, acc2, smem);
   const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-  const int m0 = blockIdx.x * TM + ty * 8, n0 = blockIdx.y * TN + tx * 4;
+  const int m0 = blockIdx.x * (16 * RM) + ty * RM, n0 = blockIdx.y * TN + tx * 4;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < RM; ++i) {
     const int m = m0 + i;
     if (m >= a.D) continue;
 #pragma unroll
@@ -298,11 +301,22 @@ extern "C" int vcb_wide_ibp_layer(int32_t D, int32_t nin, int32_t nout, const fl
   if (!mid || !rad || !W || !Wabs || !b || (lda & 3) || (mid_o && (ldo & 3)))
     return fail(VCB_ERR_INVALID, "vcb_wide_ibp_layer: NULL pointer or ld not a multiple of 4");
   IbpArgs a{D, nin, nout, lda, ldo, mid, rad, W, Wabs, b, clo, chi, sb_lo, sb_hi, mid_o, rad_o};
-  const int sm = smem_bytes(true);
-  int rc = ensure_smem(reinterpret_cast<const void*>(ibp_layer_kernel), sm);
-  if (rc) return rc;
-  ibp_layer_kernel<<<gemm_grid(D, nout), GT, sm, static_cast<cudaStream_t>(stream)>>>(a);
-  return check_launch("vcb_wide_ibp_layer");
+  auto launch = [&](auto kernel, int rm) {
+    const int sm = gemm_smem_bytes(true, rm);
+    const int rc = ensure_smem(reinterpret_cast<const void*>(kernel), sm);
+    if (rc) return rc;
+    kernel<<<gemm_grid(D, nout, rm), GT, sm, static_cast<cudaStream_t>(stream)>>>(a);
+    return check_launch("vcb_wide_ibp_layer");
+  };
+  // the largest row tile whose grid still covers every SM (short batches of
+  // domains would otherwise leave most SMs idle through the whole K loop)
+  auto ctas = [&](int rm) {
+    const dim3 g = gemm_grid(D, nout, rm);
+    return (long long)g.x * g.y;
+  };
+  if (ctas(8) >= sm_count()) return launch(ibp_layer_kernel<8>, 8);
+  if (ctas(2) >= sm_count()) return launch(ibp_layer_kernel<2>, 2);
+  return launch(ibp_layer_kernel<1>, 1);
 }
 
 extern "C" int vcb_wide_back_layer(int32_t R, int32_t Q, int32_t nin, int32_t nout,
