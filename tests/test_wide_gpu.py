@@ -333,3 +333,27 @@ def test_tc_alpha_loop_graph_replay():
         ref = wide.alpha_loop(wn, xlt, xht, sb, W_k, b_q + shift, 6, 0.1, tc=False)
         assert close(N(got), N(ref), rtol=5e-3, atol=1e-4), (k, max_excess(N(got), N(ref),
                                                                            rtol=5e-3, atol=1e-4))
+
+
+@pytest.mark.parametrize('dims', [(41, 50, 66, 30, 7), (9, 130, 3, 70, 5)])
+def test_tc_alpha_loop_odd_widths_match_simt(dims):
+    """Widths that are not multiples of 4 (the GEMM epilogue's one-column-per-
+    lane path, partial 32- and 64-column groups, K tails) on the tensor
+    cores against the SIMT layer kernels."""
+    rng = np.random.default_rng(sum(dims))
+    layers = wk.mlp_params(dims, rng)
+    D, Q = 48, 3
+    x0 = rng.uniform(0, 1, (D, dims[0]))
+    xl = (x0 - 0.08).astype(np.float32)
+    xh = (x0 + 0.08).astype(np.float32)
+    SW = rng.normal(size=(Q, dims[-1])).astype(np.float32)
+    Sb = (rng.normal(size=Q) - 5.0).astype(np.float32)
+    gg = wk.mlp_gg(layers, DEV)
+    wn = wide.wide_net(gg, DEV)
+    xlt, xht = T(xl), T(xh)
+    sb = wide.wide_ibp(wn, xlt, xht)
+    got = wide.alpha_loop(wn, xlt, xht, sb, T(SW), T(Sb), 6, 0.1, tc=True)
+    assert wide.last_stats['path'] == 'tc'
+    ref = wide.alpha_loop(wn, xlt, xht, sb, T(SW), T(Sb), 6, 0.1, tc=False)
+    assert close(N(got), N(ref), rtol=5e-3, atol=1e-4), max_excess(N(got), N(ref), rtol=5e-3,
+                                                                   atol=1e-4)

@@ -242,7 +242,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, int rowbase, int nb
       if (kSum) {
         __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) s = __fadd_rn(s, j < rows ? sm[lane * kStagePitch + j] : 0.f);
+        for (int j = 0; j < 32; ++j) s = __fadd_rn(s, sm[lane * kStagePitch + j]);  // columns of row lane
       }
     }
     if (kSum && (c & 1) == 1) {  // a 64-column group is complete
