@@ -335,14 +335,16 @@ def test_tc_alpha_loop_graph_replay():
                                                                            rtol=5e-3, atol=1e-4))
 
 
-@pytest.mark.parametrize('dims', [(41, 50, 66, 30, 7), (9, 130, 3, 70, 5)])
-def test_tc_alpha_loop_odd_widths_match_simt(dims):
+@pytest.mark.parametrize('dims, D', [((41, 50, 66, 30, 7), 48), ((9, 130, 3, 70, 5), 48),
+                                     ((40, 64, 64, 48, 8), 37)])
+def test_tc_alpha_loop_odd_widths_match_simt(dims, D):
     """Widths that are not multiples of 4 (the GEMM epilogue's one-column-per-
-    lane path, partial 32- and 64-column groups, K tails) on the tensor
+    lane path, partial 32- and 64-column groups, K tails) and row counts that
+    end in a partial warp (37 x 3 rows on the 16-byte path) on the tensor
     cores against the SIMT layer kernels."""
     rng = np.random.default_rng(sum(dims))
     layers = wk.mlp_params(dims, rng)
-    D, Q = 48, 3
+    Q = 3
     x0 = rng.uniform(0, 1, (D, dims[0]))
     xl = (x0 - 0.08).astype(np.float32)
     xh = (x0 + 0.08).astype(np.float32)
