@@ -148,7 +148,6 @@ __device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int ti
       const int o4 = 4 * ob;
       const float* ar = ain + s * pa;
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll 4
       for (int i = 0; i < nin; ++i) {
         const float av = ar[i];
         const float4 wv = *reinterpret_cast<const float4*>(sWT + i * pwt + o4);
@@ -182,41 +181,30 @@ __device__ void tile_backward(const PgdNet& n, float* sm, int tid) {
     const int nin = n.dims[l], nout = n.dims[l + 1], pwt = n.pwt[l];
     const float* sWT = sm + n.wt_soff[l];
     const float* zprev = (l > 0) ? sm + n.z_soff + (l - 1) * kPS * pz : nullptr;
-    constexpr int kMaxOut = (kPMaxW + kStep - 1) / kStep;
-    float vals[kMaxOut];
+    float vals[(kPMaxW + kStep - 1) / kStep];
     const int sl = tid % kPS, i0 = tid / kPS;
     const float* grow = g + sl * pz;
     const int kend = pad4(nout);
-    const int mine = i0 < nin ? (nin - i0 + kStep - 1) / kStep : 0;  // outputs i0 + c kStep
-#pragma unroll
-    for (int c = 0; c < kMaxOut; ++c) vals[c] = 0.f;
-    // every output sums over o in fixed ascending order, 4 at a time (g and
-    // W^T rows are zero past n_out); the thread's outputs advance together
-    for (int o = 0; o < kend; o += 4) {
-      const float4 gv = *reinterpret_cast<const float4*>(grow + o);
-#pragma unroll
-      for (int c = 0; c < kMaxOut; ++c) {
-        if (c < mine) {
-          const float4 wv = *reinterpret_cast<const float4*>(sWT + (i0 + c * kStep) * pwt + o);
-          vals[c] = fmaf(gv.x, wv.x, vals[c]);
-          vals[c] = fmaf(gv.y, wv.y, vals[c]);
-          vals[c] = fmaf(gv.z, wv.z, vals[c]);
-          vals[c] = fmaf(gv.w, wv.w, vals[c]);
-        }
+    int cnt = 0;
+    for (int i = i0; i < nin; i += kStep) {
+      // sum over o in fixed ascending order, 4 at a time (g and W^T rows are
+      // zero past n_out)
+      const float* wt = sWT + i * pwt;
+      float acc = 0.f;
+      for (int o = 0; o < kend; o += 4) {
+        const float4 gv = *reinterpret_cast<const float4*>(grow + o);
+        const float4 wv = *reinterpret_cast<const float4*>(wt + o);
+        acc = fmaf(gv.x, wv.x, acc);
+        acc = fmaf(gv.y, wv.y, acc);
+        acc = fmaf(gv.z, wv.z, acc);
+        acc = fmaf(gv.w, wv.w, acc);
       }
-    }
-    if (zprev) {
-#pragma unroll
-      for (int c = 0; c < kMaxOut; ++c)
-        if (c < mine && !(zprev[sl * pz + i0 + c * kStep] > 0.f)) vals[c] = 0.f;
+      if (zprev && !(zprev[sl * pz + i] > 0.f)) acc = 0.f;
+      vals[cnt++] = acc;
     }
     __syncthreads();  // every thread has read g
-#pragma unroll
-    for (int c = 0; c < kMaxOut; ++c) {
-      const int i = i0 + c * kStep;
-      if (i < pz) g[sl * pz + i] = c < mine ? vals[c] : 0.f;
-    }
-    for (int i = i0 + kMaxOut * kStep; i < pz; i += kStep) g[sl * pz + i] = 0.f;
+    cnt = 0;
+    for (int i = i0; i < pz; i += kStep) g[sl * pz + i] = (i < nin) ? vals[cnt++] : 0.f;
     __syncthreads();
   }
 }
