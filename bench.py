@@ -175,6 +175,7 @@ class ClockSampler:
         self._stop = threading.Event()
         self._first = threading.Event()
         self.t = None
+        self.nv = None
 
     def _nvml_handle(self):
         import pynvml
@@ -200,6 +201,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             nv, h = self._nvml_handle()
+            self.nv = nv
             self.t = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
             self.t.start()
             self._first.wait(5.0)
@@ -232,6 +234,10 @@ class ClockSampler:
                 self.proc.kill()
         elif self.t is not None:
             self.t.join(timeout=5)
+            try:
+                self.nv.nvmlShutdown()
+            except Exception:  # noqa: BLE001 -- releasing NVML is best effort
+                pass
 
     def summary(self):
         sm, mx, reasons = [], [], set()
