@@ -236,3 +236,25 @@ def test_alpha_beta_and_given_bounds_match_across_kernels(kernel_path, B):
     A0, A1 = N(outs[0]['A']).astype(np.float64), N(outs[1]['A']).astype(np.float64)
     scale = np.abs(A1).max(axis=2, keepdims=True)
     assert (np.abs(A0 - A1) <= 1e-6 + 1e-5 * scale).all()
+
+
+@pytest.mark.parametrize('Q', [3, 4, 5, 16])
+def test_split_tail_matches_unsplit(Q, kernel_path):
+    """151 tiles of 128 boxes on the 148-CTA persistent grid: the tensor-core
+    kernel splits the 3 tiles of its last round by spec-row pass across two
+    CTAs each.  Every box's bounds must equal, bit for bit, those of the same
+    boxes bounded in two calls that need no split (148 tiles, then 3)."""
+    B = 151 * 128 - 28
+    w = wk.cfg2(seed=5, n_boxes=B, n_q=Q)
+    gg = wk.mlp_gg(w['layers'], DEV)
+    spec_ew = wk.spec_ew_from(w['spec_W'], w['spec_b'], DEV)
+    xl, xh = T(w['xl']), T(w['xh'])
+
+    def run(lo, hi):
+        return ops.ibp_crown_batched(lo, hi, gg, spec_ew, DEV, return_input_linear=True)
+
+    whole = run(xl, xh)
+    cut = 148 * 128
+    first, rest = run(xl[:cut], xh[:cut]), run(xl[cut:], xh[cut:])
+    for a, b0, b1 in zip(whole, first, rest):
+        assert torch.equal(a, torch.cat([b0, b1])), Q

@@ -88,6 +88,7 @@ struct TcParams {
   long long slot_f2;       // float2 per CTA slot
   const uint8_t* img;      // (n_fc - 1) x 3 images of kImg bytes
   int B, Q, ntiles, npass;
+  int split_tail;          // the last, partial round's tiles are split by pass (see item_at)
   const float *xl, *xh, *clo, *chi, *sblo, *sbhi, *alpha, *beta, *specW, *specb;
   float *lb, *A, *accout, *sbolo, *sbohi;
   float2* slopes;
@@ -95,6 +96,30 @@ struct TcParams {
 };
 
 __host__ __device__ inline int pad16(int n) { return (n + 15) & ~15; }
+
+// Work items of this CTA.  Item i < full is tile i * gridDim.x + blockIdx.x
+// with every spec-row pass.  The rem tiles of the last, partial round either
+// go whole to CTAs 0 .. rem-1, or (split_tail, 2 rem <= gridDim.x) each to
+// two CTAs, b and b + rem, that recompute the forward and take the first and
+// second half of the passes: the round then costs a forward and half the
+// passes instead of a whole tile while the other CTAs idle.
+struct TcItem {
+  int tile, pass_lo, pass_hi;
+};
+
+__device__ __forceinline__ int items_of(const TcParams& p) {
+  const int g = gridDim.x, b = blockIdx.x;
+  const int full = p.ntiles / g, rem = p.ntiles - full * g;
+  return full + (b < (p.split_tail ? 2 * rem : rem) ? 1 : 0);
+}
+
+__device__ __forceinline__ TcItem item_at(const TcParams& p, int i) {
+  const int g = gridDim.x, b = blockIdx.x;
+  const int full = p.ntiles / g, rem = p.ntiles - full * g;
+  if (i < full || !p.split_tail) return TcItem{i * g + b, 0, p.npass};
+  const int half = b / rem, hp = (p.npass + 1) / 2;
+  return TcItem{full * g + b % rem, half * hp, min(p.npass, (half + 1) * hp)};
+}
 
 // Weight images, one thread per (image, row, k); thread 0 also clears the
 // error word.  Image 3 l + 0: W_l
@@ -225,8 +250,11 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
     fence_after_sync();
     return true;
   };
-  int tile = blockIdx.x;
-  for (; tile < p.ntiles; tile += gridDim.x) {
+  const int nitems = items_of(p);
+  int it = 0;
+  for (; it < nitems; ++it) {
+    const TcItem item = item_at(p, it);
+    const int tile = item.tile;
     const int box = tile * kTB + row;
     const bool valid = box < p.B;
     const bool full = (tile + 1) * kTB <= p.B;  // every row of the tile is a box
@@ -316,7 +344,7 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
       }
     }
     // ---- CROWN back-substitution, spec rows in pairs
-    for (int pass = 0; ok && pass < p.npass; ++pass) {
+    for (int pass = item.pass_lo; ok && pass < item.pass_hi; ++pass) {
       const int nch = min(2, Q - 2 * pass);
       float racc[2] = {0.f, 0.f}, conc[2] = {0.f, 0.f};
       // step l relaxes the product of fc layer l with relu layer l - 1; the
@@ -444,8 +472,8 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
   if (ok) return true;
   // NaN for every box of this CTA from the unfinished tile on
   const float nan = __int_as_float(0x7fffffff);
-  for (; tile < p.ntiles; tile += gridDim.x) {
-    const int box = tile * kTB + row;
+  for (; it < nitems; ++it) {
+    const int box = item_at(p, it).tile * kTB + row;
     if (box >= p.B || gi != 0) continue;
     for (int q = 0; q < Q; ++q) {
       p.lb[(long long)box * Q + q] = nan;
@@ -534,9 +562,14 @@ __global__ void __launch_bounds__(kThreads, 1) crown_tc_kernel(const __grid_cons
       const unsigned nl = (unsigned)(nfc - 1);
       const unsigned fwdlen = fwd ? 2 * nl : 0;
       const unsigned T = fwdlen + (unsigned)p.npass * nl;
-      const unsigned ntl =
-          blockIdx.x < (unsigned)p.ntiles ? (p.ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-      const unsigned total = ntl * T;
+      // image count of this CTA's items (a split item has fewer passes; its
+      // images are the first ones of a whole tile's sequence)
+      const int nitems = items_of(p);
+      unsigned total = 0;
+      for (int i = 0; i < nitems; ++i) {
+        const TcItem item = item_at(p, i);
+        total += fwdlen + (unsigned)(item.pass_hi - item.pass_lo) * nl;
+      }
       unsigned issued = 0, used = 0, ua[2] = {0, 0};
       bool ok = true;
       auto image_of = [&](unsigned n) {
@@ -570,7 +603,8 @@ __global__ void __launch_bounds__(kThreads, 1) crown_tc_kernel(const __grid_cons
         return true;
       };
       ok = refill();
-      for (int tile = blockIdx.x; ok && tile < p.ntiles; tile += gridDim.x) {
+      for (int i = 0; ok && i < nitems; ++i) {
+        const TcItem item = item_at(p, i);
         if (fwd) {
           for (int l = 0; ok && l < nfc - 1; ++l) {
             int sw, sa;
@@ -585,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1) crown_tc_kernel(const __grid_cons
             ok = refill();
           }
         }
-        for (int pass = 0; ok && pass < p.npass; ++pass) {
+        for (int pass = item.pass_lo; ok && pass < item.pass_hi; ++pass) {
           for (int l = nfc - 2; ok && l >= 0; --l) {
             int st;
             if (!(ok = take(st))) break;
@@ -705,6 +739,10 @@ int crown_tc_launch(const vcb_mlp* net, int32_t B, const float* xl, const float*
   p.Q = Q;
   p.ntiles = (B + kTB - 1) / kTB;
   p.npass = (Q + 1) / 2;
+  {
+    const int rem = p.ntiles % plan.grid;
+    p.split_tail = (rem > 0 && 2 * rem <= plan.grid && p.npass >= 2) ? 1 : 0;
+  }
   p.xl = xl;
   p.xh = xh;
   p.clo = clamp_lo;
