@@ -67,7 +67,7 @@ def test_invalid_arguments_return_status_not_crash():
 def test_status_mapping():
     with pytest.raises(torch.cuda.OutOfMemoryError):
         _lib.check(_lib.VCB_ERR_OOM)
-    with pytest.raises(RuntimeError):
+    with pytest.raises(_lib.KernelError):
         _lib.check(_lib.VCB_ERR_CUDA)
     with pytest.raises(TimeoutError):
         _lib.check(_lib.VCB_ERR_TIMEOUT)
@@ -98,7 +98,7 @@ def test_lower_rejects_unsupported():
 def test_cpu_device_is_refused():
     from vibecheck_nn_b200 import ops
     gg = wk.mlp_gg(wk.mlp_params((4, 6, 3), np.random.default_rng(0)))
-    with pytest.raises(RuntimeError):
+    with pytest.raises(_lib.UnsupportedInput):
         ops._ibp_forward_graph_batched(torch.zeros(2, 4), torch.ones(2, 4), gg,
                                        'cpu', torch.float32)
 

@@ -43,6 +43,7 @@ SIGNATURES = {
     'vcb_mlp_crown_workspace': [ctypes.POINTER(VcbMlp), _I, _I],
     'vcb_mlp_crown_tc_min_batch': [_I],
     'vcb_mlp_crown_path': [ctypes.POINTER(VcbMlp), _I, _I],
+    'vcb_fault_check': [_P],
     'vcb_mlp_flirpa': [ctypes.POINTER(VcbMlp), _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P,
                        _P, _P, _P, _P],
     'vcb_mlp_crown_noalloc': [ctypes.POINTER(VcbMlp), _I, _P, _P, _P, _P, _P,
@@ -117,6 +118,22 @@ RESTYPES = {'vcb_last_error': ctypes.c_char_p,
 _lib = None
 
 
+class KernelError(RuntimeError):
+    """A kernel of this package failed: a CUDA launch or runtime error
+    (VCB_ERR_CUDA).  Nothing in this package catches it; the reference's own
+    callers report it like any RuntimeError (verify_graph.py:9949-9980 turns
+    it into an ``unknown`` verdict that carries the message)."""
+
+
+class UnsupportedInput(NotImplementedError):
+    """Inputs outside the B200 path: CPU or float64 tensors, or a graph the
+    kernels do not take.  A ``NotImplementedError``, the type the reference
+    raises for an op it cannot bound (verify_zono_bnb.py:4071, :5115), so the
+    reference's callers fall back exactly as they do for their own refusals;
+    the installed delegating bindings hand these calls, and only these, to
+    the reference's function."""
+
+
 def lib():
     """Load libvcb.so once; raises if it has not been built."""
     global _lib
@@ -148,12 +165,22 @@ def check(rc, what='vcb'):
     if rc == VCB_ERR_INVALID:
         raise ValueError(msg)
     if rc == VCB_ERR_UNSUPPORTED:
-        raise NotImplementedError(msg)
+        raise UnsupportedInput(msg)
     if rc == VCB_ERR_OOM:
         raise torch.cuda.OutOfMemoryError(msg)
     if rc == VCB_ERR_TIMEOUT:
         raise TimeoutError(msg)
-    raise RuntimeError(msg)
+    raise KernelError(msg)
+
+
+def fault_check(device=None):
+    """Synchronise ``device``'s current stream and raise ``TimeoutError`` if a
+    kernel of the library gave up a bounded wait since the last check (its
+    outputs for the unfinished boxes are NaN).  The drivers call it where
+    they synchronise anyway (each BaB iteration's counter read, the end of a
+    verdict); a caller of the raw operators calls it at its own sync points."""
+    stream = stream_of(device if device is not None else torch.device('cuda'))
+    check(lib().vcb_fault_check(stream), 'vcb_fault_check')
 
 
 def ptr(t):
@@ -178,6 +205,6 @@ def stream_of(device):
 
 def require_cuda(t, name='tensor'):
     if not (isinstance(t, torch.Tensor) and t.is_cuda):
-        raise RuntimeError(
+        raise UnsupportedInput(
             f'vibecheck_nn_b200: {name} must be a CUDA tensor (the B200 path '
             'has no CPU fallback)')

@@ -21,7 +21,7 @@ import torch
 from .interm import mlp_zono
 from .netdesc import mlp_desc
 from .ops import F32, _check_dtype, _dev, _f32, _unpack_layers, spec_matrix
-from . import wide
+from . import _lib, wide
 
 
 def _sb_dict(desc, B, lo, hi):
@@ -33,7 +33,7 @@ def _sb_dict(desc, B, lo, hi):
 def zonotope_sb(desc, xl, xh):
     try:
         lo, hi, _, _ = mlp_zono(desc, xl, xh)
-    except NotImplementedError:  # too wide for the shared-memory kernel
+    except _lib.UnsupportedInput:  # too wide for the shared-memory kernel
         from .zono_wide import wide_zono
         wn = desc.__dict__.get('_wide') or wide.WideNet(desc)
         desc.__dict__['_wide'] = wn
@@ -90,8 +90,10 @@ def alpha_boundary_refine(desc, xl, xh, lb, W_q, b_q, qd, D, eps, iters,
         # reference's with this path's fp32 arithmetic
         new = wide.alpha_loop(wn, xl_c, xh_c, sb, W_q, b_q, iters, 0.25, 0.98, 1e-6,
                               tc=False)
-    except (RuntimeError, torch.cuda.OutOfMemoryError):
-        return lb  # opportunistic tightener, as in the reference
+    except torch.cuda.OutOfMemoryError:
+        # an opportunistic tightener, as in the reference (verify_graph.py:
+        # 12970-12974); a kernel fault is not swallowed
+        return lb
     lb = lb.clone()
     lb[idx] = torch.maximum(lb[idx], new)
     return lb
@@ -125,7 +127,7 @@ class _SpecBackwardAlpha(torch.autograd.Function):
     def backward(ctx, grad, *unused):
         w = grad.flatten()
         if not bool((w == w[0]).all()):
-            raise NotImplementedError(
+            raise _lib.UnsupportedInput(
                 'vibecheck_nn_b200: alpha / beta gradients only for a uniform weighting '
                 'of the spec lower bounds (the loss -sum(lb) the reference uses)')
         scale = w[0]

@@ -282,7 +282,7 @@ class WideBoundEngine(BoundEngine):
     def __init__(self, spec, gg, settings, device):
         super().__init__(spec, gg, settings, device)
         if self.cfg.crown_intermediate:
-            raise NotImplementedError(
+            raise _lib.UnsupportedInput(
                 'vibecheck_nn_b200: CROWN intermediates for networks outside the '
                 'shared-memory kernels')
         from .wide import wide_net
@@ -310,7 +310,7 @@ def make_engine(spec, gg, settings, device):
         try:  # the zonotope kernel has its own limits
             xl0, xh0 = eng.root()
             mlp_zono(eng.desc, xl0.reshape(1, -1), xh0.reshape(1, -1))
-        except NotImplementedError:
+        except _lib.UnsupportedInput:
             fused = False
     return eng if fused else WideBoundEngine(spec, gg, settings, device)
 
@@ -328,6 +328,16 @@ class LocalState:
         self.oom = False
 
 
+def is_oom(e):
+    """Out of memory, as main.py:89-99 (``_is_oom_exception``) decides it: a
+    host MemoryError, torch's OutOfMemoryError (what VCB_ERR_OOM maps to), or
+    a RuntimeError whose message says so.  A KernelError is never an OOM."""
+    if isinstance(e, _lib.KernelError):
+        return False
+    return isinstance(e, (MemoryError, torch.cuda.OutOfMemoryError)) or (
+        isinstance(e, RuntimeError) and 'out of memory' in str(e).lower())
+
+
 def local_iteration(engine, st):
     """Pop a batch, bound and split it, push the children (LIFO: low block,
     then high block) -- one iteration of verify_graph.py:12840-13429.  On a
@@ -338,11 +348,13 @@ def local_iteration(engine, st):
     xl_b, xh_b = wl.pop(B)
     try:
         res = engine.process(xl_b, xh_b, st.n_iters)
-    except (torch.cuda.OutOfMemoryError, RuntimeError) as e:
+    except (MemoryError, RuntimeError) as e:
+        if not is_oom(e):
+            raise
         new_bs = max(1, st.batch_size // 2)
         wl.push(xl_b, xh_b)
         if new_bs == st.batch_size:
-            if isinstance(e, torch.cuda.OutOfMemoryError) and engine.cfg.raise_on_oom:
+            if engine.cfg.raise_on_oom:
                 raise
             st.oom = True
             return
@@ -390,6 +402,7 @@ def _input_split_batched(graph, spec, settings, gg, device, dtype):
                                'batched_n_leaves': st.n_leaves,
                                'batched_n_iters': st.n_iters,
                                'worklist_size': wl.size()}
+    _lib.fault_check(device)  # a bounded-wait expiry makes the verdict void
     if not wl and st.n_open == 0:
         return 'verified', {'phase': 'batched_verified',
                             'batched_n_leaves': st.n_leaves,

@@ -13,6 +13,7 @@ from __future__ import annotations
 import torch
 
 from .graph import graph_forward, graph_net, graph_vjp
+from . import _lib
 from .ops import F32
 
 
@@ -35,9 +36,9 @@ class _Forward(torch.autograd.Function):
 
 def _forward_batch_graph(x, gg, capture=None):
     if not isinstance(x, torch.Tensor) or x.device.type != 'cuda':
-        raise RuntimeError('vibecheck_nn_b200: _forward_batch_graph needs a CUDA tensor')
+        raise _lib.UnsupportedInput("vibecheck_nn_b200: _forward_batch_graph needs a CUDA tensor")
     if x.dtype != F32:
-        raise NotImplementedError('vibecheck_nn_b200: _forward_batch_graph runs in float32')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200: _forward_batch_graph runs in float32')
     G = graph_net(gg, x.device)
     N = x.shape[0]
     x2 = x.reshape(N, -1).contiguous()
@@ -46,7 +47,7 @@ def _forward_batch_graph(x, gg, capture=None):
             return _Forward.apply(x2, G)
         return graph_forward(G, x2)
     if x.requires_grad and torch.is_grad_enabled():
-        raise NotImplementedError('vibecheck_nn_b200: capture with gradients')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200: capture with gradients')
     idx = G.layer_of(capture)
     if idx < 0:
         return x2

@@ -42,7 +42,7 @@ class GraphNet:
         for op in gg['ops']:
             t = op['type']
             if op['inputs'][0] != cur:
-                raise NotImplementedError(f'vibecheck_nn_b200: non-chain graph at {op["name"]!r}')
+                raise _lib.UnsupportedInput(f'vibecheck_nn_b200: non-chain graph at {op["name"]!r}')
             if t in ('add', 'sub') and not op.get('is_merge') and op.get('bias') is not None \
                     and self.layers and self.layers[-1]['type'] in ('fc', 'conv'):
                 self._fold_bias(op, t, device)
@@ -68,9 +68,9 @@ class GraphNet:
                 sh, sw = (int(v) for v in op['stride'])
                 ph, pw = (int(v) for v in op['padding'])
                 if K.shape[1] != C or K.shape[0] != Co:
-                    raise NotImplementedError('vibecheck_nn_b200: grouped conv')
+                    raise _lib.UnsupportedInput('vibecheck_nn_b200: grouped conv')
                 if (C * H * Wd) % 4 or (Co * Ho * Wo) % 4:
-                    raise NotImplementedError('vibecheck_nn_b200: conv sizes must be multiples of 4')
+                    raise _lib.UnsupportedInput('vibecheck_nn_b200: conv sizes must be multiples of 4')
                 geom = np.array([C, H, Wd, Co, Ho, Wo, kh, kw, sh, sw, ph, pw], np.int32)
                 self.layers.append({'type': 'conv', 'K': K, 'Kabs': K.abs().contiguous(),
                                     'b': b.contiguous(), 'geom': geom, 'nin': C * H * Wd,
@@ -84,7 +84,7 @@ class GraphNet:
                 cur = op['name']
                 continue
             else:
-                raise NotImplementedError(f'vibecheck_nn_b200: unsupported op {t!r}')
+                raise _lib.UnsupportedInput(f'vibecheck_nn_b200: unsupported op {t!r}')
             self.names[len(self.layers) - 1] = [op['name']]
             cur = op['name']
         self.n_out = n
@@ -107,7 +107,7 @@ class GraphNet:
         elif layer['type'] == 'conv' and shape == (layer['Co'], 1, 1):
             vec = raw.reshape(-1)
         else:
-            raise NotImplementedError('vibecheck_nn_b200: broadcast bias')
+            raise _lib.UnsupportedInput('vibecheck_nn_b200: broadcast bias')
         bias = torch.as_tensor(vec, dtype=F32, device=device)
         layer['b'] = (layer['b'] + bias if t == 'add' else layer['b'] - bias).contiguous()
         if layer['type'] == 'fc':
@@ -119,7 +119,7 @@ class GraphNet:
     def layer_of(self, name):
         """Index of the layer whose output is op ``name`` (-1: the input)."""
         if name in self.stale:
-            raise NotImplementedError(
+            raise _lib.UnsupportedInput(
                 f'vibecheck_nn_b200: {name!r} has a bias folded into it; capture the add')
         for idx, names in self.names.items():
             if name in names:
@@ -319,7 +319,7 @@ def graph_vjp(G, pre, g):
     L_ = _lib.lib()
     layers = G.layers
     if layers[-1]['type'] == 'relu':
-        raise NotImplementedError('vibecheck_nn_b200: network output after a relu')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200: network output after a relu')
     cur = g.contiguous()
     for idx in range(len(layers) - 1, -1, -1):
         layer = layers[idx]

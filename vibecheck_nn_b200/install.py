@@ -14,6 +14,8 @@ from __future__ import annotations
 
 import importlib
 
+from . import _lib
+
 BINDINGS = {
     'vibecheck.verify_zono_bnb': {
         '_ibp_forward_graph_batched': ('ops', '_ibp_forward_graph_batched'),
@@ -59,14 +61,18 @@ def _delegating(impl, original):
     """``impl`` for the inputs it supports; the reference's own function for
     the rest.  Used for the concrete forward, which the reference also calls
     off the hot path (CPU / float64 tensors, merge graphs, ND fc ops) where no
-    caller catches NotImplementedError."""
+    caller catches NotImplementedError, and for the multi-subbox and
+    ReLU-split drivers on CPU or float64 calls.  Only ``UnsupportedInput``
+    (inputs outside the B200 path, raised before any kernel runs) hands the
+    call over; a kernel failure (``KernelError``), a time-out or an
+    out-of-memory error propagates to the caller unchanged."""
     if original is None:
         return impl
 
     def fn(*args, **kwargs):
         try:
             return impl(*args, **kwargs)
-        except (NotImplementedError, RuntimeError):
+        except _lib.UnsupportedInput:
             return original(*args, **kwargs)
     fn.__wrapped__ = impl
     fn.__name__ = getattr(impl, '__name__', 'fn')

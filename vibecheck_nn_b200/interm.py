@@ -88,7 +88,7 @@ def _forward_zonotope_graph_batched(xl, xh, gg, device, dtype):
     B = xl.shape[0]
     try:
         sb_lo, sb_hi, _, (c, G, K) = mlp_zono(desc, xl, xh, full=True)
-    except NotImplementedError:  # too wide for the shared-memory kernel
+    except _lib.UnsupportedInput:  # too wide for the shared-memory kernel
         from .wide import wide_net
         from .zono_wide import wide_zono
         sb, (c, G) = wide_zono(wide_net(gg, device), xl, xh, want_output=True)
@@ -154,22 +154,22 @@ def spec_backward_seeded(tight, xl, xh, gg, seed_ew_at, seed_acc, device, alpha_
     relaxation with those slopes."""
     device = _dev(device)
     if len(seed_ew_at) != 1:
-        raise NotImplementedError('vibecheck_nn_b200: one seed op supported')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200: one seed op supported')
     (name, seed), = seed_ew_at.items()
     names = [op['name'] for op in gg['ops'] if op['type'] == 'fc']
     if name not in names:
-        raise NotImplementedError(f'vibecheck_nn_b200: seed at non-fc op {name!r}')
+        raise _lib.UnsupportedInput(f'vibecheck_nn_b200: seed at non-fc op {name!r}')
     L = names.index(name)
     seed = torch.as_tensor(seed, device=device)
     B = xl.shape[0]
     s0 = seed[0]
     if B > 1 and not (seed.stride(0) == 0 or bool((seed == s0).all())):
-        raise NotImplementedError('vibecheck_nn_b200: per-box seeds')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200: per-box seeds')
     acc0 = torch.zeros(s0.shape[0], dtype=F32, device=device) if seed_acc is None \
         else torch.as_tensor(seed_acc, device=device)[0].to(F32)
     if seed_acc is not None and B > 1 and not bool(
             (torch.as_tensor(seed_acc, device=device) == acc0).all()):
-        raise NotImplementedError('vibecheck_nn_b200: per-box seed_acc')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200: per-box seed_acc')
     desc = mlp_desc(gg, device)
     sub = truncated(desc, L + 1)
     xl = _f32(xl, device)

@@ -144,7 +144,7 @@ def _multi_sub_input_split_bab(sub_idx_list, groups, order, gg, device, dtype, t
     live = {int(ki): 1 for ki in sub_idx_list}
     try:
         desc = mlp_desc(gg, device)
-    except NotImplementedError:
+    except _lib.UnsupportedInput:
         desc = None
     n_iters = 0
     n_visited = 0
@@ -167,7 +167,9 @@ def _multi_sub_input_split_bab(sub_idx_list, groups, order, gg, device, dtype, t
         if desc is not None:
             try:
                 lirpa = forward_linear_spec(desc, xl_b, xh_b, var_idx, W_q)
-            except (NotImplementedError, RuntimeError):
+            except (_lib.UnsupportedInput, torch.cuda.OutOfMemoryError):
+                # the reference falls back on these (verify_graph.py:11458); a
+                # KernelError is a fault and propagates
                 lirpa = None
         clip_lA = clip_lbias = margins = None
         if lirpa is not None:

@@ -71,28 +71,28 @@ def lower_mlp(gg):
     for op in ops:
         t = op['type']
         if op['inputs'][0] != cur:
-            raise NotImplementedError(
+            raise _lib.UnsupportedInput(
                 f'vibecheck_nn_b200: op {op["name"]!r} does not consume the '
                 f'previous op (non-chain graph)')
         if t == 'fc':
             if not expect_fc:
-                raise NotImplementedError('vibecheck_nn_b200: fc after fc')
+                raise _lib.UnsupportedInput('vibecheck_nn_b200: fc after fc')
             W = _as_np(op['W'])
             b = _as_np(op['bias']) if op.get('bias') is not None else np.zeros(W.shape[0])
             if W.ndim != 2 or (layers and W.shape[1] != layers[-1][0].shape[0]):
-                raise NotImplementedError(
+                raise _lib.UnsupportedInput(
                     f'vibecheck_nn_b200: fc {op["name"]!r} shape {W.shape}')
             in_nd = op.get('in_shapes_nd', [None])[0]
             if in_nd is not None and len(in_nd) >= 2 and W.shape[1] == in_nd[-1] \
                     and int(np.prod(in_nd)) != W.shape[1]:
-                raise NotImplementedError('vibecheck_nn_b200: ND-batched fc')
+                raise _lib.UnsupportedInput('vibecheck_nn_b200: ND-batched fc')
             layers.append([W, b.reshape(-1)])
             expect_fc = False
         elif t == 'relu':
             if expect_fc:
-                raise NotImplementedError('vibecheck_nn_b200: relu not after fc')
+                raise _lib.UnsupportedInput('vibecheck_nn_b200: relu not after fc')
             if op.get('layer_idx', relu_seen) != relu_seen:
-                raise NotImplementedError('vibecheck_nn_b200: relu layer_idx order')
+                raise _lib.UnsupportedInput('vibecheck_nn_b200: relu layer_idx order')
             relu_seen += 1
             expect_fc = True
         elif t == 'reshape':
@@ -101,16 +101,16 @@ def lower_mlp(gg):
                 and op.get('bias') is not None:
             bias = _as_np(op['bias']).reshape(-1)
             if bias.size != layers[-1][1].size:
-                raise NotImplementedError('vibecheck_nn_b200: broadcast bias')
+                raise _lib.UnsupportedInput('vibecheck_nn_b200: broadcast bias')
             layers[-1][1] = layers[-1][1] + (bias if t == 'add' else -bias)
         else:
-            raise NotImplementedError(
+            raise _lib.UnsupportedInput(
                 f'vibecheck_nn_b200: unsupported op {t!r} at {op["name"]!r}')
         cur = op['name']
     if expect_fc or not layers:
-        raise NotImplementedError('vibecheck_nn_b200: graph must end in an fc')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200: graph must end in an fc')
     if len(layers) > _lib.MAX_FC:
-        raise NotImplementedError(f'vibecheck_nn_b200: more than {_lib.MAX_FC} fc layers')
+        raise _lib.UnsupportedInput(f'vibecheck_nn_b200: more than {_lib.MAX_FC} fc layers')
     return layers
 
 

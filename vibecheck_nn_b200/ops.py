@@ -22,8 +22,8 @@ F32 = torch.float32
 def _dev(device):
     device = torch.device(device) if device is not None else torch.device('cuda')
     if device.type != 'cuda':
-        raise RuntimeError('vibecheck_nn_b200 runs on CUDA devices only '
-                           f'(got device={device}); there is no CPU fallback')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200 runs on CUDA devices only '
+                                    f'(got device={device}); there is no CPU fallback')
     return device
 
 
@@ -36,7 +36,7 @@ def _f32(t, device):
 
 def _check_dtype(dtype):
     if dtype not in (None, torch.float32):
-        raise NotImplementedError(
+        raise _lib.UnsupportedInput(
             f'vibecheck_nn_b200 computes in float32 (bits=32); got {dtype}')
 
 
@@ -167,7 +167,7 @@ def _mlp_or_graph(gg, device):
     with convolutions; NotImplementedError for anything else."""
     try:
         return mlp_desc(gg, device), None
-    except NotImplementedError:
+    except _lib.UnsupportedInput:
         from .graph import graph_net
         return None, graph_net(gg, device)
 
@@ -240,7 +240,7 @@ def _spec_backward_graph_batched(tight, xl, xh, gg, spec_ew, device, dtype,
         return spec_backward_seeded(tight, xl, xh, gg, seed_ew_at, seed_acc,
                                     device, alpha_at_layer=alpha_at_layer)
     if alpha_mccormick or alpha_recip:
-        raise NotImplementedError('vibecheck_nn_b200: bilinear alpha terms')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200: bilinear alpha terms')
     xl = _f32(xl, device)
     xh = _f32(xh, device)
     desc, G = _mlp_or_graph(gg, device)
@@ -248,7 +248,7 @@ def _spec_backward_graph_batched(tight, xl, xh, gg, spec_ew, device, dtype,
         from .graph import graph_crown
         if alpha_at_layer is not None and any(bool(a.requires_grad) for a in alpha_at_layer.values()) \
                 and torch.is_grad_enabled():
-            raise NotImplementedError('vibecheck_nn_b200: alpha gradients on conv graphs')
+            raise _lib.UnsupportedInput('vibecheck_nn_b200: alpha gradients on conv graphs')
         W_q, b_q = spec_matrix(spec_ew, device)
         sb = {L: (_f32(v[0], device), _f32(v[1], device)) for L, v in tight.items()}
         out = graph_crown(G, xl, xh, sb, W_q, b_q,
@@ -269,7 +269,7 @@ def _spec_backward_graph_batched(tight, xl, xh, gg, spec_ew, device, dtype,
     if alpha_at_layer is not None:
         for a in alpha_at_layer.values():
             if a.dim() not in (2, 3):
-                raise NotImplementedError('vibecheck_nn_b200: alpha must be (B, n) or (B, Q, n)')
+                raise _lib.UnsupportedInput('vibecheck_nn_b200: alpha must be (B, n) or (B, Q, n)')
             per_query |= a.dim() == 3
             needs_grad |= bool(a.requires_grad)
     if relu_split_beta is not None:

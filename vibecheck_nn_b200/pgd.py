@@ -146,7 +146,7 @@ def _simple_run(gg, x, lo, hi, R, C, cb, cdis, D, n_iter, lr):
         desc = mlp_desc(gg, dev)
         key, _ = pgd_run(desc, x, lo, hi, R, C, cb, cdis, D, n_iter, lr)
         return None if key == NO_SAT else key & 0xFFFFFFFF
-    except NotImplementedError:
+    except _lib.UnsupportedInput:
         pass
     return simple_layerwise(_graph(gg, dev), x, lo, hi, R, C, cb, cdis, D, n_iter, lr)
 
@@ -272,7 +272,7 @@ def pgd_attack_general(xl, xh, spec, gg, settings, restrict_disj=None,
     dev = xl.device
     dt = xl.dtype
     if dt != F32:
-        raise NotImplementedError('vibecheck_nn_b200: pgd_attack_general runs in float32')
+        raise _lib.UnsupportedInput('vibecheck_nn_b200: pgd_attack_general runs in float32')
     if isinstance(seed, (int, float)):
         torch.manual_seed(int(seed))
     n_restarts = int(_num(settings, 'pgd_restarts', 10))
@@ -313,7 +313,7 @@ def pgd_attack_general(xl, xh, spec, gg, settings, restrict_disj=None,
     try:
         net = mlp_desc(gg, dev)
         n_out, n_in = net.n_out, net.dims[0]
-    except NotImplementedError:
+    except _lib.UnsupportedInput:
         net = _graph(gg, dev)
         n_out, n_in = net.n_out, x[0].numel()
     w_d = None
@@ -348,7 +348,7 @@ def pgd_attack_general(xl, xh, spec, gg, settings, restrict_disj=None,
                         return result(i)
                 return finish
             idx = fin()
-        except NotImplementedError:  # wider than the shared-memory kernel
+        except _lib.UnsupportedInput:  # wider than the shared-memory kernel
             net = _graph(gg, dev)
     if idx == -1:
         deadline = None if time_budget is None else t_start + time_budget
@@ -528,7 +528,7 @@ def root_pgd(spec, gg, n_output, device, settings):
         with torch.cuda.stream(side):
             r = pgd_attack_general(xl, xh, spec, gg, settings, time_budget=budget, defer=True)
         general = r if callable(r) else (lambda: r)
-    except (RuntimeError, torch.cuda.OutOfMemoryError):
+    except _BEST_EFFORT:
         pass
     # the simple stage reseeds torch's generators; when the general stage
     # wins, the sequential order would not have run it, so its states return
@@ -537,13 +537,13 @@ def root_pgd(spec, gg, n_output, device, settings):
     try:
         simple = _simple_pgd(xl.flatten().unsqueeze(0), xh.flatten().unsqueeze(0), spec,
                              gg, n_output, device, torch.float32, n_restarts=10000, n_iter=50)
-    except (RuntimeError, torch.cuda.OutOfMemoryError):
+    except _BEST_EFFORT:
         pass
     gen = (False, None)
     if general is not None:
         try:
             gen = general()
-        except (RuntimeError, torch.cuda.OutOfMemoryError):
+        except _BEST_EFFORT:
             pass
     main.wait_stream(side)
     if gen[0] and gen[1] is not None:
@@ -553,6 +553,12 @@ def root_pgd(spec, gg, n_output, device, settings):
     if simple[0]:
         return True, simple[1], 'batched_simple_pgd'
     return False, None, None
+
+
+# The root PGD stages are best-effort SAT finders (verify_graph.py:12566-12605
+# skips a stage that fails for lack of memory or support); a KernelError is a
+# fault and propagates.
+_BEST_EFFORT = (_lib.UnsupportedInput, torch.cuda.OutOfMemoryError)
 
 
 def leaf_pgd(xl_b, xh_b, lb, qd, D, spec, gg, n_output, device, settings):

@@ -32,6 +32,7 @@ import heapq
 import numpy as np
 import torch
 
+from . import _lib
 from .netdesc import mlp_desc
 from .ops import _check_dtype, _dev, _ibp_forward_graph_batched, _spec_backward_graph_batched
 
@@ -173,7 +174,7 @@ def _ibp_crown_bab(gg, xl, xh, sb_root, w_q, b_q, device, dtype, *, time_left, e
             if no_reforward and ew_w is not None:
                 try:
                     ew_dom = _domain_relu_coeffs(gg, sb, w_t, device, dtype)
-                except NotImplementedError:
+                except _lib.UnsupportedInput:
                     ew_dom = None
             for bi in range(B):
                 if float(best_h[bi]) > 0:
