@@ -51,6 +51,14 @@ int vcb_version(void);
 /* Message for the last non-zero status returned on this thread. */
 const char* vcb_last_error(void);
 
+/* Deferred device-fault report (no counterpart in the reference, whose
+ * PyTorch ops have no bounded device-side waits).  Synchronises `stream`,
+ * then returns VCB_ERR_TIMEOUT if the tensor-core CROWN kernel gave up one of
+ * its bounded waits on this device since the last call (the boxes it had not
+ * finished got NaN bounds), and clears the report; VCB_OK otherwise.
+ * Callers check it where they synchronise anyway. */
+int vcb_fault_check(void* stream);
+
 /* Fused IBP forward + CROWN back-substitution for ReLU MLPs whose weights fit
  * in shared memory (the ACAS-Xu-sized path).
  *

@@ -38,6 +38,18 @@ def max_excess(a, b, rtol=1e-5, atol=1e-6):
     return float(np.max(np.abs(a - b) - (atol + rtol * np.abs(b)), initial=-1))
 
 
+def close_linear_form(A, A_ref, rtol=1e-5, atol=1e-6):
+    """Input-space linear forms (the A output, one row per box and spec row):
+    each coefficient within atol + rtol * the largest |coefficient| of its
+    reference row.  The coefficients of a row are the sums whose signs
+    cancel in the concretisation, so their rounding is relative to the row's
+    scale; the bounds themselves are held to ``close``."""
+    A = np.asarray(A, np.float64)
+    A_ref = np.asarray(A_ref, np.float64)
+    scale = np.abs(A_ref).max(axis=-1, keepdims=True)
+    return bool((np.abs(A - A_ref) <= atol + rtol * scale).all())
+
+
 def fp32_equivalent(ours, ref32, ref64, rtol=1e-5, atol=1e-6, slack=2.0):
     """fp32-equivalence against exact (float64) arithmetic: every element of
     ``ours`` within the parity tolerance of the float64 result plus ``slack``

@@ -65,7 +65,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--ref-src', required=True)
     ap.add_argument('--only', default=None,
-                    choices=['pgd_general', 'forward', 'relu_bab', 'hybrid', 'multisub'],
+                    choices=['pgd_general', 'forward', 'relu_bab', 'hybrid', 'multisub',
+                             'cfg2'],
                     help='regenerate one fixture only')
     args = ap.parse_args()
     vz, vg, vh, vs, vspec = _import_reference(args.ref_src)
@@ -85,6 +86,9 @@ def main():
         return
     if args.only == 'multisub':
         _golden_multisub(wk)
+        return
+    if args.only == 'cfg2':
+        _golden_cfg2(vz, wk)
         return
 
     # ------------------------------------------------------------------ slopes
@@ -595,6 +599,48 @@ def multisub_problem(seed, n_sub, margins, half=(0.1, 0.3)):
         t1 = float(y[:, 1].min() - m)
         subs.append((lo, hi, [[('ge', 0, t0), ('le', 1, t1)]]))
     return layers, subs
+
+
+# cfg2 benchmark workloads whose tensor-core IBP bounds put a ReLU at the
+# min-area tie, and one box of each that sits there
+CFG2_SEEDS = (0, 1, 3)
+CFG2_TIE_BOXES = (53604, 60678, 53706)
+CFG2_LB_BOXES = 4096
+
+
+def ibp_digest(arrays):
+    """SHA-256 of a list of float32 arrays' bytes (bit-exact equality of
+    65,536-box IBP bounds without committing them)."""
+    import hashlib
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a, np.float32).tobytes())
+    return h.hexdigest()
+
+
+def _golden_cfg2(vz, wk):
+    """The reference's own float32 IBP forward + CROWN back-substitution
+    (_ibp_forward_graph_batched, verify_zono_bnb.py:1066, then
+    _spec_backward_graph_batched, :4270) on the full 65,536-box cfg2
+    workload, on CPU: a digest of every layer's IBP bounds and the lower
+    bounds of the first CFG2_LB_BOXES boxes plus the tie box."""
+    import torch
+    out = {}
+    for seed, tie in zip(CFG2_SEEDS, CFG2_TIE_BOXES):
+        w = wk.cfg2(seed=seed)
+        gg = wk.mlp_gg(w['layers'])
+        xl, xh = _t(w['xl'], torch.float32), _t(w['xh'], torch.float32)
+        spec_ew = wk.spec_ew_from(w['spec_W'], w['spec_b'], 'cpu')
+        sb = vz._ibp_forward_graph_batched(xl, xh, gg, 'cpu', torch.float32)
+        lb = _n(vz._spec_backward_graph_batched(sb, xl, xh, gg, spec_ew, 'cpu',
+                                                torch.float32))
+        keys = sorted(sb)
+        out[f's{seed}_ibp_digest'] = np.array(
+            ibp_digest([_n(sb[L][k]) for L in keys for k in (0, 1)]))
+        idx = np.concatenate([np.arange(CFG2_LB_BOXES), [tie]])
+        out[f's{seed}_idx'] = idx
+        out[f's{seed}_lb'] = lb[idx]
+    _save('cfg2_ref', **out)
 
 
 def _golden_multisub(wk):

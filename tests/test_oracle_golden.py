@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import (close, forward_fixture, golden_layers, load_golden, max_excess,
+from conftest import (close, forward_fixture, golden_layers, golden_script, load_golden, max_excess,
                       oracle_pgd_general, pgd_general_case)
 from oracle import bab as obab
 from oracle import bounds as ob
@@ -262,3 +262,27 @@ def test_forward_batch_graph():
         outm, actm = ob.forward_batch_graph(g['mlp_x'], ggm, dt, keep=True)
         assert close(outm, g['mlp_out'], **tol)
         assert close(ob.forward_vjp(ggm, actm, g['mlp_gw'], dt), g['mlp_grad'], **tol)
+
+
+def test_oracle_fp32_is_the_reference_fp32_on_cfg2():
+    """On the 65,536-box cfg2 benchmark workload the oracle's float32 IBP
+    bounds are bit-equal to the reference's (digest of every layer), so the
+    GPU tests may use the oracle as the reference's float32 bounds at full
+    size; its lower bounds are within the parity tolerance of the
+    reference's on the recorded boxes, the tie boxes included."""
+    from oracle import bounds as ob
+    from vibecheck_nn_b200 import workloads as wk
+    mg = golden_script()
+    g = load_golden('cfg2_ref')
+    for seed in mg.CFG2_SEEDS:
+        w = wk.cfg2(seed=seed)
+        ggc = wk.mlp_gg(w['layers'])
+        sb = ob.ibp_forward_batched(w['xl'], w['xh'], ggc)
+        keys = sorted(sb)
+        assert mg.ibp_digest([sb[L][k] for L in keys for k in (0, 1)]) == \
+            str(g[f's{seed}_ibp_digest']), seed
+        idx = g[f's{seed}_idx']
+        lb = ob.spec_backward_batched({L: (lo[idx], hi[idx]) for L, (lo, hi) in sb.items()},
+                                      w['xl'][idx], w['xh'][idx], ggc, w['spec_W'],
+                                      w['spec_b'])
+        assert close(lb, g[f's{seed}_lb']), (seed, max_excess(lb, g[f's{seed}_lb']))

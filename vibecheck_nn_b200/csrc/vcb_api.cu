@@ -4,6 +4,7 @@
 #include <unordered_map>
 
 #include "vcb_common.cuh"
+#include "vcb_crown_tc.cuh"
 
 namespace vcb {
 
@@ -67,7 +68,18 @@ int ensure_smem(const void* kernel, int bytes) {
 
 }  // namespace vcb
 
-extern "C" int vcb_version(void) { return 100; }
+extern "C" int vcb_version(void) { return 101; }
+
+extern "C" int vcb_fault_check(void* stream) {
+  int set = 0;
+  const int rc = vcb::crown_tc_fault_take(static_cast<cudaStream_t>(stream), &set);
+  if (rc) return rc;
+  if (set)
+    return vcb::fail(VCB_ERR_TIMEOUT,
+                     "crown_tc_kernel: a bounded device-side wait expired; the bounds of the "
+                     "boxes it had not finished are NaN");
+  return VCB_OK;
+}
 
 extern "C" const char* vcb_last_error(void) {
   return vcb::g_last_error.c_str();

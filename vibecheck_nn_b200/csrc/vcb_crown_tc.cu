@@ -57,6 +57,10 @@ namespace {
 
 using namespace tc5;
 
+// Set by crown_tc_kernel when a bounded wait expired (its unfinished boxes
+// got NaN bounds); read and cleared by vcb_fault_check.
+__device__ int g_tc_fault;
+
 constexpr int kTB = 128;                   // boxes per tile (MMA rows)
 constexpr int kEpi = 12;                   // epilogue warps
 constexpr int kCtlWarp = kEpi;             // weight loads + MMA issue
@@ -71,6 +75,22 @@ constexpr int kMaxQ = 16;
 constexpr unsigned kSpin = 1u << 24;
 constexpr unsigned kSpinSleep = 1u << 20;  // polls of at most ~1 us each
 constexpr int kSmem = 1024 + kStages * kImg + (kMaxQ * kW + VCB_MAX_FC * kW + 2 * 2 * 4 * kTB) * 4;
+// Half-width of the band around the min-area threshold (lower slope 1 iff
+// up_s > 0.5, verify_zono_bnb.py:516) inside which a box's bounds are
+// recomputed by crown_tie_kernel.  The tensor cores' IBP bounds differ from
+// the fp32 reference's sequential dot products by rounding; on the cfg2
+// workload their upper slopes differ by at most 1.7e-6 near 0.5, so a slope
+// further than this from 0.5 takes the reference's decision.
+constexpr float kTieBand = 8e-6f;
+
+// Row pitch of crown_tie_kernel's network image (floats): covers the bias
+// column and a whole number of 16-float blocks, a multiple of 4 with an odd
+// number of 16-byte words; rows are padded to a multiple of 8.
+__host__ __device__ inline int tie_pitch(int nin) {
+  const int need = max(nin + 1, (nin + 15) & ~15);
+  return 4 * ((need + 3) / 4 | 1);
+}
+__host__ __device__ inline int tie_rows(int nout) { return (nout + 7) & ~7; }
 
 // Batches of the input-split BaB (<= 4096 boxes) stay on the SIMT kernel, whose
 // rounding the leaf-count parity of the BaB tests is pinned to.
@@ -93,6 +113,16 @@ struct TcParams {
   float *lb, *A, *accout, *sbolo, *sbohi;
   float2* slopes;
   int* err;
+  // near-tie re-bound (crown_tie_kernel): on when the kernel computes the IBP
+  // bounds itself with the min-area lower slope (no caller bounds, no alpha)
+  int tie_on;
+  int* tie_flag;          // (B) the box is listed
+  int* tie_list;          // boxes with an unstable neuron inside the band, each once
+  int* tie_count;
+  float* tnet;            // the row images of crown_tie_kernel (see there)
+  int tsoff[VCB_MAX_FC];  // fc layer l: tie_rows(dims[l+1]) rows of pitch tpitch[l]
+  int tpitch[VCB_MAX_FC];
+  int tnet_floats;
 };
 
 __host__ __device__ inline int pad16(int n) { return (n + 15) & ~15; }
@@ -127,10 +157,31 @@ __device__ __forceinline__ TcItem item_at(const TcParams& p, int i) {
 // then the bias row, K = outputs).  Each is split into tf32 hi (first 16 KB)
 // and lo, laid out as two 64-row x 32-column blocks with the 128-byte swizzle
 // of a K-major tcgen05 operand.
+// When the near-tie re-bound is on, the same launch clears the tie flags and
+// writes the plain fp32 rows of the network that crown_tie_kernel reads.
 __global__ void crown_tc_images(const TcParams p) {
   const int nimg = 3 * (p.n_fc - 1);
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx == 0) *p.err = 0;  // the error word of the launch that follows
+  if (idx == 0) {  // the error word and tie count of the launch that follows
+    *p.err = 0;
+    *p.tie_count = 0;
+  }
+  if (p.tie_on) {
+    if (idx < p.B) p.tie_flag[idx] = 0;
+    if (idx < p.tnet_floats) {
+      // rows [W_l[o, :], b_l[o], 0 ..], zero rows from dims[l+1] to tie_rows
+      int l = 0;
+      while (l + 1 < p.n_fc && idx >= p.tsoff[l + 1]) ++l;
+      const int nin = p.dims[l], nout = p.dims[l + 1], pitch = p.tpitch[l];
+      const int o = (idx - p.tsoff[l]) / pitch, c = (idx - p.tsoff[l]) % pitch;
+      float v = 0.f;
+      if (o < nout) {
+        if (c < nin) v = p.W[p.w_goff[l] + (long long)o * nin + c];
+        else if (c == nin) v = p.b[p.b_goff[l] + o];
+      }
+      p.tnet[idx] = v;
+    }
+  }
   if (idx >= nimg * kW * kW) return;
   const int im = idx / (kW * kW), n = (idx / kW) % kW, k = idx % kW;
   const int l = im / 3, use = im % 3;
@@ -258,6 +309,7 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
     const int box = tile * kTB + row;
     const bool valid = box < p.B;
     const bool full = (tile + 1) * kTB <= p.B;  // every row of the tile is a box
+    bool tie = false;
     if (fwd) {
       // ---- layer-0 operands: centre and radius of the box
       for (int k = 0; k < nck; ++k) {
@@ -308,7 +360,13 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
               p.sbolo[gi0 + o] = lo;
               p.sbohi[gi0 + o] = hi;
             }
-            if (o < nout) sl[o * kTB] = encode_slope(lo, hi);
+            if (o < nout) {
+              const float2 e = encode_slope(lo, hi);
+              sl[o * kTB] = e;
+              // unstable (neither sign bit set) with the upper slope inside
+              // the band where rounding can move it across 0.5
+              tie |= !signbit(e.x) && !signbit(e.y) && fabsf(__fsub_rn(e.x, 0.5f)) <= kTieBand;
+            }
             const float lc = fmaxf(lo, 0.f), hc = fmaxf(hi, 0.f);
             mc[j] = o < nout ? __fmul_rn(__fadd_rn(lc, hc), 0.5f) : 0.f;
             rc[j] = o < nout ? __fmul_rn(__fsub_rn(hc, lc), 0.5f) : 0.f;
@@ -329,6 +387,10 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
         if (!last) publish(&a_ready[0]);
       }
       if (!ok) break;
+      // list the box for crown_tie_kernel once (the column warps of a row and
+      // the two CTAs of a split tile may all flag it)
+      if (tie && valid && p.tie_on && atomicExch(p.tie_flag + box, 1) == 0)
+        p.tie_list[atomicAdd(p.tie_count, 1)] = box;
     } else {
       // ---- caller-supplied intermediate bounds: slopes only
       for (int L = 0; L < nfc - 1; ++L) {
@@ -653,7 +715,321 @@ __global__ void __launch_bounds__(kThreads, 1) crown_tc_kernel(const __grid_cons
   __syncthreads();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
-  if (threadIdx.x == 0 && failed) atomicExch(p.err, 1);
+  if (threadIdx.x == 0 && failed) {
+    atomicExch(p.err, 1);
+    atomicExch(&g_tc_fault, 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Near-tie re-bound.  The min-area rule makes the lower slope jump from 0 to
+// 1 at up_s = 0.5, so where a box has an unstable neuron with up_s inside
+// kTieBand of 0.5 the tensor cores' rounding could pick the other slope than
+// the reference and give a different (equally valid) bound.  crown_tc_kernel
+// lists those boxes; here each is bounded again with the fp32 SIMT kernel's
+// operation order, so that its lb, A and acc equal crown_mlp_kernel's bit
+// for bit and its slope decisions are the reference's (the SIMT kernel's
+// fp32 IBP bounds are bit-identical to the reference's on these networks).
+// Outside the band the two upper slopes cannot straddle 0.5: on the cfg2
+// workload they differ by at most 1.7e-6 near 0.5.  The IBP bounds written
+// by crown_tc_kernel (sb_out) stay.
+//
+// 64 threads per box, kTieBoxes boxes per CTA.  In the IBP forward thread o
+// owns output o: its sequential chains of fused multiply-adds over the layer
+// inputs for the centre and the radius.  In the back-substitution thread c
+// owns coefficient column c of every spec row (chains over the layer
+// outputs, all rows side by side on one weight load); 8-column intercept
+// groups and per-row sums follow in crown_mlp_kernel's order.  Operands are
+// loaded in blocks ahead of their chains.
+//
+// The network is read from one row image written by crown_tc_images and
+// staged into shared memory by a bulk copy: fc layer l as pad4(dims[l+1])
+// rows [W_l[o, :], b_l[o], 0 ..] (zero rows beyond dims[l+1]) of pitch
+// tpitch[l], a multiple of 4 with an odd number of 16-byte words, so the
+// forward's per-thread 16-byte reads along a row and the back-substitution's
+// reads of one row across threads are both conflict-free.  Zero padding adds
+// exact zeros, as in crown_mlp_kernel.
+constexpr int kTieBoxes = 8;  // boxes per CTA, 64 threads each
+
+struct TieLayout {
+  int net_in_smem;  // the network image is staged in shared memory
+  int boxes;        // boxes per CTA
+  int bar_off;      // mbarrier (8 bytes) at this float offset
+  int v_off;        // Q x kW spec-times-last-layer table
+  int box_off, box_floats;
+  int sl_floats, qp;  // slopes; spec rows padded to 4
+  int bytes;
+};
+
+__device__ __forceinline__ void tie_bar(int id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+
+// kNetSmem: the network image is staged in shared memory (else read from
+// the workspace); QG: spec rows in groups of 4 (Q <= 4 QG, padded rows zero).
+template <bool kNetSmem, int QG>
+__global__ void __launch_bounds__(64 * kTieBoxes, 1)
+    crown_tie_kernel(const __grid_constant__ TcParams p, const TieLayout t) {
+  extern __shared__ __align__(16) float tsm[];
+  const int count = *p.tie_count;
+  const int nb = t.boxes;
+  if ((int)blockIdx.x * nb >= count) return;
+  const int tid = threadIdx.x, slot = tid >> 6, lt = tid & 63;
+  const int nfc = p.n_fc, Q = p.Q, n0 = p.dims[0], QP = t.qp;
+  const float* net = kNetSmem ? tsm : p.tnet;
+  __shared__ int failed;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(tsm + t.bar_off);
+  if (kNetSmem && tid == 0) {
+    failed = 0;
+    mbar_init(bar, 1);
+    mbar_fence_init();
+    mbar_expect_tx(bar, p.tnet_floats * 4);
+    bulk_load(tsm, p.tnet, p.tnet_floats * 4, bar);
+  }
+  float* V = tsm + t.v_off;
+  {  // spec rows times [W_last | b_last], o ascending (crown_mlp_kernel's
+     // order), from global memory while the copy lands
+    const int nprev = p.dims[nfc - 1], nL = p.dims[nfc];
+    const float* Wl = p.W + p.w_goff[nfc - 1];
+    const float* bl = p.b + p.b_goff[nfc - 1];
+    for (int idx = tid; idx < Q * kW; idx += blockDim.x) {
+      const int q = idx / kW, c = idx % kW;
+      float acc = 0.f;
+      if (c <= nprev)
+        for (int o = 0; o < nL; ++o)
+          acc = fmaf(__ldg(p.specW + q * nL + o),
+                     c < nprev ? __ldg(Wl + (long long)o * nprev + c) : __ldg(bl + o), acc);
+      V[idx] = acc;
+    }
+  }
+  if (kNetSmem) {
+    if (tid == 0 && !mbar_wait(bar, 0, kSpin)) {
+      failed = 1;
+      atomicExch(&g_tc_fault, 1);
+      mbar_wait(bar, 0, kSpin);  // let the copy land before the CTA exits
+    }
+    __syncthreads();
+    if (failed) return;  // the listed boxes keep crown_tc_kernel's bounds
+  }
+  __syncthreads();
+  // per-box state
+  float* bx = tsm + t.box_off + slot * t.box_floats;
+  float* sxl = bx;
+  float* sxh = sxl + kW;
+  float* mid = sxh + kW;      // [2][kW]
+  float* rad = mid + 2 * kW;  // [2][kW]
+  float2* sl = reinterpret_cast<float2*>(rad + 2 * kW);
+  float* ewt = rad + 2 * kW + t.sl_floats;  // [2][kW][QP], column-major: row q of column k at k*QP+q
+  float* vneg = ewt + 2 * kW * QP;          // [Q][kW]
+  float* vicp = vneg + Q * kW;              // [Q][kW]
+  float* part = vicp + Q * kW;              // [Q][8]
+  float* racc = part + 8 * Q;               // [QP]
+  float* bd = racc + QP;                    // [QP]
+  const int bid = 1 + slot;
+  for (int base = blockIdx.x * nb; base < count; base += gridDim.x * nb) {
+    const int item = base + slot;
+    if (item >= count) continue;  // this slot's 64 threads have no box this round
+    const int box = p.tie_list[item];
+    {
+      float lo = 0.f, hi = 0.f;
+      if (lt < n0) {
+        lo = __ldg(p.xl + (long long)box * n0 + lt);
+        hi = __ldg(p.xh + (long long)box * n0 + lt);
+      }
+      sxl[lt] = lo;
+      sxh[lt] = hi;
+      mid[lt] = __fmul_rn(__fadd_rn(lo, hi), 0.5f);  // 0 beyond n0
+      rad[lt] = __fmul_rn(__fsub_rn(hi, lo), 0.5f);
+      if (lt < Q) racc[lt] = __ldg(p.specb + lt);
+    }
+    tie_bar(bid);
+    // ---- IBP forward: thread lt owns output lt
+    int soff = 0;
+    for (int l = 0; l < nfc - 1; ++l) {
+      const int nin = p.dims[l], nout = p.dims[l + 1], pitch = p.tpitch[l];
+      const float* m_in = mid + (l & 1) * kW;
+      const float* r_in = rad + (l & 1) * kW;
+      float* m_out = mid + ((l + 1) & 1) * kW;
+      float* r_out = rad + ((l + 1) & 1) * kW;
+      if (lt < nout) {
+        const float* wr = net + p.tsoff[l] + lt * pitch;
+        float am = 0.f, ar = 0.f;
+        // whole 16-column blocks: the row's bias column and zero padding
+        // meet the zero input padding (exact zeros, as the SIMT kernel's)
+        const int kend = (nin + 15) & ~15;
+        for (int kb = 0; kb < kend; kb += 16) {
+          float4 w[4], m[4], r[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            w[j] = *reinterpret_cast<const float4*>(wr + kb + 4 * j);
+            m[j] = *reinterpret_cast<const float4*>(m_in + kb + 4 * j);
+            r[j] = *reinterpret_cast<const float4*>(r_in + kb + 4 * j);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            am = fmaf(m[j].x, w[j].x, am);
+            ar = fmaf(r[j].x, fabsf(w[j].x), ar);
+            am = fmaf(m[j].y, w[j].y, am);
+            ar = fmaf(r[j].y, fabsf(w[j].y), ar);
+            am = fmaf(m[j].z, w[j].z, am);
+            ar = fmaf(r[j].z, fabsf(w[j].z), ar);
+            am = fmaf(m[j].w, w[j].w, am);
+            ar = fmaf(r[j].w, fabsf(w[j].w), ar);
+          }
+        }
+        const float mc = __fadd_rn(am, wr[nin]);
+        float lo = __fsub_rn(mc, ar);
+        float hi = __fadd_rn(mc, ar);
+        if (p.clo) {
+          const long long gi = p.relu_goff[l] + (long long)box * nout + lt;
+          lo = fmaxf(lo, __ldg(p.clo + gi));
+          hi = fminf(hi, __ldg(p.chi + gi));
+        }
+        hi = fmaxf(hi, lo);
+        sl[soff + lt] = encode_slope(lo, hi);
+        const float lc = fmaxf(lo, 0.f), hc = fmaxf(hi, 0.f);
+        m_out[lt] = __fmul_rn(__fadd_rn(lc, hc), 0.5f);
+        r_out[lt] = __fmul_rn(__fsub_rn(hc, lc), 0.5f);
+      } else {
+        m_out[lt] = 0.f;  // the next layer's input padding
+        r_out[lt] = 0.f;
+      }
+      soff += nout;
+      tie_bar(bid);
+    }
+    // ---- back-substitution: thread lt owns column lt of every spec row
+    int cur = 0;
+    for (int l = nfc - 1; l >= 0; --l) {
+      const int nin = p.dims[l], nout = p.dims[l + 1], pitch = p.tpitch[l];
+      const float* Wl = net + p.tsoff[l];
+      const int L = l - 1;
+      const int NC = nin + 1, CG = (NC + 7) >> 3;
+      soff -= (L >= 0) ? nin : 0;
+      const float* e_in = ewt + cur * kW * QP;
+      float* e_out = ewt + (cur ^ 1) * kW * QP;
+      const int c = lt;
+      if (c <= nin) {
+        float a[4 * QG];
+#pragma unroll
+        for (int q = 0; q < 4 * QG; ++q) a[q] = 0.f;
+        if (l == nfc - 1) {
+#pragma unroll
+          for (int q = 0; q < 4 * QG; ++q)
+            if (q < Q) a[q] = V[q * kW + c];
+        } else {
+          // blocks of 8 rows: the rows past dims[l+1] are zero and meet zero
+          // coefficients, so the padded steps add exact zeros
+          const int kend = tie_rows(nout);
+          for (int kb = 0; kb < kend; kb += 8) {
+            float wv[8];
+            float4 ev[8][QG];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              wv[i] = Wl[(kb + i) * pitch + c];
+#pragma unroll
+              for (int g = 0; g < QG; ++g)
+                ev[i][g] = *reinterpret_cast<const float4*>(e_in + (kb + i) * QP + 4 * g);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+#pragma unroll
+              for (int g = 0; g < QG; ++g) {
+                a[4 * g + 0] = fmaf(ev[i][g].x, wv[i], a[4 * g + 0]);
+                a[4 * g + 1] = fmaf(ev[i][g].y, wv[i], a[4 * g + 1]);
+                a[4 * g + 2] = fmaf(ev[i][g].z, wv[i], a[4 * g + 2]);
+                a[4 * g + 3] = fmaf(ev[i][g].w, wv[i], a[4 * g + 3]);
+              }
+            }
+          }
+        }
+        Slope sv;
+        if (c < nin && L >= 0) {
+          sv = decode_slope(sl[soff + c], nullptr);
+        } else {
+          sv.pos = sv.neg = (c < nin) ? 1.f : 0.f;  // input layer: identity
+          sv.icp = 0.f;
+        }
+        const bool has_beta = L >= 0 && p.beta && c < nin;  // one value per neuron
+        const float bv = has_beta ? __ldg(p.beta + p.relu_goff[L] + (long long)box * nin + c) : 0.f;
+#pragma unroll
+        for (int q = 0; q < 4 * QG; ++q) {
+          {
+            const float v = a[q];
+            const float m = v < 0.f ? sv.neg : sv.pos;
+            float o = __fmul_rn(v, m);  // the bias column's entry is a zero product
+            if (has_beta) o = __fadd_rn(o, bv);
+            e_out[c * QP + q] = q < Q ? o : 0.f;
+            if (q < Q) {
+              vneg[q * kW + c] = fminf(v, 0.f);
+              vicp[q * kW + c] = sv.icp;
+              if (c == nin) bd[q] = v;
+            }
+          }
+        }
+      } else {
+        // columns past the bias: the next layer's padded rows read zeros here
+#pragma unroll
+        for (int q = 0; q < 4 * QG; ++q) e_out[c * QP + q] = 0.f;
+      }
+      tie_bar(bid);
+      if (l > 0) {  // intercept partial of every 8-column group, in column order
+        for (int it = lt; it < Q * CG; it += 64) {
+          const int q = it / CG, g = it - q * CG;
+          float pj = 0.f;
+          for (int cc = 8 * g; cc < min(NC, 8 * g + 8); ++cc)
+            pj = fmaf(vneg[q * kW + cc], vicp[q * kW + cc], pj);
+          part[q * 8 + g] = pj;
+        }
+        tie_bar(bid);
+      }
+      if (lt < Q) {
+        float a = __fadd_rn(racc[lt], bd[lt]);
+        if (l > 0) {
+          float ps = 0.f;
+          for (int g = 0; g < CG; ++g) ps = __fadd_rn(ps, part[lt * 8 + g]);
+          a = __fadd_rn(a, ps);
+        }
+        racc[lt] = a;
+      }
+      cur ^= 1;
+      tie_bar(bid);
+    }
+    // ---- concretisation against the box
+    if (lt < Q) {
+      const float* e = ewt + cur * kW * QP + lt;
+      const long long go = (long long)box * Q + lt;
+      float* Ar = p.A ? p.A + go * n0 : nullptr;
+      float s1 = 0.f, s2 = 0.f;
+      for (int i = 0; i < n0; ++i) {
+        const float ei = e[i * QP];
+        s1 = fmaf(fmaxf(ei, 0.f), sxl[i], s1);
+        s2 = fmaf(fminf(ei, 0.f), sxh[i], s2);
+        if (Ar) Ar[i] = ei;
+      }
+      p.lb[go] = __fadd_rn(__fadd_rn(racc[lt], s1), s2);
+      if (p.accout) p.accout[go] = racc[lt];
+    }
+    tie_bar(bid);
+  }
+}
+
+TieLayout plan_tie(const TcParams& p) {
+  TieLayout t{};
+  int relu = 0;
+  for (int L = 0; L < p.n_fc - 1; ++L) relu += p.dims[L + 1];
+  t.sl_floats = (2 * relu + 3) & ~3;
+  t.qp = (std::max(1, p.Q) + 3) & ~3;
+  t.box_floats = 6 * kW + t.sl_floats + 2 * kW * t.qp + 2 * p.Q * kW + 8 * p.Q + 2 * t.qp;
+  t.box_floats = (t.box_floats + 3) & ~3;
+  const int limit = 227 * 1024 / 4;
+  const int net = (p.tnet_floats + 3) & ~3;
+  t.net_in_smem = net + 4 + kMaxQ * kW + t.box_floats <= limit ? 1 : 0;
+  t.bar_off = t.net_in_smem ? net : 0;
+  t.v_off = t.bar_off + 4;
+  t.box_off = t.v_off + kMaxQ * kW;
+  t.boxes = std::max(1, std::min(kTieBoxes, (limit - t.box_off) / t.box_floats));
+  t.bytes = (t.box_off + t.boxes * t.box_floats) * 4;
+  return t;
 }
 
 bool eligible_dims(const vcb_mlp* net) {
@@ -667,8 +1043,11 @@ bool eligible_dims(const vcb_mlp* net) {
 struct TcPlan {
   int grid;
   long long slot_f2;
-  size_t img_bytes, ws_bytes;
+  size_t img_bytes, slots_bytes, tnet_off, tnet_bytes, flag_off, list_off, ws_bytes;
+  int tnet_floats;
 };
+
+inline size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
 TcPlan plan_tc(const vcb_mlp* net, int B) {
   TcPlan t;
@@ -678,8 +1057,17 @@ TcPlan plan_tc(const vcb_mlp* net, int B) {
   for (int L = 0; L < net->n_fc - 1; ++L) slot += (long long)net->dims[L + 1] * kTB;
   t.slot_f2 = slot;
   t.img_bytes = (size_t)3 * (net->n_fc - 1) * kImg;
-  // error word, then the images, then the slope slots
-  t.ws_bytes = 256 + t.img_bytes + (size_t)t.grid * slot * sizeof(float2);
+  t.slots_bytes = (size_t)t.grid * slot * sizeof(float2);
+  t.tnet_floats = 0;
+  for (int l = 0; l < net->n_fc; ++l)
+    t.tnet_floats += tie_rows(net->dims[l + 1]) * tie_pitch(net->dims[l]);
+  // error word and tie count, the images, the slope slots, the network rows
+  // of the tie re-bound, its flags and its list
+  t.tnet_off = align256(256 + t.img_bytes + t.slots_bytes);
+  t.tnet_bytes = (size_t)t.tnet_floats * sizeof(float);
+  t.flag_off = align256(t.tnet_off + t.tnet_bytes);
+  t.list_off = align256(t.flag_off + (size_t)B * sizeof(int));
+  t.ws_bytes = t.list_off + (size_t)B * sizeof(int);
   return t;
 }
 
@@ -732,8 +1120,19 @@ int crown_tc_launch(const vcb_mlp* net, int32_t B, const float* xl, const float*
   p.W = net->W;
   p.b = net->b;
   p.err = reinterpret_cast<int*>(base);
+  p.tie_count = reinterpret_cast<int*>(base + 64);
   p.img = base + 256;
   p.slopes = reinterpret_cast<float2*>(base + 256 + plan.img_bytes);
+  p.tie_on = (!sb_in_lo && !alpha && Q > 0) ? 1 : 0;
+  p.tnet = reinterpret_cast<float*>(base + plan.tnet_off);
+  p.tie_flag = reinterpret_cast<int*>(base + plan.flag_off);
+  p.tie_list = reinterpret_cast<int*>(base + plan.list_off);
+  p.tnet_floats = plan.tnet_floats;
+  for (int l = 0, off = 0; l < nfc; ++l) {
+    p.tsoff[l] = off;
+    p.tpitch[l] = tie_pitch(net->dims[l]);
+    off += tie_rows(net->dims[l + 1]) * p.tpitch[l];
+  }
   p.slot_f2 = plan.slot_f2;
   p.B = B;
   p.Q = Q;
@@ -758,7 +1157,8 @@ int crown_tc_launch(const vcb_mlp* net, int32_t B, const float* xl, const float*
   p.accout = acc;
   p.sbolo = sb_out_lo;
   p.sbohi = sb_out_hi;
-  const int nimg = 3 * (nfc - 1) * kW * kW;
+  const int nimg = std::max(3 * (nfc - 1) * kW * kW,
+                           p.tie_on ? std::max(B, plan.tnet_floats) : 0);
   crown_tc_images<<<(nimg + 255) / 256, 256, 0, st>>>(p);
   int rc = check_launch(who);
   if (rc) return rc;
@@ -771,7 +1171,39 @@ int crown_tc_launch(const vcb_mlp* net, int32_t B, const float* xl, const float*
     crown_tc_kernel<true><<<plan.grid, kThreads, kSmem, st>>>(p);
   else
     crown_tc_kernel<false><<<plan.grid, kThreads, kSmem, st>>>(p);
+  rc = check_launch(who);
+  if (rc || !p.tie_on) return rc;
+  // the listed boxes, bounded again with the fp32 kernel's order; a launch
+  // whose list is empty returns at once
+  const TieLayout tl = plan_tie(p);
+  const int qg = tl.qp / 4;
+  const void* tie_fn = nullptr;
+#define VCB_TIE_FN(S, G) if (tl.net_in_smem == S && qg == G) tie_fn = reinterpret_cast<const void*>(crown_tie_kernel<S, G>);
+  VCB_TIE_FN(1, 1) VCB_TIE_FN(1, 2) VCB_TIE_FN(1, 3) VCB_TIE_FN(1, 4)
+  VCB_TIE_FN(0, 1) VCB_TIE_FN(0, 2) VCB_TIE_FN(0, 3) VCB_TIE_FN(0, 4)
+#undef VCB_TIE_FN
+  rc = ensure_smem(tie_fn, tl.bytes);
+  if (rc) return rc;
+  void* args[] = {const_cast<TcParams*>(&p), const_cast<TieLayout*>(&tl)};
+  rc = cuda_fail(cudaLaunchKernel(tie_fn, dim3(sm_count()), dim3(64 * tl.boxes), args,
+                                  (size_t)tl.bytes, st),
+                 who);
+  if (rc) return rc;
   return check_launch(who);
+}
+
+int crown_tc_fault_take(cudaStream_t st, int* was_set) {
+  int h = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&h, g_tc_fault, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && h) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_tc_fault, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  *was_set = h;
+  return cuda_fail(e, "vcb_fault_check");
 }
 
 }  // namespace vcb

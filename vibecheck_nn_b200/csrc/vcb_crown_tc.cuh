@@ -29,4 +29,8 @@ int crown_tc_launch(const vcb_mlp* net, int32_t B, const float* xl, const float*
                     float* sb_out_lo, float* sb_out_hi, void* ws, size_t ws_bytes,
                     cudaStream_t st, const char* who);
 
+// Reads and clears the device fault word of crown_tc_kernel (set when one of
+// its bounded waits expired) after synchronising st; *was_set = 1 if it was.
+int crown_tc_fault_take(cudaStream_t st, int* was_set);
+
 }  // namespace vcb
