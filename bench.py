@@ -272,17 +272,14 @@ class ClockSampler:
 # GPU leg
 # ---------------------------------------------------------------------------
 
-def read_traffic(name='crown_mlp_cfg2.md'):
-    """Per-launch DRAM bytes of a cfg2 kernel from its committed ncu summary
-    (profiles/<name>, line 'traffic_bytes_per_launch: N')."""
-    path = os.path.join(ROOT, 'profiles', name)
+def read_traffic(kernel):
+    """Per-launch DRAM bytes of a cfg2 kernel from bench_traffic.json (one
+    ncu capture per kernel, the command recorded beside the figure)."""
     try:
-        for ln in open(path):
-            if ln.startswith('traffic_bytes_per_launch:'):
-                return float(ln.split(':', 1)[1])
-    except OSError:
-        pass
-    return None
+        with open(os.path.join(ROOT, 'bench_traffic.json')) as f:
+            return float(json.load(f)[kernel]['bytes_per_launch'])
+    except (OSError, KeyError, ValueError):
+        return None
 
 
 def measured_fp32_peak(dev):
@@ -321,13 +318,13 @@ def roofline_cfg2(tc_path, achieved, ffma_peak, flop_per_box):
     if not tc_path:
         return {'bound': 'fp32_simt', 'achieved': achieved, 'peak': ffma_peak,
                 'unit': 'TFLOP/s', 'frac': achieved / ffma_peak if ffma_peak else None,
-                'traffic': read_traffic('crown_mlp_cfg2.md'),
+                'traffic': read_traffic('crown_mlp_kernel'),
                 'kernel': 'vcb_mlp_crown (crown_mlp_kernel)', 'flop_per_box': flop_per_box,
                 'peak_source': 'measured live: vcb_probe_ffma FFMA loop (MEASURED_PEAKS.json '
                                'has no FP32 SIMT figure)'}
     peak, source = tf32x3_peak()
     return {'bound': 'tensor', 'achieved': achieved, 'peak': peak, 'unit': 'TFLOP/s',
-            'frac': achieved / peak, 'traffic': read_traffic('crown_tc_cfg2.md'),
+            'frac': achieved / peak, 'traffic': read_traffic('crown_tc_kernel'),
             'kernel': 'vcb_mlp_crown (crown_tc_kernel, tcgen05 3xTF32; the step also runs '
                       'crown_tc_images, <1% of its time)',
             'flop_per_box': flop_per_box,

@@ -139,7 +139,9 @@ int vcb_mlp_flirpa(const vcb_mlp* net, int32_t B, int32_t K, const float* xl,
  * library holds until exit.  The array caps the number of persistent CTAs;
  * a network whose single tile needs more than the array returns
  * VCB_ERR_UNSUPPORTED.  The first call on a device looks up the array's
- * device address, so make it before any stream capture.  All calls share
+ * device address, so make it before any stream capture; the address is
+ * cached per device and context, so the first call after a device reset
+ * (which reloads the library's module) looks it up again.  All calls share
  * the array: calls that overlap on the GPU race on it.  Arguments and
  * results are those of vcb_mlp_crown. */
 int vcb_mlp_crown_noalloc(const vcb_mlp* net, int32_t B,

@@ -70,8 +70,9 @@ def test_tc_gemm_matches_fp64(M, N, K):
 
 
 def test_tc_gemm_throughput_vs_cublas_fp32():
-    """Timing line for profiles/tc_gemm_3xtf32.md (CUDA events, 3 warm-up +
-    10 launches); the tensor-core path must beat cuBLAS fp32 on a large shape."""
+    """Timing of the 3xTF32 GEMM against cuBLAS fp32 (CUDA events, 3 warm-up
+    + 10 launches); the tensor-core path must beat cuBLAS fp32 on a large
+    shape."""
     M = N = K = 4096
     A = torch.randn(M, K, device=DEV)
     B = torch.randn(N, K, device=DEV)

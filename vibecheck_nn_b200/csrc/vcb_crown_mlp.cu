@@ -730,10 +730,30 @@ __device__ __align__(256) float2 g_static_slopes[kStaticSlopeBytes / sizeof(floa
 constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
 void* g_static_addr[kMaxDevices] = {};
+unsigned long long g_static_ctx[kMaxDevices] = {};  // context the address belongs to
+
+// Unique ID of the current context (cuCtxGetId, reached through the runtime's
+// driver entry point so the library needs no link to libcuda); 0 if unknown.
+unsigned long long current_context_id() {
+  using GetId = int (*)(void*, unsigned long long*);
+  static GetId fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<GetId>(f);
+  }();
+  unsigned long long id = 0;
+  if (!fn || fn(nullptr, &id) != 0) return 0;
+  return id;
+}
 
 // Device address of g_static_slopes on the current device.  The host-side
-// symbol is only a stand-in, so the address is looked up once per device
-// (with that device current) and cached.
+// symbol is only a stand-in, so the address is looked up with the device
+// current and cached per device, together with the ID of the context it was
+// looked up in: a device reset (or any other teardown of the primary
+// context) reloads the module, and the next call looks the address up again.
 int static_slopes_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -741,12 +761,14 @@ int static_slopes_address(void** out) {
   if (dev < 0 || dev >= kMaxDevices)
     return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_crown_noalloc: device %d", dev);
   std::lock_guard<std::mutex> lk(g_static_mu);
-  if (!g_static_addr[dev]) {
+  const unsigned long long ctx = current_context_id();
+  if (!g_static_addr[dev] || ctx == 0 || ctx != g_static_ctx[dev]) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_static_slopes);
     if (e != cudaSuccess)
       return cuda_fail(e, "vcb_mlp_crown_noalloc: cudaGetSymbolAddress(g_static_slopes)");
     g_static_addr[dev] = ptr;
+    g_static_ctx[dev] = ctx;
   }
   *out = g_static_addr[dev];
   return VCB_OK;
