@@ -551,8 +551,8 @@ def run_cfg1(args):
     w = wk.cfg1(0)
     gg = wk.mlp_gg(w['layers'], dev)
     spec = bab.LinearSpec(w['xl'], w['xh'], [[('pair', 1, 0)]])
-    st = types.SimpleNamespace(input_split_batch_size=2048, input_split_crown_intermediate=True,
-                               total_timeout=600.0)
+    st = wk.reference_bab_settings(input_split_batch_size=2048, input_split_crown_intermediate=True,
+                                   total_timeout=600.0)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     res = {}
 
@@ -724,7 +724,7 @@ def run_cfg5(args, per_step=64):
     gg = wk.mlp_gg(w['layers'], dev)
     t = w['true_label']
     spec = bab.LinearSpec(w['xl'], w['xh'], wk.robustness_disjuncts(10, t))
-    st = types.SimpleNamespace(input_split_batch_size=per_step, disable_sat_finding=True)
+    st = wk.reference_bab_settings(input_split_batch_size=per_step, disable_sat_finding=True)
     eng = bab.make_engine(spec, gg, st, dev)
     assert isinstance(eng, bab.WideBoundEngine)
     n_batches = max(3, args.warmup) + args.steps

@@ -224,6 +224,48 @@ int vcb_bab_step_wide(int32_t B, int32_t n_in, int32_t Q, int32_t D,
 
 size_t vcb_bab_step_wide_workspace(int32_t B, int32_t n_in);
 
+/* Branching and clipping settings of the input-split step, the settings keys
+ * the reference driver reads in its branching block (verify_graph.py:
+ * 13036-13423, settings.py:340-368, 1364). */
+typedef struct vcb_bab_opts {
+  int32_t clip;          /* input_split_batched_clip_enabled                  */
+  int32_t clip_iters;    /* input_split_batched_clip_iters (>= 1)             */
+  int32_t branch_sb;     /* SB score (else widest dimension)                  */
+  int32_t margin_score;  /* input_split_sb_margin_score                       */
+  int32_t split_depth;   /* dimensions split at once this iteration (1..9):   */
+                         /* bab_split_depth while the popped batch is below   */
+                         /* the batch size, else 1                            */
+  float coeff_thresh;    /* input_split_sb_coeff_thresh                       */
+  float margin_weight;   /* input_split_sb_margin_weight                      */
+  const float* boost;    /* (n_in) device multipliers of the SB score (the    */
+                         /* branch boost), or NULL                            */
+} vcb_bab_opts;
+
+/* vcb_bab_step / vcb_bab_step_wide with every branching setting, replacing
+ * the whole branching block of _input_split_batched_inner (verify_graph.py:
+ * 13236-13429): iterated clipping, the SB margin score, the branch boost and
+ * K-dimension splits.  For split_depth = 1 the children go to lo_* / hi_*
+ * as above; for split_depth = K > 1 each split leaf's K best-scoring
+ * dimensions (ties to the lower index) that are wider than 1e-12 are
+ * bisected together and its 2^K' children (bit k of the child index set =
+ * high half of the k-th dimension) are written leaf by leaf to kid_xl /
+ * kid_xh (capacity B * 2^K rows); a leaf with no such dimension counts as
+ * degenerate.  counters[2] = child rows written. */
+int vcb_bab_step_ex(int32_t B, int32_t n_in, int32_t Q, int32_t D, int32_t q_sens,
+                    const int32_t* query_disjunct, const float* xl, const float* xh,
+                    const float* lb, const float* A, const float* acc,
+                    const vcb_bab_opts* opts, float* lo_xl, float* lo_xh, float* hi_xl,
+                    float* hi_xh, float* kid_xl, float* kid_xh, int64_t* counters,
+                    void* stream);
+
+int vcb_bab_step_wide_ex(int32_t B, int32_t n_in, int32_t Q, int32_t D, int32_t q_sens,
+                         const int32_t* query_disjunct, const float* xl, const float* xh,
+                         const float* lb, const float* A, const float* acc,
+                         const vcb_bab_opts* opts, float* lo_xl, float* lo_xh,
+                         float* hi_xl, float* hi_xh, float* kid_xl, float* kid_xh,
+                         int64_t* counters, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
 /* Batched sign-gradient PGD for ReLU MLPs (widths <= 128); replaces the loop
  * of _simple_pgd / _simple_pgd_batched (src/vibecheck/verify_hybrid_acasxu.py:
  * 39, 103).

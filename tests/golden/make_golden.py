@@ -66,7 +66,7 @@ def main():
     ap.add_argument('--ref-src', required=True)
     ap.add_argument('--only', default=None,
                     choices=['pgd_general', 'forward', 'relu_bab', 'hybrid', 'multisub',
-                             'cfg2'],
+                             'cfg2', 'bab_branching', 'acasxu'],
                     help='regenerate one fixture only')
     args = ap.parse_args()
     vz, vg, vh, vs, vspec = _import_reference(args.ref_src)
@@ -89,6 +89,12 @@ def main():
         return
     if args.only == 'cfg2':
         _golden_cfg2(vz, wk)
+        return
+    if args.only == 'bab_branching':
+        _golden_bab_branching(vg, vs, vspec, wk)
+        return
+    if args.only == 'acasxu':
+        _golden_acasxu(args.ref_src, vg, vs)
         return
 
     # ------------------------------------------------------------------ slopes
@@ -599,6 +605,102 @@ def multisub_problem(seed, n_sub, margins, half=(0.1, 0.3)):
         t1 = float(y[:, 1].min() - m)
         subs.append((lo, hi, [[('ge', 0, t0), ('le', 1, t1)]]))
     return layers, subs
+
+
+def _golden_acasxu(ref_src, vg, vs):
+    """The reference's bundled ACAS Xu example (README.md:40-75): the
+    network as this package's ONNX reader lowers it (weights and biases of
+    the fc layers), and for examples/prop_1 and prop_2 the property as the
+    reference's vnnlib_loader parses it (box, linear queries) and the
+    reference driver's verdict, leaves, iterations, phase and witness under
+    configs/acasxu_2023.yaml (_input_split_batched on CPU in float32, 60 s)."""
+    import types as _types
+    import torch
+    import vibecheck.config_loader as cl
+    import vibecheck.vnnlib_loader as vl
+    from vibecheck_nn_b200 import netdesc, onnx_graph
+    root = os.path.dirname(os.path.abspath(ref_src))
+    g = onnx_graph.read_onnx(os.path.join(root, 'examples', 'ACASXU_run2a_2_2_batch_2000.onnx'))
+    gg = g.to_gg('cpu', torch.float32)
+    layers = netdesc.lower_mlp(gg)
+    out = _net_arrays(layers)
+    out['op_types'] = np.array(' '.join(op['type'] for op in gg['ops']))
+    over = cl.load_config(os.path.join(root, 'configs', 'acasxu_2023.yaml'))
+    for prop in (1, 2):
+        spec = vl.load_vnnlib(os.path.join(root, 'examples', f'prop_{prop}.vnnlib'))
+        st = vs.default_settings(device='cpu', bits=32, total_timeout=60.0, **over)
+        verdict, det = vg._input_split_batched(_types.SimpleNamespace(onnx_path=None), spec, st,
+                                               gg, torch.device('cpu'), torch.float32)
+        print('acasxu prop', prop, verdict, {k: v for k, v in det.items() if k != 'witness'},
+              flush=True)
+        q = spec.as_linear_queries(5)
+        p = f'p{prop}_'
+        from vibecheck_nn_b200.pgd import _disjunct_tuples
+        out[p + 'disj'] = np.array(repr(_disjunct_tuples(spec)))
+        out[p + 'x_lo'] = np.asarray(spec.x_lo, np.float64).reshape(-1)
+        out[p + 'x_hi'] = np.asarray(spec.x_hi, np.float64).reshape(-1)
+        out[p + 'qd'] = np.array([d for d, _, _ in q])
+        out[p + 'qw'] = np.stack([np.asarray(w, np.float64).reshape(-1) for _, w, _ in q])
+        out[p + 'qb'] = np.array([float(b) for _, _, b in q])
+        out[p + 'verdict'] = np.array(verdict)
+        out[p + 'phase'] = np.array(det.get('phase', ''))
+        out[p + 'n_leaves'] = np.array(det.get('batched_n_leaves', -1))
+        out[p + 'n_iters'] = np.array(det.get('batched_n_iters', -1))
+        if det.get('witness') is not None:
+            out[p + 'witness'] = np.asarray(det['witness'], np.float64).reshape(-1)
+    _save('acasxu', **out)
+
+
+# Branching variants of the input-split BaB driver on cfg1 networks: (tag,
+# seed, settings overrides).  'sb' scores width x sum_q |A_q| (verify_graph.py:
+# 13285-13286), 'margin' the margin-augmented worst-query score (:13275-13283),
+# 'clip3' iterates the halfspace clip (:13036-13084), 'depth2' / 'depth3'
+# split 2^K ways while the popped batch is below the batch size, with the
+# branch boost (:12744-12800, :13320-13423).
+BAB_BRANCHING_CASES = (
+    ('sb', 0, {'input_split_batched_branch_sb': True}),
+    ('margin', 0, {'input_split_batched_branch_sb': True, 'input_split_sb_margin_score': True}),
+    ('margin_thr', 1, {'input_split_batched_branch_sb': True, 'input_split_sb_margin_score': True,
+                       'input_split_sb_coeff_thresh': 0.5, 'input_split_sb_margin_weight': 0.25}),
+    ('clip3', 0, {'input_split_batched_clip_iters': 3}),
+    ('clip3_s1', 1, {'input_split_batched_clip_iters': 3}),
+    ('depth2', 0, {'input_split_batched_branch_sb': True, 'bab_split_depth': 2}),
+    ('depth3_noboost', 1, {'input_split_batched_branch_sb': True, 'bab_split_depth': 3,
+                           'input_split_batched_branch_boost': False}),
+    ('depth2_b64', 0, {'input_split_batched_branch_sb': True, 'bab_split_depth': 2,
+                       'input_split_batch_size': 64}),
+    ('depth2_margin_exp2', 1, {'input_split_batched_branch_sb': True, 'bab_split_depth': 2,
+                               'input_split_sb_margin_score': True,
+                               'input_split_batched_branch_boost_exp': 2.0}),
+)
+
+
+def _golden_bab_branching(vg, vs, vspec, wk):
+    """_input_split_batched (verify_graph.py:12466) on cfg1 networks with
+    CROWN intermediates under each BAB_BRANCHING_CASES setting, on CPU in
+    float32: verdict, visited leaves, iterations and open degenerate leaves."""
+    import types as _types
+    import torch
+    out = {}
+    for tag, seed, over in BAB_BRANCHING_CASES:
+        w = wk.cfg1(seed)
+        gg = wk.mlp_gg(w['layers'], 'cpu', torch.float32)
+        spec = vspec.VNNSpec(
+            x_lo=w['xl'].astype(np.float64), x_hi=w['xh'].astype(np.float64),
+            disjuncts=[vspec.Conjunct([vspec.PairwiseConstraint(pred=1, comp=0)])])
+        kw = dict(device='cpu', bits=32, input_split_batched_enabled=True,
+                  input_split_batch_size=2048, input_split_crown_intermediate=True,
+                  disable_sat_finding=True, total_timeout=600.0)
+        kw.update(over)
+        st = vs.default_settings(**kw)
+        verdict, det = vg._input_split_batched(_types.SimpleNamespace(onnx_path=None), spec,
+                                               st, gg, torch.device('cpu'), torch.float32)
+        print('bab branching', tag, verdict, det, flush=True)
+        out[f'{tag}_verdict'] = np.array(verdict)
+        out[f'{tag}_n_leaves'] = np.array(det.get('batched_n_leaves', -1))
+        out[f'{tag}_n_iters'] = np.array(det.get('batched_n_iters', -1))
+        out[f'{tag}_open'] = np.array(det.get('batched_open_degenerate', 0))
+    _save('bab_branching', **out)
 
 
 # cfg2 benchmark workloads whose tensor-core IBP bounds put a ReLU at the

@@ -134,11 +134,9 @@ def test_bab_cfg1_matches_reference_leaf_counts(seed, ci):
     g = load_golden(f'bab_cfg1_seed{seed}')
     gg = wk.mlp_gg(golden_layers(g), DEV)
     spec = bab.LinearSpec(g['xl'], g['xh'], [[('pair', 1, 0)]])
-    st = type('S', (), {})()
-    st.input_split_batch_size = 2048
-    st.input_split_crown_intermediate = bool(ci)
-    st.disable_sat_finding = True
-    st.total_timeout = 600.0
+    st = wk.reference_bab_settings(input_split_batch_size=2048,
+                                   input_split_crown_intermediate=bool(ci),
+                                   disable_sat_finding=True, total_timeout=600.0)
     verdict, det = bab._input_split_batched(None, spec, st, gg, DEV, torch.float32)
     assert verdict == str(g[f'verdict_ci{ci}'])
     assert det['batched_n_leaves'] == int(g[f'n_leaves_ci{ci}']), det
@@ -153,10 +151,7 @@ def test_bab_multi_disjunct_matches_oracle():
     y = wk._mlp_forward64(w['layers'], ((w['xl'] + w['xh']) / 2)[None].astype(np.float64))[0]
     disj = [[('pair', 1, 0)], [('ge', 2, float(y[2]) + 60.0), ('le', 3, float(y[3]) - 60.0)]]
     spec = bab.LinearSpec(w['xl'], w['xh'], disj)
-    st = type('S', (), {})()
-    st.input_split_batch_size = 512
-    st.input_split_crown_intermediate = False
-    st.disable_sat_finding = True
+    st = wk.reference_bab_settings(input_split_batch_size=512, disable_sat_finding=True)
     verdict, det = bab._input_split_batched(None, spec, st, gg, DEV, torch.float32)
     queries = spec.as_linear_queries(5)
     W = np.stack([q[1] for q in queries]).astype(np.float32)

@@ -23,8 +23,8 @@ def _cfg1_run(monkeypatch, wide_step):
     w = wk.cfg1(0)
     gg = wk.mlp_gg(w['layers'], DEV)
     spec = LinearSpec(w['xl'], w['xh'], [[('pair', 1, 0)]])
-    st = types.SimpleNamespace(input_split_batch_size=2048, input_split_crown_intermediate=True,
-                               disable_sat_finding=True, total_timeout=600.0)
+    st = wk.reference_bab_settings(input_split_batch_size=2048, input_split_crown_intermediate=True,
+                                   disable_sat_finding=True, total_timeout=600.0)
     return bab._input_split_batched(None, spec, st, gg, DEV, torch.float32)
 
 
@@ -85,8 +85,8 @@ def test_wide_engine_bab_matches_oracle():
                                         batch_size=256, crown_intermediate=False, timeout=120.0)
     gg = wk.mlp_gg(layers, DEV)
     spec = LinearSpec(xl, xh, [[('pair', 1, 0)]])
-    st = types.SimpleNamespace(input_split_batch_size=256, disable_sat_finding=True,
-                               total_timeout=600.0)
+    st = wk.reference_bab_settings(input_split_batch_size=256, disable_sat_finding=True,
+                                   total_timeout=600.0)
     eng = bab.make_engine(spec, gg, st, DEV)
     assert isinstance(eng, bab.WideBoundEngine)
     verdict, det = bab._input_split_batched(None, spec, st, gg, DEV, torch.float32)

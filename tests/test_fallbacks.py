@@ -85,11 +85,11 @@ def test_kernel_error_propagates_out_of_the_bab_driver(fake):
 
 
 def test_timeout_status_propagates_out_of_the_bab_driver(fake):
-    f = fake(fail={'vcb_bab_step'}, status=_lib.VCB_ERR_TIMEOUT)
+    f = fake(fail={'vcb_bab_step_ex'}, status=_lib.VCB_ERR_TIMEOUT)
     spec, gg, settings = _problem()
     with pytest.raises(TimeoutError):
         bab._input_split_batched(None, spec, settings, gg, 'cuda', torch.float32)
-    assert f.calls.count('vcb_bab_step') == 1
+    assert f.calls.count('vcb_bab_step_ex') == 1
 
 
 def test_out_of_memory_halves_the_batch(fake):
@@ -146,3 +146,26 @@ def test_cpu_tensors_are_unsupported_input():
     with pytest.raises(_lib.UnsupportedInput):
         ops._ibp_forward_graph_batched(torch.zeros(2, 4), torch.ones(2, 4), gg, 'cuda',
                                        torch.float64)
+
+
+@pytest.mark.parametrize('key', ['input_split_batched_clip_full_lp',
+                                 'input_split_batched_milp_escalate'])
+def test_settings_outside_the_b200_path_are_refused(key):
+    """The Gurobi LP clip and MILP escalation are not on the B200 path: the
+    driver refuses them with UnsupportedInput (so the installed binding runs
+    the reference's own driver) instead of ignoring them."""
+    assert bab.BabConfig(types.SimpleNamespace()).split_depth == 1
+    with pytest.raises(_lib.UnsupportedInput):
+        bab.BabConfig(types.SimpleNamespace(**{key: True}))
+
+
+def test_branching_settings_are_read():
+    c = bab.BabConfig(types.SimpleNamespace(
+        bab_split_depth=3, input_split_batched_clip_iters=2, input_split_sb_margin_score=True,
+        input_split_sb_coeff_thresh=0.5, input_split_sb_margin_weight=0.25,
+        input_split_batched_branch_boost=False, input_split_batched_branch_boost_exp=2.0))
+    assert (c.split_depth, c.clip_iters, c.margin, c.branch_boost, c.boost_exp) == \
+        (3, 2, (0.5, 0.25), False, 2.0)
+    # the reference driver's fallbacks for absent keys
+    d = bab.BabConfig(types.SimpleNamespace())
+    assert d.branch_sb and d.branch_boost and d.total_budget == 60.0 and d.margin is None

@@ -286,3 +286,18 @@ def test_oracle_fp32_is_the_reference_fp32_on_cfg2():
                                       w['xl'][idx], w['xh'][idx], ggc, w['spec_W'],
                                       w['spec_b'])
         assert close(lb, g[f's{seed}_lb']), (seed, max_excess(lb, g[f's{seed}_lb']))
+
+
+def test_oracle_bab_iterated_clip_matches_reference():
+    """The numpy driver with input_split_batched_clip_iters = 3 reproduces the
+    reference's verdict, leaves and iterations on cfg1 seed 0 (the other
+    branching cases of bab_branching.npz are pinned on the GPU)."""
+    g = load_golden('bab_branching')
+    w = wk.cfg1(0)
+    ggc = wk.mlp_gg(w['layers'])
+    verdict, det = obab.input_split_bab(ggc, w['xl'], w['xh'], w['spec_W'], w['spec_b'],
+                                        batch_size=2048, crown_intermediate=True,
+                                        timeout=1e9, clip_iters=3)
+    assert verdict == str(g['clip3_verdict'])
+    assert det['batched_n_leaves'] == int(g['clip3_n_leaves'])
+    assert det['batched_n_iters'] == int(g['clip3_n_iters'])

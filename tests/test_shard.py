@@ -37,7 +37,7 @@ class SyntheticEngine:
         return (torch.full((self.n_in,), -1.0, dtype=torch.float32),
                 torch.full((self.n_in,), 1.0, dtype=torch.float32))
 
-    def process(self, xl, xh, n_iter):
+    def process(self, xl, xh, n_iter, batch_size=None, timer=None):
         xl64, xh64 = xl.double(), xh.double()
         c = (xl64 + xh64) / 2
         r = (xh64 - xl64) / 2

@@ -28,8 +28,8 @@ def _cfg1_problem(seed, device):
     w = wk.cfg1(seed)
     gg = wk.mlp_gg(w['layers'], device)
     spec = LinearSpec(w['xl'], w['xh'], [[('pair', 1, 0)]])
-    st = types.SimpleNamespace(input_split_batch_size=2048, input_split_crown_intermediate=True,
-                               disable_sat_finding=True, total_timeout=600.0)
+    st = wk.reference_bab_settings(input_split_batch_size=2048, input_split_crown_intermediate=True,
+                                   disable_sat_finding=True, total_timeout=600.0)
     return gg, spec, st
 
 

@@ -30,6 +30,17 @@ class VcbMlp(ctypes.Structure):
                 ('b', ctypes.c_void_p)]
 
 
+class VcbBabOpts(ctypes.Structure):
+    _fields_ = [('clip', ctypes.c_int32),
+                ('clip_iters', ctypes.c_int32),
+                ('branch_sb', ctypes.c_int32),
+                ('margin_score', ctypes.c_int32),
+                ('split_depth', ctypes.c_int32),
+                ('coeff_thresh', ctypes.c_float),
+                ('margin_weight', ctypes.c_float),
+                ('boost', ctypes.c_void_p)]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 
@@ -98,6 +109,11 @@ SIGNATURES = {
     'vcb_bab_step_wide': [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P,
                           _P, _P, ctypes.c_size_t, _P],
     'vcb_bab_step_wide_workspace': [_I, _I],
+    'vcb_bab_step_ex': [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, ctypes.POINTER(VcbBabOpts),
+                        _P, _P, _P, _P, _P, _P, _P, _P],
+    'vcb_bab_step_wide_ex': [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P,
+                             ctypes.POINTER(VcbBabOpts), _P, _P, _P, _P, _P, _P, _P, _P,
+                             ctypes.c_size_t, _P],
     'vcb_conv_forward': [_I, _P, _P, _P, _P, _P, _P, _P],
     'vcb_conv_backward': [_I, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P],
     'vcb_fc_forward': [_I, _I, _I, _P, _I, _P, _P, _P, _I, _P, _I, _P],

@@ -26,7 +26,9 @@ BINDINGS = {
         '_forward_batch_graph': ('forward', '_forward_batch_graph', 'delegate'),
     },
     'vibecheck.verify_graph': {
-        '_input_split_batched': ('bab', '_input_split_batched'),
+        # settings or graphs outside the B200 path (the Gurobi LP clip, MILP
+        # escalation, CPU / float64) run the reference's own driver
+        '_input_split_batched': ('bab', '_input_split_batched', 'delegate'),
         # per-disjunct sub-box verification calls it as a module global
         # (verify_graph.py:9337); CPU calls go to the reference's own
         '_multi_sub_input_split_bab': ('multisub', '_multi_sub_input_split_bab', 'delegate'),

@@ -390,3 +390,60 @@ def cfg5_leaves(xl, xh, start, count, depth=18):
 def robustness_disjuncts(n_out, true_label):
     """Unsafe iff some y_j >= y_true: one pairwise disjunct per j != true."""
     return [[('pair', true_label, j)] for j in range(n_out) if j != true_label]
+
+
+def reference_bab_settings(**overrides):
+    """The input-split driver's settings keys with the values of the
+    reference's default_settings (settings.py:319-438, :1364), as a plain
+    namespace, plus overrides.  The driver's getattr fallbacks for absent
+    keys differ for some (branch_sb True, total_timeout 60 s), so tests that
+    mirror a default_settings run pass these explicitly."""
+    import types
+    d = dict(total_timeout=120.0, input_split_batch_size=4096,
+             input_split_batched_max_worklist=200_000,
+             input_split_batched_clip_enabled=True, input_split_batched_clip_iters=1,
+             input_split_batched_branch_sb=False, input_split_sb_margin_score=False,
+             input_split_sb_coeff_thresh=0.01, input_split_sb_margin_weight=1.0,
+             input_split_crown_intermediate=False, bab_split_depth=1,
+             input_split_batched_branch_boost_exp=1.0, input_split_leaf_pgd_every=0,
+             input_split_batched_alpha_boundary_eps=0.0, input_split_batched_alpha_iters=10,
+             input_split_batched_alpha_max_leaves=200,
+             input_split_batched_alpha_all_leaves=False, disable_sat_finding=False,
+             pgd_phase0_enabled=True, raise_on_oom=True)
+    d.update(overrides)
+    return types.SimpleNamespace(**d)
+
+
+# configs/acasxu_2023.yaml of the reference (its low-dimensional ReLU FC
+# preset): CROWN intermediates, OSI root PGD, leaf PGD every 3 iterations,
+# alpha-CROWN on boundary leaves within 10 of closing.
+ACASXU_2023 = dict(
+    use_hybrid_acasxu=False, input_split_batched_enabled=True,
+    input_split_crown_intermediate=True, pgd_init_mode='osi', pgd_time_budget_phase0=5.0,
+    input_split_leaf_pgd_every=3, input_split_leaf_pgd_max_leaves=128,
+    input_split_leaf_pgd_restarts=256, input_split_leaf_pgd_iters=50,
+    input_split_batched_alpha_boundary_eps=10.0, input_split_batched_alpha_iters=20,
+    input_split_batched_alpha_max_leaves=2048, input_split_serial_disjuncts=True)
+
+
+def onnx_mlp_graph(layers, input_shape, offset=None):
+    """An OnnxGraph of the ACAS Xu export's structure for fc layers (W (out,
+    in), b): Sub(input, offset) -> Flatten -> MatMul(W^T) -> Add(b) -> Relu
+    ... -> MatMul -> Add, as onnx_graph.read_onnx returns such a file."""
+    from .onnx_graph import OnnxGraph
+    n_in = layers[0][0].shape[1]
+    consts = {'offset': np.zeros((1,) * (len(input_shape) - 1) + (n_in,))
+              if offset is None else np.asarray(offset, np.float64)}
+    nodes = [('Sub', ['input', 'offset'], ['sub'], {}),
+             ('Flatten', ['sub'], ['flat'], {'axis': 1})]
+    cur = 'flat'
+    for i, (W, b) in enumerate(layers):
+        consts[f'W{i}'] = np.asarray(W, np.float64).T
+        consts[f'b{i}'] = np.asarray(b, np.float64)
+        nodes.append(('MatMul', [cur, f'W{i}'], [f'mm{i}'], {}))
+        nodes.append(('Add', [f'mm{i}', f'b{i}'], [f'add{i}'], {}))
+        cur = f'add{i}'
+        if i < len(layers) - 1:
+            nodes.append(('Relu', [cur], [f'relu{i}'], {}))
+            cur = f'relu{i}'
+    return OnnxGraph(nodes, consts, 'input', list(input_shape), cur)
