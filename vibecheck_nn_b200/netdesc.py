@@ -5,8 +5,9 @@ are lowered here to the packed layouts the kernels read:
 
 * ``MlpDesc`` -- an fc/relu chain: fc weights back to back (layer l row-major
   ``(n_{l+1}, n_l)``), biases back to back, plus a ``vcb_mlp`` ctypes struct.
-  ``reshape`` ops are identities; a single-input ``add``/``sub`` with a bias
-  vector right after an fc is folded into that fc's bias.
+  ``reshape`` ops are identities, and so is an all-zero ``add``/``sub`` of
+  the input; a single-input ``add``/``sub`` with a bias vector right after
+  an fc is folded into that fc's bias.
 
 Anything else raises ``NotImplementedError`` -- the exception type the
 reference's callers already treat as "route elsewhere"
@@ -97,6 +98,9 @@ def lower_mlp(gg):
             expect_fc = True
         elif t == 'reshape':
             pass
+        elif t in ('add', 'sub') and not op.get('is_merge') and not layers \
+                and op.get('bias') is not None and not np.any(_as_np(op['bias'])):
+            pass  # a zero offset of the input (ACAS Xu's input_Sub): exact identity
         elif t in ('add', 'sub') and not op.get('is_merge') and not expect_fc \
                 and op.get('bias') is not None:
             bias = _as_np(op['bias']).reshape(-1)
