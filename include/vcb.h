@@ -130,6 +130,38 @@ int vcb_mlp_flirpa(const vcb_mlp* net, int32_t B, int32_t K, const float* xl,
                    const float* spec_W, float* spec_A, float* spec_b, float* lb,
                    float* A_lo, float* A_up, float* b_lo, float* b_up, void* stream);
 
+/* Leaf fate of one multi-subbox BaB batch (verify_graph.py:11640-11802).
+ * Leaf b of B (boxes xl/xh, B x n_in; sub-box sub[b]) with the forward-LiRPA
+ * outputs of vcb_mlp_flirpa over the K varying dimensions var_idx (spec_A
+ * B x Q x K, spec_b and lb B x Q) and the per-sub-box query bias sub_bias
+ * (n_sub x Q):
+ *   fate[b] = 0  some query has lb + bias > 0 (safe);
+ *             1  clip_iters rounds of _clip_input_domain (:11121-11177) over
+ *                the varying dimensions leave an empty box (safe);
+ *             2  to split: out_xl/out_xh hold the clipped box and score the
+ *                smart-branching score of every input dimension (-inf where
+ *                the dimension does not vary or is <= 1e-12 wide);
+ *   fate[B] = the largest number of dimensions wider than 1e-12 among the
+ *             leaves to split (0 when none).
+ * Rows with fate 0 / 1 leave out_xl/out_xh/score unwritten.  K <= 32, Q <= 64. */
+int vcb_multisub_fate(int32_t B, int32_t n_in, int32_t K, int32_t Q, const float* xl,
+                      const float* xh, const int32_t* var_idx, const float* spec_A,
+                      const float* spec_b, const float* lb, const float* sub_bias,
+                      const int32_t* sub, int32_t clip_iters, int32_t* fate, float* out_xl,
+                      float* out_xh, float* score, void* stream);
+
+/* Children of the U leaves rows[0..U) of a multi-subbox batch
+ * (verify_graph.py:11804-11852): each leaf ranks its dimensions by score
+ * (B x n_in) in CPU torch.topk order, bisects the first k of them that are
+ * wider than 1e-12 and writes its 2^k children (bit j of the child index set
+ * = high half of the j-th ranked dimension) to rows u 2^k .. (u+1) 2^k - 1 of
+ * kid_xl/kid_xh (U 2^k x n_in), with kid_sub = sub[rows[u]].  workspace holds
+ * vcb_multisub_emit_workspace(U, n_in, k) bytes.  k <= 16. */
+int64_t vcb_multisub_emit_workspace(int32_t U, int32_t n_in, int32_t k);
+int vcb_multisub_emit(int32_t U, int32_t n_in, int32_t k, const int32_t* rows, const float* xl,
+                      const float* xh, const float* score, const int32_t* sub, void* workspace,
+                      float* kid_xl, float* kid_xh, int32_t* kid_sub, void* stream);
+
 /* Allocation-free variant of vcb_mlp_crown (no counterpart in the
  * reference).  For callers that cannot allocate device memory while they
  * bound boxes -- a host application whose memory pool already owns the GPU,

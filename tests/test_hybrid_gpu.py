@@ -1,9 +1,9 @@
 """GPU parity of the freeze-replay hybrid pipeline (verify_hybrid_acasxu.py:
 164-539) against outcomes recorded from the reference on CPU
 (tests/golden/make_golden.py --only hybrid): verdict, phase and the BaB
-counters, plus the per-query alpha machinery it needs (seeded backward with
-per-row slopes and their gradient, input-linear outputs with alpha
-gradients)."""
+counters, plus the pieces it is built from: the per-row slope gradient of
+the seeded layer bound, replay of several slope groups in one batch, and the
+freeze's device-side early stop."""
 import types
 
 import numpy as np
@@ -11,7 +11,7 @@ import pytest
 import torch
 
 from conftest import golden_script, load_golden
-from vibecheck_nn_b200 import hybrid, ops, workloads as wk
+from vibecheck_nn_b200 import hybrid, workloads as wk
 from vibecheck_nn_b200.bab import LinearSpec
 
 pytestmark = pytest.mark.gpu
@@ -50,61 +50,100 @@ def test_verify_hybrid_matches_reference(tag):
         assert abs(res['bab_iters'] - int(G[f'{tag}_bab_iters'])) <= 1
 
 
-def test_per_query_alpha_gradient_matches_finite_differences():
-    """d sum(lb) / d alpha for (B, Q, n) slopes on the seeded backward."""
-    _, gg, _, spec, _ = _problem('unsat0')
-    xl = torch.as_tensor(spec.x_lo, device=DEV, dtype=torch.float32)[None].repeat(3, 1)
-    xh = torch.as_tensor(spec.x_hi, device=DEV, dtype=torch.float32)[None].repeat(3, 1)
-    xh[1] = xl[1] + (xh[1] - xl[1]) * 0.5
-    xh[2] = xl[2] + (xh[2] - xl[2]) * 0.25
+def _boxes(spec, fracs):
+    xl = torch.as_tensor(spec.x_lo, device=DEV, dtype=torch.float32)[None].repeat(len(fracs), 1)
+    xh = torch.as_tensor(spec.x_hi, device=DEV, dtype=torch.float32)[None].repeat(len(fracs), 1)
+    for i, f in enumerate(fracs):
+        xh[i] = xl[i] + (xh[i] - xl[i]) * f
+    return xl.contiguous(), xh.contiguous()
+
+
+def test_seeded_head_gradient_matches_finite_differences():
+    """d sum(lb) / d alpha for per-row slopes (B, 2 n_L, n_k) on the network
+    cut after fc layer L with the rows [I; -I] -- the freeze's layer stage."""
     from vibecheck_nn_b200.interm import _forward_zonotope_graph_batched
+    from vibecheck_nn_b200.wide import wide_alpha_grad, wide_crown, wide_net
+    layers, gg, _, spec, _ = _problem('unsat0')
+    xl, xh = _boxes(spec, (1.0, 0.5, 0.25))
     sb, _ = _forward_zonotope_graph_batched(xl, xh, gg, DEV, torch.float32)
     L = 2
     n = sb[L][0].shape[1]
-    seed, acc = hybrid._layer_seeds(gg, n, 3, DEV, torch.float32)
-    feed = [op for op in gg['ops'] if op['type'] == 'relu' and op.get('layer_idx') == L][0]['inputs'][0]
+    head = hybrid._Head(wide_net(gg, DEV), L)
+    W_q, b_q = hybrid._seed_rows(n, DEV)
     g = torch.Generator(device=DEV).manual_seed(0)
-    alpha = {k: torch.rand((3, 2 * n, sb[k][0].shape[1]), generator=g, device=DEV).requires_grad_(True)
+    alpha = {k: torch.rand((3, 2 * n, sb[k][0].shape[1]), generator=g, device=DEV)
              for k in range(L)}
-    lb = ops._spec_backward_graph_batched(sb, xl, xh, gg, None, DEV, torch.float32,
-                                          alpha_at_layer=alpha, seed_ew_at={feed: seed},
-                                          seed_acc=acc)
-    lb.sum().backward()
-    # the same bounds through the shared-memory kernel with the slopes of one row
-    with torch.no_grad():
-        for k in range(L):
-            for (b, q) in ((0, 3), (2, 71)):
-                unstable = (sb[k][0][b] < 0) & (sb[k][1][b] > 0)
-                j = int(torch.nonzero(unstable)[0]) if bool(unstable.any()) else 0
-                h = 1e-2
-                a_p = {kk: v.detach().clone() for kk, v in alpha.items()}
-                a_m = {kk: v.detach().clone() for kk, v in alpha.items()}
-                a_p[k][b, q, j] += h
-                a_m[k][b, q, j] -= h
-                f = [ops._spec_backward_graph_batched(sb, xl, xh, gg, None, DEV, torch.float32,
-                                                      alpha_at_layer=a, seed_ew_at={feed: seed},
-                                                      seed_acc=acc).sum().double()
-                     for a in (a_p, a_m)]
-                fd = float((f[0] - f[1]) / (2 * h))
-                assert abs(float(alpha[k].grad[b, q, j]) - fd) <= 2e-3 * max(1.0, abs(fd)), \
-                    (k, b, q, j, float(alpha[k].grad[b, q, j]), fd)
+    lb, contrib = wide_alpha_grad(head, xl, xh, sb, W_q, b_q, alpha)
+    # sound: the rows bound the pre-activations of layer L on samples
+    rng = np.random.default_rng(0)
+    lo, hi = xl.cpu().numpy().astype(np.float64), xh.cpu().numpy().astype(np.float64)
+    pts = lo[:, None] + (hi - lo)[:, None] * rng.random((3, 512, lo.shape[1]))
+    z = pts
+    for i, (W, b) in enumerate(layers[:L + 1]):
+        z = z @ np.asarray(W, np.float64).T + np.asarray(b, np.float64)
+        if i < L:
+            z = np.maximum(z, 0)
+    lbn = lb.double().cpu().numpy()
+    assert (lbn[:, None, :n] <= z + 1e-4).all() and (-lbn[:, None, n:] >= z - 1e-4).all()
+    for k in range(L):
+        dc, ldc = contrib[k]
+        for (b, q) in ((0, 3), (2, 2 * n - 5)):
+            unstable = (sb[k][0][b] < 0) & (sb[k][1][b] > 0)
+            if not bool(unstable.any()):
+                continue
+            j = int(torch.nonzero(unstable)[0])
+            h = 1e-2
+            f = []
+            for sgn in (1, -1):
+                a2 = {kk: v.clone() for kk, v in alpha.items()}
+                a2[k][b, q, j] += sgn * h
+                f.append(wide_crown(head, xl, xh, sb, W_q, b_q, alpha=a2)['lb'].double().sum())
+            fd = float((f[0] - f[1]) / (2 * h))
+            got = float(dc.view(3 * 2 * n, ldc)[b * 2 * n + q, j])
+            assert abs(got - fd) <= 2e-3 * max(1.0, abs(fd)), (k, b, q, j, got, fd)
 
 
-def test_input_linear_with_alpha_gradient():
+def test_replay_groups_are_independent_rows():
+    """One replay over leaves of two slope groups gives every leaf the bounds
+    (and A) of a per-group replay, bit for bit: the bounds, the Adam steps and
+    the best-of rules act row by row."""
     _, gg, _, spec, _ = _problem('unsat0')
-    xl = torch.as_tensor(spec.x_lo, device=DEV, dtype=torch.float32)[None].repeat(2, 1)
-    xh = torch.as_tensor(spec.x_hi, device=DEV, dtype=torch.float32)[None].repeat(2, 1)
-    sb = ops._ibp_forward_graph_batched(xl, xh, gg, DEV, torch.float32)
+    xl, xh = _boxes(spec, (0.5, 0.25))
+    W_s = torch.tensor([[-1.0, 1.0, 0, 0, 0]], device=DEV)
+    spec_ew = {0: (W_s[0], 0.0)}
+    tight, alpha_layer, alpha_spec, _ = hybrid._full_freeze(xl, xh, gg, spec_ew, DEV,
+                                                            torch.float32, 20, 20)
+    xb = torch.cat([xl, xl + (xh - xl) * 0.25])
+    hb = torch.cat([xh, xl + (xh - xl) * 0.75])
+    gid = torch.tensor([0, 1, 1, 0], device=DEV)
+    from vibecheck_nn_b200.wide import wide_net
+    best, A = hybrid._replay(wide_net(gg, DEV), gg, xb, hb, W_s, torch.zeros(1, device=DEV),
+                             alpha_layer, alpha_spec, gid, 10, 0.1, want_A=True)
+    for i, gi in enumerate(gid.tolist()):
+        lay = {L: {k: a[gi:gi + 1] for k, a in g.items()} for L, g in alpha_layer.items()}
+        spc = {k: a[gi:gi + 1] for k, a in alpha_spec.items()}
+        b1, A1 = hybrid._replay_batched(xb[i:i + 1], hb[i:i + 1], gg, spec_ew, lay, spc, DEV,
+                                        torch.float32)
+        assert torch.equal(b1[0], best[i]) and torch.equal(A1[0], A[i]), i
+
+
+def test_freeze_tightens_layers_and_stops_early():
+    """The freeze never loosens a layer's zonotope bounds, stops its Adam
+    stages on the device flag (the early-stop rule) and returns per-row
+    slopes in [0, 1]."""
+    from vibecheck_nn_b200.interm import _forward_zonotope_graph_batched
+    _, gg, _, spec, _ = _problem('unsat0')
+    xl, xh = _boxes(spec, (1.0, 0.5))
     spec_ew = {0: (torch.tensor([-1.0, 1.0, 0, 0, 0], device=DEV), 0.0)}
-    alpha = {L: torch.full((2, 1, lo.shape[1]), 0.5, device=DEV).requires_grad_(True)
-             for L, (lo, _) in sb.items()}
-    lb, A, acc = ops._spec_backward_graph_batched(sb, xl, xh, gg, spec_ew, DEV, torch.float32,
-                                                  alpha_at_layer=alpha,
-                                                  return_input_linear=True)
-    lb2 = ops._spec_backward_graph_batched(sb, xl, xh, gg, spec_ew, DEV, torch.float32,
-                                           alpha_at_layer={L: a.detach() for L, a in alpha.items()})
-    assert torch.allclose(lb, lb2)
-    conc = acc + (A.clamp(min=0) * xl[:, None]).sum(-1) + (A.clamp(max=0) * xh[:, None]).sum(-1)
-    assert torch.allclose(conc, lb, rtol=1e-5, atol=1e-5)
-    (-lb.sum()).backward()
-    assert all(a.grad is not None for a in alpha.values())
+    sb, _ = _forward_zonotope_graph_batched(xl, xh, gg, DEV, torch.float32)
+    tight, alpha_layer, alpha_spec, best = hybrid._full_freeze(xl, xh, gg, spec_ew, DEV,
+                                                               torch.float32, 100, 100)
+    for L, (lo, hi) in tight.items():
+        assert (lo >= sb[L][0]).all() and (hi <= sb[L][1]).all() and (lo <= hi).all()
+        for k, a in alpha_layer[L].items():
+            assert a.shape == (2, 2 * lo.shape[1], tight[k][0].shape[1])
+            assert float(a.min()) >= 0 and float(a.max()) <= 1
+    assert best.shape == (2, 1) and set(alpha_spec) == set(tight)
+    steps = [int(t) for t in hybrid.last_stats['stage_steps']]
+    assert len(steps) == len(tight) and all(1 <= s <= 100 for s in steps)
+    assert min(steps) < 100, steps  # some stage met the 1e-6 rule

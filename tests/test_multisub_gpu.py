@@ -58,17 +58,49 @@ def test_forward_linear_bounds_match_reference():
     assert (lb.cpu().numpy()[:, None, :] <= y + 1e-5).all()
 
 
-def test_clip_input_domain_is_sound_and_shrinks():
-    g = torch.Generator(device=DEV).manual_seed(0)
-    B, S, K = 64, 3, 4
-    xl = torch.rand((B, K), generator=g, device=DEV)
-    xh = xl + torch.rand((B, K), generator=g, device=DEV)
-    lA = torch.randn((B, S, K), generator=g, device=DEV)
-    lb = torch.randn((B, S), generator=g, device=DEV)
-    cl, ch = multisub._clip_input_domain(xl, xh, lA, lb, num_iters=2)
-    assert (cl >= xl).all() and (ch <= xh).all()
-    # every removed point is verified by some query (its linear bound >= 0)
-    pts = xl[:, None] + (xh - xl)[:, None] * torch.rand((B, 512, K), generator=g, device=DEV)
-    inside = ((pts >= cl[:, None]) & (pts <= ch[:, None])).all(-1)
-    val = torch.einsum('bsk,bpk->bps', lA, pts) + lb[:, None]
-    assert (val[~inside].max(dim=-1).values >= -1e-4).all()
+def _fate_problem(seed, B=512, n=8, Q=3, nsub=4):
+    rng = np.random.default_rng(seed)
+    var = np.array([0, 1, 3, 4, 6, 7])
+    xl = rng.random((B, n), np.float32)
+    xh = xl + rng.random((B, n), np.float32)
+    xh[:, [2, 5]] = xl[:, [2, 5]]
+    xh[::7, 1] = xl[::7, 1]  # a varying dimension that is degenerate in some leaves
+    A = rng.standard_normal((B, Q, var.size)).astype(np.float32)
+    sb = (rng.standard_normal((B, Q)) * 2 - 1).astype(np.float32)
+    lb = sb.copy()
+    for k, d in enumerate(var):
+        a = A[:, :, k]
+        lb += np.maximum(a, 0) * xl[:, None, d] + np.minimum(a, 0) * xh[:, None, d]
+    bias = (rng.standard_normal((nsub, Q)) * 0.3).astype(np.float32)
+    sub = rng.integers(0, nsub, B).astype(np.int32)
+    return xl, xh, var, A, sb, lb, bias, sub
+
+
+def _same(a, b):
+    return np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.parametrize('seed', [0, 1, 2])
+def test_leaf_fate_and_children_match_the_oracle_bitwise(seed):
+    """vcb_multisub_fate / vcb_multisub_emit against the numpy restatement
+    of the reference's tensor expressions: fates, clipped boxes, scores and
+    children bit for bit."""
+    from oracle import multisub as oms
+    prob = _fate_problem(seed)
+    xl, xh, var, A, sb, lb, bias, sub = prob
+    T = [torch.as_tensor(v, device=DEV) for v in prob]
+    T[2] = T[2].to(torch.int32)
+    fate, lo, hi, sc = multisub.leaf_fate(*T, clip_iters=2)
+    fo, loo, hio, sco = oms.leaf_fate(*prob, clip_iters=2)
+    fate = fate.cpu().numpy()
+    assert fate.tolist() == fo.tolist()
+    assert set(fo[:-1].tolist()) == {0, 1, 2}
+    s = np.nonzero(fo[:-1] == 2)[0]
+    for got, want in ((lo, loo), (hi, hio), (sc, sco)):
+        assert _same(got.cpu().numpy()[s], want[s])
+    for k in (1, 2, 3):
+        rows = torch.as_tensor(s.astype(np.int32), device=DEV)
+        kid = multisub.emit_children(rows, lo, hi, sc, T[7], k)
+        want = oms.emit_children(s, loo, hio, sco, sub, k)
+        for g, w in zip(kid, want):
+            assert np.array_equal(g.cpu().numpy(), w), k

@@ -57,6 +57,10 @@ SIGNATURES = {
     'vcb_fault_check': [_P],
     'vcb_mlp_flirpa': [ctypes.POINTER(VcbMlp), _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P,
                        _P, _P, _P, _P],
+    'vcb_multisub_fate': [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P,
+                          _P],
+    'vcb_multisub_emit': [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    'vcb_multisub_emit_workspace': [_I, _I, _I],
     'vcb_mlp_crown_noalloc': [ctypes.POINTER(VcbMlp), _I, _P, _P, _P, _P, _P,
                               _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P],
     'vcb_mlp_crown_noalloc_capacity': [],
@@ -129,7 +133,8 @@ RESTYPES = {'vcb_last_error': ctypes.c_char_p,
             'vcb_mlp_crown_noalloc_capacity': ctypes.c_size_t,
             'vcb_conv_back_workspace': ctypes.c_size_t,
             'vcb_bab_step_wide_workspace': ctypes.c_size_t,
-            'vcb_zw_colsum_workspace': ctypes.c_size_t}
+            'vcb_zw_colsum_workspace': ctypes.c_size_t,
+            'vcb_multisub_emit_workspace': ctypes.c_int64}
 
 _lib = None
 

@@ -12,11 +12,16 @@ dimensions):
   dimensions and the spec rows (``vcb_mlp_flirpa``); a leaf is safe when any
   of its sub-box's queries has a positive margin (lower bound + the sub-box's
   query bias); a sub-box closes when its last live leaf is safe;
-* unsafe leaves are clipped twice (``_clip_input_domain``,
-  verify_graph.py:11121-11177); a leaf clipped to an empty box is safe;
-* the rest split on their top K (``bab_split_depth``, at most the number of
-  non-degenerate dimensions) smart-branching dimensions at once, 2^K
-  children each, appended to the worklist.
+* one kernel (``vcb_multisub_fate``) decides every leaf of the batch: safe
+  by its bound, safe because two rounds of input-domain clipping
+  (``_clip_input_domain``, verify_graph.py:11121-11177) leave an empty box,
+  or to split, with its clipped box and smart-branching scores;
+* a second (``vcb_multisub_emit``) ranks the dimensions of the leaves to
+  split in CPU torch.topk order and writes their children: the top K
+  (``bab_split_depth``, at most the number of non-degenerate dimensions)
+  dimensions at once, 2^K children per leaf, appended to the worklist.
+  One device-to-host copy per iteration (the fates) keeps the per-sub-box
+  live-leaf counts on the host.
 
 Networks the forward-LiRPA kernel does not take (widths > 64, more than 31
 varying dimensions) use the zonotope + CROWN bounds per query and split on
@@ -66,28 +71,53 @@ def forward_linear_spec(desc, xl, xh, var_idx, W_q, want_bounds=False):
     return res + tuple(outs) if want_bounds else res
 
 
-def _clip_input_domain(x_L, x_U, lA, lbias, num_iters=1):
-    """Closed-form input-domain shrinking (verify_graph.py:11121-11177): for
-    every dimension k and query j, the point where the query's linear lower
-    bound (other dimensions at their worst) crosses 0; the part of the box
-    beyond it is verified by that query and dropped, minimum over queries."""
-    x_L = x_L.clone()
-    x_U = x_U.clone()
-    for _ in range(num_iters):
-        xhat = (x_U + x_L) / 2
-        eps = (x_U - x_L) / 2
-        lA_pos = lA.clamp(min=0)
-        lA_neg = lA.clamp(max=0)
-        dm_lb = (lA_pos * x_L.unsqueeze(1) + lA_neg * x_U.unsqueeze(1)).sum(dim=2) + lbias
-        contrib = lA * xhat.unsqueeze(1) - lA.abs() * eps.unsqueeze(1)
-        concrete_minus_one = dm_lb.unsqueeze(2) - contrib
-        denom = torch.where(lA.abs() > 1e-30, lA, torch.ones_like(lA))
-        curr_x = -concrete_minus_one / denom
-        x_U_cand = torch.where(lA > 0, curr_x, torch.full_like(curr_x, float('inf')))
-        x_L_cand = torch.where(lA < 0, curr_x, torch.full_like(curr_x, float('-inf')))
-        x_U = torch.min(x_U_cand.amin(dim=1), x_U)
-        x_L = torch.max(x_L_cand.amax(dim=1), x_L)
-    return x_L, x_U
+def leaf_fate(xl, xh, var_idx, spec_A, spec_b, lb, sub_bias, sub, clip_iters=2):
+    """``vcb_multisub_fate``: (fate, box_lo, box_hi, score) of a batch.
+
+    ``fate`` (B + 1, int32, on the device): 0 safe by its bound, 1 safe by
+    the input-domain clip (``_clip_input_domain``, verify_graph.py:11121-11177,
+    ``clip_iters`` rounds), 2 to split; ``fate[B]`` is the largest number of
+    dimensions wider than 1e-12 among the leaves to split.  For those leaves
+    ``box_lo``/``box_hi`` hold the clipped box and ``score`` the smart-branching
+    score of every input dimension (verify_graph.py:11780-11802)."""
+    dev = xl.device
+    B, n = xl.shape
+    K = int(var_idx.numel())
+    Q = lb.shape[1]
+    fate = torch.empty(B + 1, dtype=torch.int32, device=dev)
+    box_lo = torch.empty((B, n), dtype=F32, device=dev)
+    box_hi = torch.empty((B, n), dtype=F32, device=dev)
+    score = torch.empty((B, n), dtype=F32, device=dev)
+    P = _lib.ptr
+    rc = _lib.lib().vcb_multisub_fate(B, n, K, Q, P(xl.contiguous()), P(xh.contiguous()),
+                                      P(var_idx), P(spec_A), P(spec_b), P(lb),
+                                      P(sub_bias.contiguous()), P(sub), int(clip_iters),
+                                      P(fate), P(box_lo), P(box_hi), P(score),
+                                      _lib.stream_of(dev))
+    _lib.check(rc, 'vcb_multisub_fate')
+    return fate, box_lo, box_hi, score
+
+
+def emit_children(rows, xl, xh, score, sub, k):
+    """``vcb_multisub_emit``: the 2^k children of each batch row in ``rows``
+    (int32, on the device), leaf by leaf, split on its top-k dimensions by
+    ``score`` in CPU torch.topk order (verify_graph.py:11804-11852).  Returns
+    (kid_xl, kid_xh, kid_sub)."""
+    dev = xl.device
+    U = int(rows.numel())
+    n = xl.shape[1]
+    kid_xl = torch.empty((U << k, n), dtype=F32, device=dev)
+    kid_xh = torch.empty((U << k, n), dtype=F32, device=dev)
+    kid_sub = torch.empty(U << k, dtype=torch.int32, device=dev)
+    lib = _lib.lib()
+    ws = torch.empty(max(1, int(lib.vcb_multisub_emit_workspace(U, n, k))), dtype=torch.uint8,
+                     device=dev)
+    P = _lib.ptr
+    rc = lib.vcb_multisub_emit(U, n, k, P(rows), P(xl.contiguous()), P(xh.contiguous()),
+                               P(score.contiguous()), P(sub), P(ws), P(kid_xl), P(kid_xh),
+                               P(kid_sub), _lib.stream_of(dev))
+    _lib.check(rc, 'vcb_multisub_emit')
+    return kid_xl, kid_xh, kid_sub
 
 
 def _sub_queries(group, n_out):
@@ -138,47 +168,56 @@ def _multi_sub_input_split_bab(sub_idx_list, groups, order, gg, device, dtype, t
                            .astype(np.float64), dtype=F32, device=device)
     xh_t = torch.as_tensor(np.stack([groups[order[ki]][1] for ki in sub_idx_list])
                            .astype(np.float64), dtype=F32, device=device)
-    sub_idx_t = torch.as_tensor(sub_idx_list, dtype=torch.long, device=device)
+    sub_idx_t = torch.as_tensor(sub_idx_list, dtype=torch.int32, device=device)
     batch_size = int(getattr(settings, 'input_split_batch_size', 1024))
     K_max = int(getattr(settings, 'bab_split_depth', 4))
     live = {int(ki): 1 for ki in sub_idx_list}
+    open_sub = torch.zeros(bias_np.shape[0], dtype=torch.bool, device=device)
+    open_sub[sub_idx_t.long()] = True
     try:
         desc = mlp_desc(gg, device)
     except _lib.UnsupportedInput:
         desc = None
     n_iters = 0
     n_visited = 0
+    newly_closed = []
+
+    def retire(rows, si_h):
+        for i in rows:
+            sk = si_h[i]
+            live[sk] -= 1
+            if live[sk] == 0:
+                closed.add(sk)
+                newly_closed.append(sk)
+
     while xl_t.shape[0] > 0:
         if time.perf_counter() - t0 > total_budget:
             break
-        B = min(batch_size, xl_t.shape[0])
-        keep = torch.as_tensor([live.get(int(s), 0) > 0 for s in sub_idx_t.tolist()],
-                               device=device)
-        if not bool(keep.all()):
+        if newly_closed:
+            # leaves of closed sub-boxes leave the worklist
+            open_sub[torch.as_tensor(newly_closed, dtype=torch.long, device=device)] = False
+            newly_closed.clear()
+            keep = open_sub[sub_idx_t.long()]
             xl_t, xh_t, sub_idx_t = xl_t[keep], xh_t[keep], sub_idx_t[keep]
-            B = min(batch_size, xl_t.shape[0])
-            if B == 0:
+            if xl_t.shape[0] == 0:
                 break
+        B = min(batch_size, xl_t.shape[0])
         xl_b, xh_b, si_b = xl_t[:B], xh_t[:B], sub_idx_t[:B]
         # varying dimensions of this batch (the forward LiRPA's compression)
         varying = (((xh_b - xl_b) / 2).abs().max(dim=0).values > 0)
         var_idx = varying.nonzero(as_tuple=True)[0].to(torch.int32)
         lirpa = None
-        if desc is not None:
+        if desc is not None and var_idx.numel() > 0:
             try:
                 lirpa = forward_linear_spec(desc, xl_b, xh_b, var_idx, W_q)
             except (_lib.UnsupportedInput, torch.cuda.OutOfMemoryError):
                 # the reference falls back on these (verify_graph.py:11458); a
                 # KernelError is a fault and propagates
                 lirpa = None
-        clip_lA = clip_lbias = margins = None
         if lirpa is not None:
             spec_A, spec_b, lbs = lirpa
-            biases = bias_table[si_b]
-            margins = lbs + biases
-            safe = (margins > 0).any(dim=1)
-            clip_lA, clip_lbias = spec_A, spec_b + biases
-            xl_c, xh_c = xl_b[:, varying], xh_b[:, varying]
+            fate_d, box_lo, box_hi, score = leaf_fate(xl_b, xh_b, var_idx, spec_A, spec_b, lbs,
+                                                      bias_table, si_b, clip_iters=2)
         else:
             from .interm import _forward_zonotope_graph_batched
             from .ops import _spec_backward_graph_batched
@@ -187,88 +226,28 @@ def _multi_sub_input_split_bab(sub_idx_list, groups, order, gg, device, dtype, t
             for qi in range(max_q):
                 lbs_q = _spec_backward_graph_batched(sb, xl_b, xh_b, gg, {0: (W_q[qi], 0.0)},
                                                      device, dtype)[:, 0]
-                safe |= (lbs_q + bias_table[si_b, qi]) > 0
+                safe |= (lbs_q + bias_table[si_b.long(), qi]) > 0
+            # widest dimensions (verify_graph.py:11816)
+            box_lo, box_hi, score = xl_b, xh_b, xh_b - xl_b
+            nz = ((score > 1e-12).sum(dim=1) * (~safe)).max().reshape(1)
+            fate_d = torch.cat([torch.where(safe, 0, 2), nz]).to(torch.int32)
+        fate = fate_d.cpu().numpy()
         n_visited += B
         si_h = si_b.tolist()
-        for i in np.nonzero(safe.cpu().numpy())[0].tolist():
-            sk = si_h[i]
-            live[sk] -= 1
-            if live[sk] == 0:
-                closed.add(sk)
-        unsafe_idx = (~safe).nonzero(as_tuple=True)[0]
+        retire(np.nonzero(fate[:B] == 0)[0].tolist(), si_h)
+        retire(np.nonzero(fate[:B] == 1)[0].tolist(), si_h)
+        split = np.nonzero(fate[:B] == 2)[0]
         rest_xl, rest_xh, rest_si = xl_t[B:], xh_t[B:], sub_idx_t[B:]
-        if clip_lA is not None and unsafe_idx.numel() > 0:
-            xl_cl, xh_cl = _clip_input_domain(xl_c[unsafe_idx], xh_c[unsafe_idx],
-                                              clip_lA[unsafe_idx], clip_lbias[unsafe_idx],
-                                              num_iters=2)
-            vfull = varying.nonzero(as_tuple=True)[0]
-            rows = unsafe_idx.unsqueeze(1).expand(-1, vfull.numel())
-            cols = vfull.unsqueeze(0).expand(unsafe_idx.numel(), -1)
-            xl_b = xl_b.clone()
-            xh_b = xh_b.clone()
-            xl_b[rows, cols] = xl_cl
-            xh_b[rows, cols] = xh_cl
-            newly = (xl_b[unsafe_idx] > xh_b[unsafe_idx]).any(dim=1)
-            if bool(newly.any()):
-                safe = safe.clone()
-                add = unsafe_idx[newly]
-                safe[add] = True
-                for ai in add.tolist():
-                    sk = si_h[ai]
-                    live[sk] -= 1
-                    if live[sk] == 0:
-                        closed.add(sk)
-                unsafe_idx = (~safe).nonzero(as_tuple=True)[0]
-        if unsafe_idx.numel() > 0:
+        if split.size:
             n_in = xl_b.shape[1]
-            xl_u, xh_u, si_u = xl_b[unsafe_idx], xh_b[unsafe_idx], si_b[unsafe_idx]
-            widths = xh_u - xl_u
-            n_u = xl_u.shape[0]
-            nz = (widths > 1e-12).sum(dim=1)
-            K_eff = max(1, int(min(K_max, int(nz.max().item()), n_in)))
-            if clip_lA is not None:
-                lA_u = clip_lA[unsafe_idx]
-                wK = xh_c[unsafe_idx] - xl_c[unsafe_idx]
-                score = (lA_u.abs().clamp(min=0.1) * wK.unsqueeze(1) * 0.5
-                         + margins[unsafe_idx].unsqueeze(-1) * 1.0)
-                sb_score = score.amax(dim=1)
-                sb_full = torch.full((n_u, n_in), float('-inf'), dtype=F32, device=device)
-                sb_full[:, varying.nonzero(as_tuple=True)[0]] = sb_score
-                sb_full = torch.where(widths > 1e-12, sb_full, torch.full_like(sb_full,
-                                                                               float('-inf')))
-                # ranked on the host: tie order as the reference's CPU topk
-                top = torch.topk(sb_full.cpu(), K_eff, dim=1).indices.to(device)
-            else:
-                top = torch.topk(widths.cpu(), K_eff, dim=1).indices.to(device)
-            xl_top, xh_top = xl_u.gather(1, top), xh_u.gather(1, top)
-            mids = (xl_top + xh_top) * 0.5
-            usable = (xh_top - xl_top) > 1e-12
-            n_ch = 1 << K_eff
-            combos = torch.arange(n_ch, device=device)
-            bits = (combos.unsqueeze(-1) >> torch.arange(K_eff, device=device)) & 1
-            xl_e = xl_u.unsqueeze(1).expand(-1, n_ch, -1).contiguous()
-            xh_e = xh_u.unsqueeze(1).expand(-1, n_ch, -1).contiguous()
-            leaf_ax = torch.arange(n_u, device=device).unsqueeze(1).expand(-1, n_ch)
-            child_ax = combos.unsqueeze(0).expand(n_u, -1)
-            for k in range(K_eff):
-                dim_k = top[:, k:k + 1].expand(-1, n_ch)
-                mid_k = mids[:, k:k + 1].expand(-1, n_ch)
-                use_k = usable[:, k:k + 1].expand(-1, n_ch)
-                bit_k = bits[:, k].unsqueeze(0).expand(n_u, -1).bool()
-                hi_m = bit_k & use_k
-                lo_m = (~bit_k) & use_k
-                if bool(hi_m.any()):
-                    xl_e[leaf_ax[hi_m], child_ax[hi_m], dim_k[hi_m]] = mid_k[hi_m]
-                if bool(lo_m.any()):
-                    xh_e[leaf_ax[lo_m], child_ax[lo_m], dim_k[lo_m]] = mid_k[lo_m]
-            xl_new = xl_e.reshape(-1, n_in)
-            xh_new = xh_e.reshape(-1, n_in)
-            si_new = si_u.unsqueeze(1).expand(-1, n_ch).reshape(-1)
-            for s_val in si_u.tolist():
-                live[int(s_val)] += n_ch - 1
-            xl_t = torch.cat([rest_xl, xl_new])
-            xh_t = torch.cat([rest_xh, xh_new])
-            sub_idx_t = torch.cat([rest_si, si_new])
+            k = max(1, min(K_max, int(fate[B]), n_in))
+            rows = torch.as_tensor(split.astype(np.int32), device=device)
+            kid_xl, kid_xh, kid_si = emit_children(rows, box_lo, box_hi, score, si_b, k)
+            for i in split.tolist():
+                live[si_h[i]] += (1 << k) - 1
+            xl_t = torch.cat([rest_xl, kid_xl])
+            xh_t = torch.cat([rest_xh, kid_xh])
+            sub_idx_t = torch.cat([rest_si, kid_si])
         else:
             xl_t, xh_t, sub_idx_t = rest_xl, rest_xh, rest_si
         n_iters += 1
