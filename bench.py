@@ -18,9 +18,14 @@ leaves of the depth-18 input-split tree of the 3072->[1024]x8->10 MLP.
 
 N > 1 runs under torchrun, one rank per GPU; every rank bounds its own
 65,536 boxes (weak scaling, no data-path collective); the time is the max
-over ranks.  ``--impl reference`` times the CPU restatement of the
-reference's algorithm (oracle/, numpy, all host cores) on a bounded sample of
-the same workload.  Prints one JSON line on rank 0.
+over ranks.  ``--impl reference`` times the reference's own CPU path
+(its torch code, installed under baseline/_ref by ``pip install --target``)
+in one single-threaded process per host core on a bounded sample of the same
+workload, or the numpy restatement in oracle/ when the reference is not
+installed.  The default cfg2 line also carries a ``cfg1`` record: the
+input-split BaB time-to-verdict on this GPU and the reference's own CPU
+driver on the same problem at 1 thread and at a thread per core.  Prints one
+JSON line on rank 0.
 """
 from __future__ import annotations
 
@@ -53,74 +58,166 @@ def parse():
     ap.add_argument('--config', default='cfg2', choices=['cfg2', 'cfg1', 'cfg3', 'cfg4', 'cfg5'],
                     help='cfg2 (default) is the headline; the others time the '
                          'remaining BASELINE configs on their own metrics')
+    ap.add_argument('--full', action='store_true',
+                    help='cfg5: the whole input-split BaB through the sharded driver '
+                         '(worklist bound 262,144 leaves) instead of single iterations')
     return ap.parse_args()
 
 
 # ---------------------------------------------------------------------------
-# CPU leg: the oracle (numpy restatement of the reference algorithm)
+# CPU legs: the reference's own torch CPU path when it is installed under
+# baseline/_ref (pip install --target of the reference), else the oracle
+# (numpy restatement of the reference algorithm)
 # ---------------------------------------------------------------------------
 
+REF_DIR = os.path.join(ROOT, 'baseline', '_ref')
 _WORKER = {}
 
 
+def reference_installed():
+    return os.path.isfile(os.path.join(REF_DIR, 'vibecheck', 'verify_graph.py'))
+
+
+def _pool_init(threads):
+    """Spawned worker: its torch / BLAS thread count, fixed before torch is
+    imported."""
+    for k in ('OMP_NUM_THREADS', 'MKL_NUM_THREADS', 'OPENBLAS_NUM_THREADS'):
+        os.environ[k] = str(threads)
+    import torch
+    torch.set_num_threads(threads)
+
+
+def _reference_modules():
+    """The installed reference's modules (gurobipy is only imported by its
+    LP/MILP code, which these paths do not reach: an empty stand-in)."""
+    import types
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    sys.modules.setdefault('gurobipy', types.ModuleType('gurobipy'))
+    from vibecheck import settings as vs, spec as vspec, verify_graph as vg, verify_zono_bnb as vz
+    return vz, vg, vs, vspec
+
+
 def _cpu_worker(args):
-    os.environ['OMP_NUM_THREADS'] = '1'
-    os.environ['OPENBLAS_NUM_THREADS'] = '1'
-    lo, hi = args
-    from oracle import bounds as ob
+    """Seconds to bound cfg2 boxes [lo, hi): 'reference' = the reference's
+    _ibp_forward_graph_batched + _spec_backward_graph_batched on the CPU
+    (verify_zono_bnb.py:1066, :4270), 'port' = oracle/bounds.py."""
+    kind, lo, hi = args
     if 'w' not in _WORKER:
         from vibecheck_nn_b200 import workloads as wk
         _WORKER['w'] = wk.cfg2(seed=0, n_boxes=N_BOXES, n_q=N_Q)
-        _WORKER['gg'] = wk.mlp_gg(_WORKER['w']['layers'])
-    w, gg = _WORKER['w'], _WORKER['gg']
+    w = _WORKER['w']
+    if kind == 'port':
+        from oracle import bounds as ob
+        if 'gg' not in _WORKER:
+            from vibecheck_nn_b200 import workloads as wk
+            _WORKER['gg'] = wk.mlp_gg(w['layers'])
+        gg = _WORKER['gg']
+        t0 = time.perf_counter()
+        sb = ob.ibp_forward_batched(w['xl'][lo:hi], w['xh'][lo:hi], gg)
+        ob.spec_backward_batched(sb, w['xl'][lo:hi], w['xh'][lo:hi], gg,
+                                 w['spec_W'], w['spec_b'])
+        return time.perf_counter() - t0
+    import torch
+    if 'ref' not in _WORKER:
+        from vibecheck_nn_b200 import workloads as wk
+        vz = _reference_modules()[0]
+        _WORKER['ref'] = (vz, wk.mlp_gg(w['layers'], 'cpu', torch.float32),
+                          wk.spec_ew_from(w['spec_W'], w['spec_b'], 'cpu'),
+                          torch.as_tensor(w['xl']), torch.as_tensor(w['xh']))
+    vz, gg, spec_ew, xl, xh = _WORKER['ref']
     t0 = time.perf_counter()
-    sb = ob.ibp_forward_batched(w['xl'][lo:hi], w['xh'][lo:hi], gg)
-    ob.spec_backward_batched(sb, w['xl'][lo:hi], w['xh'][lo:hi], gg,
-                             w['spec_W'], w['spec_b'])
+    sb = vz._ibp_forward_graph_batched(xl[lo:hi], xh[lo:hi], gg, 'cpu', torch.float32)
+    vz._spec_backward_graph_batched(sb, xl[lo:hi], xh[lo:hi], gg, spec_ew, 'cpu',
+                                    torch.float32)
     return time.perf_counter() - t0
 
 
-def cpu_rate(pool, cores, sample):
-    """Boxes/s of the oracle on `sample` boxes split over `cores` processes."""
-    per = (sample + cores - 1) // cores
-    chunks = [(i * per, min(sample, (i + 1) * per)) for i in range(cores)]
+def cpu_rate(pool, procs, sample, kind):
+    """Boxes/s of `kind` on `sample` boxes split over `procs` processes."""
+    per = (sample + procs - 1) // procs
+    chunks = [(kind, i * per, min(sample, (i + 1) * per)) for i in range(procs)]
     t0 = time.perf_counter()
     pool.map(_cpu_worker, chunks)
     return sample / (time.perf_counter() - t0)
 
 
-def make_pool():
+def make_pool(procs, threads=1, kinds=('port',)):
     import multiprocessing as mp
-    cores = os.cpu_count() or 1
-    pool = mp.get_context('spawn').Pool(cores)
-    pool.map(_cpu_worker, [(0, 64)] * cores)  # import + warm each worker
-    return pool, cores
+    pool = mp.get_context('spawn').Pool(procs, initializer=_pool_init, initargs=(threads,))
+    for kind in kinds:
+        pool.map(_cpu_worker, [(kind, 0, 64)] * procs)  # import + warm each worker
+    return pool
 
 
-def cpu_baseline(pool, cores, budget_s=12.0):
-    sample = 4096 * cores
+class CpuPools:
+    """Spawned CPU workers, started before the first GPU call: all cores as
+    single-threaded processes, one single-threaded process, and (reference
+    only) one process with a torch thread per core."""
+
+    def __init__(self):
+        self.cores = os.cpu_count() or 1
+        self.ref = reference_installed()
+        kinds = ('reference', 'port') if self.ref else ('port',)
+        self.procs = make_pool(self.cores, 1, kinds)
+        self.one = make_pool(1, 1, kinds[:1])
+        self.threaded = make_pool(1, self.cores, ('reference',)) if self.ref else None
+
+    def close(self):
+        for p in (self.procs, self.one, self.threaded):
+            if p is not None:
+                p.close()
+
+
+def _median_rate(pool, procs, sample, kind, budget_s):
     rates = []
     t0 = time.perf_counter()
     while time.perf_counter() - t0 < budget_s or len(rates) < 2:
-        rates.append(cpu_rate(pool, cores, sample))
-    return {'value': statistics.median(rates), 'unit': UNIT, 'cores': cores,
-            'kind': 'port',
-            'sample': f'{sample} of the 65,536 cfg2 boxes per repetition, '
-                      f'{len(rates)} repetitions (median), numpy oracle '
-                      f'(oracle/bounds.py) in {cores} spawn processes'}
+        rates.append(cpu_rate(pool, procs, sample, kind))
+    return statistics.median(rates), len(rates)
+
+
+def cpu_baseline(pools, budget_s=6.0):
+    """The reference's CPU throughput on cfg2 boxes: its torch path in one
+    process per core (the value), in one single-threaded process and with a
+    torch thread per core in one process, next to the numpy port."""
+    c = pools.cores
+    port, n_port = _median_rate(pools.procs, c, 4096 * c, 'port', budget_s)
+    if not pools.ref:
+        return {'value': port, 'unit': UNIT, 'cores': c, 'kind': 'port',
+                'sample': f'{4096 * c} cfg2 boxes per repetition, {n_port} repetitions '
+                          f'(median), numpy oracle (oracle/bounds.py) in {c} spawn processes; '
+                          f'the reference is not installed under baseline/_ref'}
+    procs, n1 = _median_rate(pools.procs, c, 4096 * c, 'reference', budget_s)
+    one, n2 = _median_rate(pools.one, 1, 4096, 'reference', budget_s)
+    thr, n3 = _median_rate(pools.threaded, 1, 4096 * c, 'reference', budget_s)
+    return {'value': procs, 'unit': UNIT, 'cores': c, 'kind': 'reference',
+            'sample': f'{4096 * c} cfg2 boxes per repetition, {n1} repetitions (median): the '
+                      f'reference\'s _ibp_forward_graph_batched + _spec_backward_graph_batched '
+                      f'on the CPU (torch, fp32) in {c} spawn processes of 1 thread',
+            'one_thread': {'value': one, 'sample': f'4096 boxes, {n2} repetitions'},
+            'threads_in_one_process': {'value': thr, 'threads': c,
+                                       'sample': f'{4096 * c} boxes, {n3} repetitions'},
+            'port': {'value': port, 'cores': c, 'kind': 'port',
+                     'sample': f'numpy oracle, {4096 * c} boxes, {n_port} repetitions'}}
 
 
 def run_reference(args):
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return
-    pool, cores = make_pool()
+    cores = os.cpu_count() or 1
+    kind = 'reference' if reference_installed() else 'port'
+    pool = make_pool(cores, 1, (kind,))
     sample = 4096 * cores
     for _ in range(args.warmup):
-        cpu_rate(pool, cores, sample)
-    rates = [cpu_rate(pool, cores, sample) for _ in range(args.steps)]
+        cpu_rate(pool, cores, sample, kind)
+    rates = [cpu_rate(pool, cores, sample, kind) for _ in range(args.steps)]
     pool.close()
     v = statistics.median(rates)
+    what = ("the reference's own CPU path (_ibp_forward_graph_batched + "
+            "_spec_backward_graph_batched, torch fp32, installed under baseline/_ref)"
+            if kind == 'reference' else 'the numpy oracle (oracle/bounds.py)')
     line = {
         'impl': 'reference', 'metric': METRIC, 'value': v, 'unit': UNIT,
         'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
@@ -128,10 +225,9 @@ def run_reference(args):
         'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
         'data': 'synthetic (seeded)',
         'config': config_dict(args.gpus),
-        'cpu_baseline': {'value': v, 'unit': UNIT, 'cores': cores,
-                         'kind': 'port',
-                         'sample': f'each step: {sample} cfg2 boxes, numpy '
-                                   f'oracle in {cores} spawn processes'},
+        'cpu_baseline': {'value': v, 'unit': UNIT, 'cores': cores, 'kind': kind,
+                         'sample': f'each step: {sample} cfg2 boxes, {what}, in {cores} '
+                                   f'spawn processes of 1 thread'},
         'e2e': {'value': v, 'unit': UNIT, 'h2d_bytes_per_step': 0,
                 'd2h_bytes_per_step': 0},
     }
@@ -353,9 +449,9 @@ def run_ours(args):
     rank = int(os.environ.get('RANK', '0'))
     world = int(os.environ.get('WORLD_SIZE', '1'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
-    pool = None
+    pools = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        pool, cores = make_pool()  # spawn before the first GPU call
+        pools = CpuPools()  # spawned before the first GPU call
     dev = torch.device(f'cuda:{local}')
     torch.cuda.set_device(dev)
     if world > 1:
@@ -454,10 +550,13 @@ def run_ours(args):
     achieved = N_BOXES * flop_per_box / (mean_ms * 1e-3) / 1e12
     desc = ops.mlp_desc(gg, dev)
     tc_path = bool(_lib_path(desc, N_BOXES, N_Q))
+    cfg1 = cfg1_record(dev, gpu_id) if world == 1 else None
     cpu = None
-    if pool is not None:
-        cpu = cpu_baseline(pool, cores)
-        pool.close()
+    if pools is not None:
+        cpu = cpu_baseline(pools)
+        if pools.ref:
+            cfg1.update(cfg1_reference_cpu(pools))
+        pools.close()
     if rank == 0:
         line = {
             'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world,
@@ -477,9 +576,97 @@ def run_ours(args):
         }
         if cpu is not None:
             line['cpu_baseline'] = cpu
+        if cfg1 is not None:
+            line['cfg1'] = cfg1
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def _cfg1_problem(dev):
+    from vibecheck_nn_b200 import bab, workloads as wk
+    w = wk.cfg1(0)
+    spec = bab.LinearSpec(w['xl'], w['xh'], [[('pair', 1, 0)]])
+    st = wk.reference_bab_settings(input_split_batch_size=2048,
+                                   input_split_crown_intermediate=True, total_timeout=600.0)
+    return w, spec, st, wk.mlp_gg(w['layers'], dev)
+
+
+def _cfg1_reference_worker(budget_s):
+    """Verdicts of the reference's own input-split driver on cfg1 on the CPU
+    (_input_split_batched, verify_graph.py:9947, default_settings with the
+    bench's overrides, root PGD included) for about budget_s seconds:
+    (verdict, leaves, seconds per verdict, verdicts)."""
+    import contextlib
+    import types
+    import torch
+    from vibecheck_nn_b200 import workloads as wk
+    _, vg, vs, vspec = _reference_modules()
+    w = wk.cfg1(0)
+    gg = wk.mlp_gg(w['layers'], 'cpu', torch.float32)
+    spec = vspec.VNNSpec(x_lo=w['xl'].astype('float64'), x_hi=w['xh'].astype('float64'),
+                         disjuncts=[vspec.Conjunct([vspec.PairwiseConstraint(pred=1, comp=0)])])
+    st = vs.default_settings(device='cpu', bits=32, input_split_batched_enabled=True,
+                             input_split_batch_size=2048, input_split_crown_intermediate=True,
+                             total_timeout=600.0)
+    times = []
+    t0 = time.perf_counter()
+    with open(os.devnull, 'w') as null, contextlib.redirect_stdout(null):  # progress lines
+        while not times or (time.perf_counter() - t0 < budget_s and len(times) < 5):
+            t = time.perf_counter()
+            verdict, det = vg._input_split_batched(types.SimpleNamespace(onnx_path=None), spec,
+                                                   st, gg, torch.device('cpu'), torch.float32)
+            times.append(time.perf_counter() - t)
+    return verdict, int(det.get('batched_n_leaves', -1)), statistics.median(times), len(times)
+
+
+def cfg1_record(dev, gpu_id, n_verdicts=10):
+    """cfg1 time-to-verdict on this GPU: 3 warm-up verdicts, then n_verdicts
+    timed with CUDA events, L2 flushed before each."""
+    import torch
+    from vibecheck_nn_b200 import bab
+    w, spec, st, gg = _cfg1_problem(dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        bab._input_split_batched(None, spec, st, gg, dev, torch.float32)
+    torch.cuda.synchronize(dev)
+    ms = []
+    with ClockSampler(gpu_id) as clk:
+        for _ in range(n_verdicts):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            verdict, det = bab._input_split_batched(None, spec, st, gg, dev, torch.float32)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms.append(e0.elapsed_time(e1))
+    rec = {'workload': 'cfg1: 5x[50]x6x5 MLP, y0 - y1 <= d, input-split BaB, leaf batch 2048, '
+                       'CROWN intermediates, root PGD included',
+           'verdict': verdict, 'leaves': det['batched_n_leaves'],
+           'iterations': det['batched_n_iters'], 'ms': statistics.median(ms),
+           'ms_all': ms, 'clocks': clk.summary()}
+    return rec
+
+
+def cfg1_reference_cpu(pools, limit_s=60.0):
+    """The reference's own CPU driver on cfg1 at 1 thread and with a torch
+    thread per core (each bounded by limit_s; a leg that runs out reports
+    its limit instead of a time)."""
+    import multiprocessing as mp
+    out = {}
+    for key, pool, threads in (('reference_cpu_1_thread', pools.one, 1),
+                               ('reference_cpu_all_threads', pools.threaded, pools.cores)):
+        job = pool.apply_async(_cfg1_reference_worker, (8.0,))
+        try:
+            v, leaves, s_, n = job.get(timeout=limit_s)
+            out[key] = {'verdict': v, 'leaves': leaves, 'ms': 1e3 * s_, 'verdicts': n,
+                        'threads': threads}
+        except mp.TimeoutError:
+            pool.terminate()
+            out[key] = {'ms': None, 'threads': threads,
+                        'note': f'no verdict within {limit_s:.0f} s'}
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -584,10 +771,28 @@ def run_cfg1(args):
         }
         if world == 1 and not args.no_cpu_baseline:
             rate = _cpu_cfg1()
-            line['cpu_baseline'] = {
-                'value': n_leaves / rate, 'unit': 's', 'cores': 1, 'kind': 'port',
-                'sample': f'oracle/bab.py input-split BaB for 15 s ({rate:.0f} leaves/s, '
-                          f'numpy), extrapolated to the {n_leaves} leaves of the verdict'}
+            port = {'value': n_leaves / rate, 'unit': 's', 'cores': 1, 'kind': 'port',
+                    'sample': f'oracle/bab.py input-split BaB for 15 s ({rate:.0f} leaves/s, '
+                              f'numpy), extrapolated to the {n_leaves} leaves of the verdict'}
+            line['cpu_baseline'] = port
+            if reference_installed():
+                cores = os.cpu_count() or 1
+                pools = types.SimpleNamespace(one=make_pool(1, 1, ()), cores=cores,
+                                              threaded=make_pool(1, cores, ()))
+                ref = cfg1_reference_cpu(pools)
+                pools.one.close()
+                pools.threaded.close()
+                legs = [v for v in ref.values() if v.get('ms') is not None]
+                if legs:
+                    best = min(legs, key=lambda v: v['ms'])
+                    line['cpu_baseline'] = {
+                        'value': best['ms'] / 1e3, 'unit': 's', 'cores': best['threads'],
+                        'kind': 'reference',
+                        'sample': "the reference's own _input_split_batched on the CPU "
+                                  f"(torch fp32, installed under baseline/_ref), median of "
+                                  f"{best['verdicts']} verdict(s) ({best['verdict']}, "
+                                  f"{best['leaves']} leaves) at {best['threads']} thread(s)",
+                        'legs': ref, 'port': port}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -798,6 +1003,88 @@ def run_cfg5(args, per_step=64):
         dist.destroy_process_group()
 
 
+def run_cfg5_full(args, per_rank=64):
+    """cfg5's stated workload end to end: the input-split BaB of the cfg5
+    robustness property through the sharded driver
+    (shard._input_split_batched_sharded: root expansion on every rank, leaves
+    dealt round-robin, NCCL all_gather of the status and send / recv
+    rebalancing every 8 iterations) with per_rank leaves per GPU iteration,
+    the worklist bounded at 262,144 leaves (the size of the depth-18 tree),
+    root PGD off.  One timed run after one warm-up batch; the time is the max
+    over ranks of CUDA events around the driver."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    dev = torch.device(f'cuda:{local}')
+    torch.cuda.set_device(dev)
+    os.environ.setdefault('MASTER_ADDR', '127.0.0.1')
+    os.environ.setdefault('MASTER_PORT', '29533')
+    dist.init_process_group('nccl', rank=rank, world_size=world, timeout=timedelta(seconds=600),
+                            device_id=dev)
+    from vibecheck_nn_b200 import bab, shard, workloads as wk
+    w = wk.cfg5(0)
+    gg = wk.mlp_gg(w['layers'], dev)
+    spec = bab.LinearSpec(w['xl'], w['xh'], wk.robustness_disjuncts(10, w['true_label']))
+    max_wl = 262_144
+    st = wk.reference_bab_settings(input_split_batch_size=per_rank, disable_sat_finding=True,
+                                   input_split_batched_max_worklist=max_wl,
+                                   total_timeout=3600.0)
+    eng = bab.make_engine(spec, gg, st, dev)
+    lo, hi = wk.cfg5_leaves(w['xl'], w['xh'], 0, per_rank)
+    eng.process(torch.as_tensor(lo, device=dev), torch.as_tensor(hi, device=dev), 0)
+    del eng
+    props = torch.cuda.get_device_properties(dev)
+    gid = getattr(props, 'uuid', None)
+    gid = f'GPU-{gid}' if gid is not None else local
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(gid) as clk:
+        e0.record(stream)
+        verdict, det = shard._input_split_batched_sharded(None, spec, st, gg, dev,
+                                                          torch.float32, per_rank=per_rank)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    mine = torch.tensor([e0.elapsed_time(e1) / 1e3, det.get('shard_expand_s', 0.0),
+                         det.get('shard_sync_s', 0.0), det.get('shard_transfer_s', 0.0)],
+                        dtype=torch.float64, device=dev)
+    allv = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allv, mine)
+    per = torch.stack(allv).cpu().numpy()
+    t = float(per[:, 0].max())
+    leaves = int(det['batched_n_leaves'])
+    if rank == 0:
+        line = {
+            'metric': 'cfg5 leaves/s (sharded input-split BaB, full run)',
+            'value': leaves / t, 'unit': 'leaves/s', 'n_gpus': world, 'steps': 1,
+            'warmup': 1, 'ms_per_step': 1e3 * t, 'higher_is_better': True,
+            'scaling': 'strong', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic (seeded numpy rng)',
+            'config': {'workload': 'cfg5: 3072x[1024]x8x10 MLP, eps 1/255 box, 9 robustness '
+                                   'disjuncts, input-split BaB (zonotope intermediates + '
+                                   'CROWN spec bound, widest-dimension bisection) until the '
+                                   f'worklist exceeds {max_wl} leaves',
+                       'leaves_per_gpu_iteration': per_rank, 'parallelism':
+                           f'{world} GPU(s): leaves dealt round-robin, NCCL status all_gather '
+                           'and send/recv rebalancing every 8 iterations'},
+            'verdict': verdict, 'phase': det.get('phase'), 'leaves': leaves,
+            'worklist_at_stop': det.get('worklist_size'),
+            'shard_leaves': det.get('shard_leaves'), 'shard_rounds': det.get('shard_rounds'),
+            'shard_transfers': det.get('shard_transfers'),
+            'phases_s': {'total_per_rank': per[:, 0].tolist(),
+                         'root_expansion_per_rank': per[:, 1].tolist(),
+                         'status_all_gather_incl_wait_per_rank': per[:, 2].tolist(),
+                         'rebalance_send_recv_per_rank': per[:, 3].tolist()},
+            'clocks': clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == 'reference':
@@ -806,6 +1093,8 @@ def main():
         run_cfg1(args)
     elif args.config in ('cfg3', 'cfg4'):
         run_cfg34(args)
+    elif args.config == 'cfg5' and args.full:
+        run_cfg5_full(args)
     elif args.config == 'cfg5':
         run_cfg5(args)
     else:

@@ -150,6 +150,15 @@ int vcb_multisub_fate(int32_t B, int32_t n_in, int32_t K, int32_t Q, const float
                       const int32_t* sub, int32_t clip_iters, int32_t* fate, float* out_xl,
                       float* out_xh, float* score, void* stream);
 
+/* vcb_mlp_flirpa followed by vcb_multisub_fate in one kernel: the spec rows
+ * stay in shared memory and only the fates, clipped boxes and scores are
+ * written (same arguments and outputs as the two calls, same values). */
+int vcb_mlp_flirpa_fate(const vcb_mlp* net, int32_t B, int32_t K, const float* xl,
+                        const float* xh, const int32_t* var_idx, int32_t Q,
+                        const float* spec_W, const float* sub_bias, const int32_t* sub,
+                        int32_t clip_iters, int32_t* fate, float* out_xl, float* out_xh,
+                        float* score, void* stream);
+
 /* Children of the U leaves rows[0..U) of a multi-subbox batch
  * (verify_graph.py:11804-11852): each leaf ranks its dimensions by score
  * (B x n_in) in CPU torch.topk order, bisects the first k of them that are

@@ -104,3 +104,33 @@ def test_leaf_fate_and_children_match_the_oracle_bitwise(seed):
         want = oms.emit_children(s, loo, hio, sco, sub, k)
         for g, w in zip(kid, want):
             assert np.array_equal(g.cpu().numpy(), w), k
+
+
+def test_fused_forward_fate_equals_the_two_calls():
+    """vcb_mlp_flirpa_fate gives the fates, boxes and scores of
+    vcb_mlp_flirpa followed by vcb_multisub_fate, bit for bit."""
+    _, seed, n_sub, margins, half = CASES['mixed'][:5]
+    layers, subs = golden_script().multisub_problem(seed, n_sub, margins, half)
+    desc = netdesc.mlp_desc(wk.mlp_gg(layers, DEV, torch.float32), DEV)
+    rng = np.random.default_rng(1)
+    lo = np.concatenate([s[0] for s in subs for _ in range(8)]).reshape(-1, 6).astype(np.float32)
+    hi = np.concatenate([s[1] for s in subs for _ in range(8)]).reshape(-1, 6).astype(np.float32)
+    # widen the fixed dimensions 0-3, shrink some boxes, fix dimension 4
+    lo[:, :4] -= 0.05 * rng.random((lo.shape[0], 4)).astype(np.float32)
+    hi[:, :4] += 0.05 * rng.random((lo.shape[0], 4)).astype(np.float32)
+    f = rng.random(lo.shape).astype(np.float32)
+    hi = np.where(rng.random(lo.shape) < 0.5, lo + (hi - lo) * f, hi).astype(np.float32)
+    hi[:, 4] = lo[:, 4]
+    xl, xh = torch.as_tensor(lo, device=DEV), torch.as_tensor(hi, device=DEV)
+    var_idx = torch.tensor([0, 1, 2, 3, 5], dtype=torch.int32, device=DEV)
+    W_q = torch.tensor([[1.0, -1.0], [-1.0, 1.0]], device=DEV)
+    bias = torch.as_tensor(rng.normal(0, 0.5, (n_sub, 2)).astype(np.float32), device=DEV)
+    sub = torch.as_tensor(np.repeat(np.arange(n_sub), 8).astype(np.int32), device=DEV)
+    fused = multisub.forward_fate(desc, xl, xh, var_idx, W_q, bias, sub, clip_iters=2)
+    spec_A, spec_b, lb = multisub.forward_linear_spec(desc, xl, xh, var_idx, W_q)
+    two = multisub.leaf_fate(xl, xh, var_idx, spec_A, spec_b, lb, bias, sub, clip_iters=2)
+    f1, f2 = fused[0].cpu().numpy(), two[0].cpu().numpy()
+    assert np.array_equal(f1, f2) and len(set(f1[:-1].tolist())) >= 2, np.bincount(f1[:-1])
+    s = np.nonzero(f1[:-1] == 2)[0]
+    for a, b in zip(fused[1:], two[1:]):
+        assert _same(a.cpu().numpy()[s], b.cpu().numpy()[s])

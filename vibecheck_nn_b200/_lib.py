@@ -57,6 +57,8 @@ SIGNATURES = {
     'vcb_fault_check': [_P],
     'vcb_mlp_flirpa': [ctypes.POINTER(VcbMlp), _I, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P,
                        _P, _P, _P, _P],
+    'vcb_mlp_flirpa_fate': [ctypes.POINTER(VcbMlp), _I, _I, _P, _P, _P, _I, _P, _P, _P, _I, _P,
+                            _P, _P, _P, _P],
     'vcb_multisub_fate': [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P,
                           _P],
     'vcb_multisub_emit': [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],

@@ -17,9 +17,13 @@
 //   * spec rows w (Q x n_out): spec_A = w+ A_lo + w- A_up, spec_b likewise,
 //     lb = spec_A+ x_lo + spec_A- x_hi + spec_b over the varying dimensions.
 // One CTA of 128 threads per box; weights read through the read-only cache.
+// vcb_mlp_flirpa_fate goes on to the multi-subbox leaf fate (input-domain
+// clip, smart-branching scores; vcb_multisub.cuh) on the spec rows while
+// they are still in shared memory.
 #include <algorithm>
 
 #include "vcb_common.cuh"
+#include "vcb_multisub.cuh"
 
 namespace vcb {
 namespace {
@@ -38,6 +42,12 @@ struct FlParams {
   const float *xl, *xh, *specW;
   const int* var_idx;
   float *spec_A, *spec_b, *lb, *A_lo, *A_up, *b_lo, *b_up;
+  // leaf fate (vcb_mlp_flirpa_fate), fate == NULL otherwise
+  const float* sub_bias;
+  const int* sub;
+  int clip_iters;
+  int* fate;
+  float *oxl, *oxh, *score;
 };
 
 __global__ void __launch_bounds__(kFT) flirpa_kernel(const FlParams p) {
@@ -45,6 +55,7 @@ __global__ void __launch_bounds__(kFT) flirpa_kernel(const FlParams p) {
   __shared__ float mid_s[kFMaxW * (kFMaxK + 1)], half_s[kFMaxW * (kFMaxK + 1)];
   __shared__ float xmid[kFMaxK], xhalf[kFMaxK], xlc[kFMaxK], xhc[kFMaxK];
   __shared__ float box_lo[kFMaxW], box_hi[kFMaxW];
+  __shared__ float lb_sh[kFMaxW];
   const int box = blockIdx.x;
   const int tid = threadIdx.x;
   const int K = p.K, Kp = K + 1;
@@ -166,36 +177,33 @@ __global__ void __launch_bounds__(kFT) flirpa_kernel(const FlParams p) {
     }
     const float sb = mid_s[q * Kp + K];
     if (p.spec_b) p.spec_b[(long long)box * p.Q + q] = sb;
-    p.lb[(long long)box * p.Q + q] = __fadd_rn(s, sb);
+    lb_sh[q] = __fadd_rn(s, sb);
+    if (p.lb) p.lb[(long long)box * p.Q + q] = lb_sh[q];
+  }
+  if (p.fate) {
+    __syncthreads();
+    if (tid == 0)
+      ms_leaf_fate(box, p.B, n0, K, p.Q, p.clip_iters, p.xl, p.xh, p.var_idx, mid_s, Kp,
+                   mid_s + K, Kp, lb_sh, p.sub_bias + (long long)p.sub[box] * p.Q, p.fate,
+                   p.oxl, p.oxh, p.score);
   }
 }
 
-}  // namespace
-}  // namespace vcb
-
-extern "C" int vcb_mlp_flirpa(const vcb_mlp* net, int32_t B, int32_t K, const float* xl,
-                              const float* xh, const int32_t* var_idx, int32_t Q,
-                              const float* spec_W, float* spec_A, float* spec_b, float* lb,
-                              float* A_lo, float* A_up, float* b_lo, float* b_up,
-                              void* stream) {
-  using namespace vcb;
-  if (!net || B < 0 || Q < 0) return fail(VCB_ERR_INVALID, "vcb_mlp_flirpa: bad arguments");
+int flirpa_setup(const vcb_mlp* net, int32_t B, int32_t K, int32_t Q, const char* who,
+                 FlParams& p) {
+  if (!net || B < 0 || Q < 0) return fail(VCB_ERR_INVALID, "%s: bad arguments", who);
   const int nfc = net->n_fc;
-  if (nfc < 1 || nfc > VCB_MAX_FC)
-    return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_flirpa: n_fc=%d", nfc);
+  if (nfc < 1 || nfc > VCB_MAX_FC) return fail(VCB_ERR_UNSUPPORTED, "%s: n_fc=%d", who, nfc);
   for (int l = 0; l <= nfc; ++l)
     if (net->dims[l] < 1 || net->dims[l] > kFMaxW)
-      return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_flirpa: width %d outside [1, %d]",
-                  net->dims[l], kFMaxW);
+      return fail(VCB_ERR_UNSUPPORTED, "%s: width %d outside [1, %d]", who, net->dims[l],
+                  kFMaxW);
   if (K < 1 || K > kFMaxK || K > net->dims[0])
-    return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_flirpa: K=%d varying dimensions outside [1, %d]",
-                K, kFMaxK);
-  if (Q > kFMaxW) return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_flirpa: Q=%d > %d", Q, kFMaxW);
-  if (B == 0) return VCB_OK;
-  if (!net->W || !net->b || !xl || !xh || !var_idx || !lb || (Q > 0 && !spec_W) ||
-      ((A_lo == nullptr) != (A_up == nullptr)) || (A_lo && (!b_lo || !b_up)))
-    return fail(VCB_ERR_INVALID, "vcb_mlp_flirpa: NULL pointer");
-  FlParams p{};
+    return fail(VCB_ERR_UNSUPPORTED, "%s: K=%d varying dimensions outside [1, %d]", who, K,
+                kFMaxK);
+  if (Q > kFMaxW) return fail(VCB_ERR_UNSUPPORTED, "%s: Q=%d > %d", who, Q, kFMaxW);
+  if (!net->W || !net->b) return fail(VCB_ERR_INVALID, "%s: NULL weights", who);
+  p = FlParams{};
   p.n_fc = nfc;
   long long woff = 0;
   int boff = 0;
@@ -211,6 +219,26 @@ extern "C" int vcb_mlp_flirpa(const vcb_mlp* net, int32_t B, int32_t K, const fl
   p.B = B;
   p.K = K;
   p.Q = Q;
+  return VCB_OK;
+}
+
+}  // namespace
+}  // namespace vcb
+
+extern "C" int vcb_mlp_flirpa(const vcb_mlp* net, int32_t B, int32_t K, const float* xl,
+                              const float* xh, const int32_t* var_idx, int32_t Q,
+                              const float* spec_W, float* spec_A, float* spec_b, float* lb,
+                              float* A_lo, float* A_up, float* b_lo, float* b_up,
+                              void* stream) {
+  using namespace vcb;
+  const char* who = "vcb_mlp_flirpa";
+  FlParams p;
+  int rc = flirpa_setup(net, B, K, Q, who, p);
+  if (rc) return rc;
+  if (B == 0) return VCB_OK;
+  if (!xl || !xh || !var_idx || !lb || (Q > 0 && !spec_W) ||
+      ((A_lo == nullptr) != (A_up == nullptr)) || (A_lo && (!b_lo || !b_up)))
+    return fail(VCB_ERR_INVALID, "%s: NULL pointer", who);
   p.xl = xl;
   p.xh = xh;
   p.specW = spec_W;
@@ -223,5 +251,39 @@ extern "C" int vcb_mlp_flirpa(const vcb_mlp* net, int32_t B, int32_t K, const fl
   p.b_lo = b_lo;
   p.b_up = b_up;
   flirpa_kernel<<<B, kFT, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch("vcb_mlp_flirpa");
+  return check_launch(who);
+}
+
+extern "C" int vcb_mlp_flirpa_fate(const vcb_mlp* net, int32_t B, int32_t K, const float* xl,
+                                   const float* xh, const int32_t* var_idx, int32_t Q,
+                                   const float* spec_W, const float* sub_bias,
+                                   const int32_t* sub, int32_t clip_iters, int32_t* fate,
+                                   float* out_xl, float* out_xh, float* score, void* stream) {
+  using namespace vcb;
+  const char* who = "vcb_mlp_flirpa_fate";
+  FlParams p;
+  int rc = flirpa_setup(net, B, K, Q, who, p);
+  if (rc) return rc;
+  if (Q < 1 || clip_iters < 0)
+    return fail(VCB_ERR_INVALID, "%s: Q=%d clip_iters=%d", who, Q, clip_iters);
+  if (!fate || !xl || !xh || !var_idx || !spec_W || !sub_bias || !sub || !out_xl || !out_xh ||
+      !score)
+    return fail(VCB_ERR_INVALID, "%s: NULL pointer", who);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(fate + B, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, who);
+  if (B == 0) return VCB_OK;
+  p.xl = xl;
+  p.xh = xh;
+  p.specW = spec_W;
+  p.var_idx = var_idx;
+  p.sub_bias = sub_bias;
+  p.sub = sub;
+  p.clip_iters = clip_iters;
+  p.fate = fate;
+  p.oxl = out_xl;
+  p.oxh = out_xh;
+  p.score = score;
+  flirpa_kernel<<<B, kFT, 0, st>>>(p);
+  return check_launch(who);
 }

@@ -15,21 +15,19 @@
 //           combinations of low / high halves per leaf, leaf by leaf; a
 //           dimension at most 1e-12 wide is left whole     (:11816-11852)
 //
-// The fate kernel runs one thread per leaf with the leaf's varying box in
-// registers: the queries' coefficients are read once per clip round, so the
-// clip costs Q K loads and a few flops per leaf.  Every fp32 operation is
-// rounded as the reference's tensor expression rounds it (products, sums,
-// the division) and sums run in dimension order.  The emit kernel writes the
-// children with one thread per output element after one thread per leaf has
-// ranked its dimensions.
+// The fate of a leaf (ms_leaf_fate, vcb_multisub.cuh) runs in one thread
+// with the leaf's varying box in registers; vcb_mlp_flirpa_fate calls it at
+// the end of the forward-LiRPA kernel, on the spec rows still in shared
+// memory, and vcb_multisub_fate on spec rows in global memory.  The emit
+// kernel writes the children with one thread per output element after one
+// thread per leaf has ranked its dimensions.
 #include "vcb_common.cuh"
+#include "vcb_multisub.cuh"
 #include "vcb_topk.cuh"
 
 namespace vcb {
 namespace {
 
-constexpr int kMsMaxVar = 32;  // varying dimensions (the forward-LiRPA limit)
-constexpr int kMsMaxQ = 64;
 constexpr int kMsMaxDepth = 16;
 constexpr int kMsThreads = 128;
 
@@ -48,88 +46,10 @@ struct MsFateParams {
 __global__ void __launch_bounds__(kMsThreads) ms_fate_kernel(const MsFateParams p) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= p.B) return;
-  const int n = p.n, K = p.K, Q = p.Q;
-  const float* bias = p.bias + (long long)p.sub[b] * Q;
-  const float* lbb = p.lb + (long long)b * Q;
-  const float* A = p.A + (long long)b * Q * K;
-  const float* xl = p.xl + (long long)b * n;
-  const float* xh = p.xh + (long long)b * n;
-  float* oxl = p.oxl + (long long)b * n;
-  float* oxh = p.oxh + (long long)b * n;
-  float* sc = p.score + (long long)b * n;
-  bool safe = false;
-  for (int q = 0; q < Q; ++q) safe |= __fadd_rn(lbb[q], bias[q]) > 0.f;
-  if (safe) {
-    p.fate[b] = 0;
-    return;
-  }
-  float cl[kMsMaxVar], ch[kMsMaxVar], w0[kMsMaxVar];
-  for (int k = 0; k < K; ++k) {
-    cl[k] = xl[p.var[k]];
-    ch[k] = xh[p.var[k]];
-    w0[k] = __fsub_rn(ch[k], cl[k]);
-  }
-  for (int it = 0; it < p.iters; ++it) {
-    float nl[kMsMaxVar], nh[kMsMaxVar];
-    for (int k = 0; k < K; ++k) {
-      nl[k] = -INFINITY;
-      nh[k] = INFINITY;
-    }
-    for (int q = 0; q < Q; ++q) {
-      const float* a = A + (long long)q * K;
-      // the query's lower bound over the current box
-      float lo = 0.f;
-      for (int k = 0; k < K; ++k)
-        lo = __fadd_rn(lo, __fadd_rn(__fmul_rn(fmaxf(a[k], 0.f), cl[k]),
-                                     __fmul_rn(fminf(a[k], 0.f), ch[k])));
-      lo = __fadd_rn(lo, __fadd_rn(p.sb[(long long)b * Q + q], bias[q]));
-      for (int k = 0; k < K; ++k) {
-        const float ak = a[k];
-        const float mid = __fmul_rn(__fadd_rn(ch[k], cl[k]), 0.5f);
-        const float rad = __fmul_rn(__fsub_rn(ch[k], cl[k]), 0.5f);
-        // lower bound with dimension k left free: its crossing with 0
-        const float rest = __fsub_rn(lo, __fsub_rn(__fmul_rn(ak, mid), __fmul_rn(fabsf(ak), rad)));
-        const float x0 = __fdiv_rn(-rest, fabsf(ak) > 1e-30f ? ak : 1.f);
-        if (ak > 0.f) nh[k] = fminf(nh[k], x0);
-        if (ak < 0.f) nl[k] = fmaxf(nl[k], x0);
-      }
-    }
-    for (int k = 0; k < K; ++k) {
-      ch[k] = fminf(nh[k], ch[k]);
-      cl[k] = fmaxf(nl[k], cl[k]);
-    }
-  }
-  bool empty = false;
-  for (int k = 0; k < K; ++k) empty |= cl[k] > ch[k];
-  if (empty) {
-    p.fate[b] = 1;
-    return;
-  }
-  p.fate[b] = 2;
-  for (int i = 0; i < n; ++i) {
-    oxl[i] = xl[i];
-    oxh[i] = xh[i];
-    sc[i] = -INFINITY;
-  }
-  for (int k = 0; k < K; ++k) {
-    const int d = p.var[k];
-    oxl[d] = cl[k];
-    oxh[d] = ch[k];
-    float s = -INFINITY;
-    for (int q = 0; q < Q; ++q) {
-      const float c = fmaxf(fabsf(A[(long long)q * K + k]), 0.1f);
-      const float m = __fadd_rn(lbb[q], bias[q]);
-      s = fmaxf(s, __fadd_rn(__fmul_rn(__fmul_rn(c, w0[k]), 0.5f), m));
-    }
-    sc[d] = s;
-  }
-  int nz = 0;
-  for (int i = 0; i < n; ++i) {
-    const bool wide = __fsub_rn(oxh[i], oxl[i]) > 1e-12f;
-    nz += wide;
-    if (!wide) sc[i] = -INFINITY;
-  }
-  atomicMax(p.fate + p.B, nz);
+  const long long q0 = (long long)b * p.Q;
+  ms_leaf_fate(b, p.B, p.n, p.K, p.Q, p.iters, p.xl, p.xh, p.var, p.A + q0 * p.K, p.K,
+               p.sb + q0, 1, p.lb + q0, p.bias + (long long)p.sub[b] * p.Q, p.fate, p.oxl,
+               p.oxh, p.score);
 }
 
 struct MsEmitParams {

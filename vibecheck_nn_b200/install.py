@@ -38,10 +38,11 @@ BINDINGS = {
         '_simple_pgd_batched': ('pgd', '_simple_pgd_batched'),
         '_forward_batch_graph': ('forward', '_forward_batch_graph', 'delegate'),
         # the freeze-replay pipeline; verify_graph imports verify_hybrid at
-        # call time (verify_graph.py:9890)
-        '_full_freeze': ('hybrid', '_full_freeze'),
-        '_replay_batched': ('hybrid', '_replay_batched'),
-        'verify_hybrid': ('hybrid', 'verify_hybrid'),
+        # call time (verify_graph.py:9890); networks other than fc / ReLU
+        # MLPs run the reference's own
+        '_full_freeze': ('hybrid', '_full_freeze', 'delegate'),
+        '_replay_batched': ('hybrid', '_replay_batched', 'delegate'),
+        'verify_hybrid': ('hybrid', 'verify_hybrid', 'delegate'),
     },
     # verify_milp._pgd_attack_general (verify_milp.py:111-124), which every
     # caller uses, looks this attribute up at call time

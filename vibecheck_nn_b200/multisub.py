@@ -12,7 +12,8 @@ dimensions):
   dimensions and the spec rows (``vcb_mlp_flirpa``); a leaf is safe when any
   of its sub-box's queries has a positive margin (lower bound + the sub-box's
   query bias); a sub-box closes when its last live leaf is safe;
-* one kernel (``vcb_multisub_fate``) decides every leaf of the batch: safe
+* one kernel (``vcb_mlp_flirpa_fate``: the forward-LiRPA bound with the
+  leaf fate in its epilogue) decides every leaf of the batch: safe
   by its bound, safe because two rounds of input-domain clipping
   (``_clip_input_domain``, verify_graph.py:11121-11177) leave an empty box,
   or to split, with its clipped box and smart-branching scores;
@@ -69,6 +70,26 @@ def forward_linear_spec(desc, xl, xh, var_idx, W_q, want_bounds=False):
     _lib.check(rc, 'vcb_mlp_flirpa')
     res = (spec_A, spec_b, lb)
     return res + tuple(outs) if want_bounds else res
+
+
+def forward_fate(desc, xl, xh, var_idx, W_q, sub_bias, sub, clip_iters=2):
+    """``vcb_mlp_flirpa_fate``: the forward-LiRPA spec bound and the leaf fate
+    in one kernel; returns (fate, box_lo, box_hi, score) as ``leaf_fate``."""
+    dev = xl.device
+    B, n = xl.shape
+    K = int(var_idx.numel())
+    fate = torch.empty(B + 1, dtype=torch.int32, device=dev)
+    box_lo = torch.empty((B, n), dtype=F32, device=dev)
+    box_hi = torch.empty((B, n), dtype=F32, device=dev)
+    score = torch.empty((B, n), dtype=F32, device=dev)
+    P = _lib.ptr
+    rc = _lib.lib().vcb_mlp_flirpa_fate(desc.struct, B, K, P(xl.contiguous()), P(xh.contiguous()),
+                                        P(var_idx), W_q.shape[0], P(W_q.contiguous()),
+                                        P(sub_bias.contiguous()), P(sub), int(clip_iters),
+                                        P(fate), P(box_lo), P(box_hi), P(score),
+                                        _lib.stream_of(dev))
+    _lib.check(rc, 'vcb_mlp_flirpa_fate')
+    return fate, box_lo, box_hi, score
 
 
 def leaf_fate(xl, xh, var_idx, spec_A, spec_b, lb, sub_bias, sub, clip_iters=2):
@@ -209,15 +230,14 @@ def _multi_sub_input_split_bab(sub_idx_list, groups, order, gg, device, dtype, t
         lirpa = None
         if desc is not None and var_idx.numel() > 0:
             try:
-                lirpa = forward_linear_spec(desc, xl_b, xh_b, var_idx, W_q)
+                lirpa = forward_fate(desc, xl_b, xh_b, var_idx, W_q, bias_table, si_b,
+                                     clip_iters=2)
             except (_lib.UnsupportedInput, torch.cuda.OutOfMemoryError):
                 # the reference falls back on these (verify_graph.py:11458); a
                 # KernelError is a fault and propagates
                 lirpa = None
         if lirpa is not None:
-            spec_A, spec_b, lbs = lirpa
-            fate_d, box_lo, box_hi, score = leaf_fate(xl_b, xh_b, var_idx, spec_A, spec_b, lbs,
-                                                      bias_table, si_b, clip_iters=2)
+            fate_d, box_lo, box_hi, score = lirpa
         else:
             from .interm import _forward_zonotope_graph_batched
             from .ops import _spec_backward_graph_batched

@@ -116,15 +116,24 @@ def _broadcast_witness(st, src, n_in, device, group, rank):
 def input_split_sharded(engine, group=None, per_rank=64, sync_every=8, t_start=None):
     """Sharded worklist BaB over the process group; returns (verdict,
     details) -- the single-GPU driver's keys, with global counts, plus
-    ``shard_leaves`` (per rank) and ``shard_transfers``."""
+    ``shard_leaves`` (per rank), ``shard_transfers``, ``shard_rounds`` and
+    this rank's host seconds in the root expansion (``shard_expand_s``), the
+    status all_gather including the wait for the slowest rank
+    (``shard_sync_s``) and the rebalancing send / recv (``shard_transfer_s``)."""
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     cfg = engine.cfg
     device = engine.device
     n_in = engine.n_in
     t_start = time.perf_counter() if t_start is None else t_start
+    sync = (lambda: torch.cuda.synchronize(device)) if torch.device(device).type == 'cuda' \
+        else (lambda: None)
     st = LocalState(Worklist(*engine.root()), cfg.batch_size)
+    t0 = time.perf_counter()
     expand_root(engine, st, world * per_rank)
+    sync()
+    t_expand = time.perf_counter() - t0
+    t_sync = t_transfer = 0.0
     if rank != 0:  # the expansion ran on every rank; count it once
         st.n_leaves = 0
         st.n_open = 0
@@ -143,13 +152,16 @@ def input_split_sharded(engine, group=None, per_rank=64, sync_every=8, t_start=N
         timed_out = time.perf_counter() - t_start > cfg.total_budget - 0.5
         status = [st.wl.size(), st.n_leaves, st.n_open, int(st.witness is not None),
                   int(timed_out), int(st.oom)]
+        t0 = time.perf_counter()
         allv = _gather_status(status, world, device, group)
+        t_sync += time.perf_counter() - t0
         rounds += 1
         tot = allv.sum(0)
         details = {'batched_n_leaves': int(tot[S_LEAVES]), 'batched_n_iters': st.n_iters,
                    'shard_leaves': [int(v) for v in allv[:, S_LEAVES]],
                    'shard_transfers': n_transfers, 'shard_rounds': rounds,
-                   'batched_batch_size': st.batch_size}
+                   'batched_batch_size': st.batch_size, 'shard_expand_s': t_expand,
+                   'shard_sync_s': t_sync, 'shard_transfer_s': t_transfer}
         if tot[S_SAT] > 0:
             src = int(np.nonzero(allv[:, S_SAT])[0][0])
             wit = _broadcast_witness(st, src, n_in, device, group, rank)
@@ -170,7 +182,10 @@ def input_split_sharded(engine, group=None, per_rank=64, sync_every=8, t_start=N
                                    batched_open_degenerate=int(tot[S_OPEN] + tot[S_WL]))
         plan = rebalance_plan(allv[:, S_WL], cfg.batch_size)
         if plan:
+            t0 = time.perf_counter()
             _transfer(st.wl, plan, rank, n_in, device, group)
+            sync()
+            t_transfer += time.perf_counter() - t0
             n_transfers += len(plan)
 
 
