@@ -162,6 +162,9 @@ __device__ __forceinline__ TcItem item_at(const TcParams& p, int i) {
 // When the near-tie re-bound is on, the same launch clears the tie flags and
 // writes the plain fp32 rows of the network that crown_tie_kernel reads.
 __global__ void crown_tc_images(const TcParams p) {
+  // crown_tc_kernel may be scheduled now; it waits for this grid's writes
+  // (griddepcontrol.wait) before it reads them
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int nimg = 3 * (p.n_fc - 1);
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx == 0) {  // the error word and tie count of the launch that follows
@@ -617,6 +620,11 @@ __global__ void __launch_bounds__(kThreads, 1) crown_tc_kernel(const __grid_cons
   __syncthreads();
   fence_after_sync();
   const uint32_t tmem = tmem_slot;
+  // The prologue above reads only the network and the spec; the weight
+  // images, the cleared tie flags and error word come from crown_tc_images,
+  // launched just before with a programmatic dependency.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == kCtlWarp) {
     // ----------------------- control: weight loads and MMA issue (lane 0)
@@ -773,6 +781,9 @@ template <bool kNetSmem, int QG>
 __global__ void __launch_bounds__(64 * kTieBoxes, 1)
     crown_tie_kernel(const __grid_constant__ TcParams p, const TieLayout t) {
   extern __shared__ __align__(16) float tsm[];
+  // launched with a programmatic dependency on crown_tc_kernel: its list and
+  // outputs are complete and visible after this wait
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int count = *p.tie_count;
   const int nb = t.boxes;
   // listed box i goes to CTA i % grid (slot i / grid): the few hundred boxes
@@ -1171,10 +1182,22 @@ int crown_tc_launch(const vcb_mlp* net, int32_t B, const float* xl, const float*
                          : reinterpret_cast<const void*>(crown_tc_kernel<false>);
   rc = ensure_smem(fn, kSmem);
   if (rc) return rc;
-  if (plain)
-    crown_tc_kernel<true><<<plan.grid, kThreads, kSmem, st>>>(p);
-  else
-    crown_tc_kernel<false><<<plan.grid, kThreads, kSmem, st>>>(p);
+  // programmatic dependent launches: each kernel of the chain is scheduled
+  // while the previous one drains and waits on the device for its results
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = st;
+  cfg.attrs = pdl;
+  cfg.numAttrs = 1;
+  rc = cuda_fail(plain ? cudaLaunchKernelEx(&cfg, crown_tc_kernel<true>, p)
+                       : cudaLaunchKernelEx(&cfg, crown_tc_kernel<false>, p),
+                 who);
+  if (rc) return rc;
   rc = check_launch(who);
   if (rc || !p.tie_on) return rc;
   // the listed boxes, bounded again with the fp32 kernel's order; a launch
@@ -1189,9 +1212,10 @@ int crown_tc_launch(const vcb_mlp* net, int32_t B, const float* xl, const float*
   rc = ensure_smem(tie_fn, tl.bytes);
   if (rc) return rc;
   void* args[] = {const_cast<TcParams*>(&p), const_cast<TieLayout*>(&tl)};
-  rc = cuda_fail(cudaLaunchKernel(tie_fn, dim3(sm_count()), dim3(64 * tl.boxes), args,
-                                  (size_t)tl.bytes, st),
-                 who);
+  cfg.gridDim = dim3(sm_count());
+  cfg.blockDim = dim3(64 * tl.boxes);
+  cfg.dynamicSmemBytes = (size_t)tl.bytes;
+  rc = cuda_fail(cudaLaunchKernelExC(&cfg, tie_fn, args), who);
   if (rc) return rc;
   return check_launch(who);
 }
