@@ -28,6 +28,7 @@ import time
 
 import numpy as np
 import torch
+from torch.cuda import nvtx
 
 from . import _lib
 from .interm import crown_intermediate_packed, mlp_zono
@@ -315,6 +316,9 @@ class BoundEngine:
         c = self.cfg
         if timer is not None:
             timer.mark()
+        # NVTX ranges name the phases for a profiler's timeline (no cost
+        # without one attached)
+        nvtx.range_push('vcb.bound')
         # the input-space linear form exists only with clipping, and SB
         # scoring needs it (verify_graph.py:12862-12870, :13244)
         lb, A, acc = self.bounds(xl_b, xh_b, c.clip)
@@ -328,9 +332,12 @@ class BoundEngine:
             sat, wit = leaf_pgd(xl_b, xh_b, lb, self.qd, self.D, self.spec, self.gg,
                                 self.n_output, self.device, self.settings)
             if sat:
+                nvtx.range_pop()
                 return StepResult(None, None, 0, 0, wit)
+        nvtx.range_pop()
         if timer is not None:
             timer.mark('bound')
+        nvtx.range_push('vcb.step')
         sb = c.branch_sb and c.clip
         B = xl_b.shape[0]
         K = c.split_depth if (sb and batch_size is not None and B < batch_size) else 1
@@ -339,6 +346,7 @@ class BoundEngine:
             clip_iters=c.clip_iters, margin=c.margin, split_depth=K,
             boost=self.boost if sb else None)
         cnt = cnt.tolist()  # host sync: chunk sizes
+        nvtx.range_pop()
         if timer is not None:
             timer.mark('step')
         n_split, n_degen = int(cnt[2]), int(cnt[3])
