@@ -468,6 +468,11 @@ RELU_BAB_CASES = (
     ('warm', 3, (12, 24, 24, 24, 4), 0.04, {'alpha_half': True, 'ew_ones': True}),
     ('warm_noref', 3, (12, 24, 24, 24, 4), 0.04,
      {'alpha_half': True, 'ew_ones': True, 'no_reforward': True}),
+    # cfg3's input and layer widths (784 -> 256 ...), depth and radius chosen
+    # so that the run closes after tens to hundreds of domains
+    ('wide2', 0, (784, 256, 256, 10), 0.001, {}),
+    ('wide3', 0, (784, 256, 256, 256, 10), 0.0002, {}),
+    ('wide4', 0, (784, 256, 256, 256, 256, 10), 0.000035, {}),
 )
 
 
