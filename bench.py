@@ -58,6 +58,9 @@ def parse():
     ap.add_argument('--config', default='cfg2', choices=['cfg2', 'cfg1', 'cfg3', 'cfg4', 'cfg5'],
                     help='cfg2 (default) is the headline; the others time the '
                          'remaining BASELINE configs on their own metrics')
+    ap.add_argument('--cfg5-leaves', type=int, default=64,
+                    help='cfg5: leaves per GPU per step (the default is the workload; fewer '
+                         'make a small case for counter captures)')
     ap.add_argument('--full', action='store_true',
                     help='cfg5: the whole input-split BaB through the sharded driver '
                          '(worklist bound 262,144 leaves) instead of single iterations')
@@ -1096,7 +1099,7 @@ def main():
     elif args.config == 'cfg5' and args.full:
         run_cfg5_full(args)
     elif args.config == 'cfg5':
-        run_cfg5(args)
+        run_cfg5(args, per_step=args.cfg5_leaves)
     else:
         run_ours(args)
 
