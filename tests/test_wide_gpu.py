@@ -170,16 +170,14 @@ def test_bab_with_boundary_alpha_and_leaf_pgd():
     w = wk.cfg1(0)
     gg = wk.mlp_gg(w['layers'], DEV)
     spec = bab.LinearSpec(w['xl'], w['xh'], [[('pair', 1, 0)]])
-    st = type('S', (), {})()
-    st.input_split_batch_size = 2048
-    st.input_split_crown_intermediate = True
-    st.input_split_batched_alpha_boundary_eps = 10.0
-    st.input_split_batched_alpha_iters = 20
-    st.input_split_batched_alpha_max_leaves = 2048
-    st.input_split_leaf_pgd_every = 3
-    st.input_split_leaf_pgd_max_leaves = 128
-    st.input_split_leaf_pgd_restarts = 256
-    st.input_split_leaf_pgd_iters = 50
+    # the reference's default_settings values (width branching) plus the
+    # preset's keys
+    st = wk.reference_bab_settings(
+        input_split_batch_size=2048, input_split_crown_intermediate=True,
+        input_split_batched_alpha_boundary_eps=10.0, input_split_batched_alpha_iters=20,
+        input_split_batched_alpha_max_leaves=2048, input_split_leaf_pgd_every=3,
+        input_split_leaf_pgd_max_leaves=128, input_split_leaf_pgd_restarts=256,
+        input_split_leaf_pgd_iters=50, total_timeout=600.0)
     v, det = bab._input_split_batched(None, spec, st, gg, DEV, torch.float32)
     assert v == 'verified', det
     assert det['batched_n_leaves'] <= int(load_golden('bab_cfg1_seed0')['n_leaves_ci1'])
