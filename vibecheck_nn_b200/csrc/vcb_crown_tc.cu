@@ -237,7 +237,7 @@ __device__ __forceinline__ float2* slot_base(const TcParams& p) {
   return p.slopes + (long long)blockIdx.x * p.slot_f2;
 }
 
-// Split NC (8 or 16) finite values and store the hi / lo parts at
+// Split NC (4, 8 or 16) finite values and store the hi / lo parts at
 // tensor-memory columns taddr and taddr + 64 of this warp's lanes.
 template <int NC>
 __device__ __forceinline__ void store_operand(uint32_t taddr, const float (&v)[NC]) {
@@ -252,10 +252,21 @@ __device__ __forceinline__ void store_operand(uint32_t taddr, const float (&v)[N
   if constexpr (NC == 16) {
     tmem_st16(taddr, h);
     tmem_st16(taddr + kW, l);
-  } else {
+  } else if constexpr (NC == 8) {
     tmem_st8(taddr, h);
     tmem_st8(taddr + kW, l);
+  } else {
+    tmem_st4(taddr, h);
+    tmem_st4(taddr + kW, l);
   }
+}
+
+// Zero hi / lo parts of four columns: the padding of the next MMA's K range
+// past a 4-column chunk.
+__device__ __forceinline__ void store_zero4(uint32_t taddr) {
+  const uint32_t z[4] = {0u, 0u, 0u, 0u};
+  tmem_st4(taddr, z);
+  tmem_st4(taddr + kW, z);
 }
 
 // Sum of the two accumulators (hi_A hi_B and corrections) at tensor-memory
@@ -266,15 +277,19 @@ __device__ __forceinline__ void load_acc(uint32_t taddr, float (&v)[NC]) {
   if constexpr (NC == 16) {
     tmem_ld16(taddr, a);
     tmem_ld16(taddr + kW, e);
-  } else {
+  } else if constexpr (NC == 8) {
     tmem_ld8(taddr, a);
     tmem_ld8(taddr + kW, e);
+  } else {
+    tmem_ld4(taddr, a);
+    tmem_ld4(taddr + kW, e);
   }
   tmem_wait_ld(a, e);
 #pragma unroll
   for (int j = 0; j < NC; ++j) v[j] = __fadd_rn(__uint_as_float(a[j]), __uint_as_float(e[j]));
 }
 
+using C4 = std::integral_constant<int, 4>;
 using C8 = std::integral_constant<int, 8>;
 using C16 = std::integral_constant<int, 16>;
 
@@ -384,10 +399,17 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
         for (int k = 0; k < nck; ++k) {
           const int c0 = chunk_c0(k);
           if (c0 >= nout) continue;
-          if (nout - c0 <= 8)
+          if (nout - c0 <= 4) {  // a short tail: 4 columns, then zeros to pad8
+            chunk(C4{}, c0);
+            if (!last) {
+              store_zero4(tl + c0 + 4);
+              store_zero4(tl + 128 + c0 + 4);
+            }
+          } else if (nout - c0 <= 8) {
             chunk(C8{}, c0);
-          else
+          } else {
             chunk(C16{}, c0);
+          }
         }
         if (!last) publish(&a_ready[0]);
       }
@@ -497,10 +519,14 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
           for (int k = 0; k < nck; ++k) {
             const int c0 = chunk_c0(k);
             if (c0 > nin) continue;  // no neurons and no bias column here
-            if (nin + 1 - c0 <= 8)
+            if (nin + 1 - c0 <= 4) {  // a short tail: 4 columns, then zeros to pad8
+              chunk(C4{}, c0);
+              if (L >= 0) store_zero4(tl + 128 * c + c0 + 4);
+            } else if (nin + 1 - c0 <= 8) {
               chunk(C8{}, c0);
-            else
+            } else {
               chunk(C16{}, c0);
+            }
           }
           if (L >= 0) publish(&a_ready[c]);
         }
