@@ -289,6 +289,20 @@ __device__ __forceinline__ void load_acc(uint32_t taddr, float (&v)[NC]) {
   for (int j = 0; j < NC; ++j) v[j] = __fadd_rn(__uint_as_float(a[j]), __uint_as_float(e[j]));
 }
 
+// encode_slope with CUDA's fast division for up_s = ub / (ub - lb) (within
+// 2 ulp): the tensor-core bounds already differ from the fp32 reference by
+// rounding, a box whose up_s lies near the 0.5 threshold is listed for the
+// exact re-bound, and the upper relaxation moves by ulps of its terms.
+__device__ __forceinline__ float2 encode_slope_fast(float lo, float hi) {
+  if (lo >= 0.f) return make_float2(1.f, -0.0f);  // active
+  const bool dead = hi <= 0.f;
+  const float ub_r = fmaxf(fmaxf(hi, 0.f), __fadd_rn(lo, 1e-8f));
+  if (ub_r == 0.f) return make_float2(-0.0f, 0.0f);  // dead, up_s = 0
+  const float up_s = __fdividef(ub_r, __fsub_rn(ub_r, lo));
+  const float up_t = __fmul_rn(-lo, up_s);
+  return make_float2(dead ? -up_s : up_s, up_t);
+}
+
 using C4 = std::integral_constant<int, 4>;
 using C8 = std::integral_constant<int, 8>;
 using C16 = std::integral_constant<int, 16>;
@@ -381,7 +395,7 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
               p.sbohi[gi0 + o] = hi;
             }
             if (o < nout) {
-              const float2 e = encode_slope(lo, hi);
+              const float2 e = encode_slope_fast(lo, hi);
               sl[o * kTB] = e;
               // unstable (neither sign bit set) with the upper slope inside
               // the band where rounding can move it across 0.5
