@@ -572,7 +572,9 @@ def run_ours(args):
                     'h2d_bytes_per_step': int(xl_h.numel() * 4 * 2),
                     'd2h_bytes_per_step': int(N_BOXES * N_Q * 4),
                     'pipelining': 'steps alternate between 2 CUDA streams'},
-            'gpu_launches': (2 if tc_path else 1) * args.steps,
+            # per step: crown_tc_images, crown_tc_kernel, crown_tie_kernel (tensor-core
+            # route) or crown_mlp_kernel (SIMT route)
+            'gpu_launches': (3 if tc_path else 1) * args.steps,
             'roofline': roofline_cfg2(tc_path, achieved, peak, flop_per_box),
             'clocks': clk.summary(),
             'wall_s_timed_region': t_wall,
