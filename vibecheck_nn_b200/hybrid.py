@@ -239,7 +239,7 @@ def _replay_batched(xl_b, xh_b, gg, spec_ew, alpha_layer_b, alpha_spec_b, device
 
 def _fan_out(x_lo, x_hi, init_leaves):
     """Initial leaves by widest-dimension bisection in the reference's order
-    (verify_hybrid_acasxu.py:392-410): each round splits the boxes in order
+    (verify_hybrid_acasxu.py:377-390): each round splits the boxes in order
     and stops once ``init_leaves`` children exist."""
     boxes = [(x_lo, x_hi)]
     while len(boxes) < init_leaves:
@@ -286,7 +286,7 @@ class _Stack:
 def _pgd_leaves(xl, xh, spec, gg, n_output, restarts, n_iter, box_expand):
     """``_simple_pgd`` on each of the k boxes (xl, xh) (k, n), as one attack
     of k x restarts rows: every box draws the same seed-0 starts the
-    reference draws in its per-box calls (verify_hybrid_acasxu.py:476-489).
+    reference draws in its per-box calls (verify_hybrid_acasxu.py:488-505).
     Returns (sat, witness)."""
     dev = xl.device
     rows = _constraint_rows(spec, n_output)
