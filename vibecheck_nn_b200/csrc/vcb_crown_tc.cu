@@ -303,6 +303,38 @@ __device__ __forceinline__ float2 encode_slope_fast(float lo, float hi) {
   return make_float2(dead ? -up_s : up_s, up_t);
 }
 
+// The two sums of load_acc for two column ranges at once: all four loads
+// in flight, one wait.
+template <int NC>
+__device__ __forceinline__ void load_acc2(uint32_t ta, float (&va)[NC], uint32_t tb,
+                                          float (&vb)[NC]) {
+  uint32_t a[NC], e[NC], c[NC], d[NC];
+  if constexpr (NC == 16) {
+    tmem_ld16(ta, a);
+    tmem_ld16(ta + kW, e);
+    tmem_ld16(tb, c);
+    tmem_ld16(tb + kW, d);
+  } else if constexpr (NC == 8) {
+    tmem_ld8(ta, a);
+    tmem_ld8(ta + kW, e);
+    tmem_ld8(tb, c);
+    tmem_ld8(tb + kW, d);
+  } else {
+    tmem_ld4(ta, a);
+    tmem_ld4(ta + kW, e);
+    tmem_ld4(tb, c);
+    tmem_ld4(tb + kW, d);
+  }
+  tmem_wait_ld(a, e);
+  tmem_tie(c);
+  tmem_tie(d);
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    va[j] = __fadd_rn(__uint_as_float(a[j]), __uint_as_float(e[j]));
+    vb[j] = __fadd_rn(__uint_as_float(c[j]), __uint_as_float(d[j]));
+  }
+}
+
 using C4 = std::integral_constant<int, 4>;
 using C8 = std::integral_constant<int, 8>;
 using C16 = std::integral_constant<int, 16>;
@@ -376,8 +408,7 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
         auto chunk = [&](auto nc, int c0) {
           constexpr int NC = decltype(nc)::value;
           float mc[NC], rc[NC];
-          load_acc<NC>(tl + 256 + c0, mc);
-          load_acc<NC>(tl + 384 + c0, rc);
+          load_acc2<NC>(tl + 256 + c0, mc, tl + 384 + c0, rc);
           const float* bias = sBias + l * kW + c0;
 #pragma unroll
           for (int j = 0; j < NC; ++j) {
