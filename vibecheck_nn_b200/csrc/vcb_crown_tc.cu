@@ -34,10 +34,11 @@
 // of slot s at 128 s (hi) and 128 s + 64 (lo), its accumulators at
 // 256 + 128 s (hi_A hi_B) and 256 + 128 s + 64 (corrections).
 //
-// Warps: 0-11 epilogue (warp w reads tensor-memory lanes 32 (w % 4) ..
-// 32 (w % 4) + 31, i.e. boxes of the tile, and 16-column chunks {0, 3}, {1}
-// or {2} for w / 4 = 0, 1, 2), warp 12 loads the weights and issues the MMAs
-// (13 warps leave 128 registers per thread).  The ReLU slopes of a tile go
+// Warps: 0-15 epilogue (warp w reads tensor-memory lanes 32 (w % 4) ..
+// 32 (w % 4) + 31, i.e. boxes of the tile, and the 16-column chunk 16 (w /
+// 4)), warp 16 loads the weights and issues the MMAs (17 warps leave 96
+// registers per thread; the extra warps hide more tensor-memory and L2
+// latency than the few spilled registers cost).  The ReLU slopes of a tile go
 // to the CTA's workspace slot in neuron-major order ([layer][neuron][box],
 // coalesced across a warp) and are read back by the thread that wrote them.
 // Every wait is bounded; on expiry the kernel stops, writes NaN to the lower
@@ -62,9 +63,9 @@ using namespace tc5;
 __device__ int g_tc_fault;
 
 constexpr int kTB = 128;                   // boxes per tile (MMA rows)
-constexpr int kEpi = 12;                   // epilogue warps
+constexpr int kEpi = 16;                   // epilogue warps
 constexpr int kCtlWarp = kEpi;             // weight loads + MMA issue
-constexpr int kThreads = (kEpi + 1) * 32;  // 416: at most 4 warps per SM sub-partition
+constexpr int kThreads = (kEpi + 1) * 32;  // 544
 constexpr int kW = 64;                     // padded operand width
 constexpr int kMaxWidth = 63;              // widest hidden / input layer
 constexpr int kBlk = kW * 128;             // 8 KB: 64 rows x 32 tf32 (one swizzle column)
@@ -303,46 +304,12 @@ __device__ __forceinline__ float2 encode_slope_fast(float lo, float hi) {
   return make_float2(dead ? -up_s : up_s, up_t);
 }
 
-// The two sums of load_acc for two column ranges at once: all four loads
-// in flight, one wait.
-template <int NC>
-__device__ __forceinline__ void load_acc2(uint32_t ta, float (&va)[NC], uint32_t tb,
-                                          float (&vb)[NC]) {
-  uint32_t a[NC], e[NC], c[NC], d[NC];
-  if constexpr (NC == 16) {
-    tmem_ld16(ta, a);
-    tmem_ld16(ta + kW, e);
-    tmem_ld16(tb, c);
-    tmem_ld16(tb + kW, d);
-  } else if constexpr (NC == 8) {
-    tmem_ld8(ta, a);
-    tmem_ld8(ta + kW, e);
-    tmem_ld8(tb, c);
-    tmem_ld8(tb + kW, d);
-  } else {
-    tmem_ld4(ta, a);
-    tmem_ld4(ta + kW, e);
-    tmem_ld4(tb, c);
-    tmem_ld4(tb + kW, d);
-  }
-  tmem_wait_ld(a, e);
-  tmem_tie(c);
-  tmem_tie(d);
-#pragma unroll
-  for (int j = 0; j < NC; ++j) {
-    va[j] = __fadd_rn(__uint_as_float(a[j]), __uint_as_float(e[j]));
-    vb[j] = __fadd_rn(__uint_as_float(c[j]), __uint_as_float(d[j]));
-  }
-}
-
 using C4 = std::integral_constant<int, 4>;
 using C8 = std::integral_constant<int, 8>;
 using C16 = std::integral_constant<int, 16>;
 
-// The 12 epilogue warps: warp w owns the tile's boxes 32 (w % 4) + lane
-// (tensor-memory lanes) and the 16-column operand chunks {0, 3}, {1} or {2}
-// (w / 4 = 0, 1, 2; the light fourth chunk shares a warp, which balances
-// 50-wide layers).  kPlain: no alpha, beta, clamps or sb outputs (the common
+// The 16 epilogue warps: warp w owns the tile's boxes 32 (w % 4) + lane
+// (tensor-memory lanes) and the 16-column operand chunk 16 (w / 4).  kPlain: no alpha, beta, clamps or sb outputs (the common
 // case, without their guards).  Returns false when a wait expired or another
 // role failed; then every box of this CTA from the unfinished tile on gets
 // NaN outputs.
@@ -355,8 +322,8 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
   const int qd = warp & 3, gi = warp >> 2;
   const int row = 32 * qd + lane;
   const uint32_t tl = tmem + ((uint32_t)(32 * qd) << 16);
-  const int nck = gi == 0 ? 2 : 1;  // chunks of this warp
-  auto chunk_c0 = [&](int k) { return gi == 0 ? 48 * k : 16 * gi; };
+  const int nck = 1;  // chunks of this warp
+  auto chunk_c0 = [&](int) { return 16 * gi; };
   const int nfc = p.n_fc, Q = p.Q, n0 = p.dims[0];
   const bool fwd = p.sblo == nullptr;
   unsigned uacc[2] = {0, 0}, urows = 0;
@@ -408,7 +375,8 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
         auto chunk = [&](auto nc, int c0) {
           constexpr int NC = decltype(nc)::value;
           float mc[NC], rc[NC];
-          load_acc2<NC>(tl + 256 + c0, mc, tl + 384 + c0, rc);
+          load_acc<NC>(tl + 256 + c0, mc);
+          load_acc<NC>(tl + 384 + c0, rc);
           const float* bias = sBias + l * kW + c0;
 #pragma unroll
           for (int j = 0; j < NC; ++j) {

@@ -218,19 +218,6 @@ __device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&r)[4])
                : "memory");
 }
 
-// Orders later uses of r after a tcgen05.wait::ld issued before this call
-// (volatile asm keeps program order; the "+r" ties the registers to it), so
-// one wait can complete the loads of several arrays.
-__device__ __forceinline__ void tmem_tie(uint32_t (&r)[16]) {
-  asm volatile("" : VCB_RW16(r)::"memory");
-}
-__device__ __forceinline__ void tmem_tie(uint32_t (&r)[8]) {
-  asm volatile("" : VCB_RW8(r)::"memory");
-}
-__device__ __forceinline__ void tmem_tie(uint32_t (&r)[4]) {
-  asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3])::"memory");
-}
-
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
