@@ -7,7 +7,10 @@
 // compensated 3xTF32 operands: both operands split into TF32 hi and lo parts
 // (each rounded to nearest); hi_A hi_B goes to one tensor-memory accumulator
 // and the corrections lo_A hi_B + hi_A lo_B to a second, added by the
-// epilogue with a round-to-nearest fp32 add.  The tensor cores' fp32
+// epilogue with a round-to-nearest fp32 add.  A tf32 MMA of 128 rows takes
+// the same time for every N up to 128 (measured on B200: about 64 cycles), so
+// each K step is two MMAs: hi_A against the 128 rows [hi_B; lo_B] (both
+// accumulators at once) and lo_A against hi_B.  The tensor cores' fp32
 // accumulation truncates inside each K = 8 step, so results carry about twice
 // the rounding noise of an fp32 dot product (fp32-class, not bit-parity with
 // the SIMT kernel).
@@ -29,7 +32,8 @@
 // by the epilogue with tcgen05.st as tf32 hi / lo parts, in two slots (slot 0
 // = chain 0 / forward mid, slot 1 = chain 1 / forward rad); the weights (B)
 // are pre-split, pre-swizzled 64 x 64 images (W, |W| and [W^T; b] per layer,
-// built by crown_tc_images into the workspace) streamed through a 4-stage
+// built by crown_tc_images into the workspace; per 32-column K block the 64
+// hi rows, then the 64 lo rows) streamed through a 4-stage
 // shared-memory ring by one bulk copy each.  Tensor memory (512 columns): A
 // of slot s at 128 s (hi) and 128 s + 64 (lo), its accumulators at
 // 256 + 128 s (hi_A hi_B) and 256 + 128 s + 64 (corrections).
@@ -69,8 +73,8 @@ constexpr int kThreads = (kEpi + 1) * 32;  // 544
 constexpr int kW = 64;                     // padded operand width
 constexpr int kMaxWidth = 63;              // widest hidden / input layer
 constexpr int kBlk = kW * 128;             // 8 KB: 64 rows x 32 tf32 (one swizzle column)
-constexpr int kHalf = 2 * kBlk;            // 16 KB: one tf32 part of a 64 x 64 image
-constexpr int kImg = 2 * kHalf;            // hi + lo
+constexpr int kKBlk = 2 * kBlk;            // 16 KB: hi rows then lo rows of one K block
+constexpr int kImg = 2 * kKBlk;            // a 64 x 64 image, hi + lo
 constexpr int kStages = 4;
 constexpr int kMaxQ = 16;
 constexpr unsigned kSpin = 1u << 24;
@@ -128,8 +132,6 @@ struct TcParams {
   int tnet_floats;
 };
 
-__host__ __device__ inline int pad16(int n) { return (n + 15) & ~15; }
-
 // Work items of this CTA.  Item i < full is tile i * gridDim.x + blockIdx.x
 // with every spec-row pass.  The rem tiles of the last, partial round either
 // go whole to CTAs 0 .. rem-1, or (split_tail, 2 rem <= gridDim.x) each to
@@ -157,9 +159,11 @@ __device__ __forceinline__ TcItem item_at(const TcParams& p, int i) {
 // Weight images, one thread per (image, row, k); thread 0 also clears the
 // error word.  Image 3 l + 0: W_l
 // (rows = outputs, K = inputs), + 1: |W_l|, + 2: [W_l^T; b_l] (rows = inputs
-// then the bias row, K = outputs).  Each is split into tf32 hi (first 16 KB)
-// and lo, laid out as two 64-row x 32-column blocks with the 128-byte swizzle
-// of a K-major tcgen05 operand.
+// then the bias row, K = outputs).  Each is split into tf32 hi and lo parts,
+// laid out per 32-column K block as 128 rows (the 64 hi rows, then the 64 lo
+// rows) with the 128-byte swizzle of a K-major tcgen05 operand, so that one
+// descriptor covers [hi; lo] as an N = 128 operand and its first 64 rows hi
+// alone.
 // When the near-tie re-bound is on, the same launch clears the tie flags and
 // writes the plain fp32 rows of the network that crown_tie_kernel reads.
 __global__ void crown_tc_images(const TcParams p) {
@@ -203,25 +207,25 @@ __global__ void crown_tc_images(const TcParams p) {
   }
   uint32_t h, lo;
   tf32_split_rn(v, h, lo);
-  const int off = (k >> 5) * kBlk + (n >> 3) * 1024 + (n & 7) * 128 +
+  const int off = (k >> 5) * kKBlk + (n >> 3) * 1024 + (n & 7) * 128 +
                   ((((k & 31) >> 2) ^ (n & 7)) << 4) + (k & 3) * 4;
   uint8_t* base = const_cast<uint8_t*>(p.img) + (long long)im * kImg;
   *reinterpret_cast<uint32_t*>(base + off) = h;
-  *reinterpret_cast<uint32_t*>(base + kHalf + off) = lo;
+  *reinterpret_cast<uint32_t*>(base + kBlk + off) = lo;
 }
 
 // A B^T over `ksteps` K steps of 8 with 3xTF32: A in tensor memory (hi at
-// column a, lo at a + 64), B a weight image in shared memory (hi at b, lo at
-// b + kHalf, 8 KB per 32-column block); hi_A hi_B into accumulator d,
-// lo_A hi_B + hi_A lo_B into d + 64.
-__device__ __forceinline__ void gemm_ts(uint32_t d, uint32_t a, uint32_t b, int ksteps,
-                                        uint32_t idesc) {
+// column a, lo at a + 64), B a weight image in shared memory (16 KB per
+// 32-column K block: hi rows, then lo rows); hi_A hi_B into accumulator d,
+// hi_A lo_B + lo_A hi_B into d + 64.  Per K step one N = 128 MMA of hi_A
+// against [hi_B; lo_B] writes both accumulators, one N = 64 MMA adds lo_A
+// hi_B (padding rows of B are zero, so the unused columns stay zero).
+__device__ __forceinline__ void gemm_ts(uint32_t d, uint32_t a, uint32_t b, int ksteps) {
+  constexpr uint32_t id_both = idesc_tf32(kTB, 2 * kW), id_hi = idesc_tf32(kTB, kW);
   for (int j = 0; j < ksteps; ++j) {
-    const uint32_t bo = (uint32_t)((j >> 2) * kBlk + (j & 3) * 32);
-    const uint64_t bh = sw128_desc(b + bo), bl = sw128_desc(b + kHalf + bo);
-    mma_tf32_ts(d + kW, a + kW + 8 * j, bh, idesc, j > 0 ? 1u : 0u);
-    mma_tf32_ts(d + kW, a + 8 * j, bl, idesc, 1u);
-    mma_tf32_ts(d, a + 8 * j, bh, idesc, j > 0 ? 1u : 0u);
+    const uint64_t bd = sw128_desc(b + (uint32_t)((j >> 2) * kKBlk + (j & 3) * 32));
+    mma_tf32_ts(d, a + 8 * j, bd, id_both, j > 0 ? 1u : 0u);
+    mma_tf32_ts(d + kW, a + kW + 8 * j, bd, id_hi, 1u);
   }
 }
 
@@ -239,7 +243,9 @@ __device__ __forceinline__ float2* slot_base(const TcParams& p) {
 }
 
 // Split NC (4, 8 or 16) finite values and store the hi / lo parts at
-// tensor-memory columns taddr and taddr + 64 of this warp's lanes.
+// tensor-memory columns taddr and taddr + 64 of this warp's lanes.  The tensor
+// cores read only a tf32 operand's top 19 bits (its low 13 bits are ignored:
+// measured on B200), so the lo part is stored rounded but unmasked.
 template <int NC>
 __device__ __forceinline__ void store_operand(uint32_t taddr, const float (&v)[NC]) {
   uint32_t h[NC], l[NC];
@@ -248,7 +254,7 @@ __device__ __forceinline__ void store_operand(uint32_t taddr, const float (&v)[N
     const uint32_t u = (__float_as_uint(v[j]) + 0x1000u) & 0xFFFFE000u;
     const float r = __fsub_rn(v[j], __uint_as_float(u));
     h[j] = u;
-    l[j] = (__float_as_uint(r) + 0x1000u) & 0xFFFFE000u;
+    l[j] = __float_as_uint(r) + 0x1000u;
   }
   if constexpr (NC == 16) {
     tmem_st16(taddr, h);
@@ -396,9 +402,10 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
             if (o < nout) {
               const float2 e = encode_slope_fast(lo, hi);
               sl[o * kTB] = e;
-              // unstable (neither sign bit set) with the upper slope inside
-              // the band where rounding can move it across 0.5
-              tie |= !signbit(e.x) && !signbit(e.y) && fabsf(__fsub_rn(e.x, 0.5f)) <= kTieBand;
+              // unstable with the upper slope inside the band where rounding
+              // can move it across 0.5 (active records have e.x = 1, dead
+              // ones e.x <= 0: both are at least 0.5 away)
+              tie |= fabsf(__fsub_rn(e.x, 0.5f)) <= kTieBand;
             }
             const float lc = fmaxf(lo, 0.f), hc = fmaxf(hi, 0.f);
             mc[j] = o < nout ? __fmul_rn(__fadd_rn(lc, hc), 0.5f) : 0.f;
@@ -721,9 +728,8 @@ __global__ void __launch_bounds__(kThreads, 1) crown_tc_kernel(const __grid_cons
             int sw, sa;
             if (!(ok = wait_a(0) && take(sw) && take(sa))) break;
             const int ks = (p.dims[l] + 7) >> 3;
-            const uint32_t id = idesc_tf32(kTB, pad16(p.dims[l + 1]));
-            gemm_ts(tmem + 256, tmem, smem_u32(ring + sw * kImg), ks, id);
-            gemm_ts(tmem + 384, tmem + 128, smem_u32(ring + sa * kImg), ks, id);
+            gemm_ts(tmem + 256, tmem, smem_u32(ring + sw * kImg), ks);
+            gemm_ts(tmem + 384, tmem + 128, smem_u32(ring + sa * kImg), ks);
             mma_commit(&w_empty[sw]);
             mma_commit(&w_empty[sa]);
             mma_commit(&acc_ready[0]);
@@ -735,10 +741,9 @@ __global__ void __launch_bounds__(kThreads, 1) crown_tc_kernel(const __grid_cons
             int st;
             if (!(ok = take(st))) break;
             const int ks = (p.dims[l + 1] + 7) >> 3;
-            const uint32_t id = idesc_tf32(kTB, pad16(p.dims[l] + 1));
             for (int c = 0; c < 2 && 2 * pass + c < Q; ++c) {
               if (!(ok = wait_a(c))) break;
-              gemm_ts(tmem + 256 + 128 * c, tmem + 128 * c, smem_u32(ring + st * kImg), ks, id);
+              gemm_ts(tmem + 256 + 128 * c, tmem + 128 * c, smem_u32(ring + st * kImg), ks);
               mma_commit(&acc_ready[c]);
             }
             mma_commit(&w_empty[st]);
