@@ -300,14 +300,14 @@ __device__ __forceinline__ void load_acc(uint32_t taddr, float (&v)[NC]) {
 // 2 ulp): the tensor-core bounds already differ from the fp32 reference by
 // rounding, a box whose up_s lies near the 0.5 threshold is listed for the
 // exact re-bound, and the upper relaxation moves by ulps of its terms.
+// Branch-free: the same records as encode_slope's early returns (active:
+// (1, -0); ub_r = 0: up_s = 0, so (-0, 0)) come out of the selects.
 __device__ __forceinline__ float2 encode_slope_fast(float lo, float hi) {
-  if (lo >= 0.f) return make_float2(1.f, -0.0f);  // active
-  const bool dead = hi <= 0.f;
   const float ub_r = fmaxf(fmaxf(hi, 0.f), __fadd_rn(lo, 1e-8f));
-  if (ub_r == 0.f) return make_float2(-0.0f, 0.0f);  // dead, up_s = 0
   const float up_s = __fdividef(ub_r, __fsub_rn(ub_r, lo));
-  const float up_t = __fmul_rn(-lo, up_s);
-  return make_float2(dead ? -up_s : up_s, up_t);
+  const float up_t = ub_r == 0.f ? 0.f : __fmul_rn(-lo, up_s);
+  const bool active = lo >= 0.f, dead = hi <= 0.f;
+  return make_float2(active ? 1.f : (dead ? -up_s : up_s), active ? -0.0f : up_t);
 }
 
 using C4 = std::integral_constant<int, 4>;
@@ -377,10 +377,15 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
         const bool last = l == nfc - 2;
         const long long gi0 = p.relu_goff[l] + (long long)box * nout;
         float2* sl = slot + p.sl_off[l] + row;
-        // one chunk of NC output columns starting at c0
-        auto chunk = [&](auto nc, int c0) {
+        bool published = false;
+        // one chunk of NC output columns starting at c0 (pad4: zeros in the
+        // four columns after it, the rest of the next MMA's K step).  The
+        // next layer's operands are stored and published first; the ReLU
+        // slopes, which only the back-substitution reads, follow while the
+        // tensor cores run the next layer.
+        auto chunk = [&](auto nc, int c0, bool pad4) {
           constexpr int NC = decltype(nc)::value;
-          float mc[NC], rc[NC];
+          float mc[NC], rc[NC], lo[NC], hi[NC];
           load_acc<NC>(tl + 256 + c0, mc);
           load_acc<NC>(tl + 384 + c0, rc);
           const float* bias = sBias + l * kW + c0;
@@ -388,50 +393,56 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
           for (int j = 0; j < NC; ++j) {
             const int o = c0 + j;
             const float mid = __fadd_rn(mc[j], bias[j]);
-            float lo = __fsub_rn(mid, rc[j]);
-            float hi = __fadd_rn(mid, rc[j]);
+            lo[j] = __fsub_rn(mid, rc[j]);
+            hi[j] = __fadd_rn(mid, rc[j]);
             if (!kPlain && p.clo && valid && o < nout) {
-              lo = fmaxf(lo, __ldg(p.clo + gi0 + o));
-              hi = fminf(hi, __ldg(p.chi + gi0 + o));
+              lo[j] = fmaxf(lo[j], __ldg(p.clo + gi0 + o));
+              hi[j] = fminf(hi[j], __ldg(p.chi + gi0 + o));
             }
-            hi = fmaxf(hi, lo);
-            if (!kPlain && p.sbolo && valid && o < nout) {
-              p.sbolo[gi0 + o] = lo;
-              p.sbohi[gi0 + o] = hi;
-            }
-            if (o < nout) {
-              const float2 e = encode_slope_fast(lo, hi);
-              sl[o * kTB] = e;
-              // unstable with the upper slope inside the band where rounding
-              // can move it across 0.5 (active records have e.x = 1, dead
-              // ones e.x <= 0: both are at least 0.5 away)
-              tie |= fabsf(__fsub_rn(e.x, 0.5f)) <= kTieBand;
-            }
-            const float lc = fmaxf(lo, 0.f), hc = fmaxf(hi, 0.f);
+            hi[j] = fmaxf(hi[j], lo[j]);
+            const float lc = fmaxf(lo[j], 0.f), hc = fmaxf(hi[j], 0.f);
             mc[j] = o < nout ? __fmul_rn(__fadd_rn(lc, hc), 0.5f) : 0.f;
             rc[j] = o < nout ? __fmul_rn(__fsub_rn(hc, lc), 0.5f) : 0.f;
           }
           if (!last) {
             store_operand<NC>(tl + c0, mc);
             store_operand<NC>(tl + 128 + c0, rc);
+            if (pad4) {
+              store_zero4(tl + c0 + NC);
+              store_zero4(tl + 128 + c0 + NC);
+            }
+            publish(&a_ready[0]);
+          }
+          published = true;
+#pragma unroll
+          for (int j = 0; j < NC; ++j) {
+            const int o = c0 + j;
+            if (o < nout) {
+              if (!kPlain && p.sbolo && valid) {
+                p.sbolo[gi0 + o] = lo[j];
+                p.sbohi[gi0 + o] = hi[j];
+              }
+              const float2 e = encode_slope_fast(lo[j], hi[j]);
+              sl[o * kTB] = e;
+              // unstable with the upper slope inside the band where rounding
+              // can move it across 0.5 (active records have e.x = 1, dead
+              // ones e.x <= 0: both are at least 0.5 away)
+              tie |= fabsf(__fsub_rn(e.x, 0.5f)) <= kTieBand;
+            }
           }
         };
         for (int k = 0; k < nck; ++k) {
           const int c0 = chunk_c0(k);
           if (c0 >= nout) continue;
           if (nout - c0 <= 4) {  // a short tail: 4 columns, then zeros to pad8
-            chunk(C4{}, c0);
-            if (!last) {
-              store_zero4(tl + c0 + 4);
-              store_zero4(tl + 128 + c0 + 4);
-            }
+            chunk(C4{}, c0, true);
           } else if (nout - c0 <= 8) {
-            chunk(C8{}, c0);
+            chunk(C8{}, c0, false);
           } else {
-            chunk(C16{}, c0);
+            chunk(C16{}, c0, false);
           }
         }
-        if (!last) publish(&a_ready[0]);
+        if (!last && !published) publish(&a_ready[0]);
       }
       if (!ok) break;
       // list the box for crown_tie_kernel once (the column warps of a row and
