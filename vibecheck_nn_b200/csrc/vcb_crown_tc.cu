@@ -313,6 +313,8 @@ __device__ __forceinline__ float2 encode_slope_fast(float lo, float hi) {
 using C4 = std::integral_constant<int, 4>;
 using C8 = std::integral_constant<int, 8>;
 using C16 = std::integral_constant<int, 16>;
+using In = std::true_type;    // the chunk lies inside the layer width
+using Out = std::false_type;  // it may reach past it (guards on)
 
 // The 16 epilogue warps: warp w owns the tile's boxes 32 (w % 4) + lane
 // (tensor-memory lanes) and the 16-column operand chunk 16 (w / 4).  kPlain: no alpha, beta, clamps or sb outputs (the common
@@ -379,12 +381,14 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
         float2* sl = slot + p.sl_off[l] + row;
         bool published = false;
         // one chunk of NC output columns starting at c0 (pad4: zeros in the
-        // four columns after it, the rest of the next MMA's K step).  The
-        // next layer's operands are stored and published first; the ReLU
+        // four columns after it, the rest of the next MMA's K step; IN: every
+        // column of the chunk is an output of the layer, no width guards).
+        // The next layer's operands are stored and published first; the ReLU
         // slopes, which only the back-substitution reads, follow while the
         // tensor cores run the next layer.
-        auto chunk = [&](auto nc, int c0, bool pad4) {
+        auto chunk = [&](auto nc, int c0, bool pad4, auto in) {
           constexpr int NC = decltype(nc)::value;
+          constexpr bool IN = decltype(in)::value;
           float mc[NC], rc[NC], lo[NC], hi[NC];
           load_acc<NC>(tl + 256 + c0, mc);
           load_acc<NC>(tl + 384 + c0, rc);
@@ -395,14 +399,14 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
             const float mid = __fadd_rn(mc[j], bias[j]);
             lo[j] = __fsub_rn(mid, rc[j]);
             hi[j] = __fadd_rn(mid, rc[j]);
-            if (!kPlain && p.clo && valid && o < nout) {
+            if (!kPlain && p.clo && valid && (IN || o < nout)) {
               lo[j] = fmaxf(lo[j], __ldg(p.clo + gi0 + o));
               hi[j] = fminf(hi[j], __ldg(p.chi + gi0 + o));
             }
             hi[j] = fmaxf(hi[j], lo[j]);
             const float lc = fmaxf(lo[j], 0.f), hc = fmaxf(hi[j], 0.f);
-            mc[j] = o < nout ? __fmul_rn(__fadd_rn(lc, hc), 0.5f) : 0.f;
-            rc[j] = o < nout ? __fmul_rn(__fsub_rn(hc, lc), 0.5f) : 0.f;
+            mc[j] = (IN || o < nout) ? __fmul_rn(__fadd_rn(lc, hc), 0.5f) : 0.f;
+            rc[j] = (IN || o < nout) ? __fmul_rn(__fsub_rn(hc, lc), 0.5f) : 0.f;
           }
           if (!last) {
             store_operand<NC>(tl + c0, mc);
@@ -417,7 +421,7 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
 #pragma unroll
           for (int j = 0; j < NC; ++j) {
             const int o = c0 + j;
-            if (o < nout) {
+            if (IN || o < nout) {
               if (!kPlain && p.sbolo && valid) {
                 p.sbolo[gi0 + o] = lo[j];
                 p.sbohi[gi0 + o] = hi[j];
@@ -435,11 +439,13 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
           const int c0 = chunk_c0(k);
           if (c0 >= nout) continue;
           if (nout - c0 <= 4) {  // a short tail: 4 columns, then zeros to pad8
-            chunk(C4{}, c0, true);
+            chunk(C4{}, c0, true, Out{});
           } else if (nout - c0 <= 8) {
-            chunk(C8{}, c0, false);
+            chunk(C8{}, c0, false, Out{});
+          } else if (nout - c0 >= 16) {
+            chunk(C16{}, c0, false, In{});
           } else {
-            chunk(C16{}, c0, false);
+            chunk(C16{}, c0, false, Out{});
           }
         }
         if (!last && !published) publish(&a_ready[0]);
@@ -479,9 +485,11 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
         for (int c = 0; c < nch; ++c) {
           const int q = 2 * pass + c;
           if (l < nfc - 1 && !(ok = wait_acc(c))) break;
-          // one chunk of NC columns starting at c0 (neurons and / or the bias column)
-          auto chunk = [&](auto nc, int c0) {
+          // one chunk of NC columns starting at c0 (neurons and / or the bias
+          // column; IN: neurons only, no width guards)
+          auto chunk = [&](auto nc, int c0, auto in) {
             constexpr int NC = decltype(nc)::value;
+            constexpr bool IN = decltype(in)::value;
             float v[NC];
             if (l == nfc - 1) {
 #pragma unroll
@@ -495,7 +503,7 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
             }
             const int bc = nin - c0;  // bias column within the chunk
             float bj = 0.f;
-            if (bc < NC) {
+            if (!IN && bc < NC) {
 #pragma unroll
               for (int j = 0; j < NC; ++j)
                 if (j == bc) bj = v[j];
@@ -504,7 +512,7 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
               float2 sv[NC];  // slopes, zero beyond the layer width
 #pragma unroll
               for (int j = 0; j < NC; ++j)
-                sv[j] = c0 + j < nin ? sl[(c0 + j) * kTB] : make_float2(0.f, 0.f);
+                sv[j] = (IN || c0 + j < nin) ? sl[(c0 + j) * kTB] : make_float2(0.f, 0.f);
               float pj = 0.f;
 #pragma unroll
               for (int j = 0; j < NC; ++j) {
@@ -518,7 +526,7 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
                 } else {
                   const int i = c0 + j;
                   v[j] = 0.f;
-                  if (i < nin) {
+                  if (IN || i < nin) {
                     const Slope s = decode_slope(sv[j], arow ? arow + i : nullptr);
                     const float mlt = x < 0.f ? s.neg : s.pos;
                     pj = fmaf(fminf(x, 0.f), s.icp, pj);
@@ -551,12 +559,14 @@ __device__ __forceinline__ bool epilogue(const TcParams& p, uint32_t tmem, float
             const int c0 = chunk_c0(k);
             if (c0 > nin) continue;  // no neurons and no bias column here
             if (nin + 1 - c0 <= 4) {  // a short tail: 4 columns, then zeros to pad8
-              chunk(C4{}, c0);
+              chunk(C4{}, c0, Out{});
               if (L >= 0) store_zero4(tl + 128 * c + c0 + 4);
             } else if (nin + 1 - c0 <= 8) {
-              chunk(C8{}, c0);
+              chunk(C8{}, c0, Out{});
+            } else if (c0 + 16 <= nin) {
+              chunk(C16{}, c0, In{});
             } else {
-              chunk(C16{}, c0);
+              chunk(C16{}, c0, Out{});
             }
           }
           if (L >= 0) publish(&a_ready[c]);
