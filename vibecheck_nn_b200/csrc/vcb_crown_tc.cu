@@ -735,8 +735,10 @@ __global__ void __launch_bounds__(kThreads, 1) crown_tc_kernel(const __grid_cons
         ++used;
         return true;
       };
+      // polled without a suspend hint: this thread issues every MMA, and a
+      // late wake-up would delay them all
       auto wait_a = [&](int c) {
-        if (!mbar_wait_sleep(&a_ready[c], ua[c] & 1, kSpinSleep, vfailed)) return false;
+        if (!mbar_wait(&a_ready[c], ua[c] & 1, kSpin, vfailed)) return false;
         ++ua[c];
         fence_after_sync();
         return true;
