@@ -63,6 +63,7 @@ struct PgdNet {
 struct PgdParams {
   PgdNet net;
   int N, R, n_iter, ncon, D;
+  int ntiles;             // tiles of N / ntiles samples, a multiple of the grid
   float lr;
   float* x;               // (N, n_in) in/out
   const float *lo, *hi;   // (N / R, n_in) box of each group of R samples
@@ -124,14 +125,16 @@ __device__ void load_net(const PgdNet& n, float* sm, int tid) {
   }
 }
 
-// Forward pass of the tile's samples xs (kPS x n0): z_l kept for the masks,
-// a_{l+1} = relu(z_l); the network output is z_{n_fc-1}.  A thread computes
-// 4 consecutive outputs of one sample: z[o] = sum_i a[i] W[o][i] in ascending
-// i, then + b[o].
-__device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int tid) {
+// Forward pass of the tile's first ns samples xs (kPS x n0): z_l kept for the
+// masks, a_{l+1} = relu(z_l); the network output is z_{n_fc-1}.  A thread
+// computes 4 consecutive outputs of one sample: z[o] = sum_i a[i] W[o][i] in
+// ascending i, then + b[o].  Rows from ns on are left as they were (the
+// passes are bound by shared-memory traffic, which scales with the samples
+// processed).
+__device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int tid, int ns) {
   const int n0 = n.dims[0], pa = n.pa, pz = n.pz;
   float* a_cur = sm + n.act_soff;
-  for (int idx = tid; idx < kPS * n0; idx += kPT) {
+  for (int idx = tid; idx < ns * n0; idx += kPT) {
     const int s = idx / n0, i = idx - s * n0;
     a_cur[s * pa + i] = xs[idx];
   }
@@ -143,8 +146,8 @@ __device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int ti
     float* aout = sm + n.act_soff + ((l + 1) & 1) * kPS * pa;
     float* z = sm + n.z_soff + l * kPS * pz;
     const int nob = pwt >> 2;
-    for (int idx = tid; idx < kPS * nob; idx += kPT) {
-      const int ob = idx / kPS, s = idx - ob * kPS;
+    for (int idx = tid; idx < ns * nob; idx += kPT) {
+      const int ob = idx / ns, s = idx - ob * ns;
       const int o4 = 4 * ob;
       const float* ar = ain + s * pa;
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
@@ -172,21 +175,25 @@ __device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int ti
   }
 }
 
-// Backward pass: g (kPS x pz, seeded with d loss / d y, zero past n_out) is
-// replaced by d loss / d x in its first n0 columns.
-__device__ void tile_backward(const PgdNet& n, float* sm, int tid) {
+// Backward pass of the tile's first ns samples: g (kPS x pz, seeded with
+// d loss / d y, zero past n_out) is replaced by d loss / d x in its first n0
+// columns.  Sample sl of the tile gets the kPT / ns threads tid = sl + ns k
+// (at least kStep of them), each summing whole input columns.
+__device__ void tile_backward(const PgdNet& n, float* sm, int tid, int ns) {
   const int pz = n.pz;
   float* g = sm + n.g_soff;
+  const int step = kPT / ns;
+  const int sl = tid % ns, i0 = tid / ns;
+  const bool active = i0 < step;
   for (int l = n.n_fc - 1; l >= 0; --l) {
     const int nin = n.dims[l], nout = n.dims[l + 1], pwt = n.pwt[l];
     const float* sWT = sm + n.wt_soff[l];
     const float* zprev = (l > 0) ? sm + n.z_soff + (l - 1) * kPS * pz : nullptr;
     float vals[(kPMaxW + kStep - 1) / kStep];
-    const int sl = tid % kPS, i0 = tid / kPS;
     const float* grow = g + sl * pz;
     const int kend = pad4(nout);
     int cnt = 0;
-    for (int i = i0; i < nin; i += kStep) {
+    for (int i = active ? i0 : nin; i < nin; i += step) {
       // sum over o in fixed ascending order, 4 at a time (g and W^T rows are
       // zero past n_out)
       const float* wt = sWT + i * pwt;
@@ -204,7 +211,7 @@ __device__ void tile_backward(const PgdNet& n, float* sm, int tid) {
     }
     __syncthreads();  // every thread has read g
     cnt = 0;
-    for (int i = i0; i < pz; i += kStep) g[sl * pz + i] = (i < nin) ? vals[cnt++] : 0.f;
+    for (int i = active ? i0 : pz; i < pz; i += step) g[sl * pz + i] = (i < nin) ? vals[cnt++] : 0.f;
     __syncthreads();
   }
 }
@@ -227,10 +234,11 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
   const int pz = n.pz;
   float* xs = sm + n.x_soff;  // kPS x n0 current samples
   float* g = sm + n.g_soff;   // kPS x pz gradient rows
-  const int ntiles = (p.N + kPS - 1) / kPS;
-  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int s0 = tile * kPS;
-    const int ns = min(kPS, p.N - s0);
+  // p.ntiles tiles of N / ntiles samples each (at most kPS), a whole number
+  // of rounds of the grid: no round with a few tiles while the other CTAs idle
+  for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
+    const int s0 = (int)((long long)tile * p.N / p.ntiles);
+    const int ns = (int)((long long)(tile + 1) * p.N / p.ntiles) - s0;
     for (int idx = tid; idx < kPS * n0; idx += kPT) {
       const int s = idx / n0, i = idx - s * n0;
       xs[idx] = s < ns ? p.x[(long long)(s0 + s) * n0 + i] : 0.f;
@@ -245,7 +253,7 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
       }
       __syncthreads();
       if (stop) break;
-      tile_forward(n, sm, xs, tid);
+      tile_forward(n, sm, xs, tid, ns);
       // ---- margins, SAT check and the output gradient row
       const float* y = sm + n.z_soff + (nfc - 1) * kPS * pz;
       for (int s = tid; s < kPS; s += kPT) {
@@ -283,7 +291,7 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
         g[idx] = (o < nL && !done[s]) ? Cs[cstar[s] * nL + o] : 0.f;
       }
       __syncthreads();
-      tile_backward(n, sm, tid);
+      tile_backward(n, sm, tid, ns);
       // ---- sign step and clamp (SAT samples keep the x that was SAT)
       for (int idx = tid; idx < ns * n0; idx += kPT) {
         const int s = idx / n0, i = idx - s * n0;
@@ -356,13 +364,13 @@ __global__ void __launch_bounds__(kPT, 1)
     __syncthreads();
     // ---- OSI: x <- clamp(x + step0 * sign(d (w_r . f(x)) / dx), lo, hi)
     for (int k = 0; k < p.n_osi; ++k) {
-      tile_forward(n, sm, xs, tid);
+      tile_forward(n, sm, xs, tid, ns);
       for (int idx = tid; idx < kPS * pz; idx += kPT) {
         const int s = idx / pz, o = idx - s * pz;
         g[idx] = (o < nL && s < ns) ? p.w_d[(long long)((s0 + s) % p.R) * nL + o] : 0.f;
       }
       __syncthreads();
-      tile_backward(n, sm, tid);
+      tile_backward(n, sm, tid, ns);
       for (int idx = tid; idx < ns * n0; idx += kPT) {
         const int s = idx / n0, i = idx - s * n0;
         const long long bi = (long long)((s0 + s) / p.R) * n0 + i;
@@ -386,8 +394,8 @@ __global__ void __launch_bounds__(kPT, 1)
       }
       __syncthreads();
       if (stop) break;
-      tile_forward(n, sm, xs, tid);
-      for (int idx = tid; idx < kPS * ncon; idx += kPT) {
+      tile_forward(n, sm, xs, tid, ns);
+      for (int idx = tid; idx < ns * ncon; idx += kPT) {
         const int s = idx / ncon, c = idx - s * ncon;
         float m = 0.f;
         for (int o = 0; o < nL; ++o) m = fmaf(y[s * pz + o], Cs[c * nL + o], m);
@@ -460,7 +468,7 @@ __global__ void __launch_bounds__(kPT, 1)
         g[idx] = gv;
       }
       __syncthreads();
-      tile_backward(n, sm, tid);
+      tile_backward(n, sm, tid, ns);
       // ---- optimiser step, clamp, step decay
       const float sc1 = p.inv_bc1[t - 1], sc2 = p.inv_sbc2[t - 1];
       for (int idx = tid; idx < ns * n0; idx += kPT) {
@@ -713,6 +721,9 @@ extern "C" int vcb_mlp_pgd(const vcb_mlp* net, int32_t N, int32_t R, float* x,
   if (rc) return rc;
   const int ntiles = (N + kPS - 1) / kPS;
   const int grid = std::max(1, std::min(ntiles, sm_count()));
+  // whole rounds of the grid; each tile N / p.ntiles <= kPS samples (and at
+  // least one: p.ntiles < 2 ntiles <= N + 1)
+  p.ntiles = grid * ((ntiles + grid - 1) / grid);
   pgd_mlp_kernel<<<grid, kPT, bytes, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("vcb_mlp_pgd: launch");
 }
