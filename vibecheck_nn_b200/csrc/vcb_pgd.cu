@@ -1,8 +1,9 @@
 // Batched PGD counterexample search for ReLU MLPs.
 //
 // Two kernels share one shared-memory layout (fc weights resident, one tile of
-// kPS samples per CTA, pre-activations kept for the ReLU masks) and the same
-// tile forward / backward passes:
+// up to kPS samples per CTA -- kPSBig for the simple attack when the network
+// leaves room -- pre-activations kept for the ReLU masks) and the same tile
+// forward / backward passes:
 //
 // * pgd_mlp_kernel -- the sign-gradient PGD of _simple_pgd / _simple_pgd_batched
 //   (verify_hybrid_acasxu.py:39-161).  Each sample x (a restart inside its box
@@ -38,8 +39,8 @@ namespace {
 
 constexpr int kPT = 1024;  // threads per CTA (16 per sample: the iterations are latency-bound)
 constexpr int kPS = 64;    // samples per tile
+constexpr int kPSBig = 72; // tile of the simple attack when the network leaves room for it
 constexpr int kPMaxW = 128;
-constexpr int kStep = kPT / kPS;
 
 // Shared-memory layout of the network and one sample tile (offsets in floats).
 // The activation rows need no padding beyond n: every loop over inputs stops
@@ -131,6 +132,7 @@ __device__ void load_net(const PgdNet& n, float* sm, int tid) {
 // ascending i, then + b[o].  Rows from ns on are left as they were (the
 // passes are bound by shared-memory traffic, which scales with the samples
 // processed).
+template <int PS>
 __device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int tid, int ns) {
   const int n0 = n.dims[0], pa = n.pa, pz = n.pz;
   float* a_cur = sm + n.act_soff;
@@ -142,9 +144,9 @@ __device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int ti
   for (int l = 0; l < n.n_fc; ++l) {
     const int nin = n.dims[l], nout = n.dims[l + 1], pwt = n.pwt[l];
     const float* sWT = sm + n.wt_soff[l];
-    const float* ain = sm + n.act_soff + (l & 1) * kPS * pa;
-    float* aout = sm + n.act_soff + ((l + 1) & 1) * kPS * pa;
-    float* z = sm + n.z_soff + l * kPS * pz;
+    const float* ain = sm + n.act_soff + (l & 1) * PS * pa;
+    float* aout = sm + n.act_soff + ((l + 1) & 1) * PS * pa;
+    float* z = sm + n.z_soff + l * PS * pz;
     const int nob = pwt >> 2;
     for (int idx = tid; idx < ns * nob; idx += kPT) {
       const int ob = idx / ns, s = idx - ob * ns;
@@ -178,7 +180,8 @@ __device__ void tile_forward(const PgdNet& n, float* sm, const float* xs, int ti
 // Backward pass of the tile's first ns samples: g (kPS x pz, seeded with
 // d loss / d y, zero past n_out) is replaced by d loss / d x in its first n0
 // columns.  Sample sl of the tile gets the kPT / ns threads tid = sl + ns k
-// (at least kStep of them), each summing whole input columns.
+// (at least kPT / PS of them), each summing whole input columns.
+template <int PS>
 __device__ void tile_backward(const PgdNet& n, float* sm, int tid, int ns) {
   const int pz = n.pz;
   float* g = sm + n.g_soff;
@@ -188,8 +191,8 @@ __device__ void tile_backward(const PgdNet& n, float* sm, int tid, int ns) {
   for (int l = n.n_fc - 1; l >= 0; --l) {
     const int nin = n.dims[l], nout = n.dims[l + 1], pwt = n.pwt[l];
     const float* sWT = sm + n.wt_soff[l];
-    const float* zprev = (l > 0) ? sm + n.z_soff + (l - 1) * kPS * pz : nullptr;
-    float vals[(kPMaxW + kStep - 1) / kStep];
+    const float* zprev = (l > 0) ? sm + n.z_soff + (l - 1) * PS * pz : nullptr;
+    float vals[(kPMaxW + kPT / PS - 1) / (kPT / PS)];
     const float* grow = g + sl * pz;
     const int kend = pad4(nout);
     int cnt = 0;
@@ -216,10 +219,11 @@ __device__ void tile_backward(const PgdNet& n, float* sm, int tid, int ns) {
   }
 }
 
+template <int PS>
 __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__ PgdParams p) {
   extern __shared__ __align__(16) float sm[];
-  __shared__ int done[kPS];
-  __shared__ int cstar[kPS];
+  __shared__ int done[PS];
+  __shared__ int cstar[PS];
   __shared__ int stop;
   const PgdNet& n = p.net;
   const int tid = threadIdx.x;
@@ -232,18 +236,18 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
   for (int idx = tid; idx < p.ncon; idx += kPT) Cs[p.ncon * nL + idx] = p.cb[idx];
   __syncthreads();
   const int pz = n.pz;
-  float* xs = sm + n.x_soff;  // kPS x n0 current samples
-  float* g = sm + n.g_soff;   // kPS x pz gradient rows
-  // p.ntiles tiles of N / ntiles samples each (at most kPS), a whole number
+  float* xs = sm + n.x_soff;  // PS x n0 current samples
+  float* g = sm + n.g_soff;   // PS x pz gradient rows
+  // p.ntiles tiles of N / ntiles samples each (at most PS), a whole number
   // of rounds of the grid: no round with a few tiles while the other CTAs idle
   for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
     const int s0 = (int)((long long)tile * p.N / p.ntiles);
     const int ns = (int)((long long)(tile + 1) * p.N / p.ntiles) - s0;
-    for (int idx = tid; idx < kPS * n0; idx += kPT) {
+    for (int idx = tid; idx < PS * n0; idx += kPT) {
       const int s = idx / n0, i = idx - s * n0;
       xs[idx] = s < ns ? p.x[(long long)(s0 + s) * n0 + i] : 0.f;
     }
-    for (int s = tid; s < kPS; s += kPT) done[s] = s < ns ? 0 : 1;
+    for (int s = tid; s < PS; s += kPT) done[s] = s < ns ? 0 : 1;
     __syncthreads();
     for (int it = 0; it < p.n_iter; ++it) {
       // once a SAT sample exists at an earlier iteration nothing here can win
@@ -253,10 +257,10 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
       }
       __syncthreads();
       if (stop) break;
-      tile_forward(n, sm, xs, tid, ns);
+      tile_forward<PS>(n, sm, xs, tid, ns);
       // ---- margins, SAT check and the output gradient row
-      const float* y = sm + n.z_soff + (nfc - 1) * kPS * pz;
-      for (int s = tid; s < kPS; s += kPT) {
+      const float* y = sm + n.z_soff + (nfc - 1) * PS * pz;
+      for (int s = tid; s < PS; s += kPT) {
         if (done[s]) continue;
         float dmin = 0.f;
         int cbest = 0;
@@ -286,12 +290,12 @@ __global__ void __launch_bounds__(kPT, 1) pgd_mlp_kernel(const __grid_constant__
       }
       __syncthreads();
       // ---- backward: g = C[c*], then g <- (g W_l) masked by z_{l-1} > 0
-      for (int idx = tid; idx < kPS * pz; idx += kPT) {
+      for (int idx = tid; idx < PS * pz; idx += kPT) {
         const int s = idx / pz, o = idx - s * pz;
         g[idx] = (o < nL && !done[s]) ? Cs[cstar[s] * nL + o] : 0.f;
       }
       __syncthreads();
-      tile_backward(n, sm, tid, ns);
+      tile_backward<PS>(n, sm, tid, ns);
       // ---- sign step and clamp (SAT samples keep the x that was SAT)
       for (int idx = tid; idx < ns * n0; idx += kPT) {
         const int s = idx / n0, i = idx - s * n0;
@@ -364,13 +368,13 @@ __global__ void __launch_bounds__(kPT, 1)
     __syncthreads();
     // ---- OSI: x <- clamp(x + step0 * sign(d (w_r . f(x)) / dx), lo, hi)
     for (int k = 0; k < p.n_osi; ++k) {
-      tile_forward(n, sm, xs, tid, ns);
+      tile_forward<kPS>(n, sm, xs, tid, ns);
       for (int idx = tid; idx < kPS * pz; idx += kPT) {
         const int s = idx / pz, o = idx - s * pz;
         g[idx] = (o < nL && s < ns) ? p.w_d[(long long)((s0 + s) % p.R) * nL + o] : 0.f;
       }
       __syncthreads();
-      tile_backward(n, sm, tid, ns);
+      tile_backward<kPS>(n, sm, tid, ns);
       for (int idx = tid; idx < ns * n0; idx += kPT) {
         const int s = idx / n0, i = idx - s * n0;
         const long long bi = (long long)((s0 + s) / p.R) * n0 + i;
@@ -394,7 +398,7 @@ __global__ void __launch_bounds__(kPT, 1)
       }
       __syncthreads();
       if (stop) break;
-      tile_forward(n, sm, xs, tid, ns);
+      tile_forward<kPS>(n, sm, xs, tid, ns);
       for (int idx = tid; idx < ns * ncon; idx += kPT) {
         const int s = idx / ncon, c = idx - s * ncon;
         float m = 0.f;
@@ -468,7 +472,7 @@ __global__ void __launch_bounds__(kPT, 1)
         g[idx] = gv;
       }
       __syncthreads();
-      tile_backward(n, sm, tid, ns);
+      tile_backward<kPS>(n, sm, tid, ns);
       // ---- optimiser step, clamp, step decay
       const float sc1 = p.inv_bc1[t - 1], sc2 = p.inv_sbc2[t - 1];
       for (int idx = tid; idx < ns * n0; idx += kPT) {
@@ -637,7 +641,7 @@ __global__ void __launch_bounds__(256) pgd_step_kernel(const StepArgs a) {
 
 // Shared-memory plan of the network and a sample tile; returns the next free
 // offset (floats) or -1 when a width is out of range.
-int plan_net(const vcb_mlp* net, int ncon, PgdNet& n, const char* who) {
+int plan_net(const vcb_mlp* net, int ncon, PgdNet& n, const char* who, int ps = kPS) {
   const int nfc = net->n_fc;
   n.n_fc = nfc;
   int off = 0, maxw = 1;
@@ -663,13 +667,13 @@ int plan_net(const vcb_mlp* net, int ncon, PgdNet& n, const char* who) {
   n.pa = maxw | 1;         // odd: scalar loads of 32 samples' rows hit 32 banks
   n.pz = pad4odd(maxw);    // 4 x odd: float4 loads of 8 samples' rows hit 32 banks
   n.act_soff = off;
-  off += 2 * kPS * n.pa;
+  off += 2 * ps * n.pa;
   n.z_soff = off;
-  off += pad4(nfc * kPS * n.pz);
+  off += pad4(nfc * ps * n.pz);
   n.g_soff = off;
-  off += pad4(kPS * n.pz);
+  off += pad4(ps * n.pz);
   n.x_soff = off;
-  off += pad4(kPS * net->dims[0]);
+  off += pad4(ps * net->dims[0]);
   n.c_soff = off;
   off += pad4(ncon * net->dims[nfc] + ncon);
   n.W = net->W;
@@ -699,8 +703,15 @@ extern "C" int vcb_mlp_pgd(const vcb_mlp* net, int32_t N, int32_t R, float* x,
   if (!x || !lo || !hi || !C || !cb || !cdis || !best || !net->W || !net->b)
     return fail(VCB_ERR_INVALID, "vcb_mlp_pgd: NULL pointer");
   PgdParams p{};
-  const int off = plan_net(net, ncon, p.net, "vcb_mlp_pgd");
+  // tiles of kPSBig samples when the network leaves room for them (10,000
+  // restarts of a 50-wide network: one round of 139 tiles), else kPS
+  int ps = kPSBig;
+  int off = plan_net(net, ncon, p.net, "vcb_mlp_pgd", ps);
   if (off < 0) return VCB_ERR_UNSUPPORTED;
+  if (off * 4 > kSmemCap) {
+    ps = kPS;
+    off = plan_net(net, ncon, p.net, "vcb_mlp_pgd", ps);
+  }
   const int bytes = off * 4;
   if (bytes > kSmemCap)
     return fail(VCB_ERR_UNSUPPORTED, "vcb_mlp_pgd: network needs %d bytes of shared memory", bytes);
@@ -717,14 +728,15 @@ extern "C" int vcb_mlp_pgd(const vcb_mlp* net, int32_t N, int32_t R, float* x,
   p.cb = cb;
   p.cdis = cdis;
   p.best = best;
-  int rc = ensure_smem(reinterpret_cast<const void*>(pgd_mlp_kernel), bytes);
+  auto kern = ps == kPSBig ? pgd_mlp_kernel<kPSBig> : pgd_mlp_kernel<kPS>;
+  int rc = ensure_smem(reinterpret_cast<const void*>(kern), bytes);
   if (rc) return rc;
-  const int ntiles = (N + kPS - 1) / kPS;
+  const int ntiles = (N + ps - 1) / ps;
   const int grid = std::max(1, std::min(ntiles, sm_count()));
-  // whole rounds of the grid; each tile N / p.ntiles <= kPS samples (and at
+  // whole rounds of the grid; each tile N / p.ntiles <= ps samples (and at
   // least one: p.ntiles < 2 ntiles <= N + 1)
   p.ntiles = grid * ((ntiles + grid - 1) / grid);
-  pgd_mlp_kernel<<<grid, kPT, bytes, static_cast<cudaStream_t>(stream)>>>(p);
+  kern<<<grid, kPT, bytes, static_cast<cudaStream_t>(stream)>>>(p);
   return check_launch("vcb_mlp_pgd: launch");
 }
 
